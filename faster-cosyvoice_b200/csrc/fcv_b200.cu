@@ -1,0 +1,623 @@
+// fcv_b200.cu -- C ABI of the B200 DiT estimator (include/fcv_b200.h).
+//
+// One translation unit: the kernels live in the .cuh files included below and
+// share the device error word.  Host code here validates arguments, encodes
+// TMA tensor maps, picks tile shapes and launches; fcv_dit_forward is the
+// native executor of one estimator call (embed, 22 DiT blocks, output).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "fcv_b200.h"
+#include "fcv_common.cuh"
+#include "gemm.cuh"
+#include "attn.cuh"
+#include "rows.cuh"
+
+using namespace fcv;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+#define FCV_CUDA(expr)                                                                 \
+  do {                                                                                 \
+    cudaError_t e_ = (expr);                                                           \
+    if (e_ != cudaSuccess)                                                             \
+      return fail(FCV_ECUDA, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, \
+                  __LINE__);                                                           \
+  } while (0)
+
+#define FCV_LAUNCH_CHECK(name)                                                          \
+  do {                                                                                 \
+    cudaError_t e_ = cudaGetLastError();                                               \
+    if (e_ != cudaSuccess) return fail(FCV_ECUDA, "launch of %s failed: %s", name, cudaGetErrorString(e_)); \
+  } while (0)
+
+#define FCV_TRY(expr)      \
+  do {                     \
+    int s_ = (expr);       \
+    if (s_ != FCV_OK) return s_; \
+  } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+// ------------------------------------------------------------------ tensor maps
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                      const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                      const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                      CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PFN_encodeTiled_t encode_fn() {
+  static PFN_encodeTiled_t fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled_t>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor of `rows` x `cols` (row stride `ld` elements), box 64 x box_rows,
+// 128-byte swizzle, zero fill out of bounds.
+int make_tmap_bf16(CUtensorMap* m, const void* ptr, long rows, long cols, long ld, int box_rows) {
+  PFN_encodeTiled_t enc = encode_fn();
+  if (!enc) return fail(FCV_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || ((ld * 2) & 15))
+    return fail(FCV_EINVAL, "TMA operand must be 16-byte aligned with a 16-byte multiple row stride");
+  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), gdim, gstride, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FCV_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FCV_OK;
+}
+
+// ------------------------------------------------------------------ GEMM launch
+struct GemmCall {
+  const void* A;
+  long lda;        // elements
+  long a_rows;     // rows of A (M, or gapped rows in conv mode)
+  const void* W;   // (N, K)
+  const float* bias;
+  int M, N, K;
+  int conv;
+  EpiParams epi;
+};
+
+template <int BN, typename Tact>
+int launch_tc(const GemmCall& g, cudaStream_t s) {
+  using Cfg = TcGemmCfg<BN>;
+  CUtensorMap ta, tb;
+  const long a_cols = g.conv ? 1024 : g.K;
+  FCV_TRY(make_tmap_bf16(&ta, g.A, g.a_rows, a_cols, g.lda, 128));
+  FCV_TRY(make_tmap_bf16(&tb, g.W, g.N, g.K, g.K, BN));
+  TcGemmArgs args;
+  args.num_kb = g.conv ? 31 : (g.K + 63) / 64;
+  args.m_blocks = (g.M + 127) / 128;
+  args.n_blocks = (g.N + BN - 1) / BN;
+  args.conv = g.conv;
+  args.epi = g.epi;
+  const int tiles = args.m_blocks * args.n_blocks;
+  const int grid = std::min(tiles, num_sms());
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    FCV_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<BN, Tact>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Cfg::SMEM_BYTES));
+    attr_set[dev & 63] = true;
+  }
+  tc_gemm_kernel<BN, Tact><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, args);
+  FCV_LAUNCH_CHECK("tc_gemm_kernel");
+  return FCV_OK;
+}
+
+int run_gemm(const GemmCall& g, int dtype, cudaStream_t s, int force_bn = 0) {
+  if (g.M <= 0 || g.N <= 0) return FCV_OK;
+  if (dtype == FCV_DTYPE_BF16) {
+    if (g.conv) return launch_tc<64, bf16>(g, s);
+    if (g.K % 64 != 0) return fail(FCV_EUNSUPPORTED, "bf16 GEMM needs K %% 64 == 0 (K=%d)", g.K);
+    int bn = force_bn;
+    if (bn == 0) {
+      const long mb = (g.M + 127) / 128;
+      const long t256 = mb * ((g.N + 255) / 256);
+      bn = (g.N <= 128 || t256 < 2L * num_sms()) ? 128 : 256;
+    }
+    if (bn == 128) return launch_tc<128, bf16>(g, s);
+    return launch_tc<256, bf16>(g, s);
+  }
+  SimtGemmArgs a;
+  a.A = static_cast<const float*>(g.A);
+  a.lda = g.lda;
+  a.W = static_cast<const float*>(g.W);
+  a.M = g.M;
+  a.N = g.N;
+  a.K = g.K;
+  a.conv = g.conv;
+  a.epi = g.epi;
+  dim3 grid((g.N + 63) / 64, (g.M + 63) / 64);
+  simt_gemm_f32_kernel<<<grid, 256, 0, s>>>(a);
+  FCV_LAUNCH_CHECK("simt_gemm_f32_kernel");
+  return FCV_OK;
+}
+
+EpiParams make_epi(int epi, int M, int N, void* C, long ldc, const float* bias) {
+  EpiParams e;
+  memset(&e, 0, sizeof(e));
+  e.epi = epi;
+  e.M = M;
+  e.N = N;
+  e.C = C;
+  e.ldc = ldc;
+  e.bias = bias;
+  return e;
+}
+
+// ------------------------------------------------------------------ attention launch
+int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, const int32_t* tiles,
+                  int n_tiles, void* out, cudaStream_t s) {
+  if (n_tiles <= 0) return FCV_OK;
+  dim3 grid(n_tiles, FCV_HEADS);
+  const int2* t2 = reinterpret_cast<const int2*>(tiles);
+  if (dtype == FCV_DTYPE_BF16) {
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+      FCV_CUDA(cudaFuncSetAttribute(attn_bf16_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 49152));
+      attr[dev & 63] = true;
+    }
+    attn_bf16_mma_kernel<<<grid, 256, 49152, s>>>(static_cast<const bf16*>(qkv), cu, t2, chunk,
+                                                  static_cast<bf16*>(out));
+    FCV_LAUNCH_CHECK("attn_bf16_mma_kernel");
+  } else {
+    attn_f32_kernel<<<grid, 128, 0, s>>>(static_cast<const float*>(qkv), cu, t2, chunk,
+                                         static_cast<float*>(out));
+    FCV_LAUNCH_CHECK("attn_f32_kernel");
+  }
+  return FCV_OK;
+}
+
+template <typename Th, typename To>
+int launch_ln(const void* h, const float* shift, const float* scale, const int32_t* doc_ids, long stride,
+              int N, void* out, cudaStream_t s) {
+  if (N <= 0) return FCV_OK;
+  ln_modulate_kernel<Th, To><<<(N + 7) / 8, 256, 0, s>>>(static_cast<const Th*>(h), shift, scale, doc_ids,
+                                                        stride, N, static_cast<To*>(out));
+  FCV_LAUNCH_CHECK("ln_modulate_kernel");
+  return FCV_OK;
+}
+
+int run_ln(const void* h, int h_dtype, const float* shift, const float* scale, const int32_t* doc_ids,
+           long stride, int N, void* out, int out_dtype, cudaStream_t s) {
+  if (h_dtype == FCV_DTYPE_F32 && out_dtype == FCV_DTYPE_BF16)
+    return launch_ln<float, bf16>(h, shift, scale, doc_ids, stride, N, out, s);
+  if (h_dtype == FCV_DTYPE_F32 && out_dtype == FCV_DTYPE_F32)
+    return launch_ln<float, float>(h, shift, scale, doc_ids, stride, N, out, s);
+  if (h_dtype == FCV_DTYPE_BF16 && out_dtype == FCV_DTYPE_BF16)
+    return launch_ln<bf16, bf16>(h, shift, scale, doc_ids, stride, N, out, s);
+  if (h_dtype == FCV_DTYPE_BF16 && out_dtype == FCV_DTYPE_F32)
+    return launch_ln<bf16, float>(h, shift, scale, doc_ids, stride, N, out, s);
+  return fail(FCV_EINVAL, "unknown dtype");
+}
+
+bool valid_dtype(int d) { return d == FCV_DTYPE_F32 || d == FCV_DTYPE_BF16; }
+size_t dsize(int d) { return d == FCV_DTYPE_BF16 ? 2 : 4; }
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Workspace carve-up for fcv_dit_forward.
+struct Workspace {
+  float* temb;
+  void* silu;
+  float* mods;
+  float* h;
+  void* a_in;
+  void* gap0;
+  void* gap1;
+  void* norm;
+  void* qkv;
+  void* attn;
+  void* mid;
+  size_t total;
+};
+
+Workspace carve(uint8_t* base, int N, int B, int depth, int dtype) {
+  const size_t es = dsize(dtype);
+  const long G = (long)N + 30L * (B + 1);
+  const long MS = (long)depth * 6144 + 2048;
+  Workspace w;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    void* p = base ? base + off : nullptr;
+    off += align256(bytes);
+    return p;
+  };
+  w.temb = static_cast<float*>(take((size_t)B * 1024 * 4));
+  w.silu = take((size_t)std::max(B, 1) * 1024 * es);
+  w.mods = static_cast<float*>(take((size_t)B * MS * 4));
+  w.h = static_cast<float*>(take((size_t)N * 1024 * 4));
+  w.a_in = take((size_t)N * 320 * es);
+  w.gap0 = take((size_t)G * 1024 * es);
+  w.gap1 = take((size_t)G * 1024 * es);
+  w.norm = take((size_t)N * 1024 * es);
+  w.qkv = take((size_t)N * 3072 * es);
+  w.attn = take((size_t)N * 1024 * es);
+  w.mid = take((size_t)N * 2048 * es);
+  w.total = off;
+  return w;
+}
+
+template <typename T>
+int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Workspace& ws, cudaStream_t s) {
+  const int dtype = w->dtype;
+  const int N = bt->N, B = bt->B, depth = w->depth;
+  const long MS = (long)depth * 6144 + 2048;
+  const long G = (long)N + 30L * (B + 1);
+  const int G_rows = N + 30 * B;  // gapped rows that can hold data
+  const bool is_bf16 = dtype == FCV_DTYPE_BF16;
+
+  // 1. time embedding + all AdaLN projections (one GEMM, flashinfer_dit.py:430-445)
+  time_embed_kernel<T><<<B, 256, 0, s>>>(static_cast<const T*>(w->time_w1), w->time_b1,
+                                        static_cast<const T*>(w->time_w2), w->time_b2,
+                                        static_cast<const T*>(bt->t), is_bf16 ? 1 : 0, ws.temb,
+                                        static_cast<T*>(ws.silu));
+  FCV_LAUNCH_CHECK("time_embed_kernel");
+  {
+    GemmCall g{};
+    g.A = ws.silu; g.lda = 1024; g.a_rows = B; g.W = w->ada_w; g.M = B; g.N = (int)MS; g.K = 1024;
+    g.epi = make_epi(EPI_F32, B, (int)MS, ws.mods, MS, w->ada_b);
+    FCV_TRY(run_gemm(g, dtype, s));
+  }
+  if (N == 0) return FCV_OK;
+
+  // 2. input embedding: gather, proj (K=320), causal grouped conv x2 + Mish + residual
+  {
+    dim3 grid((bt->T + 31) / 32, B);
+    embed_gather_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(bt->x), static_cast<const T*>(bt->cond),
+                                                static_cast<const T*>(bt->mu), static_cast<const T*>(bt->spks),
+                                                bt->cu_seqlens, bt->T, static_cast<T*>(ws.a_in));
+    FCV_LAUNCH_CHECK("embed_gather_kernel");
+    zero_gap_rows_kernel<T><<<(unsigned)G, 128, 0, s>>>(bt->gap_rows, (int)G, static_cast<T*>(ws.gap0),
+                                                       static_cast<T*>(ws.gap1));
+    FCV_LAUNCH_CHECK("zero_gap_rows_kernel");
+    GemmCall g{};
+    g.A = ws.a_in; g.lda = 320; g.a_rows = N; g.W = w->in_w; g.M = N; g.N = 1024; g.K = 320;
+    g.epi = make_epi(EPI_EMBED_GAP, N, 1024, ws.gap0, 1024, w->in_b);
+    g.epi.aux = bt->doc_ids;
+    FCV_TRY(run_gemm(g, dtype, s));
+    GemmCall c1{};
+    c1.A = ws.gap0; c1.lda = 1024; c1.a_rows = G; c1.W = w->conv1_w; c1.M = G_rows; c1.N = 1024;
+    c1.K = 31 * 64; c1.conv = 1;
+    c1.epi = make_epi(EPI_MISH_GAP, G_rows, 1024, ws.gap1, 1024, w->conv1_b);
+    c1.epi.aux = bt->gap_rows;
+    FCV_TRY(run_gemm(c1, dtype, s));
+    GemmCall c2 = c1;
+    c2.A = ws.gap1; c2.W = w->conv2_w;
+    c2.epi = make_epi(EPI_MISH_RES, G_rows, 1024, ws.h, 1024, w->conv2_b);
+    c2.epi.aux = bt->gap_rows;
+    c2.epi.res = ws.gap0;
+    FCV_TRY(run_gemm(c2, dtype, s));
+  }
+
+  // 3. DiT blocks (flashinfer_dit.py:485-533; DiTBlock.forward modules.py:516-530)
+  const size_t es = dsize(dtype);
+  for (int i = 0; i < depth; ++i) {
+    const float* mi = ws.mods + (long)i * 6144;
+    FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mi + 0, mi + 1024, bt->doc_ids, MS, N, ws.norm, dtype, s));
+    GemmCall q{};
+    q.A = ws.norm; q.lda = 1024; q.a_rows = N; q.M = N; q.N = 3072; q.K = 1024;
+    q.W = static_cast<const uint8_t*>(w->qkv_w) + (size_t)i * 3072 * 1024 * es;
+    q.epi = make_epi(EPI_ROPE, N, 3072, ws.qkv, 3072, w->qkv_b + (long)i * 3072);
+    q.epi.aux = bt->positions;
+    q.epi.rope_cos = w->rope_cos;
+    q.epi.rope_sin = w->rope_sin;
+    FCV_TRY(run_gemm(q, dtype, s));
+    FCV_TRY(run_attention(ws.qkv, dtype, bt->cu_seqlens, bt->chunk, bt->attn_tiles, bt->n_attn_tiles,
+                          ws.attn, s));
+    GemmCall o{};
+    o.A = ws.attn; o.lda = 1024; o.a_rows = N; o.M = N; o.N = 1024; o.K = 1024;
+    o.W = static_cast<const uint8_t*>(w->o_w) + (size_t)i * 1024 * 1024 * es;
+    o.epi = make_epi(EPI_GATE_RES, N, 1024, ws.h, 1024, w->o_b + (long)i * 1024);
+    o.epi.aux = bt->doc_ids;
+    o.epi.gate = mi + 2048;
+    o.epi.gate_stride = MS;
+    FCV_TRY(run_gemm(o, dtype, s));
+    FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mi + 3072, mi + 4096, bt->doc_ids, MS, N, ws.norm, dtype, s));
+    GemmCall f1{};
+    f1.A = ws.norm; f1.lda = 1024; f1.a_rows = N; f1.M = N; f1.N = 2048; f1.K = 1024;
+    f1.W = static_cast<const uint8_t*>(w->ff1_w) + (size_t)i * 2048 * 1024 * es;
+    f1.epi = make_epi(EPI_GELU, N, 2048, ws.mid, 2048, w->ff1_b + (long)i * 2048);
+    FCV_TRY(run_gemm(f1, dtype, s));
+    GemmCall f2{};
+    f2.A = ws.mid; f2.lda = 2048; f2.a_rows = N; f2.M = N; f2.N = 1024; f2.K = 2048;
+    f2.W = static_cast<const uint8_t*>(w->ff2_w) + (size_t)i * 1024 * 2048 * es;
+    f2.epi = make_epi(EPI_GATE_RES, N, 1024, ws.h, 1024, w->ff2_b + (long)i * 1024);
+    f2.epi.aux = bt->doc_ids;
+    f2.epi.gate = mi + 5120;
+    f2.epi.gate_stride = MS;
+    FCV_TRY(run_gemm(f2, dtype, s));
+  }
+
+  // 4. final AdaLN (chunk order scale, shift: modules.py:260-265), proj_out, unpack
+  const float* mf = ws.mods + (long)depth * 6144;
+  FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mf + 1024, mf + 0, bt->doc_ids, MS, N, ws.norm, dtype, s));
+  zero_padding_kernel<T><<<std::max(1, std::min(4096, (int)(((long)B * 80 * bt->T + 255) / 256))), 256, 0, s>>>(
+      bt->cu_seqlens, B, bt->T, static_cast<T*>(bt->out));
+  FCV_LAUNCH_CHECK("zero_padding_kernel");
+  GemmCall po{};
+  po.A = ws.norm; po.lda = 1024; po.a_rows = N; po.M = N; po.N = 80; po.K = 1024; po.W = w->out_w;
+  po.epi = make_epi(EPI_UNPACK, N, 80, bt->out, 0, w->out_b);
+  po.epi.aux = bt->doc_ids;
+  po.epi.aux2 = bt->positions;
+  po.epi.T = bt->T;
+  FCV_TRY(run_gemm(po, dtype, s));
+  return FCV_OK;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+
+extern "C" {
+
+int fcv_version(void) { return 1; }
+
+const char* fcv_last_error(void) { return t_last_error.c_str(); }
+
+int fcv_device_error(int* code, void* stream) {
+  if (!code) return fail(FCV_EINVAL, "code is null");
+  FCV_CUDA(cudaStreamSynchronize(as_stream(stream)));
+  int v = 0;
+  FCV_CUDA(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+  const int zero = 0;
+  FCV_CUDA(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+  *code = v;
+  return FCV_OK;
+}
+
+int fcv_mask_lengths(const void* mask, int dtype, int B, int T, int32_t* lengths, void* stream) {
+  if (!mask || !lengths || B < 0 || T < 0) return fail(FCV_EINVAL, "fcv_mask_lengths: bad arguments");
+  if (!valid_dtype(dtype)) return fail(FCV_EINVAL, "fcv_mask_lengths: bad dtype");
+  if (B == 0) return FCV_OK;
+  if (dtype == FCV_DTYPE_BF16)
+    mask_lengths_kernel<bf16><<<B, 256, 0, as_stream(stream)>>>(static_cast<const bf16*>(mask), T, lengths);
+  else
+    mask_lengths_kernel<float><<<B, 256, 0, as_stream(stream)>>>(static_cast<const float*>(mask), T, lengths);
+  FCV_LAUNCH_CHECK("mask_lengths_kernel");
+  return FCV_OK;
+}
+
+int fcv_pack_layout(const int32_t* lengths, int B, int T, int max_rows, int64_t* gather, int32_t* doc_ids,
+                    int32_t* positions, int32_t* cu_seqlens, int32_t* gap_rows, void* stream) {
+  if (!lengths || !doc_ids || !positions || !cu_seqlens || B < 1 || T < 0 || max_rows < 0)
+    return fail(FCV_EINVAL, "fcv_pack_layout: bad arguments");
+  cudaStream_t s = as_stream(stream);
+  lengths_scan_kernel<<<1, 1024, 0, s>>>(lengths, B, cu_seqlens);
+  FCV_LAUNCH_CHECK("lengths_scan_kernel");
+  const long work = std::max<long>((long)max_rows + 30L * (B + 1), 1);
+  const int grid = (int)std::min<long>((work + 255) / 256, 8L * num_sms());
+  layout_fill_kernel<<<grid, 256, 0, s>>>(cu_seqlens, B, T, max_rows, gather, doc_ids, positions, gap_rows);
+  FCV_LAUNCH_CHECK("layout_fill_kernel");
+  return FCV_OK;
+}
+
+int fcv_unpack_output(const void* packed, int dtype, const int32_t* cu_seqlens, int B, int T, int N, void* out,
+                      void* stream) {
+  (void)N;
+  if (!packed || !cu_seqlens || !out || B < 0 || T < 0) return fail(FCV_EINVAL, "fcv_unpack_output: bad arguments");
+  if (!valid_dtype(dtype)) return fail(FCV_EINVAL, "fcv_unpack_output: bad dtype");
+  const long total = (long)B * 80 * T;
+  if (total == 0) return FCV_OK;
+  const int grid = (int)std::min<long>((total + 255) / 256, 4096);
+  if (dtype == FCV_DTYPE_BF16)
+    unpack_kernel<bf16><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const bf16*>(packed), cu_seqlens, B, T,
+                                                            static_cast<bf16*>(out));
+  else
+    unpack_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const float*>(packed), cu_seqlens, B, T,
+                                                             static_cast<float*>(out));
+  FCV_LAUNCH_CHECK("unpack_kernel");
+  return FCV_OK;
+}
+
+int fcv_ln_modulate(const void* h, int h_dtype, const float* shift, const float* scale, const int32_t* doc_ids,
+                    long mod_stride, int N, void* out, int out_dtype, void* stream) {
+  if (!h || !shift || !scale || !doc_ids || !out || N < 0) return fail(FCV_EINVAL, "fcv_ln_modulate: bad arguments");
+  if (!valid_dtype(h_dtype) || !valid_dtype(out_dtype)) return fail(FCV_EINVAL, "fcv_ln_modulate: bad dtype");
+  if ((mod_stride & 3) || (reinterpret_cast<uintptr_t>(shift) & 15) || (reinterpret_cast<uintptr_t>(scale) & 15))
+    return fail(FCV_EINVAL, "fcv_ln_modulate: modulation rows must be 16-byte aligned");
+  return run_ln(h, h_dtype, shift, scale, doc_ids, mod_stride, N, out, out_dtype, as_stream(stream));
+}
+
+int fcv_gate_res_ln_modulate(const void* h, const float* gate, const void* r, const float* shift, const float* scale,
+                             const int32_t* doc_ids, long mod_stride, int N, void* h_out, void* norm, int dtype,
+                             void* stream) {
+  if (!h || !gate || !r || !shift || !scale || !doc_ids || !h_out || !norm || N < 0)
+    return fail(FCV_EINVAL, "fcv_gate_res_ln_modulate: bad arguments");
+  if (!valid_dtype(dtype)) return fail(FCV_EINVAL, "fcv_gate_res_ln_modulate: bad dtype");
+  if ((mod_stride & 3) || (reinterpret_cast<uintptr_t>(shift) & 15) || (reinterpret_cast<uintptr_t>(scale) & 15))
+    return fail(FCV_EINVAL, "fcv_gate_res_ln_modulate: modulation rows must be 16-byte aligned");
+  if (N == 0) return FCV_OK;
+  cudaStream_t s = as_stream(stream);
+  if (dtype == FCV_DTYPE_BF16)
+    gate_res_ln_modulate_kernel<bf16><<<(N + 7) / 8, 256, 0, s>>>(
+        static_cast<const bf16*>(h), gate, static_cast<const bf16*>(r), shift, scale, doc_ids, mod_stride, N,
+        static_cast<bf16*>(h_out), static_cast<bf16*>(norm));
+  else
+    gate_res_ln_modulate_kernel<float><<<(N + 7) / 8, 256, 0, s>>>(
+        static_cast<const float*>(h), gate, static_cast<const float*>(r), shift, scale, doc_ids, mod_stride, N,
+        static_cast<float*>(h_out), static_cast<float*>(norm));
+  FCV_LAUNCH_CHECK("gate_res_ln_modulate_kernel");
+  return FCV_OK;
+}
+
+int fcv_gemm(const void* A, const void* W, const float* bias, int M, int Nout, int K, int dtype, int epi, void* C,
+             const int32_t* aux_i32, const float* gate, long gate_stride, const float* rope_cos,
+             const float* rope_sin, void* stream) {
+  if (!A || !W || !C || M < 0 || Nout <= 0 || K <= 0) return fail(FCV_EINVAL, "fcv_gemm: bad arguments");
+  if (!valid_dtype(dtype)) return fail(FCV_EINVAL, "fcv_gemm: bad dtype");
+  int internal;
+  switch (epi) {
+    case FCV_EPI_BIAS: internal = EPI_BIAS; break;
+    case FCV_EPI_BIAS_GELU: internal = EPI_GELU; break;
+    case FCV_EPI_BIAS_ROPE_QKV:
+      if (!aux_i32 || !rope_cos || !rope_sin) return fail(FCV_EINVAL, "fcv_gemm: RoPE needs positions and tables");
+      if (Nout != 3072) return fail(FCV_EINVAL, "fcv_gemm: RoPE epilogue expects Nout = 3072");
+      internal = EPI_ROPE;
+      break;
+    case FCV_EPI_BIAS_GATE_RES:
+      if (!aux_i32 || !gate) return fail(FCV_EINVAL, "fcv_gemm: gated residual needs doc_ids and gate");
+      if ((gate_stride & 3) || (reinterpret_cast<uintptr_t>(gate) & 15) || (Nout & 3))
+        return fail(FCV_EINVAL, "fcv_gemm: gate rows must be 16-byte aligned");
+      internal = EPI_GATE_RES;
+      break;
+    case FCV_EPI_BIAS_F32: internal = EPI_F32; break;
+    default: return fail(FCV_EINVAL, "fcv_gemm: unknown epilogue %d", epi);
+  }
+  const bool f32_out = internal == EPI_GATE_RES || internal == EPI_F32;
+  const size_t out_es = f32_out ? 4 : dsize(dtype);
+  if (((size_t)Nout * out_es) % 16 != 0 || (reinterpret_cast<uintptr_t>(C) & 15))
+    return fail(FCV_EINVAL, "fcv_gemm: output rows must be 16-byte aligned");
+  GemmCall g{};
+  g.A = A; g.lda = K; g.a_rows = M; g.W = W; g.M = M; g.N = Nout; g.K = K;
+  g.epi = make_epi(internal, M, Nout, C, Nout, bias);
+  g.epi.aux = aux_i32;
+  g.epi.gate = gate;
+  g.epi.gate_stride = gate_stride;
+  g.epi.rope_cos = rope_cos;
+  g.epi.rope_sin = rope_sin;
+  return run_gemm(g, dtype, as_stream(stream));
+}
+
+int fcv_attention(const void* qkv, int dtype, const int32_t* cu_seqlens, int B, int max_len, int chunk,
+                  const int32_t* tiles, int n_tiles, void* out, void* stream) {
+  (void)B;
+  (void)max_len;
+  if (!qkv || !cu_seqlens || !out || (n_tiles > 0 && !tiles) || chunk < 0)
+    return fail(FCV_EINVAL, "fcv_attention: bad arguments");
+  if (!valid_dtype(dtype)) return fail(FCV_EINVAL, "fcv_attention: bad dtype");
+  return run_attention(qkv, dtype, cu_seqlens, chunk, tiles, n_tiles, out, as_stream(stream));
+}
+
+int fcv_attn_tiles(const int32_t* lengths_host, int B, int chunk, int32_t* tiles, int cap) {
+  if (!lengths_host || !tiles || B < 0 || cap < 0 || chunk < 0) return fail(FCV_EINVAL, "fcv_attn_tiles: bad arguments");
+  struct Item {
+    long cost;
+    int doc, q0;
+  };
+  std::vector<Item> items;
+  for (int d = 0; d < B; ++d) {
+    const int L = lengths_host[d];
+    if (L < 0) return fail(FCV_EINVAL, "fcv_attn_tiles: negative length");
+    for (int q0 = 0; q0 < L; q0 += kAttnQTile) {
+      const int rows = std::min(kAttnQTile, L - q0);
+      const int q_last = q0 + rows - 1;
+      const int kv = chunk > 0 ? std::min(L, (q_last / chunk + 1) * chunk) : L;
+      items.push_back({(long)rows * kv, d, q0});
+    }
+  }
+  if ((int)items.size() > cap) return fail(FCV_EINVAL, "fcv_attn_tiles: capacity %d < %zu tiles", cap, items.size());
+  std::stable_sort(items.begin(), items.end(), [](const Item& a, const Item& b) { return a.cost > b.cost; });
+  for (size_t i = 0; i < items.size(); ++i) {
+    tiles[2 * i] = items[i].doc;
+    tiles[2 * i + 1] = items[i].q0;
+  }
+  return (int)items.size();
+}
+
+int fcv_time_embed(const fcv_dit_weights* w, const void* t, int B, float* temb, void* silu_act, void* stream) {
+  if (!w || !t || !temb || !silu_act || B < 0) return fail(FCV_EINVAL, "fcv_time_embed: bad arguments");
+  if (!valid_dtype(w->dtype)) return fail(FCV_EINVAL, "fcv_time_embed: bad dtype");
+  if (B == 0) return FCV_OK;
+  cudaStream_t s = as_stream(stream);
+  if (w->dtype == FCV_DTYPE_BF16)
+    time_embed_kernel<bf16><<<B, 256, 0, s>>>(static_cast<const bf16*>(w->time_w1), w->time_b1,
+                                             static_cast<const bf16*>(w->time_w2), w->time_b2,
+                                             static_cast<const bf16*>(t), 1, temb, static_cast<bf16*>(silu_act));
+  else
+    time_embed_kernel<float><<<B, 256, 0, s>>>(static_cast<const float*>(w->time_w1), w->time_b1,
+                                              static_cast<const float*>(w->time_w2), w->time_b2,
+                                              static_cast<const float*>(t), 0, temb, static_cast<float*>(silu_act));
+  FCV_LAUNCH_CHECK("time_embed_kernel");
+  return FCV_OK;
+}
+
+int fcv_cfg_euler(float* x, const void* d, int d_dtype, int R, int T, float dt, float cfg_rate, void* x_next,
+                  void* stream) {
+  if (!x || !d || R < 0 || T < 0) return fail(FCV_EINVAL, "fcv_cfg_euler: bad arguments");
+  if (!valid_dtype(d_dtype)) return fail(FCV_EINVAL, "fcv_cfg_euler: bad dtype");
+  const long per = 80L * T;
+  const long total = (long)R * per;
+  if (total == 0) return FCV_OK;
+  const int grid = (int)std::min<long>((total + 255) / 256, 8L * num_sms());
+  if (d_dtype == FCV_DTYPE_BF16)
+    cfg_euler_kernel<bf16><<<grid, 256, 0, as_stream(stream)>>>(x, static_cast<const bf16*>(d), R, per, dt, cfg_rate,
+                                                               static_cast<bf16*>(x_next));
+  else
+    cfg_euler_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(x, static_cast<const float*>(d), R, per, dt, cfg_rate,
+                                                                static_cast<float*>(x_next));
+  FCV_LAUNCH_CHECK("cfg_euler_kernel");
+  return FCV_OK;
+}
+
+size_t fcv_dit_workspace_bytes(int N, int B, int depth, int dtype) {
+  if (N < 0 || B < 0 || depth < 0 || !valid_dtype(dtype)) return 0;
+  return carve(nullptr, N, B, depth, dtype).total;
+}
+
+int fcv_dit_forward(const fcv_dit_weights* w, const fcv_dit_batch* bt, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  if (!w || !bt || !workspace) return fail(FCV_EINVAL, "fcv_dit_forward: null argument");
+  if (!valid_dtype(w->dtype)) return fail(FCV_EINVAL, "fcv_dit_forward: bad dtype");
+  if (w->depth < 1) return fail(FCV_EINVAL, "fcv_dit_forward: depth must be >= 1");
+  if (bt->B < 1 || bt->T < 1 || bt->N < 0 || bt->N > bt->B * bt->T || bt->chunk < 0)
+    return fail(FCV_EINVAL, "fcv_dit_forward: bad batch geometry B=%d T=%d N=%d", bt->B, bt->T, bt->N);
+  if (bt->max_len > w->rope_max_len)
+    return fail(FCV_EUNSUPPORTED, "fcv_dit_forward: document of %d frames exceeds the RoPE table (%d)", bt->max_len,
+                w->rope_max_len);
+  if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(FCV_EINVAL, "fcv_dit_forward: workspace must be 256-byte aligned");
+  Workspace ws = carve(static_cast<uint8_t*>(workspace), bt->N, bt->B, w->depth, w->dtype);
+  if (ws.total > workspace_bytes)
+    return fail(FCV_EINVAL, "fcv_dit_forward: workspace of %zu bytes < %zu needed", workspace_bytes, ws.total);
+  cudaStream_t s = as_stream(stream);
+  if (w->dtype == FCV_DTYPE_BF16) return forward_impl<bf16>(w, bt, ws, s);
+  return forward_impl<float>(w, bt, ws, s);
+}
+
+}  // extern "C"

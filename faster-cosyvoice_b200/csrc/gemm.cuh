@@ -1,0 +1,446 @@
+// gemm.cuh -- GEMMs of the DiT estimator with fused epilogues.
+//
+//   bf16: persistent tcgen05 kernel.  One CTA per SM, 6 warps:
+//         warp 0 issues TMA loads of A/B k-blocks into a multi-stage ring,
+//         warp 1 owns TMEM and issues tcgen05.mma (128 x BN x 16) into one of
+//         two TMEM accumulators, warps 2-5 drain the other accumulator with
+//         tcgen05.ld and run the epilogue (bias, GELU, partial RoPE, gated
+//         residual, Mish, unpack) straight to global memory.
+//   f32:  CUDA-core FFMA tiles with the same epilogues (the exact-fp32 mode;
+//         tcgen05 has no fp32-input kind).
+//
+// "Conv" mode turns the kernel into the implicit GEMM of the causal grouped
+// position convolution (modules.py:115-144): A is a *gapped* activation
+// buffer in which each document is preceded by 30 zero rows, output tile
+// column block g (64 wide) is convolution group g, and k-block t (64 wide) is
+// tap t, whose A tile is the same 64 columns shifted by t - 30 rows.
+#pragma once
+
+#include "fcv_common.cuh"
+
+namespace fcv {
+
+enum Epi : int {
+  EPI_BIAS = 0,       // C(act) = acc + b
+  EPI_GELU = 1,       // C(act) = gelu_tanh(acc + b)
+  EPI_ROPE = 2,       // C(act) = acc + b with partial RoPE on columns [0,64) and [1024,1088)
+  EPI_GATE_RES = 3,   // h(f32)[row] += gate[doc] * (acc + b)
+  EPI_F32 = 4,        // C(f32) = acc + b
+  EPI_EMBED_GAP = 5,  // C(act)[row + 30*(doc+1)] = acc + b   (embed -> gapped buffer)
+  EPI_MISH_GAP = 6,   // gapped row g: C(act)[g] = mish(acc + b) unless gap_rows[g] < 0
+  EPI_MISH_RES = 7,   // gapped row g, packed p = gap_rows[g] >= 0: h(f32)[p] = mish(acc+b) + res[g]
+  EPI_UNPACK = 8,     // out(act)[doc, col, pos] = acc + b   (proj_out -> (B, 80, T))
+};
+
+constexpr int kConvPad = 30;  // kernel_size - 1 zero rows before every document
+
+struct EpiParams {
+  int epi;
+  int M, N;            // rows of A / columns of C
+  void* C;
+  long ldc;            // elements
+  const float* bias;   // may be null
+  const int32_t* aux;  // positions (ROPE), doc_ids (GATE_RES, EMBED_GAP, UNPACK), gap_rows (MISH_*)
+  const int32_t* aux2; // positions (UNPACK)
+  const void* res;     // gapped residual rows (MISH_RES), act dtype, row stride 1024
+  const float* gate;
+  long gate_stride;
+  const float* rope_cos;
+  const float* rope_sin;
+  int T;               // padded length (UNPACK)
+};
+
+// Apply the epilogue to W consecutive columns [col0, col0+W) of one row.
+// W is even and col0 is a multiple of W, so RoPE pairs (2j, 2j+1) never split.
+template <typename Tact, int W>
+__device__ __forceinline__ void epilogue_apply(const EpiParams& p, int row, int col0, float* v) {
+  if (row >= p.M) return;
+  const bool full = (col0 + W) <= p.N;
+  if (p.bias != nullptr) {
+#pragma unroll
+    for (int j = 0; j < W; ++j)
+      if (full || col0 + j < p.N) v[j] += __ldg(p.bias + col0 + j);
+  }
+  int out_row = row;
+  switch (p.epi) {
+    case EPI_GELU:
+#pragma unroll
+      for (int j = 0; j < W; ++j) v[j] = gelu_tanh(v[j]);
+      break;
+    case EPI_ROPE: {
+      const int c = col0 & 1023;
+      if (col0 < 2048 && c < 64) {
+        const int pos = __ldg(p.aux + row);
+#pragma unroll
+        for (int j = 0; j < W; j += 2) {
+          const int i = (c + j) >> 1;
+          if (c + j < 64) {
+            const float cs = __ldg(p.rope_cos + (long)pos * 32 + i);
+            const float sn = __ldg(p.rope_sin + (long)pos * 32 + i);
+            const float a = v[j], b = v[j + 1];
+            v[j] = a * cs - b * sn;
+            v[j + 1] = b * cs + a * sn;
+          }
+        }
+      }
+      break;
+    }
+    case EPI_GATE_RES: {
+      const int doc = __ldg(p.aux + row);
+      const float* g = p.gate + (long)doc * p.gate_stride + col0;
+      float* h = reinterpret_cast<float*>(p.C) + (long)row * p.ldc + col0;
+      if (full && W % 4 == 0) {
+#pragma unroll
+        for (int j = 0; j < W; j += 4) {
+          const float4 gv = __ldg(reinterpret_cast<const float4*>(g + j));
+          float4 hv = *reinterpret_cast<float4*>(h + j);
+          hv.x += gv.x * v[j];
+          hv.y += gv.y * v[j + 1];
+          hv.z += gv.z * v[j + 2];
+          hv.w += gv.w * v[j + 3];
+          *reinterpret_cast<float4*>(h + j) = hv;
+        }
+      } else {
+        for (int j = 0; j < W; ++j)
+          if (col0 + j < p.N) h[j] += g[j] * v[j];
+      }
+      return;
+    }
+    case EPI_F32: {
+      float* c = reinterpret_cast<float*>(p.C) + (long)row * p.ldc + col0;
+      if (full && W % 4 == 0) {
+#pragma unroll
+        for (int j = 0; j < W; j += 4)
+          *reinterpret_cast<float4*>(c + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      } else {
+        for (int j = 0; j < W; ++j)
+          if (col0 + j < p.N) c[j] = v[j];
+      }
+      return;
+    }
+    case EPI_EMBED_GAP:
+      out_row = row + kConvPad * (__ldg(p.aux + row) + 1);
+      break;
+    case EPI_MISH_GAP:
+      if (__ldg(p.aux + row) < 0) return;
+#pragma unroll
+      for (int j = 0; j < W; ++j) v[j] = mish(v[j]);
+      break;
+    case EPI_MISH_RES: {
+      const int pr = __ldg(p.aux + row);
+      if (pr < 0) return;
+      const Tact* r = reinterpret_cast<const Tact*>(p.res) + (long)row * 1024 + col0;
+      float* h = reinterpret_cast<float*>(p.C) + (long)pr * p.ldc + col0;
+#pragma unroll
+      for (int j = 0; j < W; ++j) h[j] = mish(v[j]) + to_f<Tact>(r[j]);
+      return;
+    }
+    case EPI_UNPACK: {
+      const int doc = __ldg(p.aux + row);
+      const int pos = __ldg(p.aux2 + row);
+      Tact* o = reinterpret_cast<Tact*>(p.C) + (long)doc * p.N * p.T + pos;
+#pragma unroll
+      for (int j = 0; j < W; ++j)
+        if (col0 + j < p.N) o[(long)(col0 + j) * p.T] = from_f<Tact>(v[j]);
+      return;
+    }
+    default:
+      break;
+  }
+  // plain activation store at out_row
+  Tact* c = reinterpret_cast<Tact*>(p.C) + (long)out_row * p.ldc + col0;
+  if constexpr (sizeof(Tact) == 2) {
+    if (full && W % 8 == 0) {
+#pragma unroll
+      for (int j = 0; j < W; j += 8) {
+        uint4 u;
+        u.x = pack_bf16x2(v[j], v[j + 1]);
+        u.y = pack_bf16x2(v[j + 2], v[j + 3]);
+        u.z = pack_bf16x2(v[j + 4], v[j + 5]);
+        u.w = pack_bf16x2(v[j + 6], v[j + 7]);
+        *reinterpret_cast<uint4*>(c + j) = u;
+      }
+      return;
+    }
+  } else {
+    if (full && W % 4 == 0) {
+#pragma unroll
+      for (int j = 0; j < W; j += 4)
+        *reinterpret_cast<float4*>(c + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      return;
+    }
+  }
+  for (int j = 0; j < W; ++j)
+    if (col0 + j < p.N) c[j] = from_f<Tact>(v[j]);
+}
+
+// ============================================================== tcgen05 GEMM
+
+struct TcGemmArgs {
+  int num_kb;      // k-blocks of 64
+  int m_blocks;
+  int n_blocks;
+  int conv;        // implicit-conv A addressing
+  EpiParams epi;
+};
+
+template <int BN>
+struct TcGemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int THREADS = 192;
+};
+
+template <int BN, typename Tact>
+__global__ void __launch_bounds__(192, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const TcGemmArgs args) {
+  using Cfg = TcGemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* bar_area = smem + STAGES * Cfg::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 4);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = args.m_blocks * args.n_blocks;
+  const uint32_t smem_base = smem_u32(smem);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      long issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m_blk = tile / args.n_blocks;
+        const int n_blk = tile - m_blk * args.n_blocks;
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, 101, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_base + stage * Cfg::STAGE_BYTES;
+          const uint32_t sb = sa + Cfg::A_BYTES;
+          const uint32_t fb = smem_u32(&full[stage]);
+          mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+          int ax, ay;
+          if (args.conv) {
+            ax = n_blk * 64;
+            ay = m_blk * 128 + kb - kConvPad;
+          } else {
+            ax = kb * 64;
+            ay = m_blk * 128;
+          }
+          tma_load_2d(sa, &tmA, fb, ax, ay);
+          tma_load_2d(sb, &tmB, fb, kb * 64, n_blk * BN);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain the loads that may still be in flight before the CTA exits.
+        long n = issued < STAGES ? issued : STAGES;
+        int s = stage;
+        uint32_t ph = phase;
+        for (long i = 0; i < n; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          mbar_wait(smem_u32(&full[s]), ph, 102, nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc = idesc_bf16_f32(128, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, 103, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, 104, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_base + stage * Cfg::STAGE_BYTES;
+          const uint32_t sb = sa + Cfg::A_BYTES;
+          const uint64_t da = sdesc_sw128(sa);
+          const uint64_t db = sdesc_sw128(sb);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            // +32 bytes per 16-element K step inside the 128-byte swizzle atom
+            umma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          }
+          umma_commit(smem_u32(&empty[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&tfull[acc]));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // Make sure no MMA is still writing TMEM when the CTA tears down.
+      umma_commit(smem_u32(drain));
+      mbar_wait(smem_u32(drain), 0, 105, nullptr);
+    }
+  } else {
+    // ---------------- epilogue warps 2..5 (TMEM lane quarter = warp % 4)
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m_blk = tile / args.n_blocks;
+      const int n_blk = tile - m_blk * args.n_blocks;
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, 106, abort_flag)) break;
+      tc_fence_after();
+      const int row = m_blk * 128 + q * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c * 32, r);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        const int col0 = n_blk * BN + c * 32;
+        if (col0 < args.epi.N) epilogue_apply<Tact, 32>(args.epi, row, col0, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ============================================================== fp32 SIMT GEMM
+
+struct SimtGemmArgs {
+  const float* A;
+  long lda;
+  const float* W;  // (N, K) row-major
+  int M, N, K;
+  int conv;        // implicit-conv A addressing (K = 31*64, N tile = one group)
+  EpiParams epi;
+};
+
+// 64x64 tile, 256 threads, 4x4 outputs per thread (4 consecutive columns).
+__global__ void __launch_bounds__(256) simt_gemm_f32_kernel(const SimtGemmArgs a) {
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64 + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  const int lr = threadIdx.x >> 2;        // 0..63 (row of the tile being loaded)
+  const int lk = (threadIdx.x & 3) * 4;   // 0,4,8,12
+  for (int k0 = 0; k0 < a.K; k0 += 16) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = k0 + lk + j;
+      // A element
+      float av = 0.f;
+      const int m = m0 + lr;
+      if (m < a.M && k < a.K) {
+        if (a.conv) {
+          const int tap = k >> 6, ci = k & 63;
+          const int r = m + tap - kConvPad;
+          if (r >= 0) av = a.A[(long)r * a.lda + blockIdx.x * 64 + ci];
+        } else {
+          av = a.A[(long)m * a.lda + k];
+        }
+      }
+      As[lk + j][lr] = av;
+      float bv = 0.f;
+      const int n = n0 + lr;
+      if (n < a.N && k < a.K) bv = a.W[(long)n * a.K + k];
+      Bs[lk + j][lr] = bv;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float ar[4], br[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ar[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) br[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  const int col0 = n0 + tx * 4;
+  if (col0 >= a.N) return;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) epilogue_apply<float, 4>(a.epi, m0 + ty * 4 + i, col0, acc[i]);
+}
+
+}  // namespace fcv

@@ -1,0 +1,353 @@
+// rows.cuh -- HBM-bound kernels of the estimator: pack layout, LayerNorm +
+// AdaLN modulation, input gather, time embedding, unpack and the fused
+// CFG + Euler update.  All are vectorised (16-byte accesses), one warp per
+// 1024-wide row where a row reduction is needed (warp-shuffle sums).
+#pragma once
+
+#include "fcv_common.cuh"
+
+namespace fcv {
+
+// ------------------------------------------------------------------ layout
+
+template <typename T>
+__global__ void mask_lengths_kernel(const T* __restrict__ mask, int T_, int32_t* __restrict__ lengths) {
+  const int b = blockIdx.x;
+  int cnt = 0;
+  for (int i = threadIdx.x; i < T_; i += blockDim.x) cnt += to_f<T>(mask[(long)b * T_ + i]) > 0.5f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  __shared__ int part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = cnt;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int w = 0; w < (blockDim.x + 31) / 32; ++w) s += part[w];
+    lengths[b] = s;
+  }
+}
+
+// cu_seqlens = [0, cumsum(lengths)] with one CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) lengths_scan_kernel(const int32_t* __restrict__ lengths, int B,
+                                                            int32_t* __restrict__ cu) {
+  __shared__ int part[1024];
+  const int per = (B + 1023) / 1024;
+  const int b0 = threadIdx.x * per;
+  int s = 0;
+  for (int i = 0; i < per; ++i)
+    if (b0 + i < B) s += lengths[b0 + i];
+  part[threadIdx.x] = s;
+  __syncthreads();
+  // Hillis-Steele inclusive scan over the 1024 partial sums
+  for (int off = 1; off < 1024; off <<= 1) {
+    const int v = threadIdx.x >= off ? part[threadIdx.x - off] : 0;
+    __syncthreads();
+    part[threadIdx.x] += v;
+    __syncthreads();
+  }
+  int run = threadIdx.x == 0 ? 0 : part[threadIdx.x - 1];
+  if (threadIdx.x == 0) cu[0] = 0;
+  for (int i = 0; i < per; ++i) {
+    if (b0 + i < B) {
+      run += lengths[b0 + i];
+      cu[b0 + i + 1] = run;
+    }
+  }
+}
+
+// Largest d in [0, B) with key(d) <= v (key monotone non-decreasing, key(0) <= v).
+template <typename F>
+__device__ __forceinline__ int upper_doc(int B, int v, F key) {
+  int lo = 0, hi = B - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (key(mid) <= v) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Packed-row indices and the gapped-row map.  Rows n < N (N = cu[B]):
+// doc_ids, positions, gather.  Gapped rows g < N + 30*(B+1): gap_rows.
+__global__ void layout_fill_kernel(const int32_t* __restrict__ cu, int B, int T_, int max_rows,
+                                   int64_t* __restrict__ gather, int32_t* __restrict__ doc_ids,
+                                   int32_t* __restrict__ positions, int32_t* __restrict__ gap_rows) {
+  const int N = cu[B];
+  const int G = N + 30 * (B + 1);
+  const int stride = gridDim.x * blockDim.x;
+  for (int n = blockIdx.x * blockDim.x + threadIdx.x; n < N && n < max_rows; n += stride) {
+    // docs of length zero share a cu value; the owner is the last doc with cu[d] <= n
+    const int d = upper_doc(B, n, [&](int i) { return cu[i]; });
+    const int p = n - cu[d];
+    doc_ids[n] = d;
+    positions[n] = p;
+    if (gather) gather[n] = (int64_t)d * T_ + p;
+  }
+  if (gap_rows) {
+    for (int g = blockIdx.x * blockDim.x + threadIdx.x; g < G && g < max_rows + 30 * (B + 1); g += stride) {
+      // document d's real rows start at gapped row cu[d] + 30*(d+1)
+      int out = -1;
+      if (g >= 30) {
+        const int d = upper_doc(B, g, [&](int i) { return cu[i] + 30 * (i + 1) - 30; });
+        const int start = cu[d] + 30 * (d + 1);
+        const int len = cu[d + 1] - cu[d];
+        if (g >= start && g < start + len) out = cu[d] + (g - start);
+      }
+      gap_rows[g] = out;
+    }
+  }
+}
+
+// Zero the gap rows (gap_rows[g] < 0) of a gapped activation buffer.
+template <typename T>
+__global__ void zero_gap_rows_kernel(const int32_t* __restrict__ gap_rows, int G, T* __restrict__ buf0,
+                                     T* __restrict__ buf1) {
+  const int g = blockIdx.x;
+  if (g >= G || gap_rows[g] >= 0) return;
+  for (int c = threadIdx.x; c < 1024; c += blockDim.x) {
+    buf0[(long)g * 1024 + c] = from_f<T>(0.f);
+    if (buf1) buf1[(long)g * 1024 + c] = from_f<T>(0.f);
+  }
+}
+
+// ------------------------------------------------------------------ LayerNorm + modulation
+
+// Loads the 32 values of `row` that lane `lane` owns: columns i*256 + lane*8 + [0,8), i < 4.
+template <typename T>
+__device__ __forceinline__ void load_row32(const T* row, int lane, float (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = i * 256 + lane * 8;
+    if constexpr (sizeof(T) == 2) {
+      const uint4 u = *reinterpret_cast<const uint4*>(row + c);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[k]);
+        const float2 f = __bfloat1622float2(b);
+        v[i * 8 + 2 * k] = f.x;
+        v[i * 8 + 2 * k + 1] = f.y;
+      }
+    } else {
+      const float4 a = *reinterpret_cast<const float4*>(row + c);
+      const float4 b = *reinterpret_cast<const float4*>(row + c + 4);
+      v[i * 8 + 0] = a.x; v[i * 8 + 1] = a.y; v[i * 8 + 2] = a.z; v[i * 8 + 3] = a.w;
+      v[i * 8 + 4] = b.x; v[i * 8 + 5] = b.y; v[i * 8 + 6] = b.z; v[i * 8 + 7] = b.w;
+    }
+  }
+}
+template <typename T>
+__device__ __forceinline__ void store_row32(T* row, int lane, const float (&v)[32]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = i * 256 + lane * 8;
+    if constexpr (sizeof(T) == 2) {
+      uint4 u;
+      u.x = pack_bf16x2(v[i * 8 + 0], v[i * 8 + 1]);
+      u.y = pack_bf16x2(v[i * 8 + 2], v[i * 8 + 3]);
+      u.z = pack_bf16x2(v[i * 8 + 4], v[i * 8 + 5]);
+      u.w = pack_bf16x2(v[i * 8 + 6], v[i * 8 + 7]);
+      *reinterpret_cast<uint4*>(row + c) = u;
+    } else {
+      *reinterpret_cast<float4*>(row + c) = make_float4(v[i * 8 + 0], v[i * 8 + 1], v[i * 8 + 2], v[i * 8 + 3]);
+      *reinterpret_cast<float4*>(row + c + 4) = make_float4(v[i * 8 + 4], v[i * 8 + 5], v[i * 8 + 6], v[i * 8 + 7]);
+    }
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float s) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+
+// v <- LN(v) * scale + shift  (two-pass statistics in fp32, eps 1e-6)
+__device__ __forceinline__ void ln_modulate32(float (&v)[32], int lane, const float* shift,
+                                              const float* scale) {
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) s += v[j];
+  const float mean = warp_sum(s) * (1.0f / 1024.0f);
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    v[j] -= mean;
+    q += v[j] * v[j];
+  }
+  const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / 1024.0f) + 1e-6f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = i * 256 + lane * 8;
+    const float4 sh0 = __ldg(reinterpret_cast<const float4*>(shift + c));
+    const float4 sh1 = __ldg(reinterpret_cast<const float4*>(shift + c + 4));
+    const float4 sc0 = __ldg(reinterpret_cast<const float4*>(scale + c));
+    const float4 sc1 = __ldg(reinterpret_cast<const float4*>(scale + c + 4));
+    const float sh[8] = {sh0.x, sh0.y, sh0.z, sh0.w, sh1.x, sh1.y, sh1.z, sh1.w};
+    const float sc[8] = {sc0.x, sc0.y, sc0.z, sc0.w, sc1.x, sc1.y, sc1.z, sc1.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[i * 8 + k] = v[i * 8 + k] * inv * sc[k] + sh[k];
+  }
+}
+
+// One warp per packed row (flashinfer_kernels.py:83-108).
+template <typename Th, typename To>
+__global__ void __launch_bounds__(256) ln_modulate_kernel(const Th* __restrict__ h, const float* __restrict__ shift,
+                                                          const float* __restrict__ scale,
+                                                          const int32_t* __restrict__ doc_ids, long mod_stride,
+                                                          int N, To* __restrict__ out) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= N) return;
+  const long doc = doc_ids[row];
+  float v[32];
+  load_row32<Th>(h + (long)row * 1024, lane, v);
+  ln_modulate32(v, lane, shift + doc * mod_stride, scale + doc * mod_stride);
+  store_row32<To>(out + (long)row * 1024, lane, v);
+}
+
+// h_out = h + gate*r ; norm = LN(h_out)*scale + shift (flashinfer_kernels.py:110-145).
+template <typename T>
+__global__ void __launch_bounds__(256) gate_res_ln_modulate_kernel(
+    const T* __restrict__ h, const float* __restrict__ gate, const T* __restrict__ r,
+    const float* __restrict__ shift, const float* __restrict__ scale, const int32_t* __restrict__ doc_ids,
+    long mod_stride, int N, T* __restrict__ h_out, T* __restrict__ norm) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= N) return;
+  const long doc = doc_ids[row];
+  float v[32], rv[32];
+  load_row32<T>(h + (long)row * 1024, lane, v);
+  load_row32<T>(r + (long)row * 1024, lane, rv);
+  const float* g = gate + doc * mod_stride;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = i * 256 + lane * 8;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[i * 8 + k] += __ldg(g + c + k) * rv[i * 8 + k];
+  }
+  // the residual is stored in T; the norm uses the unrounded fp32 sum, as the reference
+  store_row32<T>(h_out + (long)row * 1024, lane, v);
+  ln_modulate32(v, lane, shift + doc * mod_stride, scale + doc * mod_stride);
+  store_row32<T>(norm + (long)row * 1024, lane, v);
+}
+
+// ------------------------------------------------------------------ input gather
+// a_in[cu[b]+p, :] = [x[b,:,p], cond[b,:,p], mu[b,:,p], spks[b,:]]  (dit.py:91-96 order)
+template <typename T>
+__global__ void __launch_bounds__(256) embed_gather_kernel(const T* __restrict__ x, const T* __restrict__ cond,
+                                                           const T* __restrict__ mu, const T* __restrict__ spks,
+                                                           const int32_t* __restrict__ cu, int T_,
+                                                           T* __restrict__ a_in) {
+  __shared__ float tile[240][33];
+  const int b = blockIdx.y;
+  const int p0 = blockIdx.x * 32;
+  const int L = cu[b + 1] - cu[b];
+  if (p0 >= L) return;
+  for (int i = threadIdx.x; i < 240 * 32; i += blockDim.x) {
+    const int c = i >> 5, pp = i & 31;
+    const int p = p0 + pp;
+    float v = 0.f;
+    if (p < L) {
+      const T* src = c < 80 ? x : (c < 160 ? cond : mu);
+      v = to_f<T>(src[((long)b * 80 + (c % 80)) * T_ + p]);
+    }
+    tile[c][pp] = v;
+  }
+  __syncthreads();
+  const long row0 = cu[b] + p0;
+  for (int i = threadIdx.x; i < 32 * 320; i += blockDim.x) {
+    const int pp = i / 320, c = i - pp * 320;
+    if (p0 + pp >= L) continue;
+    const float v = c < 240 ? tile[c][pp] : to_f<T>(spks[(long)b * 80 + (c - 240)]);
+    a_in[(row0 + pp) * 320 + c] = from_f<T>(v);
+  }
+}
+
+// ------------------------------------------------------------------ time embedding
+// temb = W2 silu(W1 sinus(t) + b1) + b2 (modules.py:71-83, 606-616); silu_out = silu(temb).
+template <typename T>
+__global__ void __launch_bounds__(256) time_embed_kernel(const T* __restrict__ w1, const float* __restrict__ b1,
+                                                         const T* __restrict__ w2, const float* __restrict__ b2,
+                                                         const T* __restrict__ t, int round_bf16,
+                                                         float* __restrict__ temb, T* __restrict__ silu_out) {
+  __shared__ float s_sin[256];
+  __shared__ float s_h1[1024];
+  const int b = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float st = 1000.0f * to_f<T>(t[b]);
+  if (round_bf16) st = bf16_round_f(st);
+  const float neg = -0.0725223646f;  // float32(-ln(10000) / 127), as torch casts the scalar
+  for (int i = threadIdx.x; i < 128; i += blockDim.x) {
+    const float f = expf(static_cast<float>(i) * neg);
+    const float arg = st * f;
+    float sv = sinf(arg), cv = cosf(arg);
+    if (round_bf16) {
+      sv = bf16_round_f(sv);
+      cv = bf16_round_f(cv);
+    }
+    s_sin[i] = sv;
+    s_sin[128 + i] = cv;
+  }
+  __syncthreads();
+  for (int j = warp; j < 1024; j += 8) {
+    float s = 0.f;
+    for (int k = lane; k < 256; k += 32) s += to_f<T>(w1[(long)j * 256 + k]) * s_sin[k];
+    s = warp_sum(s) + b1[j];
+    s_h1[j] = silu(s);
+  }
+  __syncthreads();
+  for (int j = warp; j < 1024; j += 8) {
+    float s = 0.f;
+    for (int k = lane; k < 1024; k += 32) s += to_f<T>(w2[(long)j * 1024 + k]) * s_h1[k];
+    s = warp_sum(s) + b2[j];
+    if (lane == 0) {
+      temb[(long)b * 1024 + j] = s;
+      silu_out[(long)b * 1024 + j] = from_f<T>(silu(s));
+    }
+  }
+}
+
+// ------------------------------------------------------------------ output
+// Zero the padding frames p >= L_b of a (B, 80, T) tensor.
+template <typename T>
+__global__ void zero_padding_kernel(const int32_t* __restrict__ cu, int B, int T_, T* __restrict__ out) {
+  const long total = (long)B * 80 * T_;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int p = static_cast<int>(i % T_);
+    const int b = static_cast<int>(i / ((long)80 * T_));
+    if (p >= cu[b + 1] - cu[b]) out[i] = from_f<T>(0.f);
+  }
+}
+
+// out[b, c, p] = packed[cu[b] + p, c] for p < L_b (flashinfer_dit.py:536-543).
+template <typename T>
+__global__ void unpack_kernel(const T* __restrict__ packed, const int32_t* __restrict__ cu, int B, int T_,
+                              T* __restrict__ out) {
+  const long total = (long)B * 80 * T_;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int p = static_cast<int>(i % T_);
+    const int c = static_cast<int>((i / T_) % 80);
+    const int b = static_cast<int>(i / ((long)80 * T_));
+    const int L = cu[b + 1] - cu[b];
+    out[i] = p < L ? packed[((long)cu[b] + p) * 80 + c] : from_f<T>(0.f);
+  }
+}
+
+// ------------------------------------------------------------------ ODE step
+// x += dt * ((1+r) d[i] - r d[R+i]) ; x_next[i] = x_next[R+i] = x  (flashinfer_flow.py:55-70)
+template <typename Td>
+__global__ void cfg_euler_kernel(float* __restrict__ x, const Td* __restrict__ d, int R, long per, float dt,
+                                 float rate, Td* __restrict__ x_next) {
+  const long total = (long)R * per;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const float dc = to_f<Td>(d[i]);
+    const float du = to_f<Td>(d[i + total]);
+    const float nx = x[i] + dt * ((1.0f + rate) * dc - rate * du);
+    x[i] = nx;
+    if (x_next) {
+      x_next[i] = from_f<Td>(nx);
+      x_next[i + total] = from_f<Td>(nx);
+    }
+  }
+}
+
+}  // namespace fcv

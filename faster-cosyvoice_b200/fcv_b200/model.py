@@ -1,0 +1,388 @@
+"""``B200DiT``: the packed DiT estimator with the reference module interface.
+
+Drop-in for ``FlashInferDiT`` (reference ``faster_cosyvoice/token2wav/flashinfer_dit.py:98-362``):
+
+* the module tree, and therefore the state dict, equals the reference
+  CosyVoice3 ``DiT`` (``cosyvoice/flow/DiT/dit.py:104-143``) -- keys such as
+  ``transformer_blocks.{i}.attn.to_q.weight`` -- and parameters are created in
+  the same order, so ``torch.manual_seed(s)`` followed by construction yields
+  the same random initialisation as the reference constructor;
+* ``finalize_weights()`` derives the fused inference weights once
+  (``flashinfer_dit.py:228-313``; a second call raises ``RuntimeError``);
+* ``forward(x, mask, mu, t, spks=None, cond=None, streaming=False)`` returns
+  ``(B, 80, T)`` (``flashinfer_dit.py:315-362``; ``ValueError`` without spks/cond).
+
+All GPU work runs in ``libfcv_b200.so`` through its C ABI; this module only
+owns tensors (weights, layouts, workspace) and passes device pointers.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections import OrderedDict
+from dataclasses import dataclass, field
+from typing import Sequence
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+from ._lib import DitBatch, DitWeights, call, lib
+
+DIM = 1024
+HEADS = 16
+DIM_HEAD = 64
+MEL = 80
+CONV_K = 31
+CONV_GROUPS = 16
+ROPE_DIM = 64
+ROPE_TABLE_LEN = 16384  # positions covered by the RoPE tables (the reference stops at 4096)
+MAX_LAYOUT_CACHE = 64   # flashinfer_dit.py:62
+
+
+# ---------------------------------------------------------------------------
+# Module tree (same names, shapes and creation order as the reference DiT)
+# ---------------------------------------------------------------------------
+
+class _TimeEmbedding(nn.Module):
+    def __init__(self, dim: int, freq_dim: int = 256):
+        super().__init__()
+        self.time_mlp = nn.Sequential(nn.Linear(freq_dim, dim), nn.SiLU(), nn.Linear(dim, dim))
+
+
+class _CausalConvPos(nn.Module):
+    def __init__(self, dim: int, kernel_size: int = CONV_K, groups: int = CONV_GROUPS):
+        super().__init__()
+        self.conv1 = nn.Sequential(nn.Conv1d(dim, dim, kernel_size, groups=groups, padding=0), nn.Mish())
+        self.conv2 = nn.Sequential(nn.Conv1d(dim, dim, kernel_size, groups=groups, padding=0), nn.Mish())
+
+
+class _InputEmbedding(nn.Module):
+    def __init__(self, mel_dim: int, mu_dim: int, out_dim: int, spk_dim: int):
+        super().__init__()
+        self.proj = nn.Linear(mel_dim * 2 + mu_dim + spk_dim, out_dim)
+        self.conv_pos_embed = _CausalConvPos(out_dim)
+
+
+class _Rotary(nn.Module):
+    def __init__(self, dim: int):
+        super().__init__()
+        self.register_buffer("inv_freq", 1.0 / (10000 ** (torch.arange(0, dim, 2).float() / dim)))
+
+
+class _AdaLNZero(nn.Module):
+    def __init__(self, dim: int, chunks: int):
+        super().__init__()
+        self.linear = nn.Linear(dim, dim * chunks)
+
+
+class _Attention(nn.Module):
+    def __init__(self, dim: int, heads: int, dim_head: int, dropout: float):
+        super().__init__()
+        inner = heads * dim_head
+        self.to_q = nn.Linear(dim, inner)
+        self.to_k = nn.Linear(dim, inner)
+        self.to_v = nn.Linear(dim, inner)
+        self.to_out = nn.ModuleList([nn.Linear(inner, dim), nn.Dropout(dropout)])
+
+
+class _FeedForward(nn.Module):
+    def __init__(self, dim: int, mult: int, dropout: float):
+        super().__init__()
+        inner = dim * mult
+        self.ff = nn.Sequential(nn.Sequential(nn.Linear(dim, inner), nn.GELU(approximate="tanh")),
+                                nn.Dropout(dropout), nn.Linear(inner, dim))
+
+
+class _Block(nn.Module):
+    def __init__(self, dim: int, heads: int, dim_head: int, ff_mult: int, dropout: float):
+        super().__init__()
+        self.attn_norm = _AdaLNZero(dim, 6)
+        self.attn = _Attention(dim, heads, dim_head, dropout)
+        self.ff = _FeedForward(dim, ff_mult, dropout)
+
+
+# ---------------------------------------------------------------------------
+# Packed layout ("plan") of one batch composition
+# ---------------------------------------------------------------------------
+
+@dataclass
+class PackedLayout:
+    """Device index arrays of one batch composition (``flashinfer_dit.py:75-82``
+    plus the attention work list that replaces the FlashInfer plan)."""
+
+    lengths: tuple
+    padded_length: int
+    chunk: int
+    N: int
+    max_len: int
+    lengths_dev: torch.Tensor
+    cu_seqlens: torch.Tensor
+    gather_indices: torch.Tensor
+    document_ids: torch.Tensor
+    positions: torch.Tensor
+    gap_rows: torch.Tensor
+    attn_tiles: torch.Tensor
+    n_attn_tiles: int
+    graphs: dict = field(default_factory=dict)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.bfloat16:
+        return _lib.DTYPE_BF16
+    if dtype == torch.float32:
+        return _lib.DTYPE_F32
+    raise ValueError(f"unsupported estimator dtype {dtype}; use torch.bfloat16 or torch.float32")
+
+
+class B200DiT(nn.Module):
+    """State-dict-compatible packed DiT estimator running on ``libfcv_b200``."""
+
+    def __init__(self, dim: int = DIM, depth: int = 22, heads: int = HEADS, dim_head: int = DIM_HEAD,
+                 ff_mult: int = 2, mel_dim: int = MEL, mu_dim: int = MEL, spk_dim: int = MEL,
+                 out_channels: int = MEL, static_chunk_size: int = 50, dropout: float = 0.1):
+        super().__init__()
+        if (dim, heads, dim_head, ff_mult, mel_dim, mu_dim, spk_dim) != (DIM, HEADS, DIM_HEAD, 2, MEL, MEL, MEL):
+            raise ValueError("the kernels implement the CosyVoice3 geometry "
+                             "(dim 1024, 16x64 heads, ff_mult 2, mel/mu/spk 80)")
+        self._chunk_size = static_chunk_size
+        self.static_chunk_size = static_chunk_size
+        self.dim = dim
+        self.depth = depth
+        self.heads = heads
+        self.dim_head = dim_head
+        self.out_channels = out_channels
+        # creation order of dit.py:124-141
+        self.time_embed = _TimeEmbedding(dim)
+        self.input_embed = _InputEmbedding(mel_dim, mu_dim, dim, spk_dim)
+        self.rotary_embed = _Rotary(dim_head)
+        self.transformer_blocks = nn.ModuleList(
+            [_Block(dim, heads, dim_head, ff_mult, dropout) for _ in range(depth)])
+        self.norm_out = _AdaLNZero(dim, 2)
+        self.proj_out = nn.Linear(dim, mel_dim)
+
+        self._finalized = False
+        self._derived: dict[str, torch.Tensor] = {}
+        self._weights: DitWeights | None = None
+        self._layouts: OrderedDict = OrderedDict()
+        self._workspace: torch.Tensor | None = None
+        self.plan_calls = 0
+
+    # ------------------------------------------------------------------ weights
+    @property
+    def weight_dtype(self) -> torch.dtype:
+        return self.proj_out.weight.dtype
+
+    @torch.no_grad()
+    def finalize_weights(self) -> None:
+        """Derive the fused inference weights (``flashinfer_dit.py:228-313``).
+
+        Matrices keep the module dtype (bf16 or fp32); biases and RoPE tables
+        are fp32.  ``1 + scale`` is folded into the AdaLN scale biases in fp32.
+        """
+        if self._finalized:
+            raise RuntimeError("B200DiT weights have already been finalized")
+        dev = self.proj_out.weight.device
+        if dev.type != "cuda":
+            raise RuntimeError("B200DiT.finalize_weights() needs the module on a CUDA device")
+        dt = self.weight_dtype
+        _dtype_code(dt)
+        self._finalized = True
+
+        def mat(t):
+            return t.detach().to(device=dev, dtype=dt).contiguous()
+
+        def vec(t):
+            return t.detach().to(device=dev, dtype=torch.float32).contiguous()
+
+        blocks = self.transformer_blocks
+        d = {}
+        d["time_w1"] = mat(self.time_embed.time_mlp[0].weight)
+        d["time_b1"] = vec(self.time_embed.time_mlp[0].bias)
+        d["time_w2"] = mat(self.time_embed.time_mlp[2].weight)
+        d["time_b2"] = vec(self.time_embed.time_mlp[2].bias)
+        d["ada_w"] = mat(torch.cat([b.attn_norm.linear.weight for b in blocks] + [self.norm_out.linear.weight], 0))
+        ada_b = torch.cat([vec(b.attn_norm.linear.bias) for b in blocks] + [vec(self.norm_out.linear.bias)], 0)
+        for i in range(self.depth):  # chunk order shift, scale, gate, shift, scale, gate (modules.py:241)
+            ada_b[i * 6 * DIM + 1 * DIM:i * 6 * DIM + 2 * DIM] += 1.0
+            ada_b[i * 6 * DIM + 4 * DIM:i * 6 * DIM + 5 * DIM] += 1.0
+        ada_b[self.depth * 6 * DIM:self.depth * 6 * DIM + DIM] += 1.0  # final (scale, shift)
+        d["ada_b"] = ada_b.contiguous()
+        d["in_w"] = mat(self.input_embed.proj.weight)
+        d["in_b"] = vec(self.input_embed.proj.bias)
+        for name, conv in (("conv1", self.input_embed.conv_pos_embed.conv1[0]),
+                           ("conv2", self.input_embed.conv_pos_embed.conv2[0])):
+            w = conv.weight  # (1024 out, 64 in per group, 31 taps) -> [g*64+co, tap*64+ci]
+            d[f"{name}_w"] = mat(w.permute(0, 2, 1).reshape(DIM, CONV_K * (DIM // CONV_GROUPS)))
+            d[f"{name}_b"] = vec(conv.bias)
+        d["qkv_w"] = mat(torch.stack([torch.cat([b.attn.to_q.weight, b.attn.to_k.weight, b.attn.to_v.weight], 0)
+                                      for b in blocks]))
+        d["qkv_b"] = torch.stack([torch.cat([vec(b.attn.to_q.bias), vec(b.attn.to_k.bias), vec(b.attn.to_v.bias)])
+                                  for b in blocks]).contiguous()
+        d["o_w"] = mat(torch.stack([b.attn.to_out[0].weight for b in blocks]))
+        d["o_b"] = torch.stack([vec(b.attn.to_out[0].bias) for b in blocks]).contiguous()
+        d["ff1_w"] = mat(torch.stack([b.ff.ff[0][0].weight for b in blocks]))
+        d["ff1_b"] = torch.stack([vec(b.ff.ff[0][0].bias) for b in blocks]).contiguous()
+        d["ff2_w"] = mat(torch.stack([b.ff.ff[2].weight for b in blocks]))
+        d["ff2_b"] = torch.stack([vec(b.ff.ff[2].bias) for b in blocks]).contiguous()
+        d["out_w"] = mat(self.proj_out.weight)
+        d["out_b"] = vec(self.proj_out.bias)
+        # partial-RoPE tables, fp32 (flashinfer_dit.py:262-273)
+        inv = (1.0 / (10000 ** (torch.arange(0, ROPE_DIM, 2, dtype=torch.float32) / ROPE_DIM)))
+        theta = torch.arange(ROPE_TABLE_LEN, dtype=torch.float32)[:, None] * inv[None, :]
+        d["rope_cos"] = theta.cos().to(dev).contiguous()
+        d["rope_sin"] = theta.sin().to(dev).contiguous()
+        self._derived = d
+        w = DitWeights()
+        w.depth = self.depth
+        w.dtype = _dtype_code(dt)
+        for k, v in d.items():
+            setattr(w, k, v.data_ptr())
+        w.rope_max_len = ROPE_TABLE_LEN
+        self._weights = w
+
+    def weights_struct(self) -> DitWeights:
+        if self._weights is None:
+            raise RuntimeError("call finalize_weights() first")
+        return self._weights
+
+    # ------------------------------------------------------------------ layout
+    def prepare_layout(self, lengths: Sequence[int], padded_length: int, streaming: bool,
+                       device: torch.device | None = None, lengths_dev: torch.Tensor | None = None) -> PackedLayout:
+        """Packed layout + attention work list for a batch composition, cached
+        in a FIFO of 64 entries (``flashinfer_dit.py:364-405`` and the plan
+        pool of ``:192-226``)."""
+        device = device or self.proj_out.weight.device
+        lengths = tuple(int(x) for x in lengths)
+        chunk = self._chunk_size if streaming else 0
+        key = (lengths, int(padded_length), chunk)
+        lay = self._layouts.get(key)
+        if lay is not None:
+            return lay
+        self.plan_calls += 1
+        B = len(lengths)
+        if B < 1:
+            raise ValueError("empty batch")
+        if any(L < 0 or L > padded_length for L in lengths):
+            raise ValueError("document lengths must lie in [0, T]")
+        N = sum(lengths)
+        stream = _stream(device)
+        if lengths_dev is None:
+            lengths_dev = torch.tensor(lengths, dtype=torch.int32).to(device, non_blocking=True)
+        cu = torch.empty(B + 1, dtype=torch.int32, device=device)
+        gather = torch.empty(max(N, 1), dtype=torch.int64, device=device)
+        doc_ids = torch.empty(max(N, 1), dtype=torch.int32, device=device)
+        positions = torch.empty(max(N, 1), dtype=torch.int32, device=device)
+        gap_rows = torch.empty(N + 30 * (B + 1), dtype=torch.int32, device=device)
+        call("fcv_pack_layout", lengths_dev.data_ptr(), B, int(padded_length), N, gather.data_ptr(),
+             doc_ids.data_ptr(), positions.data_ptr(), cu.data_ptr(), gap_rows.data_ptr(), stream)
+        cap = sum((L + 127) // 128 for L in lengths)
+        tiles_host = (ctypes.c_int32 * (2 * max(cap, 1)))()
+        lens_host = (ctypes.c_int32 * B)(*lengths)
+        n_tiles = call("fcv_attn_tiles", ctypes.addressof(lens_host), B, chunk, ctypes.addressof(tiles_host), cap)
+        tiles = torch.tensor(list(tiles_host)[:2 * max(n_tiles, 1)], dtype=torch.int32).to(device)
+        lay = PackedLayout(lengths, int(padded_length), chunk, N, max(lengths) if lengths else 0, lengths_dev,
+                           cu, gather[:N], doc_ids[:N], positions[:N], gap_rows, tiles, n_tiles)
+        if len(self._layouts) >= MAX_LAYOUT_CACHE:
+            self._layouts.popitem(last=False)
+        self._layouts[key] = lay
+        return lay
+
+    def layout_from_mask(self, mask: torch.Tensor, streaming: bool) -> PackedLayout:
+        """Document lengths from the (B, 1, T) mask (``flashinfer_dit.py:460``),
+        counted on the device and read back once, like the reference's
+        ``.tolist()`` (``:370``)."""
+        B, _, T = mask.shape
+        m = mask.to(self.weight_dtype).contiguous()
+        lengths_dev = torch.empty(B, dtype=torch.int32, device=mask.device)
+        call("fcv_mask_lengths", m.data_ptr(), _dtype_code(m.dtype), B, T, lengths_dev.data_ptr(),
+             _stream(mask.device))
+        lengths = lengths_dev.cpu().tolist()
+        return self.prepare_layout(lengths, T, streaming, mask.device, lengths_dev)
+
+    # ------------------------------------------------------------------ forward
+    def _workspace_for(self, N: int, B: int, device: torch.device) -> torch.Tensor:
+        need = int(lib().fcv_dit_workspace_bytes(N, B, self.depth, _dtype_code(self.weight_dtype)))
+        if self._workspace is None or self._workspace.numel() < need or self._workspace.device != device:
+            self._workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+        return self._workspace
+
+    def batch_struct(self, layout: PackedLayout, x, mu, t, spks, cond, out) -> DitBatch:
+        b = DitBatch()
+        b.B = len(layout.lengths)
+        b.T = layout.padded_length
+        b.N = layout.N
+        b.max_len = layout.max_len
+        b.chunk = layout.chunk
+        b.x, b.mu, b.cond, b.spks, b.t = (_ptr(x), _ptr(mu), _ptr(cond), _ptr(spks), _ptr(t))
+        b.cu_seqlens = layout.cu_seqlens.data_ptr()
+        b.doc_ids = layout.document_ids.data_ptr() if layout.N else layout.cu_seqlens.data_ptr()
+        b.positions = layout.positions.data_ptr() if layout.N else layout.cu_seqlens.data_ptr()
+        b.gap_rows = layout.gap_rows.data_ptr()
+        b.attn_tiles = layout.attn_tiles.data_ptr()
+        b.n_attn_tiles = layout.n_attn_tiles
+        b.out = out.data_ptr()
+        return b
+
+    def forward_layout(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor | None = None):
+        """One estimator call on a prepared layout.  Inputs must already be
+        contiguous tensors of the weight dtype on the module's device."""
+        B = len(layout.lengths)
+        T = layout.padded_length
+        if out is None:
+            out = torch.empty(B, MEL, T, dtype=self.weight_dtype, device=x.device)
+        ws = self._workspace_for(layout.N, B, x.device)
+        bs = self.batch_struct(layout, x, mu, t, spks, cond, out)
+        call("fcv_dit_forward", ctypes.byref(self.weights_struct()), ctypes.byref(bs), ws.data_ptr(),
+             ws.numel(), _stream(x.device))
+        return out
+
+    def forward(self, x: torch.Tensor, mask: torch.Tensor, mu: torch.Tensor, t: torch.Tensor,
+                spks: torch.Tensor | None = None, cond: torch.Tensor | None = None,
+                streaming: bool = False) -> torch.Tensor:
+        """Estimate the flow field (``FlashInferDiT.forward``, ``flashinfer_dit.py:315-362``)."""
+        if spks is None or cond is None:
+            raise ValueError("spks and cond are required")
+        if not self._finalized:
+            raise RuntimeError("call finalize_weights() before forward()")
+        dt = self.weight_dtype
+        dev = self.proj_out.weight.device
+        with torch.cuda.device(dev):
+            x = x.to(device=dev, dtype=dt).contiguous()
+            mu = mu.to(device=dev, dtype=dt).contiguous()
+            cond = cond.to(device=dev, dtype=dt).contiguous()
+            spks = spks.to(device=dev, dtype=dt).contiguous()
+            B, C, T = x.shape
+            if C != MEL or mu.shape != x.shape or cond.shape != x.shape or spks.shape != (B, MEL):
+                raise ValueError("expected x, mu, cond of shape (B, 80, T) and spks of shape (B, 80)")
+            t = t.to(device=dev, dtype=dt)
+            if t.ndim == 0:
+                t = t.repeat(B)
+            t = t.reshape(B).contiguous()
+            layout = self.layout_from_mask(mask.to(dev), streaming)
+            return self.forward_layout(layout, x, mu, t, spks, cond)
+
+
+def apply_b200(model, dtype: torch.dtype = torch.bfloat16):
+    """Replace a Token2Wav model's estimator with :class:`B200DiT`
+    (mirror of ``apply_flashinfer``, ``flashinfer_dit.py:951-988``)."""
+    reference = model.flow.decoder.estimator
+    device = next(reference.parameters()).device
+    est = B200DiT(static_chunk_size=getattr(reference, "static_chunk_size", 50),
+                  depth=len(reference.transformer_blocks))
+    missing, unexpected = est.load_state_dict(reference.state_dict(), strict=False)
+    missing = [k for k in missing if "rope" not in k and "rotary" not in k]
+    if missing or unexpected:
+        raise RuntimeError(f"B200DiT state-dict mismatch: missing={missing}, unexpected={unexpected}")
+    est = est.to(device=device, dtype=dtype).eval()
+    est.finalize_weights()
+    model.flow.decoder.estimator = est
+    return model

@@ -1,0 +1,234 @@
+/*
+ * fcv_b200.h -- C ABI of the B200-native packed DiT estimator.
+ *
+ * The library replaces the GPU work of the reference estimator
+ * (faster_cosyvoice/token2wav/flashinfer_dit.py, FlashInferDiT) for one
+ * hot path: the 22-block flow-matching DiT evaluated over cross-request
+ * packed (ragged) batches.  Every entry point is stateless, takes raw device
+ * pointers, sizes and a cudaStream_t (passed as void*), enqueues work on that
+ * stream and returns an int status:
+ *
+ *    0  FCV_OK
+ *   -1  FCV_EINVAL     invalid argument (message in fcv_last_error())
+ *   -2  FCV_EUNSUPPORTED  shape / dtype outside what the kernels implement
+ *   -3  FCV_ECUDA      a CUDA runtime/driver call failed
+ *   -4  FCV_EDEVICE    a kernel reported a device-side error (bounded wait
+ *                      expired); read it with fcv_device_error()
+ *
+ * The library never allocates device memory on the compute path: callers pass
+ * a workspace sized by fcv_dit_workspace_bytes().  Nothing is synchronised
+ * inside the compute entry points (no host<->device traffic), so every
+ * compute entry point can be captured into a CUDA graph.
+ *
+ * Layout conventions (all row-major, C order):
+ *   padded inputs x, mu, cond : (B, 80, T)  element type = dtype
+ *   spks                      : (B, 80)     dtype
+ *   t                         : (B,)        dtype
+ *   packed activations        : (N, 1024)   N = sum of document lengths
+ *   qkv                       : (N, 3072)   [Q | K | V], head h of Q at
+ *                                           columns h*64 .. h*64+63 (NHD)
+ *   cu_seqlens                : (B+1,) int32, cu[0] = 0, cu[B] = N
+ */
+#ifndef FCV_B200_H
+#define FCV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FCV_OK 0
+#define FCV_EINVAL (-1)
+#define FCV_EUNSUPPORTED (-2)
+#define FCV_ECUDA (-3)
+#define FCV_EDEVICE (-4)
+
+/* element types */
+#define FCV_DTYPE_F32 0
+#define FCV_DTYPE_BF16 1
+
+/* fixed model geometry (builders.py:17-21) */
+#define FCV_DIM 1024
+#define FCV_HEADS 16
+#define FCV_DIM_HEAD 64
+#define FCV_FF_INNER 2048
+#define FCV_MEL 80
+#define FCV_IN_FEAT 320
+#define FCV_CONV_K 31
+#define FCV_CONV_GROUPS 16
+#define FCV_ROPE_DIM 64
+
+/* GEMM epilogues for fcv_gemm() */
+#define FCV_EPI_BIAS 0          /* C = A W^T + b                           */
+#define FCV_EPI_BIAS_GELU 1     /* C = gelu_tanh(A W^T + b)                */
+#define FCV_EPI_BIAS_ROPE_QKV 2 /* C = A W^T + b, partial RoPE on Q/K head 0 */
+#define FCV_EPI_BIAS_GATE_RES 3 /* h(f32) += gate[doc] * (A W^T + b)       */
+#define FCV_EPI_BIAS_F32 4      /* C(f32) = A W^T + b                      */
+
+/* Version / diagnostics ------------------------------------------------- */
+int fcv_version(void);
+/* Thread-local description of the last failure of this thread. */
+const char* fcv_last_error(void);
+/* Reads and clears the device error word of the current device (synchronises
+ * the given stream).  *code = 0 when no kernel has reported an error. */
+int fcv_device_error(int* code, void* stream);
+
+/* Weights ---------------------------------------------------------------- */
+/* Derived inference weights (FlashInferDiT.finalize_weights,
+ * flashinfer_dit.py:228-313).  Matrices have element type `dtype`; biases and
+ * tables are float32.  All pointers are device pointers. */
+typedef struct fcv_dit_weights {
+  int depth;          /* number of DiT blocks (22)                            */
+  int dtype;          /* FCV_DTYPE_BF16 or FCV_DTYPE_F32                      */
+  const void* time_w1;   /* (1024, 256)  time_embed.time_mlp.0.weight         */
+  const float* time_b1;  /* (1024)                                            */
+  const void* time_w2;   /* (1024, 1024) time_embed.time_mlp.2.weight         */
+  const float* time_b2;  /* (1024)                                            */
+  const void* ada_w;     /* (depth*6144 + 2048, 1024) all AdaLN projections   */
+  const float* ada_b;    /* (depth*6144 + 2048), +1 folded into the scales    */
+  const void* in_w;      /* (1024, 320)  input_embed.proj.weight              */
+  const float* in_b;     /* (1024)                                            */
+  const void* conv1_w;   /* (1024, 31*64) row g*64+co, column tap*64+ci        */
+  const float* conv1_b;  /* (1024)                                            */
+  const void* conv2_w;   /* (1024, 31*64)                                     */
+  const float* conv2_b;  /* (1024)                                            */
+  const void* qkv_w;     /* (depth, 3072, 1024) cat(to_q, to_k, to_v)          */
+  const float* qkv_b;    /* (depth, 3072)                                     */
+  const void* o_w;       /* (depth, 1024, 1024) attn.to_out.0                 */
+  const float* o_b;      /* (depth, 1024)                                     */
+  const void* ff1_w;     /* (depth, 2048, 1024) ff.ff.0.0                     */
+  const float* ff1_b;    /* (depth, 2048)                                     */
+  const void* ff2_w;     /* (depth, 1024, 2048) ff.ff.2                       */
+  const float* ff2_b;    /* (depth, 1024)                                     */
+  const void* out_w;     /* (80, 1024)   proj_out.weight                      */
+  const float* out_b;    /* (80)                                              */
+  const float* rope_cos; /* (rope_max_len, 32) cos(p * 10000^(-2j/64))        */
+  const float* rope_sin; /* (rope_max_len, 32)                                */
+  int rope_max_len;
+} fcv_dit_weights;
+
+/* One packed batch -------------------------------------------------------- */
+typedef struct fcv_dit_batch {
+  int B;             /* sequences (CFG rows included)                          */
+  int T;             /* padded length of x / mu / cond / out                   */
+  int N;             /* packed rows, sum of lengths                            */
+  int max_len;       /* longest document                                      */
+  int chunk;         /* 0: full attention inside a document; >0: chunk-causal */
+  const void* x;     /* (B, 80, T) */
+  const void* mu;    /* (B, 80, T) */
+  const void* cond;  /* (B, 80, T) */
+  const void* spks;  /* (B, 80)    */
+  const void* t;     /* (B,)       */
+  const int32_t* cu_seqlens;  /* (B+1)  device                                */
+  const int32_t* doc_ids;     /* (N)    device                                */
+  const int32_t* positions;   /* (N)    device                                */
+  const int32_t* gap_rows;    /* (N + 30*(B+1)) device, see fcv_pack_layout   */
+  const int32_t* attn_tiles;  /* (n_attn_tiles, 2) device: (doc, q0), 128 rows */
+  int n_attn_tiles;
+  void* out;         /* (B, 80, T) element type dtype; padding frames zeroed   */
+} fcv_dit_batch;
+
+/* Layout ------------------------------------------------------------------ */
+/* Document lengths from a right-padded 0/1 mask (B, 1, T) of element type
+ * dtype: lengths[b] = number of entries > 0.5.
+ * Replaces flashinfer_dit.py:460 (mask[:, 0].sum(-1)); counts exactly. */
+int fcv_mask_lengths(const void* mask, int dtype, int B, int T, int32_t* lengths,
+                     void* stream);
+
+/* Packed layout from device lengths (B,).  Replaces
+ * FlashInferDiT._get_packed_layout (flashinfer_dit.py:364-405) and
+ * RaggedAttentionRunner._make_indptr (flashinfer_attention.py:82-86):
+ *   gather[n]    = b*T + p          (int64, for row n = cu[b] + p)
+ *   doc_ids[n]   = b                (int32)
+ *   positions[n] = p                (int32)
+ *   cu_seqlens   = [0, cumsum(lengths)] (int32)
+ * plus gap_rows (length max_rows + 30*(B+1), int32): the embedding's causal
+ * convolution stores each document behind 30 zero rows; gap_rows[g] is the
+ * packed row held by row g of that gapped layout, or -1 for a zero row.
+ * max_rows bounds N (B*T is always safe); entries past N are not written. */
+int fcv_pack_layout(const int32_t* lengths, int B, int T, int max_rows, int64_t* gather,
+                    int32_t* doc_ids, int32_t* positions, int32_t* cu_seqlens,
+                    int32_t* gap_rows, void* stream);
+
+/* Scatter packed rows (N, 80) back to a zeroed padded (B, 80, T) tensor
+ * (flashinfer_dit.py:535-543). */
+int fcv_unpack_output(const void* packed, int dtype, const int32_t* cu_seqlens, int B, int T,
+                      int N, void* out, void* stream);
+
+/* Row kernels (flashinfer_kernels.py) ------------------------------------- */
+/* out[n] = LN(h[n]) * scale[doc[n]] + shift[doc[n]]; LN affine-free, eps 1e-6,
+ * float32 statistics.  h: (N,1024) of h_dtype; out: (N,1024) of out_dtype;
+ * shift/scale rows are float32 at stride mod_stride (elements).
+ * Replaces layer_norm_modulate_packed (flashinfer_kernels.py:83-108, 327-348). */
+int fcv_ln_modulate(const void* h, int h_dtype, const float* shift, const float* scale,
+                    const int32_t* doc_ids, long mod_stride, int N, void* out, int out_dtype,
+                    void* stream);
+
+/* h_out = h + gate[doc]*r ; norm = LN(h_out)*scale[doc] + shift[doc].
+ * Replaces gate_residual_layer_norm_modulate_packed
+ * (flashinfer_kernels.py:110-145, 351-378). h/h_out/r/norm share `dtype`. */
+int fcv_gate_res_ln_modulate(const void* h, const float* gate, const void* r,
+                             const float* shift, const float* scale,
+                             const int32_t* doc_ids, long mod_stride, int N, void* h_out,
+                             void* norm, int dtype, void* stream);
+
+/* GEMM -------------------------------------------------------------------- */
+/* C[M, Nout] = A[M, K] * W[Nout, K]^T + bias, epilogue `epi`, element type
+ * dtype for A/W (bf16 -> tcgen05 tensor cores, f32 -> CUDA cores).
+ * Replaces F.linear (flashinfer_dit.py:490, 500, 512, 535).
+ * For FCV_EPI_BIAS_ROPE_QKV: aux_i32 = positions (M), rope tables required.
+ * For FCV_EPI_BIAS_GATE_RES: C is the float32 residual h, aux_i32 = doc_ids,
+ * gate rows at `gate` with stride gate_stride. */
+int fcv_gemm(const void* A, const void* W, const float* bias, int M, int Nout, int K,
+             int dtype, int epi, void* C, const int32_t* aux_i32, const float* gate,
+             long gate_stride, const float* rope_cos, const float* rope_sin, void* stream);
+
+/* Attention --------------------------------------------------------------- */
+/* Ragged multi-head attention over packed documents: for every document d,
+ * head h and query row q: softmax(Q K^T / 8 + mask) V, where the mask keeps
+ * keys k < L_d, and, when chunk > 0, only k // chunk <= q // chunk.
+ * qkv: (N, 3072) [Q|K|V] element type dtype; out: (N, 1024).
+ * tiles: (n_tiles, 2) int32 (doc, q0) list of 128-row query tiles, built by
+ * fcv_attn_tiles().  Replaces the FlashInfer ragged prefill of
+ * flashinfer_attention.py:36-142 + flashinfer_dit.py:501. */
+int fcv_attention(const void* qkv, int dtype, const int32_t* cu_seqlens, int B, int max_len,
+                  int chunk, const int32_t* tiles, int n_tiles, void* out, void* stream);
+
+/* Host helper: fill `tiles` (capacity `cap` pairs, host memory) with the
+ * 128-row query tiles of the documents, most expensive first.  Returns the
+ * number of tiles or a negative status. */
+int fcv_attn_tiles(const int32_t* lengths_host, int B, int chunk, int32_t* tiles, int cap);
+
+/* Time embedding + AdaLN ---------------------------------------------------- */
+/* temb (B,1024) f32 = TimestepEmbedding(t) (modules.py:606-616); silu_act
+ * (B,1024, element type dtype) = SiLU(temb) for the modulation GEMM.
+ * In bf16 mode the sinusoid argument is bf16(1000*t) and the sinusoid is
+ * rounded to bf16, as the reference computes them in the input dtype. */
+int fcv_time_embed(const fcv_dit_weights* w, const void* t, int B, float* temb,
+                   void* silu_act, void* stream);
+
+/* ODE --------------------------------------------------------------------- */
+/* Fused CFG combine + Euler step on (R, 80, T) float32 samples
+ * (flashinfer_flow.py:55-70): x += dt * ((1+r) d[:R] - r d[R:]), d (2R, 80, T)
+ * of element type d_dtype.  When x_next is not NULL it receives the next
+ * estimator input, the CFG-repeated sample (2R, 80, T) in d_dtype. */
+int fcv_cfg_euler(float* x, const void* d, int d_dtype, int R, int T, float dt, float cfg_rate,
+                  void* x_next, void* stream);
+
+/* Whole estimator call ---------------------------------------------------- */
+/* Bytes of workspace fcv_dit_forward needs for N packed rows, B sequences. */
+size_t fcv_dit_workspace_bytes(int N, int B, int depth, int dtype);
+
+/* One estimator evaluation (FlashInferDiT.forward -> _forward_packed,
+ * flashinfer_dit.py:315-362, 447-543): embed, 22 DiT blocks, final norm,
+ * proj_out, unpack into batch->out.  `workspace` must be 256-byte aligned. */
+int fcv_dit_forward(const fcv_dit_weights* w, const fcv_dit_batch* batch, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FCV_B200_H */

@@ -1,0 +1,211 @@
+"""Generate the golden vectors under ``tests/golden/`` from the reference itself.
+
+Run in a container where the reference project is present (read-only) at
+``$FCV_REFERENCE_ROOT`` (default ``/root/reference``)::
+
+    python tests/golden/make_golden.py
+
+The reference's own code is imported and executed on the CPU in float32:
+
+* ``cosyvoice/flow/DiT/dit.py`` ``DiT`` (padded SDPA path, ``dit.py:145-176``);
+* ``flashinfer_dit.FlashInferDiT._get_packed_layout`` (``flashinfer_dit.py:364-405``);
+* ``flashinfer_attention.build_chunk_causal_mask`` / ``_make_indptr``
+  (``flashinfer_attention.py:16-33, 82-86``);
+* ``flashinfer_kernels.layer_norm_modulate_torch`` (``flashinfer_kernels.py:288-296``);
+* ``flashinfer_flow.solve_euler_batched`` (``flashinfer_flow.py:16-74``) with
+  ``CausalConditionalCFM`` (``flow_matching.py:196-200``);
+* ``modules.TimestepEmbedding`` in bf16 (``modules.py:71-83, 606-616``).
+
+``x_transformers`` (pinned 2.23.5, absent here) is replaced by the restatement in
+``_xt_shim``; ``omegaconf`` is bypassed by passing a ``SimpleNamespace`` as
+``cfm_params``.  Weights come from ``torch.manual_seed(seed)`` followed by the
+reference constructor; their SHA-256 fingerprints are stored so the tests can
+check that the framework's own module tree reproduces the same initialisation.
+
+None of the tests import this script or the reference; they read the ``.npz`` /
+``.json`` files it writes.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("FCV_REFERENCE_ROOT", "/root/reference"))
+sys.path.insert(0, str(HERE / "_xt_shim"))
+sys.path.insert(0, str(REF))
+
+from faster_cosyvoice.token2wav.cosyvoice.flow.DiT.dit import DiT  # noqa: E402
+from faster_cosyvoice.token2wav.cosyvoice.flow.DiT import modules as ref_modules  # noqa: E402
+from faster_cosyvoice.token2wav.cosyvoice.flow.flow_matching import CausalConditionalCFM  # noqa: E402
+from faster_cosyvoice.token2wav import flashinfer_attention as ref_attn  # noqa: E402
+from faster_cosyvoice.token2wav import flashinfer_dit as ref_fdit  # noqa: E402
+from faster_cosyvoice.token2wav import flashinfer_flow as ref_flow  # noqa: E402
+from faster_cosyvoice.token2wav import flashinfer_kernels as ref_kernels  # noqa: E402
+
+torch.set_num_threads(max(1, os.cpu_count() or 1))
+
+
+def build_ref_dit(seed: int, depth: int) -> DiT:
+    """``builders.py:17-21`` hyper-parameters, random init from ``seed``."""
+    torch.manual_seed(seed)
+    return DiT(dim=1024, depth=depth, heads=16, dim_head=64, ff_mult=2, mel_dim=80, mu_dim=80,
+               spk_dim=80, out_channels=80, static_chunk_size=50,
+               num_decoding_left_chunks=-1).eval()
+
+
+def fingerprint(model: torch.nn.Module) -> dict:
+    out = {}
+    for k, v in model.state_dict().items():
+        a = v.detach().contiguous().cpu().numpy()
+        out[k] = {"shape": list(a.shape), "dtype": str(a.dtype),
+                  "sha256": hashlib.sha256(a.tobytes()).hexdigest()}
+    return out
+
+
+def inputs(rng, B, T, lengths, cfg_pairs=False):
+    x = rng.standard_normal((B, 80, T)).astype(np.float32)
+    mu = rng.standard_normal((B, 80, T)).astype(np.float32)
+    cond = rng.standard_normal((B, 80, T)).astype(np.float32)
+    spks = rng.standard_normal((B, 80)).astype(np.float32)
+    t = rng.uniform(0, 1, size=(B,)).astype(np.float32)
+    if cfg_pairs:
+        h = B // 2
+        x[h:] = x[:h]
+        mu[h:] = 0
+        cond[h:] = 0
+        spks[h:] = 0
+        t[h:] = t[:h]
+    mask = np.zeros((B, 1, T), np.float32)
+    for b, L in enumerate(lengths):
+        mask[b, 0, :L] = 1
+    return dict(x=x, mu=mu, cond=cond, spks=spks, t=t, mask=mask)
+
+
+@torch.no_grad()
+def run_dit(model, d, streaming):
+    T = torch.from_numpy
+    y = model(T(d["x"]), T(d["mask"]), T(d["mu"]), T(d["t"]), T(d["spks"]), T(d["cond"]),
+              streaming=streaming)
+    return y.numpy()
+
+
+def dit_case(name, seed, depth, lengths, T, cfg_pairs, in_seed):
+    model = build_ref_dit(seed, depth)
+    rng = np.random.default_rng(in_seed)
+    d = inputs(rng, len(lengths), T, lengths, cfg_pairs)
+    off = run_dit(model, d, False)
+    st = run_dit(model, d, True)
+    np.savez_compressed(HERE / f"{name}.npz", **d, lengths=np.asarray(lengths, np.int64),
+                        out_offline=off, out_streaming=st, seed=seed, depth=depth)
+    return model
+
+
+def pack_cases():
+    cases = [([5], 5), ([3, 7, 1], 7), ([50, 50], 64), ([1], 1), ([120, 77, 77, 120], 130),
+             ([199, 1, 64, 51, 100], 200)]
+    fake = types.SimpleNamespace(_pack_cache=ref_fdit.OrderedDict())
+    runner = types.SimpleNamespace(device=torch.device("cpu"))
+    out = {}
+    for i, (lengths, T) in enumerate(cases):
+        lt = torch.tensor(lengths, dtype=torch.int64)
+        lay = ref_fdit.FlashInferDiT._get_packed_layout(fake, lt, T, torch.device("cpu"))
+        indptr = ref_attn.RaggedAttentionRunner._make_indptr(runner, lengths)
+        m = ref_attn.build_chunk_causal_mask(lengths, 50, "cpu")
+        out[f"c{i}_lengths"] = np.asarray(lengths, np.int64)
+        out[f"c{i}_T"] = np.int64(T)
+        out[f"c{i}_gather"] = lay.gather_indices.numpy()
+        out[f"c{i}_doc_ids"] = lay.document_ids.numpy()
+        out[f"c{i}_positions"] = lay.positions.numpy()
+        out[f"c{i}_cu"] = indptr.numpy()
+        out[f"c{i}_mask50"] = m.numpy()
+    out["n_cases"] = np.int64(len(cases))
+    np.savez_compressed(HERE / "pack_layout.npz", **out)
+
+
+def rownorm_case():
+    rng = np.random.default_rng(11)
+    h = (rng.standard_normal((37, 1024)) * 3 + 0.5).astype(np.float32)
+    shift = rng.standard_normal((37, 1024)).astype(np.float32)
+    scale = (1 + 0.3 * rng.standard_normal((37, 1024))).astype(np.float32)
+    gate = rng.standard_normal((37, 1024)).astype(np.float32)
+    r = rng.standard_normal((37, 1024)).astype(np.float32)
+    T = torch.from_numpy
+    out = ref_kernels.layer_norm_modulate_torch(T(h), T(shift), T(scale)).numpy()
+    h2 = torch.addcmul(T(h), T(gate), T(r))
+    out2 = ref_kernels.layer_norm_modulate_torch(h2, T(shift), T(scale)).numpy()
+    np.savez_compressed(HERE / "rownorm.npz", h=h, shift=shift, scale=scale, gate=gate, r=r,
+                        ln_mod=out, gres_h=h2.numpy(), gres_norm=out2)
+
+
+@torch.no_grad()
+def time_embed_case():
+    te = ref_modules.SinusPositionEmbedding(256)
+    rng = np.random.default_rng(5)
+    t = torch.from_numpy(rng.uniform(0, 1, size=(64,)).astype(np.float32)).to(torch.bfloat16)
+    sin_bf16 = te(t).to(torch.bfloat16).float().numpy()
+    sin_f32 = te(t.float()).numpy()
+    np.savez_compressed(HERE / "time_embed.npz", t_bf16=t.float().numpy(), sin_bf16=sin_bf16,
+                        sin_f32=sin_f32)
+
+
+@torch.no_grad()
+def ode_case():
+    model = build_ref_dit(3, 2)
+    cfm = types.SimpleNamespace(sigma_min=1e-6, solver="euler", t_scheduler="cosine",
+                                training_cfg_rate=0.2, inference_cfg_rate=0.7, reg_loss_type="l1")
+    decoder = CausalConditionalCFM(in_channels=240, cfm_params=cfm, n_spks=1, spk_emb_dim=80,
+                                   estimator=model)
+    lengths = [120, 77]
+    T = 120
+    rng = np.random.default_rng(21)
+    mu = rng.standard_normal((2, 80, T)).astype(np.float32)
+    cond = rng.standard_normal((2, 80, T)).astype(np.float32)
+    spks = rng.standard_normal((2, 80)).astype(np.float32)
+    mask = np.zeros((2, 1, T), np.float32)
+    for b, L in enumerate(lengths):
+        mask[b, 0, :L] = 1
+        mu[b, :, L:] = 0
+        cond[b, :, L:] = 0
+    noise = decoder.rand_noise[:, :, :T].expand(2, -1, -1).contiguous()
+    out = {}
+    for streaming in (True, False):
+        y = ref_flow.solve_euler_batched(decoder, noise, torch.from_numpy(mu),
+                                         torch.from_numpy(mask), torch.from_numpy(spks),
+                                         torch.from_numpy(cond), num_timesteps=10,
+                                         streaming=streaming)
+        out["out_streaming" if streaming else "out_offline"] = y.float().numpy()
+    np.savez_compressed(HERE / "ode.npz", mu=mu, cond=cond, spks=spks, mask=mask,
+                        lengths=np.asarray(lengths, np.int64), noise=noise.numpy(),
+                        rand_noise_head=decoder.rand_noise[0, :, :8].numpy(), **out)
+
+
+def main():
+    fps = {}
+    m = dit_case("dit_block_fp32", seed=0, depth=1, lengths=[300], T=300, cfg_pairs=False, in_seed=100)
+    fps["seed0_depth1"] = fingerprint(m)
+    m = dit_case("dit_depth22_cfg", seed=1, depth=22, lengths=[150, 77, 150, 77], T=150,
+                 cfg_pairs=True, in_seed=101)
+    fps["seed1_depth22"] = fingerprint(m)
+    m = dit_case("dit_depth2_edge", seed=2, depth=2, lengths=[130, 1, 64, 51], T=130,
+                 cfg_pairs=False, in_seed=102)
+    fps["seed2_depth2"] = fingerprint(m)
+    fps["seed3_depth2"] = fingerprint(build_ref_dit(3, 2))
+    (HERE / "weights_fingerprint.json").write_text(json.dumps(fps, indent=0, sort_keys=True))
+    pack_cases()
+    rownorm_case()
+    time_embed_case()
+    ode_case()
+    print("golden vectors written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,108 @@
+"""Pin the numpy oracle (oracle/dit_oracle.py) to golden vectors produced by the
+reference's own code (tests/golden/make_golden.py), and check that the
+framework's module tree reproduces the reference's random initialisation."""
+
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+
+from conftest import golden_fingerprints, load_golden, make_model, numpy_params, rel_l2
+from oracle import dit_oracle as O
+
+
+def test_pack_layout_matches_reference_bit_exact():
+    z = load_golden("pack_layout")
+    for i in range(int(z["n_cases"])):
+        lengths = z[f"c{i}_lengths"]
+        lay = O.pack_layout(lengths, int(z[f"c{i}_T"]))
+        np.testing.assert_array_equal(lay.gather_indices, z[f"c{i}_gather"])
+        assert lay.gather_indices.dtype == z[f"c{i}_gather"].dtype
+        np.testing.assert_array_equal(lay.document_ids, z[f"c{i}_doc_ids"])
+        np.testing.assert_array_equal(lay.positions, z[f"c{i}_positions"])
+        np.testing.assert_array_equal(lay.cu_seqlens, z[f"c{i}_cu"])
+        np.testing.assert_array_equal(O.chunk_causal_mask_flat(lengths, 50), z[f"c{i}_mask50"])
+
+
+def test_lengths_from_mask_counts_exactly():
+    m = np.zeros((3, 1, 10), np.float32)
+    m[0, 0, :10] = 1
+    m[1, 0, :1] = 1
+    np.testing.assert_array_equal(O.lengths_from_mask(m), [10, 1, 0])
+
+
+def test_rownorm_matches_reference():
+    z = load_golden("rownorm")
+    out = O.layer_norm_modulate(z["h"], z["shift"], z["scale"])
+    assert rel_l2(out, z["ln_mod"]) < 1e-6
+    h2, norm = O.gate_residual_layer_norm_modulate(z["h"], z["gate"], z["r"], z["shift"], z["scale"])
+    np.testing.assert_allclose(h2, z["gres_h"], rtol=1e-6, atol=1e-6)
+    assert rel_l2(norm, z["gres_norm"]) < 1e-6
+
+
+def test_time_sinusoid_matches_reference_fp32_and_bf16():
+    z = load_golden("time_embed")
+    s32 = O.sinus_embed(z["t_bf16"], emulate_bf16_time=False)
+    # |arg| reaches 1000 rad, so one ulp of the fp32 frequency moves sin by ~6e-5
+    np.testing.assert_allclose(s32, z["sin_f32"], atol=2e-4)
+    s16 = O.sinus_embed(z["t_bf16"], emulate_bf16_time=True)
+    # bf16 semantics: the argument 1000*t is rounded to bf16 before the sinusoid
+    np.testing.assert_allclose(s16, z["sin_bf16"], atol=1e-2)
+    assert np.mean(np.abs(s16 - z["sin_bf16"]) > 0) < 0.05
+
+
+@pytest.mark.parametrize("key,seed,depth", [("seed0_depth1", 0, 1), ("seed2_depth2", 2, 2),
+                                            ("seed3_depth2", 3, 2), ("seed1_depth22", 1, 22)])
+def test_module_tree_reproduces_reference_init(key, seed, depth):
+    fp = golden_fingerprints()[key]
+    sd = make_model(seed, depth).state_dict()
+    assert sorted(sd.keys()) == sorted(fp.keys())
+    for k, meta in fp.items():
+        a = sd[k].detach().contiguous().numpy()
+        assert list(a.shape) == meta["shape"], k
+        assert hashlib.sha256(a.tobytes()).hexdigest() == meta["sha256"], k
+
+
+def _dit_case(name, rtol):
+    z = load_golden(name)
+    params = numpy_params(make_model(int(z["seed"]), int(z["depth"])))
+    for streaming, key in ((False, "out_offline"), (True, "out_streaming")):
+        y = O.dit_forward_padded(params, z["x"], z["mask"], z["mu"], z["t"], z["spks"], z["cond"],
+                                 streaming=streaming)
+        for b, L in enumerate(z["lengths"]):
+            assert rel_l2(y[b, :, :L], z[key][b, :, :L]) < rtol, (name, streaming, b)
+
+
+def test_dit_single_block_fp32_matches_reference():
+    _dit_case("dit_block_fp32", 1e-5)
+
+
+def test_dit_depth2_ragged_edge_matches_reference():
+    _dit_case("dit_depth2_edge", 1e-5)
+
+
+def test_dit_depth22_cfg_matches_reference():
+    _dit_case("dit_depth22_cfg", 1e-4)
+
+
+def test_ode_matches_reference():
+    z = load_golden("ode")
+    params = numpy_params(make_model(3, 2))
+    lengths = z["lengths"]
+    noise = [z["noise"][i, :, :L] for i, L in enumerate(lengths)]
+    mu = [z["mu"][i, :, :L] for i, L in enumerate(lengths)]
+    cond = [z["cond"][i, :, :L] for i, L in enumerate(lengths)]
+    for streaming, key in ((True, "out_streaming"), (False, "out_offline")):
+        xs = O.solve_euler_docs(params, noise, mu, cond, list(z["spks"]), 10, streaming=streaming)
+        for i, L in enumerate(lengths):
+            assert np.abs(xs[i] - z[key][i, :, :L]).max() < 1e-4, (key, i)
+
+
+def test_flop_model_matches_survey_formula():
+    # per-row constant 378,044,416 and the 4096 FLOPs per visible pair and layer
+    f1 = O.estimator_flops([1], None, 22)
+    per_seq = 2 * 1024 * 137216 + 2 * (256 * 1024 + 1024 * 1024)
+    assert f1 == 378044416 + 22 * 4096 * 1 + per_seq
+    assert O.visible_pairs([100], 50) == 50 * 50 + 50 * 100
