@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""Benchmark of the packed DiT estimator: mel-frames/s per NFE (one estimator call).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5] [--impl b200|reference]
+
+Default workload ("config 2"): 22-layer bf16 DiT,
+8 requests with CFG doubling -> 16 sequences, lengths ~U[150, 600] frames
+(a CFG pair shares its length), inputs ~N(0,1), t ~U(0,1), random-init
+weights from seed 1, full (offline) mask, one estimator call per step.
+Synthetic data of the reference's shapes; no dataset is involved.
+
+Under torchrun (N > 1) every rank runs its own batch of the same composition
+(weak scaling, no collective on the data path); ``--config 4`` and ``--config 5``
+instead shard one fixed request set across the ranks by LPT bins (strong).
+
+``--impl reference`` times the reference's CPU path (the oracle port of its
+torch DiT, float32, all host threads) on a bounded sample of the same
+workload; under torchrun only rank 0 runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "faster-cosyvoice_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+METRIC = "DiT estimator mel-frames/s (per NFE)"
+UNIT = "mel-frames/s"
+
+
+# ---------------------------------------------------------------------------- workloads
+def request_lengths(config: str) -> tuple[list[int], int, int]:
+    """(request lengths, chunk, seed) of a BASELINE.json config."""
+    if config == "2":
+        rng = np.random.default_rng(1)
+        return [int(v) for v in rng.integers(150, 601, size=8)], 0, 1
+    if config == "3":
+        rng = np.random.default_rng(2)
+        prompt = rng.integers(100, 401, size=32)
+        gen = rng.choice([30, 60, 120], size=32)
+        return [int(a + b) for a, b in zip(prompt, gen)], 50, 2
+    if config == "4":
+        rng = np.random.default_rng(3)
+        L = np.clip(np.round(rng.lognormal(np.log(400.0), 0.6, size=128)), 50, 3000)
+        return [int(v) for v in L], 0, 3
+    if config == "5":
+        return [3000] * 16, 0, 5
+    raise ValueError(f"unknown config {config}")
+
+
+CONFIG_NAMES = {
+    "2": "config2: 22-layer bf16 DiT, 1 NFE, 8 requests x CFG = 16 seqs, L~U[150,600], offline mask",
+    "3": "config3: 22-layer bf16 DiT, 1 NFE of the 10-step CFG ODE, 32 requests x CFG = 64 seqs, "
+         "L = U[100,400] + {30,60,120}, chunk-50 streaming mask",
+    "4": "config4: 22-layer bf16 DiT, 1 NFE, 128 requests x CFG, L~LogNormal(ln 400, 0.6) in [50,3000], offline",
+    "5": "config5: 22-layer bf16 DiT, 1 NFE, 16 requests x CFG, L=3000, full mask",
+}
+
+
+def make_batch(req_lengths, seed, device, dtype):
+    import torch
+
+    R = len(req_lengths)
+    lengths = list(req_lengths) + list(req_lengths)  # [cond; uncond] (flashinfer_flow.py:45-51)
+    B = 2 * R
+    T = max(lengths)
+    g = torch.Generator().manual_seed(1000 + seed)
+    x = torch.randn(R, 80, T, generator=g)
+    x = torch.cat([x, x], 0)
+    mu = torch.cat([torch.randn(R, 80, T, generator=g), torch.zeros(R, 80, T)], 0)
+    cond = torch.cat([torch.randn(R, 80, T, generator=g), torch.zeros(R, 80, T)], 0)
+    spks = torch.cat([torch.randn(R, 80, generator=g), torch.zeros(R, 80)], 0)
+    t = torch.rand(R, generator=g)
+    t = torch.cat([t, t], 0)
+    mask = torch.zeros(B, 1, T)
+    for b, L in enumerate(lengths):
+        mask[b, 0, :L] = 1
+        x[b, :, L:] = 0
+        mu[b, :, L:] = 0
+        cond[b, :, L:] = 0
+    host = dict(x=x, mask=mask, mu=mu, t=t, spks=spks, cond=cond)
+    dev = {k: v.to(device=device, dtype=dtype).contiguous() for k, v in host.items()}
+    return lengths, T, host, dev
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """NVML sampling of SM clock and throttle reasons during the timed region (read only)."""
+
+    REASONS = {
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000080: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            import torch
+
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(device_index).uuid)
+            try:
+                self._h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._h = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------- CPU baseline
+def cpu_oracle_rate(params, req_lengths, seed, budget_s: float):
+    """Time the oracle port of the reference torch DiT (float32, numpy BLAS on
+    every host thread) on one document of the workload, trimmed so one pass
+    takes about ``budget_s`` seconds.  Returns (frames/s, seconds, rows, cores, sample)."""
+    from oracle import dit_oracle as O
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        cores = os.cpu_count() or 1
+    rng = np.random.default_rng(seed)
+
+    def doc(L):
+        return (rng.standard_normal((80, L)).astype(np.float32), rng.standard_normal((80, L)).astype(np.float32),
+                rng.standard_normal((80, L)).astype(np.float32), rng.standard_normal(80).astype(np.float32))
+
+    # calibrate on 32 rows, then size the sample to the budget
+    t0 = time.perf_counter()
+    O.dit_forward_docs(params, [doc(32)], np.array([0.5], np.float32))
+    per_row = (time.perf_counter() - t0) / 32
+    L = int(max(16, min(req_lengths[0], budget_s / max(per_row, 1e-6))))
+    d = doc(L)
+    t0 = time.perf_counter()
+    O.dit_forward_docs(params, [d], np.array([0.5], np.float32))
+    dt = time.perf_counter() - t0
+    sample = f"one document of {L} frames (22-layer fp32 oracle port, offline mask)"
+    return L / dt, dt, L, cores, sample
+
+
+# ---------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="2", choices=["2", "3", "4", "5"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    req_lengths, chunk, seed = request_lengths(args.config)
+    strong = args.config in ("4", "5") and world > 1
+    cfg = {"workload": CONFIG_NAMES[args.config], "requests": len(req_lengths), "sequences": 2 * len(req_lengths),
+           "packed_rows": 2 * sum(req_lengths), "chunk": chunk, "seed": seed,
+           "parallelism": f"dp{world} (request bins, no collective)",
+           "l2": "working set (662 MB of weights per NFE) exceeds the 126 MB L2; L2 also flushed between steps"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        import torch
+
+        from fcv_b200.model import B200DiT
+
+        torch.manual_seed(seed)
+        model = B200DiT(depth=22).eval()
+        params = {k: v.detach().float().numpy() for k, v in model.state_dict().items()}
+        budget = max(0.5, min(6.0, 150.0 / (args.steps + args.warmup)))
+        for _ in range(args.warmup):
+            cpu_oracle_rate(params, req_lengths, seed, budget)
+        rates, times = [], []
+        for _ in range(args.steps):
+            r, dt, L, cores, sample = cpu_oracle_rate(params, req_lengths, seed, budget)
+            rates.append(r)
+            times.append(dt)
+        value = float(statistics.median(rates))
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)), "higher_is_better": True,
+                "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": cfg, "impl": "reference",
+                "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from fcv_b200 import _lib
+    from fcv_b200.model import B200DiT
+    from fcv_b200.shard import lpt_bins
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+    if strong:
+        bins = lpt_bins(req_lengths, world, chunk or None)
+        my_req = [req_lengths[i] for i in bins[rank]]
+    else:
+        my_req = list(req_lengths)
+
+    torch.manual_seed(seed)
+    cpu_model = B200DiT(depth=22).eval()
+    cpu_params = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu_params = {k: v.detach().float().numpy() for k, v in cpu_model.state_dict().items()}
+    model = cpu_model.to(device=device, dtype=torch.bfloat16)
+    model.finalize_weights()
+    lengths, T, host, dev = make_batch(my_req, seed + 17 * rank, device, torch.bfloat16)
+    streaming = chunk > 0
+    N = sum(lengths)
+    layout = model.layout_from_mask(dev["mask"], streaming)
+    out = torch.empty(len(lengths), 80, T, dtype=torch.bfloat16, device=device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    lib = _lib.lib()
+
+    def step():
+        model.forward_layout(layout, dev["x"], dev["mu"], dev["t"], dev["spks"], dev["cond"], out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: device-resident inputs, CUDA events per step, L2 flushed between steps
+    stream = torch.cuda.current_stream(device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    lib.fcv_profile_enable(1)
+    cats = len(_lib.CATEGORIES)
+    import ctypes
+
+    ms_arr = (ctypes.c_float * cats)()
+    cnt_arr = (ctypes.c_int * cats)()
+    _lib.call("fcv_profile_collect", ctypes.addressof(ms_arr), ctypes.addressof(cnt_arr), cats)  # reset
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = lib.fcv_launch_count()
+    with ClockSampler(local_rank) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    launches = lib.fcv_launch_count() - launches0
+    lib.fcv_profile_enable(0)
+    _lib.call("fcv_profile_collect", ctypes.addressof(ms_arr), ctypes.addressof(cnt_arr), cats)
+    if world > 1:
+        dist.barrier()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = float(sum(step_ms))
+    t_max = torch.tensor([total_ms], dtype=torch.float64, device=device)
+    rows = torch.tensor([float(N)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+        dist.all_reduce(rows, op=dist.ReduceOp.SUM)
+    total_ms_max = float(t_max.item())
+    all_rows = float(rows.item())
+    value = all_rows * args.steps / (total_ms_max / 1000.0)
+    ms_per_step = total_ms_max / args.steps
+
+    # ---- per-kernel-class timing from the events recorded inside the timed region
+    prof = {name: {"ms_total": float(ms_arr[i]), "launches": int(cnt_arr[i])}
+            for i, name in enumerate(_lib.CATEGORIES)}
+    from fcv_b200.flops import estimator_flops, visible_pairs
+
+    gemm_flops_step = 22 * N * (2 ** 24)
+    gemm_ms = sum(prof[k]["ms_total"] for k in ("gemm_qkv", "gemm_out", "gemm_ff1", "gemm_ff2"))
+    gemm_launches = sum(prof[k]["launches"] for k in ("gemm_qkv", "gemm_out", "gemm_ff1", "gemm_ff2"))
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peak_tf, peak_src = float(peaks["bf16_tflops_sustained"]), "measured (sustained)"
+        hbm = float(peaks["hbm_gbs"])
+    except Exception:
+        peak_tf, peak_src, hbm = 1400.0, "fallback (sustained)", 6650.0
+    gemm_tf = gemm_flops_step * args.steps / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
+    per_launch_flops = gemm_flops_step / 88
+    attn_flops_step = 22 * 4096 * visible_pairs(lengths, chunk or None)
+    attn_tf = attn_flops_step * args.steps / (prof["attention"]["ms_total"] / 1000.0) / 1e12 \
+        if prof["attention"]["ms_total"] > 0 else None
+    total_flops = estimator_flops(lengths, chunk or None, 22)
+    nfe_tf = total_flops / (ms_per_step / 1000.0) / 1e12
+    traffic = None
+    try:
+        tr = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
+        traffic = tr.get(args.config, {}).get("gemm_bytes_per_launch")
+    except Exception:
+        pass
+    roofline = {"bound": "tensor", "kernel": "tc_gemm_kernel (tcgen05, 4 per block)",
+                "achieved": gemm_tf, "peak": peak_tf, "unit": "TFLOP/s",
+                "frac": (gemm_tf / peak_tf) if gemm_tf else None, "peak_source": peak_src,
+                "flops_per_launch": per_launch_flops,
+                "avg_launch_ms": gemm_ms / max(gemm_launches, 1), "traffic": traffic,
+                "attention_tflops": attn_tf, "attention_frac": (attn_tf / peak_tf) if attn_tf else None,
+                "nfe_tflops": nfe_tf, "nfe_frac": nfe_tf / peak_tf}
+
+    # ---- end to end through the public module API with host buffers
+    e2e = None
+    if True:
+        pin = {k: v.to(torch.bfloat16).pin_memory() for k, v in host.items()}
+        dev2 = {k: torch.empty_like(v, device=device) for k, v in pin.items()}
+        out_h = torch.empty(len(lengths), 80, T, dtype=torch.bfloat16).pin_memory()
+        h2d = sum(v.numel() * v.element_size() for v in pin.values())
+        d2h = out_h.numel() * out_h.element_size() + 4 * len(lengths)
+
+        def e2e_step():
+            for k in pin:
+                dev2[k].copy_(pin[k], non_blocking=True)
+            with torch.inference_mode():
+                y = model(dev2["x"], dev2["mask"], dev2["mu"], dev2["t"], dev2["spks"], dev2["cond"],
+                          streaming=streaming)
+            out_h.copy_(y, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        et = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": all_rows * args.steps / (float(et.item()) / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "api": "B200DiT.forward(x, mask, mu, t, spks, cond, streaming) with pinned host buffers"}
+
+    # ---- CPU baseline (rank 0, N=1 only)
+    cpu = None
+    if rank == 0 and world == 1 and cpu_params is not None:
+        r, dt, L, cores, sample = cpu_oracle_rate(cpu_params, req_lengths, seed, 15.0)
+        cpu = {"value": r, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample, "seconds": dt}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+                "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded N(0,1) inputs, random-init weights of the 22-layer DiT)",
+                "config": cfg, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": int(launches), "clocks": clocks.summary(),
+                "request_frames_per_s": value / 2, "kernel_ms": prof,
+                "step_ms_min": min(step_ms), "step_ms_median": float(statistics.median(step_ms))}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

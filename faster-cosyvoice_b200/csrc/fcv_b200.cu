@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -47,6 +48,7 @@ int fail(int code, const char* fmt, ...) {
 
 #define FCV_LAUNCH_CHECK(name)                                                          \
   do {                                                                                 \
+    count_launch();                                                                    \
     cudaError_t e_ = cudaGetLastError();                                               \
     if (e_ != cudaSuccess) return fail(FCV_ECUDA, "launch of %s failed: %s", name, cudaGetErrorString(e_)); \
   } while (0)
@@ -71,6 +73,54 @@ int num_sms() {
   }
   return cached[dev];
 }
+
+// ------------------------------------------------------------------ tracing
+// Launch counter and optional CUDA-event timing of the executor's launches.
+std::atomic<long> g_launches{0};
+struct ProfState {
+  bool on = false;
+  std::vector<cudaEvent_t> pool;
+  size_t next = 0;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> marks;
+  int open_cat = -1;
+  cudaEvent_t open_ev = nullptr;
+};
+ProfState g_prof;
+std::mutex g_prof_mu;
+
+inline void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+cudaEvent_t prof_event() {
+  if (g_prof.next >= g_prof.pool.size()) return nullptr;
+  return g_prof.pool[g_prof.next++];
+}
+void prof_begin(int cat, cudaStream_t s) {
+  if (!g_prof.on) return;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  cudaEvent_t e = prof_event();
+  if (!e) return;
+  cudaEventRecord(e, s);
+  g_prof.open_cat = cat;
+  g_prof.open_ev = e;
+}
+void prof_end(cudaStream_t s) {
+  if (!g_prof.on) return;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  if (g_prof.open_ev == nullptr) return;
+  cudaEvent_t e = prof_event();
+  if (!e) {
+    g_prof.open_ev = nullptr;
+    return;
+  }
+  cudaEventRecord(e, s);
+  g_prof.marks.push_back({g_prof.open_cat, {g_prof.open_ev, e}});
+  g_prof.open_ev = nullptr;
+}
+struct ProfScope {
+  cudaStream_t s;
+  ProfScope(int cat, cudaStream_t st) : s(st) { prof_begin(cat, st); }
+  ~ProfScope() { prof_end(s); }
+};
 
 // ------------------------------------------------------------------ tensor maps
 typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -294,6 +344,8 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   const bool is_bf16 = dtype == FCV_DTYPE_BF16;
 
   // 1. time embedding + all AdaLN projections (one GEMM, flashinfer_dit.py:430-445)
+  {
+  ProfScope ps(FCV_CAT_ADALN, s);
   time_embed_kernel<T><<<B, 256, 0, s>>>(static_cast<const T*>(w->time_w1), w->time_b1,
                                         static_cast<const T*>(w->time_w2), w->time_b2,
                                         static_cast<const T*>(bt->t), is_bf16 ? 1 : 0, ws.temb,
@@ -305,10 +357,12 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     g.epi = make_epi(EPI_F32, B, (int)MS, ws.mods, MS, w->ada_b);
     FCV_TRY(run_gemm(g, dtype, s));
   }
+  }
   if (N == 0) return FCV_OK;
 
   // 2. input embedding: gather, proj (K=320), causal grouped conv x2 + Mish + residual
   {
+    ProfScope ps(FCV_CAT_EMBED, s);
     dim3 grid((bt->T + 31) / 32, B);
     embed_gather_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(bt->x), static_cast<const T*>(bt->cond),
                                                 static_cast<const T*>(bt->mu), static_cast<const T*>(bt->spks),
@@ -340,7 +394,10 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   const size_t es = dsize(dtype);
   for (int i = 0; i < depth; ++i) {
     const float* mi = ws.mods + (long)i * 6144;
-    FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mi + 0, mi + 1024, bt->doc_ids, MS, N, ws.norm, dtype, s));
+    {
+      ProfScope ps(FCV_CAT_LN, s);
+      FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mi + 0, mi + 1024, bt->doc_ids, MS, N, ws.norm, dtype, s));
+    }
     GemmCall q{};
     q.A = ws.norm; q.lda = 1024; q.a_rows = N; q.M = N; q.N = 3072; q.K = 1024;
     q.W = static_cast<const uint8_t*>(w->qkv_w) + (size_t)i * 3072 * 1024 * es;
@@ -348,9 +405,15 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     q.epi.aux = bt->positions;
     q.epi.rope_cos = w->rope_cos;
     q.epi.rope_sin = w->rope_sin;
-    FCV_TRY(run_gemm(q, dtype, s));
-    FCV_TRY(run_attention(ws.qkv, dtype, bt->cu_seqlens, bt->chunk, bt->attn_tiles, bt->n_attn_tiles,
-                          ws.attn, s));
+    {
+      ProfScope ps(FCV_CAT_GEMM_QKV, s);
+      FCV_TRY(run_gemm(q, dtype, s));
+    }
+    {
+      ProfScope ps(FCV_CAT_ATTENTION, s);
+      FCV_TRY(run_attention(ws.qkv, dtype, bt->cu_seqlens, bt->chunk, bt->attn_tiles, bt->n_attn_tiles,
+                            ws.attn, s));
+    }
     GemmCall o{};
     o.A = ws.attn; o.lda = 1024; o.a_rows = N; o.M = N; o.N = 1024; o.K = 1024;
     o.W = static_cast<const uint8_t*>(w->o_w) + (size_t)i * 1024 * 1024 * es;
@@ -358,13 +421,22 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     o.epi.aux = bt->doc_ids;
     o.epi.gate = mi + 2048;
     o.epi.gate_stride = MS;
-    FCV_TRY(run_gemm(o, dtype, s));
-    FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mi + 3072, mi + 4096, bt->doc_ids, MS, N, ws.norm, dtype, s));
+    {
+      ProfScope ps(FCV_CAT_GEMM_OUT, s);
+      FCV_TRY(run_gemm(o, dtype, s));
+    }
+    {
+      ProfScope ps(FCV_CAT_LN, s);
+      FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mi + 3072, mi + 4096, bt->doc_ids, MS, N, ws.norm, dtype, s));
+    }
     GemmCall f1{};
     f1.A = ws.norm; f1.lda = 1024; f1.a_rows = N; f1.M = N; f1.N = 2048; f1.K = 1024;
     f1.W = static_cast<const uint8_t*>(w->ff1_w) + (size_t)i * 2048 * 1024 * es;
     f1.epi = make_epi(EPI_GELU, N, 2048, ws.mid, 2048, w->ff1_b + (long)i * 2048);
-    FCV_TRY(run_gemm(f1, dtype, s));
+    {
+      ProfScope ps(FCV_CAT_GEMM_FF1, s);
+      FCV_TRY(run_gemm(f1, dtype, s));
+    }
     GemmCall f2{};
     f2.A = ws.mid; f2.lda = 2048; f2.a_rows = N; f2.M = N; f2.N = 1024; f2.K = 2048;
     f2.W = static_cast<const uint8_t*>(w->ff2_w) + (size_t)i * 1024 * 2048 * es;
@@ -372,11 +444,15 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     f2.epi.aux = bt->doc_ids;
     f2.epi.gate = mi + 5120;
     f2.epi.gate_stride = MS;
-    FCV_TRY(run_gemm(f2, dtype, s));
+    {
+      ProfScope ps(FCV_CAT_GEMM_FF2, s);
+      FCV_TRY(run_gemm(f2, dtype, s));
+    }
   }
 
   // 4. final AdaLN (chunk order scale, shift: modules.py:260-265), proj_out, unpack
   const float* mf = ws.mods + (long)depth * 6144;
+  ProfScope ps_out(FCV_CAT_OUTPUT, s);
   FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mf + 1024, mf + 0, bt->doc_ids, MS, N, ws.norm, dtype, s));
   zero_padding_kernel<T><<<std::max(1, std::min(4096, (int)(((long)B * 80 * bt->T + 255) / 256))), 256, 0, s>>>(
       bt->cu_seqlens, B, bt->T, static_cast<T*>(bt->out));
@@ -595,6 +671,40 @@ int fcv_cfg_euler(float* x, const void* d, int d_dtype, int R, int T, float dt, 
   FCV_LAUNCH_CHECK("cfg_euler_kernel");
   return FCV_OK;
 }
+
+int fcv_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  if (on && g_prof.pool.empty()) {
+    g_prof.pool.resize(16384);
+    for (auto& e : g_prof.pool) FCV_CUDA(cudaEventCreate(&e));
+  }
+  g_prof.on = on != 0;
+  return FCV_OK;
+}
+
+int fcv_profile_collect(float* ms, int* launches, int n_categories) {
+  if (!ms || !launches || n_categories < 0) return fail(FCV_EINVAL, "fcv_profile_collect: bad arguments");
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (int c = 0; c < n_categories; ++c) {
+    ms[c] = 0.f;
+    launches[c] = 0;
+  }
+  for (auto& m : g_prof.marks) {
+    FCV_CUDA(cudaEventSynchronize(m.second.second));
+    float t = 0.f;
+    FCV_CUDA(cudaEventElapsedTime(&t, m.second.first, m.second.second));
+    if (m.first >= 0 && m.first < n_categories) {
+      ms[m.first] += t;
+      launches[m.first] += 1;
+    }
+  }
+  g_prof.marks.clear();
+  g_prof.next = 0;
+  g_prof.open_ev = nullptr;
+  return FCV_OK;
+}
+
+long fcv_launch_count(void) { return g_launches.load(); }
 
 size_t fcv_dit_workspace_bytes(int N, int B, int depth, int dtype) {
   if (N < 0 || B < 0 || depth < 0 || !valid_dtype(dtype)) return 0;

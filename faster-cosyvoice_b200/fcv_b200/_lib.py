@@ -29,6 +29,9 @@ EPI_BIAS_ROPE_QKV = 2
 EPI_BIAS_GATE_RES = 3
 EPI_BIAS_F32 = 4
 
+CATEGORIES = ("gemm_qkv", "gemm_out", "gemm_ff1", "gemm_ff2", "attention", "ln_modulate", "embed",
+              "adaln", "output")
+
 # Exported entry points (kept in sync with include/fcv_b200.h; a CPU test checks both).
 EXPORTS = (
     "fcv_version",
@@ -44,6 +47,9 @@ EXPORTS = (
     "fcv_attn_tiles",
     "fcv_time_embed",
     "fcv_cfg_euler",
+    "fcv_profile_enable",
+    "fcv_profile_collect",
+    "fcv_launch_count",
     "fcv_dit_workspace_bytes",
     "fcv_dit_forward",
 )
@@ -132,6 +138,9 @@ _SIGNATURES = {
     "fcv_attn_tiles": (_i, [_vp, _i, _i, _vp, _i]),
     "fcv_time_embed": (_i, [ctypes.POINTER(DitWeights), _vp, _i, _vp, _vp, _vp]),
     "fcv_cfg_euler": (_i, [_vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _vp, _vp]),
+    "fcv_profile_enable": (_i, [_i]),
+    "fcv_profile_collect": (_i, [_vp, _vp, _i]),
+    "fcv_launch_count": (ctypes.c_long, []),
     "fcv_dit_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i]),
     "fcv_dit_forward": (_i, [ctypes.POINTER(DitWeights), ctypes.POINTER(DitBatch), _vp, ctypes.c_size_t, _vp]),
 }

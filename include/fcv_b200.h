@@ -217,6 +217,27 @@ int fcv_time_embed(const fcv_dit_weights* w, const void* t, int B, float* temb,
 int fcv_cfg_euler(float* x, const void* d, int d_dtype, int R, int T, float dt, float cfg_rate,
                   void* x_next, void* stream);
 
+/* Tracing ----------------------------------------------------------------- */
+/* Kernel classes timed by the executor when profiling is on. */
+#define FCV_CAT_GEMM_QKV 0
+#define FCV_CAT_GEMM_OUT 1
+#define FCV_CAT_GEMM_FF1 2
+#define FCV_CAT_GEMM_FF2 3
+#define FCV_CAT_ATTENTION 4
+#define FCV_CAT_LN 5
+#define FCV_CAT_EMBED 6
+#define FCV_CAT_ADALN 7
+#define FCV_CAT_OUTPUT 8
+#define FCV_CAT_COUNT 9
+/* When on, fcv_dit_forward brackets every launch with CUDA events on its
+ * stream (the reference has no equivalent; it has only host wall clocks). */
+int fcv_profile_enable(int on);
+/* Synchronises the recorded events and writes, per class, the summed device
+ * milliseconds and the number of launches since the last collect. */
+int fcv_profile_collect(float* ms, int* launches, int n_categories);
+/* Number of kernels this library has launched in this process. */
+long fcv_launch_count(void);
+
 /* Whole estimator call ---------------------------------------------------- */
 /* Bytes of workspace fcv_dit_forward needs for N packed rows, B sequences. */
 size_t fcv_dit_workspace_bytes(int N, int B, int depth, int dtype);

@@ -1,0 +1,136 @@
+"""CPU checks of the C-ABI library and the host logic (no GPU needed).
+
+* the library cross-compiles for sm_100a, loads, and exports exactly the
+  entry points ``include/fcv_b200.h`` declares;
+* argument validation fails with a status and a message before any CUDA call;
+* host-only entry points (attention work list, workspace sizing) compute;
+* the layout ("plan") cache mirrors the reference's pool semantics
+  (tests/test_plan_pool.py in the reference).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, ensure_built
+
+HEADER = ROOT / "include" / "fcv_b200.h"
+
+
+def header_functions() -> set[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"\b(fcv_[a-z0-9_]+)\s*\(", text))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    ensure_built()
+    from fcv_b200 import _lib
+
+    return _lib.lib()
+
+
+def test_library_exports_every_declared_entry_point(lib):
+    from fcv_b200 import _lib
+
+    declared = header_functions()
+    assert declared == set(_lib.EXPORTS)
+    so = _lib.LIB_PATH
+    out = subprocess.run(["nm", "-D", "--defined-only", so], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (fcv_[a-z0-9_]+)", out))
+    assert declared <= exported, declared - exported
+    for name in declared:
+        assert hasattr(lib, name)
+
+
+def test_version_and_error_paths_without_gpu(lib):
+    assert lib.fcv_version() >= 1
+    rc = lib.fcv_gemm(None, None, None, 1, 1, 1, 1, 0, None, None, None, 0, None, None, None)
+    assert rc == -1
+    assert b"fcv_gemm" in lib.fcv_last_error()
+    assert lib.fcv_dit_forward(None, None, None, 0, None) == -1
+    assert lib.fcv_attention(None, 1, None, 0, 0, 0, None, 0, None, None) == -1
+    assert lib.fcv_ln_modulate(None, 0, None, None, None, 0, 0, None, 0, None) == -1
+    assert lib.fcv_pack_layout(None, 0, 0, 0, None, None, None, None, None, None) == -1
+
+
+def test_workspace_bytes_grows_with_rows(lib):
+    a = lib.fcv_dit_workspace_bytes(1000, 4, 22, 1)
+    b = lib.fcv_dit_workspace_bytes(2000, 4, 22, 1)
+    c = lib.fcv_dit_workspace_bytes(1000, 4, 22, 0)
+    assert 0 < a < b and a < c
+    assert lib.fcv_dit_workspace_bytes(-1, 4, 22, 1) == 0
+
+
+def _tiles(lib, lengths, chunk):
+    cap = sum((L + 127) // 128 for L in lengths)
+    buf = (ctypes.c_int32 * (2 * max(cap, 1)))()
+    lens = (ctypes.c_int32 * len(lengths))(*lengths)
+    n = lib.fcv_attn_tiles(ctypes.addressof(lens), len(lengths), chunk, ctypes.addressof(buf), cap)
+    return n, np.array(list(buf)[:2 * n]).reshape(-1, 2)
+
+
+@pytest.mark.parametrize("chunk", [0, 50])
+def test_attention_work_list_covers_rows_and_orders_by_cost(lib, chunk):
+    lengths = [1, 127, 128, 129, 1000, 0, 3000, 64]
+    n, tiles = _tiles(lib, lengths, chunk)
+    seen = set()
+    costs = []
+    for d, q0 in tiles:
+        rows = min(128, lengths[d] - q0)
+        assert rows > 0
+        for q in range(q0, q0 + rows):
+            assert (d, q) not in seen
+            seen.add((d, q))
+        q_last = q0 + rows - 1
+        kv = lengths[d] if not chunk else min(lengths[d], (q_last // chunk + 1) * chunk)
+        costs.append(rows * kv)
+    assert len(seen) == sum(lengths)
+    assert costs == sorted(costs, reverse=True)
+
+
+def test_attention_work_list_capacity_error(lib):
+    lens = (ctypes.c_int32 * 1)(1000)
+    buf = (ctypes.c_int32 * 4)()
+    assert lib.fcv_attn_tiles(ctypes.addressof(lens), 1, 0, ctypes.addressof(buf), 2) == -1
+
+
+def test_layout_cache_fifo_and_no_replan(monkeypatch, lib):
+    """Recurring batch compositions reuse their prepared layout (no re-plan);
+    the cache is a bounded FIFO of 64 (flashinfer_dit.py:62, 400-404)."""
+    import torch
+
+    from fcv_b200 import model as M
+
+    real_call = M.call
+
+    def fake_call(name, *args):
+        if name == "fcv_pack_layout":
+            return 0
+        return real_call(name, *args)
+
+    monkeypatch.setattr(M, "call", fake_call)
+    dit = M.B200DiT(depth=1)
+    cpu = torch.device("cpu")
+    monkeypatch.setattr(M, "_stream", lambda device: 0)
+    a = dit.prepare_layout([100, 100], 100, True, cpu)
+    b = dit.prepare_layout([200, 200], 200, True, cpu)
+    assert a is not b and dit.plan_calls == 2
+    assert dit.prepare_layout([100, 100], 100, True, cpu) is a
+    assert dit.prepare_layout([200, 200], 200, True, cpu) is b
+    assert dit.plan_calls == 2
+    # streaming and offline are different plans (chunk mask vs full)
+    assert dit.prepare_layout([100, 100], 100, False, cpu) is not a
+    for i in range(64):
+        dit.prepare_layout([i + 1], 64, False, cpu)
+    assert len(dit._layouts) == 64
+    assert dit.prepare_layout([100, 100], 100, True, cpu) is not a  # evicted, re-planned
+    with pytest.raises(ValueError):
+        dit.prepare_layout([5, 300], 100, True, cpu)

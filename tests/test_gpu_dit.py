@@ -1,0 +1,151 @@
+"""Whole-estimator parity on the GPU (B200DiT -> fcv_dit_forward through the C ABI).
+
+Gates (north star): fp32 rel-L2 <= 1e-5 and bf16 rel-L2 <= 1e-2 against the
+reference torch (padded SDPA) path on identical seeded inputs -- the golden
+vectors under tests/golden/ were produced by the reference itself -- and the
+10-step ODE mel within max-abs 2e-2.  Only valid frames are compared; the
+padding frames of our output must be exactly zero."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import ensure_built, load_golden, make_model, numpy_params, rel_l2
+from oracle import dit_oracle as O
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _built():
+    ensure_built()
+    yield
+    from fcv_b200 import ops
+
+    assert ops.device_error() == 0
+
+
+def _model(seed, depth, dtype):
+    m = make_model(seed, depth).to(DEV, dtype)
+    m.finalize_weights()
+    return m
+
+
+def _run(model, z, streaming, dtype):
+    T = lambda a: torch.tensor(a, device=DEV).to(dtype)  # noqa: E731
+    with torch.inference_mode():
+        y = model(T(z["x"]), T(z["mask"]), T(z["mu"]), T(z["t"]), T(z["spks"]), T(z["cond"]), streaming=streaming)
+    return y.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("name", ["dit_block_fp32", "dit_depth2_edge", "dit_depth22_cfg"])
+def test_fp32_matches_reference_golden(name):
+    z = load_golden(name)
+    model = _model(int(z["seed"]), int(z["depth"]), torch.float32)
+    for streaming, key in ((False, "out_offline"), (True, "out_streaming")):
+        y = _run(model, z, streaming, torch.float32)
+        for b, L in enumerate(z["lengths"]):
+            assert rel_l2(y[b, :, :L], z[key][b, :, :L]) <= 1e-5, (name, streaming, b)
+            assert not np.any(y[b, :, L:]), "padding frames must be zero"
+
+
+@pytest.mark.parametrize("name", ["dit_block_fp32", "dit_depth2_edge", "dit_depth22_cfg"])
+def test_bf16_matches_reference_within_1e2(name):
+    """bf16 estimator vs the reference on the same bf16-rounded weights and
+    inputs; the reference side is the oracle (pinned to the reference's golden
+    outputs) run in fp32 with the reference's bf16 time-argument rounding."""
+    z = load_golden(name)
+    model = _model(int(z["seed"]), int(z["depth"]), torch.bfloat16)
+    params = {k: v.float().cpu().numpy() for k, v in model.state_dict().items()}
+    zb = {k: (O.bf16_round(v) if k in ("x", "mu", "cond", "spks", "t") else v) for k, v in z.items()}
+    for streaming in (False, True):
+        y = _run(model, z, streaming, torch.bfloat16)
+        ref = O.dit_forward_padded(params, zb["x"], zb["mask"], zb["mu"], zb["t"], zb["spks"], zb["cond"],
+                                   streaming=streaming, emulate_bf16_time=True)
+        for b, L in enumerate(z["lengths"]):
+            e = rel_l2(y[b, :, :L], ref[b, :, :L])
+            assert e <= 1e-2, (name, streaming, b, e)
+
+
+def test_batch_composition_invariance_bit_exact():
+    """A document's output does not depend on its neighbours in the packed
+    batch (reference invariant: flashinfer_attention.py:104-107,
+    tests/gpu/test_stream_flashinfer.py:87-90)."""
+    model = _model(2, 2, torch.bfloat16)
+    rng = np.random.default_rng(3)
+    lengths = [173, 60, 251, 1, 129]
+    T = 260
+    B = len(lengths)
+    x = torch.tensor(rng.standard_normal((B, 80, T)), device=DEV, dtype=torch.bfloat16)
+    mu = torch.tensor(rng.standard_normal((B, 80, T)), device=DEV, dtype=torch.bfloat16)
+    cond = torch.tensor(rng.standard_normal((B, 80, T)), device=DEV, dtype=torch.bfloat16)
+    spks = torch.tensor(rng.standard_normal((B, 80)), device=DEV, dtype=torch.bfloat16)
+    t = torch.tensor(rng.uniform(size=B), device=DEV, dtype=torch.bfloat16)
+    mask = torch.zeros(B, 1, T, device=DEV, dtype=torch.bfloat16)
+    for b, L in enumerate(lengths):
+        mask[b, 0, :L] = 1
+    with torch.inference_mode():
+        for streaming in (True, False):
+            packed = model(x, mask, mu, t, spks, cond, streaming=streaming)
+            for b, L in enumerate(lengths):
+                solo = model(x[b:b + 1, :, :L].contiguous(), mask[b:b + 1, :, :L].contiguous(),
+                             mu[b:b + 1, :, :L].contiguous(), t[b:b + 1], spks[b:b + 1],
+                             cond[b:b + 1, :, :L].contiguous(), streaming=streaming)
+                assert torch.equal(packed[b:b + 1, :, :L], solo), (streaming, b)
+
+
+def test_gate_a_streaming_prefix_stability():
+    """Reference Gate A (tests/gpu/test_flashinfer_streaming_estimator.py:58-89):
+    with the chunk-50 mask the first floor(160/50)*50 = 150 output frames for
+    T=160 equal those for T=200; with the full mask they must differ."""
+    model = _model(0, 22, torch.bfloat16)
+    g = torch.Generator().manual_seed(1234)
+    T_new, T_old, stable = 200, 160, 150
+    x = torch.randn(2, 80, T_new, generator=g).to(DEV, torch.bfloat16)
+    mu = torch.randn(2, 80, T_new, generator=g).to(DEV, torch.bfloat16)
+    cond = torch.randn(2, 80, T_new, generator=g).to(DEV, torch.bfloat16)
+    spks = torch.randn(2, 80, generator=g).to(DEV, torch.bfloat16)
+    t = torch.rand(1, generator=g).to(DEV, torch.bfloat16).expand(2).contiguous()
+    mask = torch.ones(2, 1, T_new, device=DEV, dtype=torch.bfloat16)
+
+    def run(T, streaming):
+        return model(x[:, :, :T].contiguous(), mask[:, :, :T].contiguous(), mu[:, :, :T].contiguous(), t, spks,
+                     cond[:, :, :T].contiguous(), streaming=streaming)
+
+    with torch.inference_mode():
+        d_s = (run(T_old, True)[:, :, :stable] - run(T_new, True)[:, :, :stable]).abs().max().item()
+        d_o = (run(T_old, False)[:, :, :stable] - run(T_new, False)[:, :, :stable]).abs().max().item()
+    assert d_s <= 1e-3, d_s
+    assert d_o > 5e-3, d_o
+
+
+@pytest.mark.parametrize("dtype,tol", [("float32", 1e-4), ("bfloat16", 2e-2)])
+def test_ode_matches_reference_golden(dtype, tol):
+    """10-step CFG Euler (flashinfer_flow.py:16-74) vs the reference's own
+    solve_euler_batched output (golden), streaming and offline."""
+    import types
+
+    from fcv_b200.flow import solve_euler_batched
+
+    dt = getattr(torch, dtype)
+    z = load_golden("ode")
+    model = _model(3, 2, dt)
+    decoder = types.SimpleNamespace(estimator=model, inference_cfg_rate=0.7)
+    args = [torch.tensor(z[k], device=DEV) for k in ("noise", "mu", "mask", "spks", "cond")]
+    for streaming, key in ((True, "out_streaming"), (False, "out_offline")):
+        y = solve_euler_batched(decoder, *args, num_timesteps=10, streaming=streaming).float().cpu().numpy()
+        for i, L in enumerate(z["lengths"]):
+            err = np.abs(y[i, :, :L] - z[key][i, :, :L]).max()
+            assert err <= tol, (dtype, key, i, err)
+
+
+def test_forward_rejects_missing_conditions():
+    model = _model(0, 1, torch.float32)
+    x = torch.zeros(1, 80, 10, device=DEV)
+    with pytest.raises(ValueError):
+        model(x, torch.ones(1, 1, 10, device=DEV), x, torch.zeros(1, device=DEV), None, x)
+    with pytest.raises(RuntimeError):
+        model.finalize_weights()
