@@ -295,6 +295,8 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // Workspace carve-up for fcv_dit_forward.
 struct Workspace {
   float* temb;
+  void* tsin;
+  void* th1;
   void* silu;
   float* mods;
   float* h;
@@ -320,6 +322,8 @@ Workspace carve(uint8_t* base, int N, int B, int depth, int dtype) {
     return p;
   };
   w.temb = static_cast<float*>(take((size_t)B * 1024 * 4));
+  w.tsin = take((size_t)std::max(B, 1) * 256 * es);
+  w.th1 = take((size_t)std::max(B, 1) * 1024 * es);
   w.silu = take((size_t)std::max(B, 1) * 1024 * es);
   w.mods = static_cast<float*>(take((size_t)B * MS * 4));
   w.h = static_cast<float*>(take((size_t)N * 1024 * 4));
@@ -334,6 +338,25 @@ Workspace carve(uint8_t* base, int N, int B, int depth, int dtype) {
   return w;
 }
 
+// temb = W2 silu(W1 sinus(t) + b1) + b2 ; silu_act = silu(temb)  (modules.py:606-616)
+template <typename T>
+int run_time_embed(const fcv_dit_weights* w, const void* t, int B, void* tsin, void* th1, float* temb,
+                   void* silu_act, cudaStream_t s) {
+  const int dtype = w->dtype;
+  time_sinusoid_kernel<T><<<B, 128, 0, s>>>(static_cast<const T*>(t), dtype == FCV_DTYPE_BF16 ? 1 : 0,
+                                            static_cast<T*>(tsin));
+  FCV_LAUNCH_CHECK("time_sinusoid_kernel");
+  GemmCall g1{};
+  g1.A = tsin; g1.lda = 256; g1.a_rows = B; g1.W = w->time_w1; g1.M = B; g1.N = 1024; g1.K = 256;
+  g1.epi = make_epi(EPI_SILU, B, 1024, th1, 1024, w->time_b1);
+  FCV_TRY(run_gemm(g1, dtype, s));
+  GemmCall g2{};
+  g2.A = th1; g2.lda = 1024; g2.a_rows = B; g2.W = w->time_w2; g2.M = B; g2.N = 1024; g2.K = 1024;
+  g2.epi = make_epi(EPI_F32, B, 1024, temb, 1024, w->time_b2);
+  g2.epi.C2 = silu_act;
+  return run_gemm(g2, dtype, s);
+}
+
 template <typename T>
 int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Workspace& ws, cudaStream_t s) {
   const int dtype = w->dtype;
@@ -346,11 +369,7 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   // 1. time embedding + all AdaLN projections (one GEMM, flashinfer_dit.py:430-445)
   {
   ProfScope ps(FCV_CAT_ADALN, s);
-  time_embed_kernel<T><<<B, 256, 0, s>>>(static_cast<const T*>(w->time_w1), w->time_b1,
-                                        static_cast<const T*>(w->time_w2), w->time_b2,
-                                        static_cast<const T*>(bt->t), is_bf16 ? 1 : 0, ws.temb,
-                                        static_cast<T*>(ws.silu));
-  FCV_LAUNCH_CHECK("time_embed_kernel");
+  FCV_TRY(run_time_embed<T>(w, bt->t, B, ws.tsin, ws.th1, ws.temb, ws.silu, s));
   {
     GemmCall g{};
     g.A = ws.silu; g.lda = 1024; g.a_rows = B; g.W = w->ada_w; g.M = B; g.N = (int)MS; g.K = 1024;
@@ -642,16 +661,13 @@ int fcv_time_embed(const fcv_dit_weights* w, const void* t, int B, float* temb, 
   if (!valid_dtype(w->dtype)) return fail(FCV_EINVAL, "fcv_time_embed: bad dtype");
   if (B == 0) return FCV_OK;
   cudaStream_t s = as_stream(stream);
-  if (w->dtype == FCV_DTYPE_BF16)
-    time_embed_kernel<bf16><<<B, 256, 0, s>>>(static_cast<const bf16*>(w->time_w1), w->time_b1,
-                                             static_cast<const bf16*>(w->time_w2), w->time_b2,
-                                             static_cast<const bf16*>(t), 1, temb, static_cast<bf16*>(silu_act));
-  else
-    time_embed_kernel<float><<<B, 256, 0, s>>>(static_cast<const float*>(w->time_w1), w->time_b1,
-                                              static_cast<const float*>(w->time_w2), w->time_b2,
-                                              static_cast<const float*>(t), 0, temb, static_cast<float*>(silu_act));
-  FCV_LAUNCH_CHECK("time_embed_kernel");
-  return FCV_OK;
+  // silu_act holds (B, 1024) outputs followed by (B, 256) + (B, 1024) scratch rows
+  uint8_t* base = static_cast<uint8_t*>(silu_act);
+  const size_t es = dsize(w->dtype);
+  void* tsin = base + (size_t)B * 1024 * es;
+  void* th1 = base + (size_t)B * 1280 * es;
+  if (w->dtype == FCV_DTYPE_BF16) return run_time_embed<bf16>(w, t, B, tsin, th1, temb, silu_act, s);
+  return run_time_embed<float>(w, t, B, tsin, th1, temb, silu_act, s);
 }
 
 int fcv_cfg_euler(float* x, const void* d, int d_dtype, int R, int T, float dt, float cfg_rate, void* x_next,

@@ -30,6 +30,7 @@ enum Epi : int {
   EPI_MISH_GAP = 6,   // gapped row g: C(act)[g] = mish(acc + b) unless gap_rows[g] < 0
   EPI_MISH_RES = 7,   // gapped row g, packed p = gap_rows[g] >= 0: h(f32)[p] = mish(acc+b) + res[g]
   EPI_UNPACK = 8,     // out(act)[doc, col, pos] = acc + b   (proj_out -> (B, 80, T))
+  EPI_SILU = 9,       // C(act) = silu(acc + b)
 };
 
 constexpr int kConvPad = 30;  // kernel_size - 1 zero rows before every document
@@ -48,6 +49,7 @@ struct EpiParams {
   const float* rope_cos;
   const float* rope_sin;
   int T;               // padded length (UNPACK)
+  void* C2;            // EPI_F32: when set, also C2(act)[row*1024 + col] = silu(acc + b)
 };
 
 // Apply the epilogue to W consecutive columns [col0, col0+W) of one row.
@@ -106,7 +108,16 @@ __device__ __forceinline__ void epilogue_apply(const EpiParams& p, int row, int 
       }
       return;
     }
+    case EPI_SILU:
+#pragma unroll
+      for (int j = 0; j < W; ++j) v[j] = silu(v[j]);
+      break;
     case EPI_F32: {
+      if (p.C2 != nullptr) {
+        Tact* c2 = reinterpret_cast<Tact*>(p.C2) + (long)row * 1024 + col0;
+        for (int j = 0; j < W; ++j)
+          if (col0 + j < p.N) c2[j] = from_f<Tact>(silu(v[j]));
+      }
       float* c = reinterpret_cast<float*>(p.C) + (long)row * p.ldc + col0;
       if (full && W % 4 == 0) {
 #pragma unroll

@@ -263,47 +263,22 @@ __global__ void __launch_bounds__(256) embed_gather_kernel(const T* __restrict__
 }
 
 // ------------------------------------------------------------------ time embedding
-// temb = W2 silu(W1 sinus(t) + b1) + b2 (modules.py:71-83, 606-616); silu_out = silu(temb).
+// Sinusoid of the timestep (modules.py:76-83), stored in the activation type as
+// the reference casts it (modules.py:614).  In bf16 mode the argument 1000*t is
+// itself rounded to bf16, as the reference multiplies in the input dtype.
+// The two MLP layers run as GEMMs with SiLU epilogues.
 template <typename T>
-__global__ void __launch_bounds__(256) time_embed_kernel(const T* __restrict__ w1, const float* __restrict__ b1,
-                                                         const T* __restrict__ w2, const float* __restrict__ b2,
-                                                         const T* __restrict__ t, int round_bf16,
-                                                         float* __restrict__ temb, T* __restrict__ silu_out) {
-  __shared__ float s_sin[256];
-  __shared__ float s_h1[1024];
+__global__ void __launch_bounds__(128) time_sinusoid_kernel(const T* __restrict__ t, int round_bf16,
+                                                            T* __restrict__ out) {
   const int b = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int i = threadIdx.x;  // 0..127
   float st = 1000.0f * to_f<T>(t[b]);
   if (round_bf16) st = bf16_round_f(st);
   const float neg = -0.0725223646f;  // float32(-ln(10000) / 127), as torch casts the scalar
-  for (int i = threadIdx.x; i < 128; i += blockDim.x) {
-    const float f = expf(static_cast<float>(i) * neg);
-    const float arg = st * f;
-    float sv = sinf(arg), cv = cosf(arg);
-    if (round_bf16) {
-      sv = bf16_round_f(sv);
-      cv = bf16_round_f(cv);
-    }
-    s_sin[i] = sv;
-    s_sin[128 + i] = cv;
-  }
-  __syncthreads();
-  for (int j = warp; j < 1024; j += 8) {
-    float s = 0.f;
-    for (int k = lane; k < 256; k += 32) s += to_f<T>(w1[(long)j * 256 + k]) * s_sin[k];
-    s = warp_sum(s) + b1[j];
-    s_h1[j] = silu(s);
-  }
-  __syncthreads();
-  for (int j = warp; j < 1024; j += 8) {
-    float s = 0.f;
-    for (int k = lane; k < 1024; k += 32) s += to_f<T>(w2[(long)j * 1024 + k]) * s_h1[k];
-    s = warp_sum(s) + b2[j];
-    if (lane == 0) {
-      temb[(long)b * 1024 + j] = s;
-      silu_out[(long)b * 1024 + j] = from_f<T>(silu(s));
-    }
-  }
+  const float f = expf(static_cast<float>(i) * neg);
+  const float arg = st * f;
+  out[(long)b * 256 + i] = from_f<T>(sinf(arg));
+  out[(long)b * 256 + 128 + i] = from_f<T>(cosf(arg));
 }
 
 // ------------------------------------------------------------------ output

@@ -62,7 +62,8 @@ def solve_euler_batched(decoder, noise: torch.Tensor, mu: torch.Tensor, mask: to
         cond = condition.to(dev)
         cond_in = torch.cat([cond, torch.zeros_like(cond)], 0).to(dt_w).contiguous()
 
-        x = noise.to(device=dev, dtype=sdtype).to(torch.float32).contiguous()
+        # a private fp32 copy: the update is in place and must not touch the caller's noise
+        x = noise.to(device=dev, dtype=sdtype).to(torch.float32, copy=True).contiguous()
         x_in = x.repeat(2, 1, 1).to(dt_w).contiguous()
         d = torch.empty(2 * R, C, T, dtype=dt_w, device=dev)
         t_in = torch.empty(2 * R, dtype=dt_w, device=dev)

@@ -203,9 +203,11 @@ int fcv_attn_tiles(const int32_t* lengths_host, int B, int chunk, int32_t* tiles
 
 /* Time embedding + AdaLN ---------------------------------------------------- */
 /* temb (B,1024) f32 = TimestepEmbedding(t) (modules.py:606-616); silu_act
- * (B,1024, element type dtype) = SiLU(temb) for the modulation GEMM.
- * In bf16 mode the sinusoid argument is bf16(1000*t) and the sinusoid is
- * rounded to bf16, as the reference computes them in the input dtype. */
+ * (B,1024, element type dtype) = SiLU(temb) for the modulation GEMM.  The
+ * silu_act buffer must hold B*2304 elements: rows B*1024.. are scratch for the
+ * sinusoid and the hidden layer.  In bf16 mode the sinusoid argument is
+ * bf16(1000*t) and the sinusoid is rounded to bf16, as the reference computes
+ * them in the input dtype. */
 int fcv_time_embed(const fcv_dit_weights* w, const void* t, int B, float* temb,
                    void* silu_act, void* stream);
 
