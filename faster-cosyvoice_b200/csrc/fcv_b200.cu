@@ -141,22 +141,27 @@ PFN_encodeTiled_t encode_fn() {
   return fn;
 }
 
-// 2-D bf16 tensor of `rows` x `cols` (row stride `ld` elements), box 64 x box_rows,
-// 128-byte swizzle, zero fill out of bounds.
-int make_tmap_bf16(CUtensorMap* m, const void* ptr, long rows, long cols, long ld, int box_rows) {
+// 2-D tensor of `rows` x `cols` (row stride `ld` elements) with a box of
+// box_cols x box_rows, 128-byte swizzle, zero fill out of bounds.
+int make_tmap(CUtensorMap* m, const void* ptr, bool f32, long rows, long cols, long ld, int box_cols, int box_rows) {
   PFN_encodeTiled_t enc = encode_fn();
   if (!enc) return fail(FCV_ECUDA, "cuTensorMapEncodeTiled unavailable");
-  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || ((ld * 2) & 15))
+  const int es = f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || ((ld * es) & 15))
     return fail(FCV_EINVAL, "TMA operand must be 16-byte aligned with a 16-byte multiple row stride");
   cuuint64_t gdim[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld * 2)};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld * es)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), gdim, gstride, box,
-                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   const_cast<void*>(ptr), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FCV_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return FCV_OK;
+}
+
+int make_tmap_bf16(CUtensorMap* m, const void* ptr, long rows, long cols, long ld, int box_rows) {
+  return make_tmap(m, ptr, false, rows, cols, ld, 64, box_rows);
 }
 
 // ------------------------------------------------------------------ GEMM launch
@@ -174,7 +179,7 @@ struct GemmCall {
 template <int BN, typename Tact>
 int launch_tc(const GemmCall& g, cudaStream_t s) {
   using Cfg = TcGemmCfg<BN>;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tc;
   const long a_cols = g.conv ? 1024 : g.K;
   FCV_TRY(make_tmap_bf16(&ta, g.A, g.a_rows, a_cols, g.lda, 128));
   FCV_TRY(make_tmap_bf16(&tb, g.W, g.N, g.K, g.K, BN));
@@ -184,6 +189,22 @@ int launch_tc(const GemmCall& g, cudaStream_t s) {
   args.n_blocks = (g.N + BN - 1) / BN;
   args.conv = g.conv;
   args.epi = g.epi;
+  // Output path: TMA store/reduce of 32-row x 128-byte tiles where the epilogue writes a
+  // plain row-major tile; direct per-thread stores for the scattering epilogues.
+  const int e = g.epi.epi;
+  args.tma_out = 0;
+  if (!g.conv && BN >= 128) {
+    if ((e == EPI_BIAS || e == EPI_GELU || e == EPI_ROPE || e == EPI_SILU) && g.N % 64 == 0) args.tma_out = 1;
+    else if (e == EPI_F32 && g.epi.C2 == nullptr && g.N % 32 == 0) args.tma_out = 1;
+    else if (e == EPI_GATE_RES && g.N % 32 == 0) args.tma_out = 2;
+  }
+  if (args.tma_out == 1 && e != EPI_F32) {
+    FCV_TRY(make_tmap(&tc, g.epi.C, false, g.M, g.N, g.epi.ldc, 64, 32));
+  } else if (args.tma_out != 0) {
+    FCV_TRY(make_tmap(&tc, g.epi.C, true, g.M, g.N, g.epi.ldc, 32, 32));
+  } else {
+    tc = ta;  // unused
+  }
   const int tiles = args.m_blocks * args.n_blocks;
   const int grid = std::min(tiles, num_sms());
   static bool attr_set[64] = {false};
@@ -194,7 +215,7 @@ int launch_tc(const GemmCall& g, cudaStream_t s) {
                                   Cfg::SMEM_BYTES));
     attr_set[dev & 63] = true;
   }
-  tc_gemm_kernel<BN, Tact><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, args);
+  tc_gemm_kernel<BN, Tact><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, tc, args);
   FCV_LAUNCH_CHECK("tc_gemm_kernel");
   return FCV_OK;
 }

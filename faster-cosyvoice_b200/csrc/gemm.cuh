@@ -192,6 +192,7 @@ struct TcGemmArgs {
   int m_blocks;
   int n_blocks;
   int conv;        // implicit-conv A addressing
+  int tma_out;     // 0: direct stores; 1: TMA store of act/f32 tiles; 2: TMA reduce-add into f32 h
   EpiParams epi;
 };
 
@@ -202,22 +203,69 @@ struct TcGemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
-  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int STAGING_BYTES = EPI_WARPS * 4096;   // 32 rows x 128 B per epilogue warp
+  static constexpr int BIAS_BYTES = EPI_WARPS * (BN / 2) * 4;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
-  static constexpr int THREADS = 192;
+  static constexpr int BUDGET = 227 * 1024 - 1024 - STAGING_BYTES - BIAS_BYTES - BAR_BYTES;
+  static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
+  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + BIAS_BYTES + BAR_BYTES;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
 
+// Write one thread's 128-byte row piece (8 x 16 B) into a 32-row staging tile in
+// the 128-byte-swizzled layout TMA expects (16-byte chunk c of row r at c ^ (r % 8)).
+__device__ __forceinline__ void stage_row128(uint8_t* stage, int r, const uint32_t (&w)[32]) {
+  uint8_t* row = stage + r * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 u = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = u;
+  }
+}
+
+// bf16 epilogue on 32 accumulator columns held as raw bits in r[]: adds the bias,
+// applies GELU / SiLU / partial RoPE and packs bf16 pairs into r[0..15].
+__device__ __forceinline__ void epi_bf16_half(const EpiParams& P, uint32_t (&r)[32], const float* bias,
+                                              int col0, int pos) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + bias[j];
+  if (P.epi == EPI_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+  } else if (P.epi == EPI_SILU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = silu(v[j]);
+  } else if (P.epi == EPI_ROPE && col0 < 2048 && (col0 & 1023) < 64) {
+    const int i0 = (col0 & 1023) >> 1;  // first rotary pair of this 32-column piece
+    const float* cs = P.rope_cos + (long)pos * 32 + i0;
+    const float* sn = P.rope_sin + (long)pos * 32 + i0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float cv = __ldg(cs + i), sv = __ldg(sn + i);
+      const float a = v[2 * i], b = v[2 * i + 1];
+      v[2 * i] = a * cv - b * sv;
+      v[2 * i + 1] = b * cv + a * sv;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) r[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+}
+
 template <int BN, typename Tact>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const TcGemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmC, const TcGemmArgs args) {
   using Cfg = TcGemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int HALF = BN / 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* bar_area = smem + STAGES * Cfg::STAGE_BYTES;
+  uint8_t* staging = smem + STAGES * Cfg::STAGE_BYTES;
+  float* bias_s = reinterpret_cast<float*>(staging + Cfg::STAGING_BYTES);
+  uint8_t* bar_area = reinterpret_cast<uint8_t*>(bias_s) + Cfg::BIAS_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -236,13 +284,14 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&tfull[a]), 1);
-      mbar_init(smem_u32(&tempty[a]), 4);
+      mbar_init(smem_u32(&tempty[a]), Cfg::EPI_WARPS);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (args.tma_out) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
@@ -352,27 +401,113 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(smem_u32(drain), 0, 105, nullptr);
     }
   } else {
-    // ---------------- epilogue warps 2..5 (TMEM lane quarter = warp % 4)
+    // ---------------- epilogue warps 2..9: TMEM lane quarter = warp % 4, column half = (warp-2)/4
+    const int ew = warp - 2;
     const int q = warp & 3;
+    const int col_begin = (ew >> 2) * HALF;
+    uint8_t* stage_buf = staging + ew * 4096;
+    const uint32_t stage_u32 = smem_u32(stage_buf);
+    float* bias_w = bias_s + ew * HALF;
+    const EpiParams& P = args.epi;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m_blk = tile / args.n_blocks;
       const int n_blk = tile - m_blk * args.n_blocks;
+      const int n0 = n_blk * BN + col_begin;  // first output column of this warp
+      const int row = m_blk * 128 + q * 32 + lane;
+      if (args.tma_out) {
+        // stage this warp's bias slice once per tile
+        for (int c = lane * 4; c < HALF; c += 128) {
+          float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (P.bias != nullptr && n0 + c + 3 < P.N) b4 = __ldg(reinterpret_cast<const float4*>(P.bias + n0 + c));
+          *reinterpret_cast<float4*>(bias_w + c) = b4;
+        }
+        __syncwarp();
+      }
       if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, 106, abort_flag)) break;
       tc_fence_after();
-      const int row = m_blk * 128 + q * 32 + lane;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + col_begin;
+      if (args.tma_out == 0) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c * 32, r);
-        tmem_wait_ld();
-        float v[32];
+        for (int c = 0; c < HALF / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+          float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        const int col0 = n_blk * BN + c * 32;
-        if (col0 < args.epi.N) epilogue_apply<Tact, 32>(args.epi, row, col0, v);
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          const int col0 = n0 + c * 32;
+          if (col0 < P.N) epilogue_apply<Tact, 32>(P, row, col0, v);
+        }
+      } else if (args.tma_out == 1 && sizeof(Tact) == 2 && P.epi != EPI_F32) {
+        // bf16 tiles: 64 columns (128 B per row) per TMA store
+        const int pos = (P.epi == EPI_ROPE && row < P.M) ? __ldg(P.aux + row) : 0;
+#pragma unroll 1
+        for (int c = 0; c < HALF / 64; ++c) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(taddr + c * 64, r0);
+          tmem_ld32(taddr + c * 64 + 32, r1);
+          tmem_wait_ld();
+          const int col0 = n0 + c * 64;
+          // in place: bits -> float (+ bias, activation) -> packed bf16 pairs in r0[0..15], r1[0..15]
+          epi_bf16_half(P, r0, bias_w + c * 64, col0, pos);
+          epi_bf16_half(P, r1, bias_w + c * 64 + 32, col0 + 32, pos);
+          uint32_t w[32];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            w[j] = r0[j];
+            w[16 + j] = r1[j];
+          }
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          stage_row128(stage_buf, lane, w);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && col0 < P.N && m_blk * 128 + q * 32 < P.M) {
+            tma_store_2d(&tmC, stage_u32, col0, m_blk * 128 + q * 32);
+            bulk_commit();
+          }
+        }
+      } else {
+        // f32 tiles: 32 columns (128 B per row) per TMA store (EPI_F32) or reduce-add (EPI_GATE_RES)
+        const float* grow = nullptr;
+        if (P.epi == EPI_GATE_RES) {
+          const int doc = row < P.M ? __ldg(P.aux + row) : 0;
+          grow = P.gate + (long)doc * P.gate_stride;
+        }
+#pragma unroll 1
+        for (int c = 0; c < HALF / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          const int col0 = n0 + c * 32;
+          float g[32];
+          if (grow != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 gv = __ldg(reinterpret_cast<const float4*>(grow + col0 + j));
+              g[j] = gv.x; g[j + 1] = gv.y; g[j + 2] = gv.z; g[j + 3] = gv.w;
+            }
+          }
+          tmem_wait_ld();
+          uint32_t w[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(r[j]) + bias_w[c * 32 + j];
+            if (grow != nullptr) x *= g[j];
+            w[j] = __float_as_uint(x);
+          }
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          stage_row128(stage_buf, lane, w);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && col0 < P.N && m_blk * 128 + q * 32 < P.M) {
+            if (args.tma_out == 2) tma_reduce_add_2d(&tmC, stage_u32, col0, m_blk * 128 + q * 32);
+            else tma_store_2d(&tmC, stage_u32, col0, m_blk * 128 + q * 32);
+            bulk_commit();
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -382,6 +517,8 @@ __global__ void __launch_bounds__(192, 1)
         acc_phase ^= 1;
       }
     }
+    if (lane == 0) bulk_wait0();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
