@@ -244,6 +244,250 @@ __global__ void __launch_bounds__(256) attn_bf16_mma_kernel(const bf16* __restri
   }
 }
 
+// ------------------------------------------------------------------ bf16 (tcgen05)
+// One CTA per (128-row query tile, head); 6 warps:
+//   warp 0   TMA: Q once, then K/V tiles of 64 keys into a 2-stage ring
+//   warp 1   owns TMEM (128 columns: S at 0..63, P.V partial at 64..127) and
+//            issues tcgen05.mma: S_j = Q K_j^T, then O_j = P_j V_j
+//   warps 2-5 softmax, one query row per thread (TMEM lane = row): mask, online
+//            max / sum in fp32, P_j as bf16 into 128-byte-swizzled shared memory,
+//            O accumulated in registers, normalised and stored at the end.
+// S_{j+1} is issued as soon as S_j has been read, so it overlaps the softmax of
+// tile j; 2 CTAs share an SM so one CTA's MMAs overlap the other's softmax.
+constexpr int kTcKv = 64;
+constexpr int kTcSmemQ = 128 * 128;       // 16 KB
+constexpr int kTcSmemKV = kTcKv * 128;    // 8 KB per K or V tile
+constexpr int kTcSmemP = 128 * 128;       // 16 KB (128 rows x 64 keys bf16)
+constexpr int kTcSmemBytes = 1024 + kTcSmemQ + 4 * kTcSmemKV + kTcSmemP + 256;
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(192, 2)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+                   const int32_t* __restrict__ cu, const int2* __restrict__ tiles, int chunk,
+                   bf16* __restrict__ out) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sK = sQ + kTcSmemQ;                 // 2 stages
+  const uint32_t sV = sK + 2 * kTcSmemKV;            // 2 stages
+  uint8_t* pP = smem + kTcSmemQ + 4 * kTcSmemKV;
+  const uint32_t sP = smem_u32(pP);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pP + kTcSmemP);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* s_empty = bars + 6;
+  uint64_t* p_full = bars + 7;
+  uint64_t* o_full = bars + 8;
+  uint64_t* drain = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int2 tl = tiles[blockIdx.x];
+  const int doc = tl.x, q0 = tl.y;
+  const int head = blockIdx.y;
+  const int base = cu[doc];
+  const int L = cu[doc + 1] - base;
+  const int kv_end = kv_limit(q0, kAttnQTile, L, chunk);
+  const int n_kv = (kv_end + kTcKv - 1) / kTcKv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(q_full), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&kv_full[i]), 1);
+      mbar_init(smem_u32(&kv_empty[i]), 1);
+    }
+    mbar_init(smem_u32(s_full), 1);
+    mbar_init(smem_u32(s_empty), 4);
+    mbar_init(smem_u32(p_full), 4);
+    mbar_init(smem_u32(o_full), 1);
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmKV);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      mbar_arrive_expect_tx(smem_u32(q_full), kTcSmemQ);
+      tma_load_2d(sQ, &tmQ, smem_u32(q_full), head * 64, base + q0);
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(smem_u32(&kv_empty[st]), ((j >> 1) & 1) ^ 1, 201, abort_flag)) break;
+        const uint32_t fb = smem_u32(&kv_full[st]);
+        mbar_arrive_expect_tx(fb, 2 * kTcSmemKV);
+        tma_load_2d(sK + st * kTcSmemKV, &tmKV, fb, 1024 + head * 64, base + j * kTcKv);
+        tma_load_2d(sV + st * kTcSmemKV, &tmKV, fb, 2048 + head * 64, base + j * kTcKv);
+        ++issued;
+      }
+      // wait for our own copies before the CTA may exit
+      mbar_wait(smem_u32(q_full), 0, 202, nullptr);
+      for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
+        mbar_wait(smem_u32(&kv_full[j & 1]), (j >> 1) & 1, 203, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, kTcKv, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, 64, false, true);  // V is MN-major
+      const uint32_t t_s = tmem;
+      const uint32_t t_o = tmem + 64;
+      bool ok = mbar_wait(smem_u32(q_full), 0, 204, abort_flag);
+      const uint64_t dq = sdesc_sw128(sQ);
+      auto issue_s = [&](int j) -> bool {
+        if (!mbar_wait(smem_u32(&kv_full[j & 1]), (j >> 1) & 1, 205, abort_flag)) return false;
+        if (j > 0 && !mbar_wait(smem_u32(s_empty), (j - 1) & 1, 206, abort_flag)) return false;
+        tc_fence_after();
+        const uint64_t dk = sdesc_sw128(sK + (j & 1) * kTcSmemKV);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) umma_bf16(t_s, dq + 2 * k, dk + 2 * k, idesc_s, k != 0);
+        umma_commit(smem_u32(s_full));
+        return true;
+      };
+      if (ok && n_kv > 0) ok = issue_s(0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+        if (!mbar_wait(smem_u32(p_full), j & 1, 207, abort_flag)) break;
+        tc_fence_after();
+        const uint64_t dp = sdesc_sw128(sP);
+        const uint64_t dv = sdesc_sw128(sV + (j & 1) * kTcSmemKV);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)  // 16 keys per step: P +32 B (K-major), V +2048 B (16 rows of 128 B)
+          umma_bf16(t_o, dp + 2 * k, dv + 128 * k, idesc_o, k != 0);
+        umma_commit(smem_u32(o_full));
+        umma_commit(smem_u32(&kv_empty[j & 1]));
+      }
+      umma_commit(smem_u32(drain));
+      mbar_wait(smem_u32(drain), 0, 208, nullptr);
+    }
+  } else {
+    // ---------------- softmax warps 2..5
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;            // row within the tile = TMEM lane
+    const int qa = q0 + r;                   // query position in the document
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(qd * 32) << 16);
+    const float scale_log2 = 0.125f * 1.4426950408889634f;
+    const int q_chunk = chunk > 0 ? qa / chunk : 0;
+    float m_run = -INFINITY, l_run = 0.f;
+    float o[64];
+#pragma unroll
+    for (int d = 0; d < 64; ++d) o[d] = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait(smem_u32(s_full), j & 1, 209, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sa[32], sb[32];
+      tmem_ld32(lane_base + 0, sa);
+      tmem_ld32(lane_base + 32, sb);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(s_empty));
+      // mask + scale, tile max
+      const int kv0 = j * kTcKv;
+      float s[64];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const int key = kv0 + c;
+        const bool vis = key < L && (chunk <= 0 || key / chunk <= q_chunk);
+        const float v = vis ? __uint_as_float(c < 32 ? sa[c] : sb[c - 32]) * scale_log2 : -INFINITY;
+        s[c] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = ex2_approx(m_run - m_use);
+      float rs = 0.f;
+      uint32_t pw[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float p0 = ex2_approx(s[2 * c] - m_use);
+        const float p1 = ex2_approx(s[2 * c + 1] - m_use);
+        rs += p0 + p1;
+        pw[c] = pack_bf16x2(p0, p1);
+      }
+      // fold in the previous tile's P.V (its MMA has also finished reading P)
+      if (j > 0) {
+        if (!mbar_wait(smem_u32(o_full), (j - 1) & 1, 210, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t oa[32], ob[32];
+        tmem_ld32(lane_base + 64, oa);
+        tmem_ld32(lane_base + 96, ob);
+        tmem_wait_ld();
+#pragma unroll
+        for (int d = 0; d < 32; ++d) {
+          o[d] += __uint_as_float(oa[d]);
+          o[32 + d] += __uint_as_float(ob[d]);
+        }
+      }
+#pragma unroll
+      for (int d = 0; d < 64; ++d) o[d] *= alpha;
+      l_run = l_run * alpha + rs;
+      m_run = m_new;
+      // P_j -> shared memory (row r, 128 bytes, 128-byte swizzle), then hand to the MMA warp
+      uint8_t* prow = pP + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+            make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(p_full));
+    }
+    if (ok && n_kv > 0 && mbar_wait(smem_u32(o_full), (n_kv - 1) & 1, 211, abort_flag)) {
+      tc_fence_after();
+      uint32_t oa[32], ob[32];
+      tmem_ld32(lane_base + 64, oa);
+      tmem_ld32(lane_base + 96, ob);
+      tmem_wait_ld();
+#pragma unroll
+      for (int d = 0; d < 32; ++d) {
+        o[d] += __uint_as_float(oa[d]);
+        o[32 + d] += __uint_as_float(ob[d]);
+      }
+      if (qa < L) {
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        bf16* orow = out + (long)(base + qa) * 1024 + head * 64;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 u;
+          u.x = pack_bf16x2(o[8 * c] * inv, o[8 * c + 1] * inv);
+          u.y = pack_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+          u.z = pack_bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+          u.w = pack_bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+          *reinterpret_cast<uint4*>(orow + 8 * c) = u;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
 // ------------------------------------------------------------------ fp32 (CUDA cores)
 // One thread per query row (128 per CTA), 32-key tiles in shared memory.
 __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__ qkv,

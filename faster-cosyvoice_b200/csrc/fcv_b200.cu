@@ -263,21 +263,24 @@ EpiParams make_epi(int epi, int M, int N, void* C, long ldc, const float* bias) 
 
 // ------------------------------------------------------------------ attention launch
 int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, const int32_t* tiles,
-                  int n_tiles, void* out, cudaStream_t s) {
+                  int n_tiles, void* out, long n_rows, cudaStream_t s) {
   if (n_tiles <= 0) return FCV_OK;
   dim3 grid(n_tiles, FCV_HEADS);
   const int2* t2 = reinterpret_cast<const int2*>(tiles);
   if (dtype == FCV_DTYPE_BF16) {
+    // Q tiles of 128 rows and K/V tiles of 64 rows straight from the (N, 3072) [Q|K|V] buffer
+    CUtensorMap tq, tkv;
+    FCV_TRY(make_tmap(&tq, qkv, false, n_rows, 3072, 3072, 64, 128));
+    FCV_TRY(make_tmap(&tkv, qkv, false, n_rows, 3072, 3072, 64, kTcKv));
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {
-      FCV_CUDA(cudaFuncSetAttribute(attn_bf16_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 49152));
+      FCV_CUDA(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes));
       attr[dev & 63] = true;
     }
-    attn_bf16_mma_kernel<<<grid, 256, 49152, s>>>(static_cast<const bf16*>(qkv), cu, t2, chunk,
-                                                  static_cast<bf16*>(out));
-    FCV_LAUNCH_CHECK("attn_bf16_mma_kernel");
+    attn_tc_kernel<<<grid, 192, kTcSmemBytes, s>>>(tq, tkv, cu, t2, chunk, static_cast<bf16*>(out));
+    FCV_LAUNCH_CHECK("attn_tc_kernel");
   } else {
     attn_f32_kernel<<<grid, 128, 0, s>>>(static_cast<const float*>(qkv), cu, t2, chunk,
                                          static_cast<float*>(out));
@@ -452,7 +455,7 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     {
       ProfScope ps(FCV_CAT_ATTENTION, s);
       FCV_TRY(run_attention(ws.qkv, dtype, bt->cu_seqlens, bt->chunk, bt->attn_tiles, bt->n_attn_tiles,
-                            ws.attn, s));
+                            ws.attn, N, s));
     }
     GemmCall o{};
     o.A = ws.attn; o.lda = 1024; o.a_rows = N; o.M = N; o.N = 1024; o.K = 1024;
@@ -641,14 +644,15 @@ int fcv_gemm(const void* A, const void* W, const float* bias, int M, int Nout, i
   return run_gemm(g, dtype, as_stream(stream));
 }
 
-int fcv_attention(const void* qkv, int dtype, const int32_t* cu_seqlens, int B, int max_len, int chunk,
+int fcv_attention(const void* qkv, int dtype, const int32_t* cu_seqlens, int B, int N, int max_len, int chunk,
                   const int32_t* tiles, int n_tiles, void* out, void* stream) {
   (void)B;
   (void)max_len;
-  if (!qkv || !cu_seqlens || !out || (n_tiles > 0 && !tiles) || chunk < 0)
+  if (!qkv || !cu_seqlens || !out || (n_tiles > 0 && !tiles) || chunk < 0 || N < 0)
     return fail(FCV_EINVAL, "fcv_attention: bad arguments");
   if (!valid_dtype(dtype)) return fail(FCV_EINVAL, "fcv_attention: bad dtype");
-  return run_attention(qkv, dtype, cu_seqlens, chunk, tiles, n_tiles, out, as_stream(stream));
+  if (N == 0) return FCV_OK;
+  return run_attention(qkv, dtype, cu_seqlens, chunk, tiles, n_tiles, out, N, as_stream(stream));
 }
 
 int fcv_attn_tiles(const int32_t* lengths_host, int B, int chunk, int32_t* tiles, int cap) {

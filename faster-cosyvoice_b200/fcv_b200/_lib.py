@@ -134,7 +134,7 @@ _SIGNATURES = {
     "fcv_ln_modulate": (_i, [_vp, _i, _vp, _vp, _vp, _l, _i, _vp, _i, _vp]),
     "fcv_gate_res_ln_modulate": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _l, _i, _vp, _vp, _i, _vp]),
     "fcv_gemm": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _l, _vp, _vp, _vp]),
-    "fcv_attention": (_i, [_vp, _i, _vp, _i, _i, _i, _vp, _i, _vp, _vp]),
+    "fcv_attention": (_i, [_vp, _i, _vp, _i, _i, _i, _i, _vp, _i, _vp, _vp]),
     "fcv_attn_tiles": (_i, [_vp, _i, _i, _vp, _i]),
     "fcv_time_embed": (_i, [ctypes.POINTER(DitWeights), _vp, _i, _vp, _vp, _vp]),
     "fcv_cfg_euler": (_i, [_vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _vp, _vp]),

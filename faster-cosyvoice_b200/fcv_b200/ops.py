@@ -134,7 +134,7 @@ def ragged_attention(qkv: torch.Tensor, cu_seqlens: torch.Tensor, tiles: torch.T
     _check_rows(qkv, cu_seqlens, tiles)
     N = qkv.shape[0]
     out = torch.empty(N, 1024, dtype=qkv.dtype, device=qkv.device)
-    call("fcv_attention", qkv.data_ptr(), _dt(qkv), cu_seqlens.data_ptr(), cu_seqlens.numel() - 1,
+    call("fcv_attention", qkv.data_ptr(), _dt(qkv), cu_seqlens.data_ptr(), cu_seqlens.numel() - 1, N,
          int(max_len), int(chunk), tiles.data_ptr(), int(n_tiles), out.data_ptr(), _s(qkv))
     return out
 

@@ -189,12 +189,13 @@ int fcv_gemm(const void* A, const void* W, const float* bias, int M, int Nout, i
 /* Ragged multi-head attention over packed documents: for every document d,
  * head h and query row q: softmax(Q K^T / 8 + mask) V, where the mask keeps
  * keys k < L_d, and, when chunk > 0, only k // chunk <= q // chunk.
- * qkv: (N, 3072) [Q|K|V] element type dtype; out: (N, 1024).
+ * qkv: (N, 3072) [Q|K|V] element type dtype; out: (N, 1024); N = cu_seqlens[B].
  * tiles: (n_tiles, 2) int32 (doc, q0) list of 128-row query tiles, built by
  * fcv_attn_tiles().  Replaces the FlashInfer ragged prefill of
  * flashinfer_attention.py:36-142 + flashinfer_dit.py:501. */
-int fcv_attention(const void* qkv, int dtype, const int32_t* cu_seqlens, int B, int max_len,
-                  int chunk, const int32_t* tiles, int n_tiles, void* out, void* stream);
+int fcv_attention(const void* qkv, int dtype, const int32_t* cu_seqlens, int B, int N,
+                  int max_len, int chunk, const int32_t* tiles, int n_tiles, void* out,
+                  void* stream);
 
 /* Host helper: fill `tiles` (capacity `cap` pairs, host memory) with the
  * 128-row query tiles of the documents, most expensive first.  Returns the

@@ -56,7 +56,7 @@ def test_version_and_error_paths_without_gpu(lib):
     assert rc == -1
     assert b"fcv_gemm" in lib.fcv_last_error()
     assert lib.fcv_dit_forward(None, None, None, 0, None) == -1
-    assert lib.fcv_attention(None, 1, None, 0, 0, 0, None, 0, None, None) == -1
+    assert lib.fcv_attention(None, 1, None, 0, 0, 0, 0, None, 0, None, None) == -1
     assert lib.fcv_ln_modulate(None, 0, None, None, None, 0, 0, None, 0, None) == -1
     assert lib.fcv_pack_layout(None, 0, 0, 0, None, None, None, None, None, None) == -1
 
