@@ -388,7 +388,6 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   const long MS = (long)depth * 6144 + 2048;
   const long G = (long)N + 30L * (B + 1);
   const int G_rows = N + 30 * B;  // gapped rows that can hold data
-  const bool is_bf16 = dtype == FCV_DTYPE_BF16;
 
   // 1. time embedding + all AdaLN projections (one GEMM, flashinfer_dit.py:430-445)
   {
@@ -497,8 +496,11 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   const float* mf = ws.mods + (long)depth * 6144;
   ProfScope ps_out(FCV_CAT_OUTPUT, s);
   FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mf + 1024, mf + 0, bt->doc_ids, MS, N, ws.norm, dtype, s));
-  zero_padding_kernel<T><<<std::max(1, std::min(4096, (int)(((long)B * 80 * bt->T + 255) / 256))), 256, 0, s>>>(
-      bt->cu_seqlens, B, bt->T, static_cast<T*>(bt->out));
+  const int zgrid = std::max(1, std::min(4096, (int)(((long)B * 80 * bt->T + 255) / 256)));
+  if (bt->out_f32)
+    zero_padding_kernel<float><<<zgrid, 256, 0, s>>>(bt->cu_seqlens, B, bt->T, static_cast<float*>(bt->out));
+  else
+    zero_padding_kernel<T><<<zgrid, 256, 0, s>>>(bt->cu_seqlens, B, bt->T, static_cast<T*>(bt->out));
   FCV_LAUNCH_CHECK("zero_padding_kernel");
   GemmCall po{};
   po.A = ws.norm; po.lda = 1024; po.a_rows = N; po.M = N; po.N = 80; po.K = 1024; po.W = w->out_w;
@@ -506,6 +508,7 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   po.epi.aux = bt->doc_ids;
   po.epi.aux2 = bt->positions;
   po.epi.T = bt->T;
+  po.epi.out_f32 = bt->out_f32 ? 1 : 0;
   FCV_TRY(run_gemm(po, dtype, s));
   return FCV_OK;
 }
@@ -696,19 +699,27 @@ int fcv_time_embed(const fcv_dit_weights* w, const void* t, int B, float* temb, 
 }
 
 int fcv_cfg_euler(float* x, const void* d, int d_dtype, int R, int T, float dt, float cfg_rate, void* x_next,
-                  void* stream) {
+                  int x_next_dtype, void* stream) {
   if (!x || !d || R < 0 || T < 0) return fail(FCV_EINVAL, "fcv_cfg_euler: bad arguments");
-  if (!valid_dtype(d_dtype)) return fail(FCV_EINVAL, "fcv_cfg_euler: bad dtype");
+  if (!valid_dtype(d_dtype) || !valid_dtype(x_next_dtype)) return fail(FCV_EINVAL, "fcv_cfg_euler: bad dtype");
   const long per = 80L * T;
   const long total = (long)R * per;
   if (total == 0) return FCV_OK;
   const int grid = (int)std::min<long>((total + 255) / 256, 8L * num_sms());
-  if (d_dtype == FCV_DTYPE_BF16)
-    cfg_euler_kernel<bf16><<<grid, 256, 0, as_stream(stream)>>>(x, static_cast<const bf16*>(d), R, per, dt, cfg_rate,
-                                                               static_cast<bf16*>(x_next));
+  cudaStream_t s = as_stream(stream);
+  const bool db = d_dtype == FCV_DTYPE_BF16, nb = x_next_dtype == FCV_DTYPE_BF16;
+  if (db && nb)
+    cfg_euler_kernel<bf16, bf16><<<grid, 256, 0, s>>>(x, static_cast<const bf16*>(d), R, per, dt, cfg_rate,
+                                                      static_cast<bf16*>(x_next));
+  else if (db)
+    cfg_euler_kernel<bf16, float><<<grid, 256, 0, s>>>(x, static_cast<const bf16*>(d), R, per, dt, cfg_rate,
+                                                       static_cast<float*>(x_next));
+  else if (nb)
+    cfg_euler_kernel<float, bf16><<<grid, 256, 0, s>>>(x, static_cast<const float*>(d), R, per, dt, cfg_rate,
+                                                       static_cast<bf16*>(x_next));
   else
-    cfg_euler_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(x, static_cast<const float*>(d), R, per, dt, cfg_rate,
-                                                                static_cast<float*>(x_next));
+    cfg_euler_kernel<float, float><<<grid, 256, 0, s>>>(x, static_cast<const float*>(d), R, per, dt, cfg_rate,
+                                                        static_cast<float*>(x_next));
   FCV_LAUNCH_CHECK("cfg_euler_kernel");
   return FCV_OK;
 }

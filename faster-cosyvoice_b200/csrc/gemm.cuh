@@ -50,6 +50,7 @@ struct EpiParams {
   const float* rope_sin;
   int T;               // padded length (UNPACK)
   void* C2;            // EPI_F32: when set, also C2(act)[row*1024 + col] = silu(acc + b)
+  int out_f32;         // EPI_UNPACK: float32 output instead of act
 };
 
 // Apply the epilogue to W consecutive columns [col0, col0+W) of one row.
@@ -149,10 +150,18 @@ __device__ __forceinline__ void epilogue_apply(const EpiParams& p, int row, int 
     case EPI_UNPACK: {
       const int doc = __ldg(p.aux + row);
       const int pos = __ldg(p.aux2 + row);
-      Tact* o = reinterpret_cast<Tact*>(p.C) + (long)doc * p.N * p.T + pos;
+      const long off = (long)doc * p.N * p.T + pos;
+      if (p.out_f32) {
+        float* o = reinterpret_cast<float*>(p.C) + off;
 #pragma unroll
-      for (int j = 0; j < W; ++j)
-        if (col0 + j < p.N) o[(long)(col0 + j) * p.T] = from_f<Tact>(v[j]);
+        for (int j = 0; j < W; ++j)
+          if (col0 + j < p.N) o[(long)(col0 + j) * p.T] = v[j];
+      } else {
+        Tact* o = reinterpret_cast<Tact*>(p.C) + off;
+#pragma unroll
+        for (int j = 0; j < W; ++j)
+          if (col0 + j < p.N) o[(long)(col0 + j) * p.T] = from_f<Tact>(v[j]);
+      }
       return;
     }
     default:

@@ -309,9 +309,9 @@ __global__ void unpack_kernel(const T* __restrict__ packed, const int32_t* __res
 
 // ------------------------------------------------------------------ ODE step
 // x += dt * ((1+r) d[i] - r d[R+i]) ; x_next[i] = x_next[R+i] = x  (flashinfer_flow.py:55-70)
-template <typename Td>
+template <typename Td, typename Tn>
 __global__ void cfg_euler_kernel(float* __restrict__ x, const Td* __restrict__ d, int R, long per, float dt,
-                                 float rate, Td* __restrict__ x_next) {
+                                 float rate, Tn* __restrict__ x_next) {
   const long total = (long)R * per;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const float dc = to_f<Td>(d[i]);
@@ -319,8 +319,8 @@ __global__ void cfg_euler_kernel(float* __restrict__ x, const Td* __restrict__ d
     const float nx = x[i] + dt * ((1.0f + rate) * dc - rate * du);
     x[i] = nx;
     if (x_next) {
-      x_next[i] = from_f<Td>(nx);
-      x_next[i + total] = from_f<Td>(nx);
+      x_next[i] = from_f<Tn>(nx);
+      x_next[i + total] = from_f<Tn>(nx);
     }
   }
 }

@@ -114,6 +114,7 @@ class DitBatch(ctypes.Structure):
         ("attn_tiles", ctypes.c_void_p),
         ("n_attn_tiles", ctypes.c_int),
         ("out", ctypes.c_void_p),
+        ("out_f32", ctypes.c_int),
     ]
 
 
@@ -137,7 +138,7 @@ _SIGNATURES = {
     "fcv_attention": (_i, [_vp, _i, _vp, _i, _i, _i, _i, _vp, _i, _vp, _vp]),
     "fcv_attn_tiles": (_i, [_vp, _i, _i, _vp, _i]),
     "fcv_time_embed": (_i, [ctypes.POINTER(DitWeights), _vp, _i, _vp, _vp, _vp]),
-    "fcv_cfg_euler": (_i, [_vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _vp, _vp]),
+    "fcv_cfg_euler": (_i, [_vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _vp, _i, _vp]),
     "fcv_profile_enable": (_i, [_i]),
     "fcv_profile_collect": (_i, [_vp, _vp, _i]),
     "fcv_launch_count": (ctypes.c_long, []),

@@ -65,15 +65,15 @@ def solve_euler_batched(decoder, noise: torch.Tensor, mu: torch.Tensor, mask: to
         # a private fp32 copy: the update is in place and must not touch the caller's noise
         x = noise.to(device=dev, dtype=sdtype).to(torch.float32, copy=True).contiguous()
         x_in = x.repeat(2, 1, 1).to(dt_w).contiguous()
-        d = torch.empty(2 * R, C, T, dtype=dt_w, device=dev)
+        d = torch.empty(2 * R, C, T, dtype=torch.float32, device=dev)  # flow field kept in fp32
         t_in = torch.empty(2 * R, dtype=dt_w, device=dev)
         stream = _stream(dev)
         for k in range(1, num_timesteps + 1):
             t_in.fill_(float(t))
             est.forward_layout(layout, x_in, mu_in, t_in, spk_in, cond_in, out=d)
             nxt = x_in.data_ptr() if k < num_timesteps else None
-            call("fcv_cfg_euler", x.data_ptr(), d.data_ptr(), _dtype_code(dt_w), R, T, float(step), rate, nxt,
-                 stream)
+            call("fcv_cfg_euler", x.data_ptr(), d.data_ptr(), _lib.DTYPE_F32, R, T, float(step), rate, nxt,
+                 _dtype_code(dt_w), stream)
             t = t + step
             if k < num_timesteps:
                 step = span[k + 1] - t

@@ -330,11 +330,18 @@ class B200DiT(nn.Module):
         b.attn_tiles = layout.attn_tiles.data_ptr()
         b.n_attn_tiles = layout.n_attn_tiles
         b.out = out.data_ptr()
+        if out.dtype == torch.float32:
+            b.out_f32 = 1
+        elif out.dtype == self.weight_dtype:
+            b.out_f32 = 0
+        else:
+            raise ValueError(f"output must be float32 or {self.weight_dtype}")
         return b
 
     def forward_layout(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor | None = None):
         """One estimator call on a prepared layout.  Inputs must already be
-        contiguous tensors of the weight dtype on the module's device."""
+        contiguous tensors of the weight dtype on the module's device; ``out``
+        may be float32 (the solver keeps the flow field unrounded)."""
         B = len(layout.lengths)
         T = layout.padded_length
         if out is None:

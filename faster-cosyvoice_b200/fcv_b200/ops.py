@@ -153,7 +153,8 @@ def cfg_euler_(x: torch.Tensor, d: torch.Tensor, dt: float, cfg_rate: float,
     """In place ``x += dt * ((1+r) d[:R] - r d[R:])`` on float32 x (``flashinfer_flow.py:66-70``)."""
     R, _, T = x.shape
     call("fcv_cfg_euler", x.data_ptr(), d.data_ptr(), _dt(d), R, T, float(dt), float(cfg_rate),
-         None if x_next is None else x_next.data_ptr(), _s(x))
+         None if x_next is None else x_next.data_ptr(),
+         _lib.DTYPE_BF16 if x_next is None else _dt(x_next), _s(x))
     return x
 
 

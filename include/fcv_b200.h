@@ -127,7 +127,8 @@ typedef struct fcv_dit_batch {
   const int32_t* gap_rows;    /* (N + 30*(B+1)) device, see fcv_pack_layout   */
   const int32_t* attn_tiles;  /* (n_attn_tiles, 2) device: (doc, q0), 128 rows */
   int n_attn_tiles;
-  void* out;         /* (B, 80, T) element type dtype; padding frames zeroed   */
+  void* out;         /* (B, 80, T); padding frames zeroed                      */
+  int out_f32;       /* 0: out has element type dtype; 1: out is float32       */
 } fcv_dit_batch;
 
 /* Layout ------------------------------------------------------------------ */
@@ -216,9 +217,9 @@ int fcv_time_embed(const fcv_dit_weights* w, const void* t, int B, float* temb,
 /* Fused CFG combine + Euler step on (R, 80, T) float32 samples
  * (flashinfer_flow.py:55-70): x += dt * ((1+r) d[:R] - r d[R:]), d (2R, 80, T)
  * of element type d_dtype.  When x_next is not NULL it receives the next
- * estimator input, the CFG-repeated sample (2R, 80, T) in d_dtype. */
+ * estimator input, the CFG-repeated sample (2R, 80, T) in x_next_dtype. */
 int fcv_cfg_euler(float* x, const void* d, int d_dtype, int R, int T, float dt, float cfg_rate,
-                  void* x_next, void* stream);
+                  void* x_next, int x_next_dtype, void* stream);
 
 /* Tracing ----------------------------------------------------------------- */
 /* Kernel classes timed by the executor when profiling is on. */
