@@ -247,23 +247,42 @@ __global__ void __launch_bounds__(256) attn_bf16_mma_kernel(const bf16* __restri
 // ------------------------------------------------------------------ bf16 (tcgen05)
 // One CTA per (128-row query tile, head); 6 warps:
 //   warp 0   TMA: Q once, then K/V tiles of 64 keys into a 2-stage ring
-//   warp 1   owns TMEM (128 columns: S at 0..63, P.V partial at 64..127) and
-//            issues tcgen05.mma: S_j = Q K_j^T, then O_j = P_j V_j
-//   warps 2-5 softmax, one query row per thread (TMEM lane = row): mask, online
-//            max / sum in fp32, P_j as bf16 into 128-byte-swizzled shared memory,
-//            O accumulated in registers, normalised and stored at the end.
-// S_{j+1} is issued as soon as S_j has been read, so it overlaps the softmax of
-// tile j; 2 CTAs share an SM so one CTA's MMAs overlap the other's softmax.
+//   warp 1   owns TMEM (128 columns: S at 0..63, O at 64..127) and issues
+//            tcgen05.mma: S_j = Q K_j^T, then O += P_j V_j (O accumulates in TMEM)
+//   warps 2-5 softmax, one query row per thread (TMEM lane = row).
+// Online softmax with lazy rescaling: exponentials use a per-row reference max
+// m_ref that only moves when the tile max exceeds it by more than 8 (log2
+// units), so p <= 2^8 and O in TMEM is rescaled (tcgen05.ld/st) only then.
+// P_j goes to one of two 128-byte-swizzled shared buffers, so writing P_j only
+// waits for P.V of tile j-2.  S_{j+1} is issued as soon as S_j has been read.
+// Two CTAs share an SM, so one CTA's MMAs overlap the other's softmax.
+// Barrier invariant: every mbarrier is waited on with a parity that its
+// producer cannot have advanced past by two phases (per-buffer barriers for P
+// and P.V completion), so parity waits never alias.
 constexpr int kTcKv = 64;
 constexpr int kTcSmemQ = 128 * 128;       // 16 KB
 constexpr int kTcSmemKV = kTcKv * 128;    // 8 KB per K or V tile
-constexpr int kTcSmemP = 128 * 128;       // 16 KB (128 rows x 64 keys bf16)
-constexpr int kTcSmemBytes = 1024 + kTcSmemQ + 4 * kTcSmemKV + kTcSmemP + 256;
+constexpr int kTcSmemP = 128 * 128;       // 16 KB per P buffer (128 rows x 64 keys bf16)
+constexpr int kTcSmemBytes = 1024 + kTcSmemQ + 4 * kTcSmemKV + 2 * kTcSmemP + 256;
+constexpr float kRescaleThreshold = 8.0f;
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 32 TMEM lanes x 32 consecutive columns <- 32 registers per thread.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
 }
 
 __global__ void __launch_bounds__(192, 2)
@@ -275,18 +294,18 @@ __global__ void __launch_bounds__(192, 2)
   const uint32_t sQ = smem_u32(smem);
   const uint32_t sK = sQ + kTcSmemQ;                 // 2 stages
   const uint32_t sV = sK + 2 * kTcSmemKV;            // 2 stages
-  uint8_t* pP = smem + kTcSmemQ + 4 * kTcSmemKV;
+  uint8_t* pP = smem + kTcSmemQ + 4 * kTcSmemKV;     // 2 buffers
   const uint32_t sP = smem_u32(pP);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pP + kTcSmemP);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pP + 2 * kTcSmemP);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;   // [2]
   uint64_t* kv_empty = bars + 3;  // [2]
   uint64_t* s_full = bars + 5;
   uint64_t* s_empty = bars + 6;
-  uint64_t* p_full = bars + 7;
-  uint64_t* o_full = bars + 8;
-  uint64_t* drain = bars + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* p_full = bars + 7;    // [2]: P_j written to buffer j&1
+  uint64_t* o_done = bars + 9;    // [2]: P_j V_j complete for tiles j with j&1 == b (O updated, P buffer b free)
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int2 tl = tiles[blockIdx.x];
@@ -306,8 +325,10 @@ __global__ void __launch_bounds__(192, 2)
     }
     mbar_init(smem_u32(s_full), 1);
     mbar_init(smem_u32(s_empty), 4);
-    mbar_init(smem_u32(p_full), 4);
-    mbar_init(smem_u32(o_full), 1);
+    mbar_init(smem_u32(&p_full[0]), 4);
+    mbar_init(smem_u32(&p_full[1]), 4);
+    mbar_init(smem_u32(&o_done[0]), 1);
+    mbar_init(smem_u32(&o_done[1]), 1);
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -365,14 +386,14 @@ __global__ void __launch_bounds__(192, 2)
       if (ok && n_kv > 0) ok = issue_s(0);
       for (int j = 0; j < n_kv && ok; ++j) {
         if (j + 1 < n_kv && !issue_s(j + 1)) break;
-        if (!mbar_wait(smem_u32(p_full), j & 1, 207, abort_flag)) break;
+        if (!mbar_wait(smem_u32(&p_full[j & 1]), (j >> 1) & 1, 207, abort_flag)) break;
         tc_fence_after();
-        const uint64_t dp = sdesc_sw128(sP);
+        const uint64_t dp = sdesc_sw128(sP + (j & 1) * kTcSmemP);
         const uint64_t dv = sdesc_sw128(sV + (j & 1) * kTcSmemKV);
 #pragma unroll
         for (int k = 0; k < 4; ++k)  // 16 keys per step: P +32 B (K-major), V +2048 B (16 rows of 128 B)
-          umma_bf16(t_o, dp + 2 * k, dv + 128 * k, idesc_o, k != 0);
-        umma_commit(smem_u32(o_full));
+          umma_bf16(t_o, dp + 2 * k, dv + 128 * k, idesc_o, (j | k) != 0);
+        umma_commit(smem_u32(&o_done[j & 1]));
         umma_commit(smem_u32(&kv_empty[j & 1]));
       }
       umma_commit(smem_u32(drain));
@@ -384,12 +405,11 @@ __global__ void __launch_bounds__(192, 2)
     const int r = qd * 32 + lane;            // row within the tile = TMEM lane
     const int qa = q0 + r;                   // query position in the document
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-    const float scale_log2 = 0.125f * 1.4426950408889634f;
-    const int q_chunk = chunk > 0 ? qa / chunk : 0;
-    float m_run = -INFINITY, l_run = 0.f;
-    float o[64];
-#pragma unroll
-    for (int d = 0; d < 64; ++d) o[d] = 0.f;
+    const float sl2 = 0.125f * 1.4426950408889634f;  // softmax scale in log2 units
+    // keys [0, lim) are visible from this row
+    const int lim = chunk > 0 ? min(L, (qa / chunk + 1) * chunk) : L;
+    float m_ref = -INFINITY;   // reference max (scaled, log2 units) of the exponentials
+    float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       if (!mbar_wait(smem_u32(s_full), j & 1, 209, abort_flag)) { ok = false; break; }
@@ -401,50 +421,56 @@ __global__ void __launch_bounds__(192, 2)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(s_empty));
-      // mask + scale, tile max
-      const int kv0 = j * kTcKv;
-      float s[64];
+      const int nvis = lim - j * kTcKv;  // visible keys of this row in the tile (may be <= 0 or >= 64)
+      if (nvis < kTcKv) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          if (c >= nvis) sa[c] = __float_as_uint(-INFINITY);
+          if (32 + c >= nvis) sb[c] = __float_as_uint(-INFINITY);
+        }
+      }
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const int key = kv0 + c;
-        const bool vis = key < L && (chunk <= 0 || key / chunk <= q_chunk);
-        const float v = vis ? __uint_as_float(c < 32 ? sa[c] : sb[c - 32]) * scale_log2 : -INFINITY;
-        s[c] = v;
-        mx = fmaxf(mx, v);
+      for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fmaxf(__uint_as_float(sa[c]), __uint_as_float(sb[c])));
+      const float m_tile = mx * sl2;
+      // lazy rescale: move the reference only when the tile max is far above it
+      const bool need = m_tile > m_ref + kRescaleThreshold;
+      const float m_new = need ? m_tile : m_ref;
+      const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;  // 0 on the first visible tile
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // rescale O in TMEM: wait for P_{j-1} V_{j-1}, then O *= alpha row-wise
+        if (!mbar_wait(smem_u32(&o_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, 210, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t oa[32];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          tmem_ld32(lane_base + 64 + 32 * h, oa);
+          tmem_wait_ld();
+#pragma unroll
+          for (int d = 0; d < 32; ++d) oa[d] = __float_as_uint(__uint_as_float(oa[d]) * alpha);
+          tmem_st32(lane_base + 64 + 32 * h, oa);
+        }
+        tmem_wait_st();
       }
-      const float m_new = fmaxf(m_run, mx);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = ex2_approx(m_run - m_use);
+      l_run *= alpha;
+      m_ref = m_new;
+      const float mo = m_ref == -INFINITY ? 0.f : m_ref;
       float rs = 0.f;
       uint32_t pw[32];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float p0 = ex2_approx(s[2 * c] - m_use);
-        const float p1 = ex2_approx(s[2 * c + 1] - m_use);
-        rs += p0 + p1;
+      for (int c = 0; c < 16; ++c) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sa[2 * c]), sl2, -mo));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sa[2 * c + 1]), sl2, -mo));
+        const float p2 = ex2_approx(fmaf(__uint_as_float(sb[2 * c]), sl2, -mo));
+        const float p3 = ex2_approx(fmaf(__uint_as_float(sb[2 * c + 1]), sl2, -mo));
+        rs += (p0 + p1) + (p2 + p3);
         pw[c] = pack_bf16x2(p0, p1);
+        pw[16 + c] = pack_bf16x2(p2, p3);
       }
-      // fold in the previous tile's P.V (its MMA has also finished reading P)
-      if (j > 0) {
-        if (!mbar_wait(smem_u32(o_full), (j - 1) & 1, 210, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        uint32_t oa[32], ob[32];
-        tmem_ld32(lane_base + 64, oa);
-        tmem_ld32(lane_base + 96, ob);
-        tmem_wait_ld();
-#pragma unroll
-        for (int d = 0; d < 32; ++d) {
-          o[d] += __uint_as_float(oa[d]);
-          o[32 + d] += __uint_as_float(ob[d]);
-        }
-      }
-#pragma unroll
-      for (int d = 0; d < 64; ++d) o[d] *= alpha;
-      l_run = l_run * alpha + rs;
-      m_run = m_new;
-      // P_j -> shared memory (row r, 128 bytes, 128-byte swizzle), then hand to the MMA warp
-      uint8_t* prow = pP + r * 128;
+      l_run += rs;
+      // P_j -> buffer j&1; the MMA of tile j-2 read it last
+      if (j >= 2 && !mbar_wait(smem_u32(&o_done[j & 1]), ((j - 2) >> 1) & 1, 212, abort_flag)) { ok = false; break; }
+      uint8_t* prow = pP + (j & 1) * kTcSmemP + r * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c)
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
@@ -452,30 +478,31 @@ __global__ void __launch_bounds__(192, 2)
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(p_full));
+      if (lane == 0) mbar_arrive(smem_u32(&p_full[j & 1]));
     }
-    if (ok && n_kv > 0 && mbar_wait(smem_u32(o_full), (n_kv - 1) & 1, 211, abort_flag)) {
+    if (ok && n_kv > 0 && mbar_wait(smem_u32(&o_done[(n_kv - 1) & 1]), ((n_kv - 1) >> 1) & 1, 211, abort_flag)) {
       tc_fence_after();
       uint32_t oa[32], ob[32];
       tmem_ld32(lane_base + 64, oa);
       tmem_ld32(lane_base + 96, ob);
       tmem_wait_ld();
-#pragma unroll
-      for (int d = 0; d < 32; ++d) {
-        o[d] += __uint_as_float(oa[d]);
-        o[32 + d] += __uint_as_float(ob[d]);
-      }
       if (qa < L) {
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
         bf16* orow = out + (long)(base + qa) * 1024 + head * 64;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < 4; ++c) {
           uint4 u;
-          u.x = pack_bf16x2(o[8 * c] * inv, o[8 * c + 1] * inv);
-          u.y = pack_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-          u.z = pack_bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-          u.w = pack_bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+          u.x = pack_bf16x2(__uint_as_float(oa[8 * c]) * inv, __uint_as_float(oa[8 * c + 1]) * inv);
+          u.y = pack_bf16x2(__uint_as_float(oa[8 * c + 2]) * inv, __uint_as_float(oa[8 * c + 3]) * inv);
+          u.z = pack_bf16x2(__uint_as_float(oa[8 * c + 4]) * inv, __uint_as_float(oa[8 * c + 5]) * inv);
+          u.w = pack_bf16x2(__uint_as_float(oa[8 * c + 6]) * inv, __uint_as_float(oa[8 * c + 7]) * inv);
           *reinterpret_cast<uint4*>(orow + 8 * c) = u;
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(ob[8 * c]) * inv, __uint_as_float(ob[8 * c + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(ob[8 * c + 2]) * inv, __uint_as_float(ob[8 * c + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(ob[8 * c + 4]) * inv, __uint_as_float(ob[8 * c + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(ob[8 * c + 6]) * inv, __uint_as_float(ob[8 * c + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + 32 + 8 * c) = w;
         }
       }
     }
