@@ -262,8 +262,10 @@ def test_ragged_attention(dtype, chunk):
     if dt == torch.float32:
         assert rel_l2(out.cpu().numpy(), ref.cpu().numpy()) < 1e-5
     else:
-        assert (out.float() - ref).abs().max().item() < 2e-2
-        assert rel_l2(out.float().cpu().numpy(), ref.cpu().numpy()) < 1e-2
+        # bf16 output: its own rounding is up to 2^-8 relative; P is rounded to bf16 too
+        err = ((out.float() - ref).abs() / (1.0 + ref.abs())).max().item()
+        assert err < 1e-2, err
+        assert rel_l2(out.float().cpu().numpy(), ref.cpu().numpy()) < 5e-3
 
 
 def test_attention_tiles_cover_every_query_row_once():
