@@ -515,6 +515,35 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
 
 }  // namespace
 
+// ====================================================================== allocation-free entry point
+// Scratch of fcv_time_embed_noalloc: FCV_NOALLOC_MAX_B rows of the sinusoid
+// (256) plus the hidden layer (1024), sized for float32.  Host code must not
+// use this name as a device address; it looks the address up per device.
+static __device__ __align__(256) float g_noalloc_time_scratch[FCV_NOALLOC_MAX_B * 1280];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of g_noalloc_time_scratch on the current device (looked up
+// once per device, with that device current).
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  FCV_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(FCV_EUNSUPPORTED, "fcv_time_embed_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_time_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(FCV_ECUDA, "fcv_time_embed_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return FCV_OK;
+}
+}  // namespace
+
 // ====================================================================== C ABI
 
 extern "C" {
@@ -694,6 +723,24 @@ int fcv_time_embed(const fcv_dit_weights* w, const void* t, int B, float* temb, 
   const size_t es = dsize(w->dtype);
   void* tsin = base + (size_t)B * 1024 * es;
   void* th1 = base + (size_t)B * 1280 * es;
+  if (w->dtype == FCV_DTYPE_BF16) return run_time_embed<bf16>(w, t, B, tsin, th1, temb, silu_act, s);
+  return run_time_embed<float>(w, t, B, tsin, th1, temb, silu_act, s);
+}
+
+int fcv_time_embed_noalloc(const fcv_dit_weights* w, const void* t, int B, float* temb, void* silu_act,
+                           void* stream) {
+  if (!w || !t || !temb || !silu_act || B < 0) return fail(FCV_EINVAL, "fcv_time_embed_noalloc: bad arguments");
+  if (!valid_dtype(w->dtype)) return fail(FCV_EINVAL, "fcv_time_embed_noalloc: bad dtype");
+  if (B > FCV_NOALLOC_MAX_B)
+    return fail(FCV_EINVAL, "fcv_time_embed_noalloc: B=%d exceeds the static scratch limit of %d sequences", B,
+                FCV_NOALLOC_MAX_B);
+  if (B == 0) return FCV_OK;
+  void* scratch = nullptr;
+  FCV_TRY(noalloc_scratch(&scratch));
+  cudaStream_t s = as_stream(stream);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  void* tsin = base;                                            // (B, 256) sinusoid
+  void* th1 = base + (size_t)B * 256 * dsize(w->dtype);         // (B, 1024) hidden layer
   if (w->dtype == FCV_DTYPE_BF16) return run_time_embed<bf16>(w, t, B, tsin, th1, temb, silu_act, s);
   return run_time_embed<float>(w, t, B, tsin, th1, temb, silu_act, s);
 }

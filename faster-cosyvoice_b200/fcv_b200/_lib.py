@@ -23,6 +23,8 @@ FCV_EDEVICE = -4
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 
+NOALLOC_MAX_B = 512  # FCV_NOALLOC_MAX_B
+
 EPI_BIAS = 0
 EPI_BIAS_GELU = 1
 EPI_BIAS_ROPE_QKV = 2
@@ -46,6 +48,7 @@ EXPORTS = (
     "fcv_attention",
     "fcv_attn_tiles",
     "fcv_time_embed",
+    "fcv_time_embed_noalloc",
     "fcv_cfg_euler",
     "fcv_profile_enable",
     "fcv_profile_collect",
@@ -138,6 +141,7 @@ _SIGNATURES = {
     "fcv_attention": (_i, [_vp, _i, _vp, _i, _i, _i, _i, _vp, _i, _vp, _vp]),
     "fcv_attn_tiles": (_i, [_vp, _i, _i, _vp, _i]),
     "fcv_time_embed": (_i, [ctypes.POINTER(DitWeights), _vp, _i, _vp, _vp, _vp]),
+    "fcv_time_embed_noalloc": (_i, [ctypes.POINTER(DitWeights), _vp, _i, _vp, _vp, _vp]),
     "fcv_cfg_euler": (_i, [_vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _vp, _i, _vp]),
     "fcv_profile_enable": (_i, [_i]),
     "fcv_profile_collect": (_i, [_vp, _vp, _i]),

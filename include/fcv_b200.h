@@ -213,6 +213,28 @@ int fcv_attn_tiles(const int32_t* lengths_host, int B, int chunk, int32_t* tiles
 int fcv_time_embed(const fcv_dit_weights* w, const void* t, int B, float* temb,
                    void* silu_act, void* stream);
 
+/* Allocation-free time embedding (no counterpart in the reference; the
+ * reference only ever runs inside PyTorch, whose caching allocator hands out
+ * its scratch).  Same result as fcv_time_embed, but silu_act only has to hold
+ * the (B, 1024) outputs: the sinusoid and hidden-layer scratch rows live in a
+ * file-scope device array of this library.  For callers that cannot allocate
+ * device memory themselves: a host that binds only this C ABI and has no
+ * device allocator of its own, code that runs while a stream is being
+ * captured into a CUDA graph (cudaMalloc is not allowed then), or a real-time
+ * audio thread that must not enter the allocator (it may synchronise the
+ * device).  Limits and sharing:
+ *   - B <= FCV_NOALLOC_MAX_B (512); larger B returns FCV_EINVAL.
+ *   - The array holds FCV_NOALLOC_MAX_B * 1280 float32 (2.5 MiB); every GPU on
+ *     which the library is loaded keeps it until the process exits.
+ *   - The first call on a device looks up the array's device address with
+ *     that device current; make that first call before any stream capture.
+ *   - All calls on one device share the array, which keeps the last call's
+ *     contents (nothing in it needs to start at zero): calls that overlap on
+ *     the GPU (e.g. on two streams at once) race and must be serialised. */
+#define FCV_NOALLOC_MAX_B 512
+int fcv_time_embed_noalloc(const fcv_dit_weights* w, const void* t, int B, float* temb,
+                           void* silu_act, void* stream);
+
 /* ODE --------------------------------------------------------------------- */
 /* Fused CFG combine + Euler step on (R, 80, T) float32 samples
  * (flashinfer_flow.py:55-70): x += dt * ((1+r) d[:R] - r d[R:]), d (2R, 80, T)
