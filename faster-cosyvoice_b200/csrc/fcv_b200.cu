@@ -176,6 +176,9 @@ struct GemmCall {
   EpiParams epi;
 };
 
+int choose_tma_out(const GemmCall& g, int bn);
+int make_out_map(CUtensorMap* tc, const GemmCall& g, int tma_out, const CUtensorMap& fallback);
+
 template <int BN, typename Tact>
 int launch_tc(const GemmCall& g, cudaStream_t s) {
   using Cfg = TcGemmCfg<BN>;
@@ -189,22 +192,8 @@ int launch_tc(const GemmCall& g, cudaStream_t s) {
   args.n_blocks = (g.N + BN - 1) / BN;
   args.conv = g.conv;
   args.epi = g.epi;
-  // Output path: TMA store/reduce of 32-row x 128-byte tiles where the epilogue writes a
-  // plain row-major tile; direct per-thread stores for the scattering epilogues.
-  const int e = g.epi.epi;
-  args.tma_out = 0;
-  if (!g.conv && BN >= 128) {
-    if ((e == EPI_BIAS || e == EPI_GELU || e == EPI_ROPE || e == EPI_SILU) && g.N % 64 == 0) args.tma_out = 1;
-    else if (e == EPI_F32 && g.epi.C2 == nullptr && g.N % 32 == 0) args.tma_out = 1;
-    else if (e == EPI_GATE_RES && g.N % 32 == 0) args.tma_out = 2;
-  }
-  if (args.tma_out == 1 && e != EPI_F32) {
-    FCV_TRY(make_tmap(&tc, g.epi.C, false, g.M, g.N, g.epi.ldc, 64, 32));
-  } else if (args.tma_out != 0) {
-    FCV_TRY(make_tmap(&tc, g.epi.C, true, g.M, g.N, g.epi.ldc, 32, 32));
-  } else {
-    tc = ta;  // unused
-  }
+  args.tma_out = choose_tma_out(g, BN);
+  FCV_TRY(make_out_map(&tc, g, args.tma_out, ta));
   const int tiles = args.m_blocks * args.n_blocks;
   const int grid = std::min(tiles, num_sms());
   static bool attr_set[64] = {false};
@@ -220,11 +209,80 @@ int launch_tc(const GemmCall& g, cudaStream_t s) {
   return FCV_OK;
 }
 
+// Output path of a GEMM: TMA store/reduce of 32-row x 128-byte tiles where the
+// epilogue writes a plain row-major tile; direct per-thread stores otherwise.
+int choose_tma_out(const GemmCall& g, int bn) {
+  const int e = g.epi.epi;
+  if (g.conv || bn < 128) return 0;
+  if ((e == EPI_BIAS || e == EPI_GELU || e == EPI_ROPE || e == EPI_SILU) && g.N % 64 == 0) return 1;
+  if (e == EPI_F32 && g.epi.C2 == nullptr && g.N % 32 == 0) return 1;
+  if (e == EPI_GATE_RES && g.N % 32 == 0) return 2;
+  return 0;
+}
+
+int make_out_map(CUtensorMap* tc, const GemmCall& g, int tma_out, const CUtensorMap& fallback) {
+  if (tma_out == 1 && g.epi.epi != EPI_F32) return make_tmap(tc, g.epi.C, false, g.M, g.N, g.epi.ldc, 64, 32);
+  if (tma_out != 0) return make_tmap(tc, g.epi.C, true, g.M, g.N, g.epi.ldc, 32, 32);
+  *tc = fallback;  // unused by the kernel
+  return FCV_OK;
+}
+
+// Clusters of two CTAs that can be resident at once (persistent grid size).
+int max_pairs() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& c = cached[dev & 63];
+  if (c == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * num_sms(), 1, 1);
+    cfg.blockDim = dim3(TcPairCfg::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = TcPairCfg::SMEM_BYTES;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, tc_gemm_pair_kernel<bf16>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    c = std::min(n, num_sms() / 2);
+  }
+  return c;
+}
+
+template <typename Tact>
+int launch_tc_pair(const GemmCall& g, cudaStream_t s) {
+  using Cfg = TcPairCfg;
+  CUtensorMap ta, tb, tc;
+  FCV_TRY(make_tmap_bf16(&ta, g.A, g.a_rows, g.K, g.lda, 128));
+  FCV_TRY(make_tmap_bf16(&tb, g.W, g.N, g.K, g.K, 128));
+  TcGemmArgs args;
+  args.num_kb = (g.K + 63) / 64;
+  args.m_blocks = (g.M + 255) / 256;
+  args.n_blocks = (g.N + 255) / 256;
+  args.conv = 0;
+  args.epi = g.epi;
+  args.tma_out = choose_tma_out(g, 256);
+  FCV_TRY(make_out_map(&tc, g, args.tma_out, ta));
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    FCV_CUDA(cudaFuncSetAttribute(tc_gemm_pair_kernel<Tact>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Cfg::SMEM_BYTES));
+    attr_set[dev & 63] = true;
+  }
+  const int tiles = args.m_blocks * args.n_blocks;
+  const int pairs = std::max(1, std::min(tiles, max_pairs()));
+  tc_gemm_pair_kernel<Tact><<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, tc, args);
+  FCV_LAUNCH_CHECK("tc_gemm_pair_kernel");
+  return FCV_OK;
+}
+
 int run_gemm(const GemmCall& g, int dtype, cudaStream_t s, int force_bn = 0) {
   if (g.M <= 0 || g.N <= 0) return FCV_OK;
   if (dtype == FCV_DTYPE_BF16) {
     if (g.conv) return launch_tc<64, bf16>(g, s);
     if (g.K % 64 != 0) return fail(FCV_EUNSUPPORTED, "bf16 GEMM needs K %% 64 == 0 (K=%d)", g.K);
+    if (force_bn == 0 && g.N >= 256) return launch_tc_pair<bf16>(g, s);
     int bn = force_bn;
     if (bn == 0) {
       const long mb = (g.M + 127) / 128;

@@ -263,6 +263,110 @@ __device__ __forceinline__ void epi_bf16_half(const EpiParams& P, uint32_t (&r)[
   for (int j = 0; j < 16; ++j) r[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
 }
 
+// Stage this warp's bias slice (HALF columns starting at n0) in shared memory.
+template <int HALF>
+__device__ __forceinline__ void stage_bias(const EpiParams& P, int n0, int lane, float* bias_w) {
+  for (int c = lane * 4; c < HALF; c += 128) {
+    float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (P.bias != nullptr && n0 + c + 3 < P.N) b4 = __ldg(reinterpret_cast<const float4*>(P.bias + n0 + c));
+    *reinterpret_cast<float4*>(bias_w + c) = b4;
+  }
+  __syncwarp();
+}
+
+// Drain one accumulator slab through the epilogue: TMEM lanes q*32..q*32+31
+// (output rows row_base + q*32 + lane) and HALF columns starting at TMEM
+// address taddr (output columns n0..).  Direct stores, TMA stores of 32-row x
+// 128-byte tiles, or TMA reduce-add, as args.tma_out says.
+template <int HALF, typename Tact>
+__device__ __forceinline__ void epilogue_slab(const TcGemmArgs& args, const CUtensorMap* tmC, uint32_t taddr,
+                                              int row_base, int q, int lane, int n0, const float* bias_w,
+                                              uint8_t* stage_buf, uint32_t stage_u32) {
+  const EpiParams& P = args.epi;
+  const int row = row_base + q * 32 + lane;
+  if (args.tma_out == 0) {
+#pragma unroll 1
+    for (int c = 0; c < HALF / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      const int col0 = n0 + c * 32;
+      if (col0 < P.N) epilogue_apply<Tact, 32>(P, row, col0, v);
+    }
+  } else if (args.tma_out == 1 && sizeof(Tact) == 2 && P.epi != EPI_F32) {
+    // bf16 tiles: 64 columns (128 B per row) per TMA store
+    const int pos = (P.epi == EPI_ROPE && row < P.M) ? __ldg(P.aux + row) : 0;
+#pragma unroll 1
+    for (int c = 0; c < HALF / 64; ++c) {
+      uint32_t r0[32], r1[32];
+      tmem_ld32(taddr + c * 64, r0);
+      tmem_ld32(taddr + c * 64 + 32, r1);
+      tmem_wait_ld();
+      const int col0 = n0 + c * 64;
+      // in place: bits -> float (+ bias, activation) -> packed bf16 pairs in r0[0..15], r1[0..15]
+      epi_bf16_half(P, r0, bias_w + c * 64, col0, pos);
+      epi_bf16_half(P, r1, bias_w + c * 64 + 32, col0 + 32, pos);
+      uint32_t w[32];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        w[j] = r0[j];
+        w[16 + j] = r1[j];
+      }
+      if (lane == 0) bulk_wait_read0();
+      __syncwarp();
+      stage_row128(stage_buf, lane, w);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && col0 < P.N && row_base + q * 32 < P.M) {
+        tma_store_2d(tmC, stage_u32, col0, row_base + q * 32);
+        bulk_commit();
+      }
+    }
+  } else {
+    // f32 tiles: 32 columns (128 B per row) per TMA store (EPI_F32) or reduce-add (EPI_GATE_RES)
+    const float* grow = nullptr;
+    if (P.epi == EPI_GATE_RES) {
+      const int doc = row < P.M ? __ldg(P.aux + row) : 0;
+      grow = P.gate + (long)doc * P.gate_stride;
+    }
+#pragma unroll 1
+    for (int c = 0; c < HALF / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      const int col0 = n0 + c * 32;
+      float g[32];
+      if (grow != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 gv = __ldg(reinterpret_cast<const float4*>(grow + col0 + j));
+          g[j] = gv.x; g[j + 1] = gv.y; g[j + 2] = gv.z; g[j + 3] = gv.w;
+        }
+      }
+      tmem_wait_ld();
+      uint32_t w[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float x = __uint_as_float(r[j]) + bias_w[c * 32 + j];
+        if (grow != nullptr) x *= g[j];
+        w[j] = __float_as_uint(x);
+      }
+      if (lane == 0) bulk_wait_read0();
+      __syncwarp();
+      stage_row128(stage_buf, lane, w);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && col0 < P.N && row_base + q * 32 < P.M) {
+        if (args.tma_out == 2) tma_reduce_add_2d(tmC, stage_u32, col0, row_base + q * 32);
+        else tma_store_2d(tmC, stage_u32, col0, row_base + q * 32);
+        bulk_commit();
+      }
+    }
+  }
+}
+
 template <int BN, typename Tact>
 __global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -424,100 +528,11 @@ __global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
       const int m_blk = tile / args.n_blocks;
       const int n_blk = tile - m_blk * args.n_blocks;
       const int n0 = n_blk * BN + col_begin;  // first output column of this warp
-      const int row = m_blk * 128 + q * 32 + lane;
-      if (args.tma_out) {
-        // stage this warp's bias slice once per tile
-        for (int c = lane * 4; c < HALF; c += 128) {
-          float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (P.bias != nullptr && n0 + c + 3 < P.N) b4 = __ldg(reinterpret_cast<const float4*>(P.bias + n0 + c));
-          *reinterpret_cast<float4*>(bias_w + c) = b4;
-        }
-        __syncwarp();
-      }
+      if (args.tma_out) stage_bias<HALF>(P, n0, lane, bias_w);
       if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, 106, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + col_begin;
-      if (args.tma_out == 0) {
-#pragma unroll 1
-        for (int c = 0; c < HALF / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          const int col0 = n0 + c * 32;
-          if (col0 < P.N) epilogue_apply<Tact, 32>(P, row, col0, v);
-        }
-      } else if (args.tma_out == 1 && sizeof(Tact) == 2 && P.epi != EPI_F32) {
-        // bf16 tiles: 64 columns (128 B per row) per TMA store
-        const int pos = (P.epi == EPI_ROPE && row < P.M) ? __ldg(P.aux + row) : 0;
-#pragma unroll 1
-        for (int c = 0; c < HALF / 64; ++c) {
-          uint32_t r0[32], r1[32];
-          tmem_ld32(taddr + c * 64, r0);
-          tmem_ld32(taddr + c * 64 + 32, r1);
-          tmem_wait_ld();
-          const int col0 = n0 + c * 64;
-          // in place: bits -> float (+ bias, activation) -> packed bf16 pairs in r0[0..15], r1[0..15]
-          epi_bf16_half(P, r0, bias_w + c * 64, col0, pos);
-          epi_bf16_half(P, r1, bias_w + c * 64 + 32, col0 + 32, pos);
-          uint32_t w[32];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            w[j] = r0[j];
-            w[16 + j] = r1[j];
-          }
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
-          stage_row128(stage_buf, lane, w);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && col0 < P.N && m_blk * 128 + q * 32 < P.M) {
-            tma_store_2d(&tmC, stage_u32, col0, m_blk * 128 + q * 32);
-            bulk_commit();
-          }
-        }
-      } else {
-        // f32 tiles: 32 columns (128 B per row) per TMA store (EPI_F32) or reduce-add (EPI_GATE_RES)
-        const float* grow = nullptr;
-        if (P.epi == EPI_GATE_RES) {
-          const int doc = row < P.M ? __ldg(P.aux + row) : 0;
-          grow = P.gate + (long)doc * P.gate_stride;
-        }
-#pragma unroll 1
-        for (int c = 0; c < HALF / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c * 32, r);
-          const int col0 = n0 + c * 32;
-          float g[32];
-          if (grow != nullptr) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const float4 gv = __ldg(reinterpret_cast<const float4*>(grow + col0 + j));
-              g[j] = gv.x; g[j + 1] = gv.y; g[j + 2] = gv.z; g[j + 3] = gv.w;
-            }
-          }
-          tmem_wait_ld();
-          uint32_t w[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float x = __uint_as_float(r[j]) + bias_w[c * 32 + j];
-            if (grow != nullptr) x *= g[j];
-            w[j] = __float_as_uint(x);
-          }
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
-          stage_row128(stage_buf, lane, w);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && col0 < P.N && m_blk * 128 + q * 32 < P.M) {
-            if (args.tma_out == 2) tma_reduce_add_2d(&tmC, stage_u32, col0, m_blk * 128 + q * 32);
-            else tma_store_2d(&tmC, stage_u32, col0, m_blk * 128 + q * 32);
-            bulk_commit();
-          }
-        }
-      }
+      epilogue_slab<HALF, Tact>(args, &tmC, taddr, m_blk * 128, q, lane, n0, bias_w, stage_buf, stage_u32);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
@@ -534,6 +549,209 @@ __global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ============================================================== tcgen05 GEMM, CTA pairs
+// Same roles and epilogue as tc_gemm_kernel, but a cluster of two CTAs on an SM
+// pair computes 256 x 256 tiles with cta_group::2 MMAs: each CTA TMA-loads its
+// own 128 rows of A and its own 128 rows of B (no multicast), the completion
+// bytes of both land on the leader's (even CTA's) full barrier, the leader
+// issues M=256 x N=256 MMAs and multicasts its commits to both CTAs' barriers,
+// and each CTA drains its 128-row half of the accumulator from its own TMEM.
+// Per SM this halves the operand bytes per MMA compared with 128 x 256 tiles.
+struct TcPairCfg {
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = 128 * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int HALF = 128;  // columns per epilogue warp
+  static constexpr int STAGING_BYTES = EPI_WARPS * 4096;
+  static constexpr int BIAS_BYTES = EPI_WARPS * HALF * 4;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int BUDGET = 227 * 1024 - 1024 - STAGING_BYTES - BIAS_BYTES - BAR_BYTES;
+  static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + BIAS_BYTES + BAR_BYTES;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+};
+
+template <typename Tact>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const TcGemmArgs args) {
+  using Cfg = TcPairCfg;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int HALF = Cfg::HALF;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* staging = smem + STAGES * Cfg::STAGE_BYTES;
+  float* bias_s = reinterpret_cast<float*>(staging + Cfg::STAGING_BYTES);
+  uint8_t* bar_area = reinterpret_cast<uint8_t*>(bias_s) + Cfg::BIAS_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 2 * Cfg::EPI_WARPS);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (args.tma_out) tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int num_tiles = args.m_blocks * args.n_blocks;  // 256 x 256 tiles
+  const uint32_t smem_base = smem_u32(smem);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      long issued = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const int m_blk = tile / args.n_blocks;
+        const int n_blk = tile - m_blk * args.n_blocks;
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, 121, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_base + stage * Cfg::STAGE_BYTES;
+          const uint32_t sb = sa + Cfg::A_BYTES;
+          const uint32_t fb = smem_u32(&full[stage]);
+          if (leader) mbar_arrive_expect_tx(fb, 2 * Cfg::STAGE_BYTES);
+          tma_load_2d_pair(sa, &tmA, to_leader(fb), kb * 64, m_blk * 256 + rank * 128);
+          tma_load_2d_pair(sb, &tmB, to_leader(fb), kb * 64, n_blk * 256 + rank * 128);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok && leader) {
+        // the leader's full barriers count both CTAs' bytes: drain what may be in flight
+        long n = issued < STAGES ? issued : STAGES;
+        int s = stage;
+        uint32_t ph = phase;
+        for (long i = 0; i < n; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          mbar_wait(smem_u32(&full[s]), ph, 122, nullptr);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader only)
+      constexpr uint32_t idesc = idesc_bf16_f32(256, 256, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, 123, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * 256;
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, 124, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_base + stage * Cfg::STAGE_BYTES;
+          const uint32_t sb = sa + Cfg::A_BYTES;
+          const uint64_t da = sdesc_sw128(sa);
+          const uint64_t db = sdesc_sw128(sb);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) umma_bf16_pair(d_tmem, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+          umma_commit_pair_mc(smem_u32(&empty[stage]), 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(smem_u32(&tfull[acc]), 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      umma_commit_pair(smem_u32(drain));
+      mbar_wait(smem_u32(drain), 0, 125, nullptr);
+    }
+  } else {
+    // ---------------- epilogue warps 2..9 (both CTAs): this CTA's 128 rows of each tile
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int col_begin = (ew >> 2) * HALF;
+    uint8_t* stage_buf = staging + ew * 4096;
+    const uint32_t stage_u32 = smem_u32(stage_buf);
+    float* bias_w = bias_s + ew * HALF;
+    const EpiParams& P = args.epi;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs) {
+      const int m_blk = tile / args.n_blocks;
+      const int n_blk = tile - m_blk * args.n_blocks;
+      const int n0 = n_blk * 256 + col_begin;
+      if (args.tma_out) stage_bias<HALF>(P, n0, lane, bias_w);
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, 126, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256 + col_begin;
+      epilogue_slab<HALF, Tact>(args, &tmC, taddr, m_blk * 256 + rank * 128, q, lane, n0, bias_w, stage_buf,
+                                stage_u32);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(to_leader(smem_u32(&tempty[acc])));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    if (lane == 0) bulk_wait0();
+    __syncwarp();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
