@@ -265,7 +265,7 @@ def main():
     torch.manual_seed(seed)
     cpu_model = B200DiT(depth=22).eval()
     cpu_params = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_params = {k: v.detach().float().numpy() for k, v in cpu_model.state_dict().items()}
     model = cpu_model.to(device=device, dtype=torch.bfloat16)
     model.finalize_weights()
