@@ -166,12 +166,15 @@ def cpu_oracle_rate(params, req_lengths, seed, budget_s: float):
     takes about ``budget_s`` seconds.  Returns (frames/s, seconds, rows, cores, sample)."""
     from oracle import dit_oracle as O
 
+    cores = os.cpu_count() or 1
     try:
-        from threadpoolctl import threadpool_info
+        # torchrun pins OMP_NUM_THREADS=1; the CPU baseline uses every host thread
+        from threadpoolctl import threadpool_info, threadpool_limits
 
+        threadpool_limits(limits=cores)
         cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
     except Exception:
-        cores = os.cpu_count() or 1
+        pass
     rng = np.random.default_rng(seed)
 
     def doc(L):
