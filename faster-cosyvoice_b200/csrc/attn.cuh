@@ -245,25 +245,35 @@ __global__ void __launch_bounds__(256) attn_bf16_mma_kernel(const bf16* __restri
 }
 
 // ------------------------------------------------------------------ bf16 (tcgen05)
-// One CTA per (128-row query tile, head); 6 warps:
-//   warp 0   TMA: Q once, then K/V tiles of 64 keys into a 2-stage ring
-//   warp 1   owns TMEM (128 columns: S at 0..63, O at 64..127) and issues
-//            tcgen05.mma: S_j = Q K_j^T, then O += P_j V_j (O accumulates in TMEM)
+// Persistent: each CTA walks work items (128-row query tile, head) c, c+grid, ...
+// (tiles arrive most expensive first).  6 warps per CTA, 2 CTAs per SM:
+//   warp 0   TMA: Q of each item into one of two buffers, K/V tiles of 64 keys
+//            into a 2-stage ring
+//   warp 1   owns TMEM (S at column 0..63, two O buffers of 80 columns at 64 and
+//            144) and issues tcgen05.mma: S_g = Q K_g^T, then O += P_g [V_g | 1]
 //   warps 2-5 softmax, one query row per thread (TMEM lane = row).
-// Online softmax with lazy rescaling: exponentials use a per-row reference max
-// m_ref that only moves when the tile max exceeds it by more than 8 (log2
-// units), so p <= 2^8 and O in TMEM is rescaled (tcgen05.ld/st) only then.
-// P_j goes to one of two 128-byte-swizzled shared buffers, so writing P_j only
-// waits for P.V of tile j-2.  S_{j+1} is issued as soon as S_j has been read.
-// Two CTAs share an SM, so one CTA's MMAs overlap the other's softmax.
+// The softmax row sum comes from the tensor core: V is extended by a constant
+// shared block whose first column is 1 (reached through the descriptor's
+// leading byte offset), so O column 64 holds sum_k P[q,k] in the same bf16 P
+// that multiplies V.  Exponentials use a per-row reference max that moves only
+// when a tile max exceeds it by more than 8 (log2 units); O (with its sum
+// column) in TMEM is rescaled only then.  S_{g+1} -- possibly the next item's
+// first tile -- is issued as soon as S_g has been read, and the next item's Q is
+// loaded while the current item finishes, so items overlap.
 // Barrier invariant: every mbarrier is waited on with a parity that its
-// producer cannot have advanced past by two phases (per-buffer barriers for P
-// and P.V completion), so parity waits never alias.
+// producer cannot have advanced past by two phases (per-buffer barriers for Q,
+// P, P.V completion and O), so parity waits never alias.
 constexpr int kTcKv = 64;
-constexpr int kTcSmemQ = 128 * 128;       // 16 KB
-constexpr int kTcSmemKV = kTcKv * 128;    // 8 KB per K or V tile
-constexpr int kTcSmemP = 128 * 128;       // 16 KB per P buffer (128 rows x 64 keys bf16)
-constexpr int kTcSmemBytes = 1024 + kTcSmemQ + 4 * kTcSmemKV + 2 * kTcSmemP + 256;
+constexpr int kTcSmemQ = 128 * 128;      // 16 KB per Q buffer
+constexpr int kTcSmemKV = kTcKv * 128;   // 8 KB per K or V tile
+constexpr int kTcSmemP = 128 * 128;      // 16 KB per P buffer (128 rows x 64 keys)
+constexpr int kTcOffK = 2 * kTcSmemQ;
+constexpr int kTcOffV = kTcOffK + 2 * kTcSmemKV;
+constexpr int kTcOffOnes = kTcOffV + 2 * kTcSmemKV;  // 64 x 64 bf16, column 0 = 1
+constexpr int kTcOffP = kTcOffOnes + kTcSmemKV;
+constexpr int kTcOffBar = kTcOffP + 2 * kTcSmemP;
+constexpr int kTcSmemBytes = 1024 + kTcOffBar + 256;
+constexpr int kTcOCols = 80;  // 64 output columns + the row sum + 15 zero columns
 constexpr float kRescaleThreshold = 8.0f;
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -285,58 +295,76 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+struct AttnItem {
+  int base, L, q0, head, n_kv;
+};
+
+__device__ __forceinline__ AttnItem attn_item(const int32_t* cu, const int2* tiles, int chunk, int it) {
+  const int2 tl = tiles[it >> 4];
+  AttnItem a;
+  a.head = it & 15;
+  a.q0 = tl.y;
+  a.base = cu[tl.x];
+  a.L = cu[tl.x + 1] - a.base;
+  a.n_kv = (kv_limit(a.q0, kAttnQTile, a.L, chunk) + kTcKv - 1) / kTcKv;
+  return a;
+}
+
 __global__ void __launch_bounds__(192, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
-                   const int32_t* __restrict__ cu, const int2* __restrict__ tiles, int chunk,
+                   const int32_t* __restrict__ cu, const int2* __restrict__ tiles, int n_tiles, int chunk,
                    bf16* __restrict__ out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sQ = smem_u32(smem);
-  const uint32_t sK = sQ + kTcSmemQ;                 // 2 stages
-  const uint32_t sV = sK + 2 * kTcSmemKV;            // 2 stages
-  uint8_t* pP = smem + kTcSmemQ + 4 * kTcSmemKV;     // 2 buffers
-  const uint32_t sP = smem_u32(pP);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pP + 2 * kTcSmemP);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* s_empty = bars + 6;
-  uint64_t* p_full = bars + 7;    // [2]: P_j written to buffer j&1
-  uint64_t* o_done = bars + 9;    // [2]: P_j V_j complete for tiles j with j&1 == b (O updated, P buffer b free)
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  const uint32_t s0 = smem_u32(smem);
+  const uint32_t sQ = s0, sK = s0 + kTcOffK, sV = s0 + kTcOffV, sOnes = s0 + kTcOffOnes, sP = s0 + kTcOffP;
+  uint8_t* pP = smem + kTcOffP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcOffBar);
+  uint64_t* q_full = bars + 0;    // [2]
+  uint64_t* q_empty = bars + 2;   // [2]
+  uint64_t* kv_full = bars + 4;   // [2]
+  uint64_t* kv_empty = bars + 6;  // [2]
+  uint64_t* s_full = bars + 8;
+  uint64_t* s_empty = bars + 9;
+  uint64_t* p_full = bars + 10;   // [2]
+  uint64_t* o_done = bars + 12;   // [2] P_g [V_g|1] complete, per P buffer
+  uint64_t* o_empty = bars + 14;  // [2] final O of an item read, per O buffer
+  uint64_t* drain = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int2 tl = tiles[blockIdx.x];
-  const int doc = tl.x, q0 = tl.y;
-  const int head = blockIdx.y;
-  const int base = cu[doc];
-  const int L = cu[doc + 1] - base;
-  const int kv_end = kv_limit(q0, kAttnQTile, L, chunk);
-  const int n_kv = (kv_end + kTcKv - 1) / kTcKv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_items = n_tiles * 16;
 
   if (threadIdx.x == 0) {
-    mbar_init(smem_u32(q_full), 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&q_full[i]), 1);
+      mbar_init(smem_u32(&q_empty[i]), 1);
       mbar_init(smem_u32(&kv_full[i]), 1);
       mbar_init(smem_u32(&kv_empty[i]), 1);
+      mbar_init(smem_u32(&p_full[i]), 4);
+      mbar_init(smem_u32(&o_done[i]), 1);
+      mbar_init(smem_u32(&o_empty[i]), 4);
     }
     mbar_init(smem_u32(s_full), 1);
     mbar_init(smem_u32(s_empty), 4);
-    mbar_init(smem_u32(&p_full[0]), 4);
-    mbar_init(smem_u32(&p_full[1]), 4);
-    mbar_init(smem_u32(&o_done[0]), 1);
-    mbar_init(smem_u32(&o_done[1]), 1);
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmKV);
   }
+  if (warp >= 2 && threadIdx.x - 64 < 64) {
+    // constant [1 0 ... 0] rows extending V (128-byte swizzle: chunk c of row r at c ^ (r % 8))
+    const int r = threadIdx.x - 64;
+    uint8_t* row = smem + kTcOffOnes + r * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(row + c * 16) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(row + ((0 ^ (r & 7)) << 4)) = make_uint4(0x3F80u, 0, 0, 0);  // bf16 1.0 in column 0
+    fence_proxy_async_smem();
+  }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 128);
+    tmem_alloc(smem_u32(tmem_slot), 256);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -347,148 +375,196 @@ __global__ void __launch_bounds__(192, 2)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
-      mbar_arrive_expect_tx(smem_u32(q_full), kTcSmemQ);
-      tma_load_2d(sQ, &tmQ, smem_u32(q_full), head * 64, base + q0);
-      int issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(smem_u32(&kv_empty[st]), ((j >> 1) & 1) ^ 1, 201, abort_flag)) break;
-        const uint32_t fb = smem_u32(&kv_full[st]);
-        mbar_arrive_expect_tx(fb, 2 * kTcSmemKV);
-        tma_load_2d(sK + st * kTcSmemKV, &tmKV, fb, 1024 + head * 64, base + j * kTcKv);
-        tma_load_2d(sV + st * kTcSmemKV, &tmKV, fb, 2048 + head * 64, base + j * kTcKv);
-        ++issued;
+      int g = 0, i = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++i) {
+        const AttnItem a = attn_item(cu, tiles, chunk, it);
+        const int qb = i & 1;
+        if (!mbar_wait(smem_u32(&q_empty[qb]), ((i >> 1) & 1) ^ 1, 221, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(smem_u32(&q_full[qb]), kTcSmemQ);
+        tma_load_2d(sQ + qb * kTcSmemQ, &tmQ, smem_u32(&q_full[qb]), a.head * 64, a.base + a.q0);
+        for (int j = 0; j < a.n_kv; ++j, ++g) {
+          const int st = g & 1;
+          if (!mbar_wait(smem_u32(&kv_empty[st]), ((g >> 1) & 1) ^ 1, 222, abort_flag)) { ok = false; break; }
+          const uint32_t fb = smem_u32(&kv_full[st]);
+          mbar_arrive_expect_tx(fb, 2 * kTcSmemKV);
+          tma_load_2d(sK + st * kTcSmemKV, &tmKV, fb, 1024 + a.head * 64, a.base + j * kTcKv);
+          tma_load_2d(sV + st * kTcSmemKV, &tmKV, fb, 2048 + a.head * 64, a.base + j * kTcKv);
+        }
       }
-      // wait for our own copies before the CTA may exit
-      mbar_wait(smem_u32(q_full), 0, 202, nullptr);
-      for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
-        mbar_wait(smem_u32(&kv_full[j & 1]), (j >> 1) & 1, 203, nullptr);
+      // wait for our own copies before the CTA may exit (all phases already issued)
+      for (int k = (g > 2 ? g - 2 : 0); k < g; ++k) mbar_wait(smem_u32(&kv_full[k & 1]), (k >> 1) & 1, 223, nullptr);
+      for (int k = (i > 2 ? i - 2 : 0); k < i; ++k) mbar_wait(smem_u32(&q_full[k & 1]), (k >> 1) & 1, 224, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // ---------------- MMA issuer
+      // ---------------- MMA issuer: S of the next tile, then P.V of the current one
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, kTcKv, false, false);
-      constexpr uint32_t idesc_o = idesc_bf16_f32(128, 64, false, true);  // V is MN-major
-      const uint32_t t_s = tmem;
-      const uint32_t t_o = tmem + 64;
-      bool ok = mbar_wait(smem_u32(q_full), 0, 204, abort_flag);
-      const uint64_t dq = sdesc_sw128(sQ);
-      auto issue_s = [&](int j) -> bool {
-        if (!mbar_wait(smem_u32(&kv_full[j & 1]), (j >> 1) & 1, 205, abort_flag)) return false;
-        if (j > 0 && !mbar_wait(smem_u32(s_empty), (j - 1) & 1, 206, abort_flag)) return false;
-        tc_fence_after();
-        const uint64_t dk = sdesc_sw128(sK + (j & 1) * kTcSmemKV);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) umma_bf16(t_s, dq + 2 * k, dk + 2 * k, idesc_s, k != 0);
-        umma_commit(smem_u32(s_full));
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, kTcOCols, false, true);  // [V|1] is MN-major
+      struct Cur {
+        int it, i, j, n_kv;
+      };
+      auto first = [&](Cur& c) -> bool {
+        c.it = blockIdx.x;
+        c.i = 0;
+        c.j = 0;
+        if (c.it >= n_items) return false;
+        c.n_kv = attn_item(cu, tiles, chunk, c.it).n_kv;
         return true;
       };
-      if (ok && n_kv > 0) ok = issue_s(0);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        if (j + 1 < n_kv && !issue_s(j + 1)) break;
-        if (!mbar_wait(smem_u32(&p_full[j & 1]), (j >> 1) & 1, 207, abort_flag)) break;
+      auto next = [&](Cur& c) -> bool {
+        if (++c.j < c.n_kv) return true;
+        c.it += gridDim.x;
+        c.i += 1;
+        c.j = 0;
+        if (c.it >= n_items) return false;
+        c.n_kv = attn_item(cu, tiles, chunk, c.it).n_kv;
+        return true;
+      };
+      auto issue_s = [&](const Cur& c, int g) -> bool {
+        const int qb = c.i & 1;
+        if (c.j == 0 && !mbar_wait(smem_u32(&q_full[qb]), (c.i >> 1) & 1, 225, abort_flag)) return false;
+        if (!mbar_wait(smem_u32(&kv_full[g & 1]), (g >> 1) & 1, 226, abort_flag)) return false;
+        if (g > 0 && !mbar_wait(smem_u32(s_empty), (g - 1) & 1, 227, abort_flag)) return false;
         tc_fence_after();
-        const uint64_t dp = sdesc_sw128(sP + (j & 1) * kTcSmemP);
-        const uint64_t dv = sdesc_sw128(sV + (j & 1) * kTcSmemKV);
+        const uint64_t dq = sdesc_sw128(sQ + qb * kTcSmemQ);
+        const uint64_t dk = sdesc_sw128(sK + (g & 1) * kTcSmemKV);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) umma_bf16(tmem, dq + 2 * k, dk + 2 * k, idesc_s, k != 0);
+        umma_commit(smem_u32(s_full));
+        if (c.j == c.n_kv - 1) umma_commit(smem_u32(&q_empty[qb]));  // Q free once this S is done
+        return true;
+      };
+      auto issue_pv = [&](const Cur& c, int g) -> bool {
+        const int ob = c.i & 1;
+        if (!mbar_wait(smem_u32(&p_full[g & 1]), (g >> 1) & 1, 228, abort_flag)) return false;
+        if (c.j == 0 && !mbar_wait(smem_u32(&o_empty[ob]), ((c.i >> 1) & 1) ^ 1, 229, abort_flag)) return false;
+        tc_fence_after();
+        const uint64_t dp = sdesc_sw128(sP + (g & 1) * kTcSmemP);
+        const uint32_t va = sV + (g & 1) * kTcSmemKV;
+        const uint64_t dv = sdesc_sw128_lbo(va, sOnes - va);
 #pragma unroll
         for (int k = 0; k < 4; ++k)  // 16 keys per step: P +32 B (K-major), V +2048 B (16 rows of 128 B)
-          umma_bf16(t_o, dp + 2 * k, dv + 128 * k, idesc_o, (j | k) != 0);
-        umma_commit(smem_u32(&o_done[j & 1]));
-        umma_commit(smem_u32(&kv_empty[j & 1]));
+          umma_bf16(tmem + 64 + ob * kTcOCols, dp + 2 * k, dv + 128 * k, idesc_o, (c.j | k) != 0);
+        umma_commit(smem_u32(&o_done[g & 1]));
+        umma_commit(smem_u32(&kv_empty[g & 1]));
+        return true;
+      };
+      Cur pc, sc;
+      bool have = first(pc);
+      sc = pc;
+      bool ok = !have || issue_s(sc, 0);
+      int g = 0;
+      while (have && ok) {
+        sc = pc;
+        const bool more = next(sc);
+        if (more && !issue_s(sc, g + 1)) break;
+        if (!issue_pv(pc, g)) break;
+        pc = sc;
+        have = more;
+        ++g;
       }
       umma_commit(smem_u32(drain));
-      mbar_wait(smem_u32(drain), 0, 208, nullptr);
+      mbar_wait(smem_u32(drain), 0, 230, nullptr);
     }
   } else {
     // ---------------- softmax warps 2..5
     const int qd = warp & 3;
-    const int r = qd * 32 + lane;            // row within the tile = TMEM lane
-    const int qa = q0 + r;                   // query position in the document
+    const int r = qd * 32 + lane;  // row within the tile = TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(qd * 32) << 16);
     const float sl2 = 0.125f * 1.4426950408889634f;  // softmax scale in log2 units
-    // keys [0, lim) are visible from this row
-    const int lim = chunk > 0 ? min(L, (qa / chunk + 1) * chunk) : L;
-    float m_ref = -INFINITY;   // reference max (scaled, log2 units) of the exponentials
-    float l_run = 0.f;
+    int g = 0, i = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait(smem_u32(s_full), j & 1, 209, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t sa[32], sb[32];
-      tmem_ld32(lane_base + 0, sa);
-      tmem_ld32(lane_base + 32, sb);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(s_empty));
-      const int nvis = lim - j * kTcKv;  // visible keys of this row in the tile (may be <= 0 or >= 64)
-      if (nvis < kTcKv) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          if (c >= nvis) sa[c] = __float_as_uint(-INFINITY);
-          if (32 + c >= nvis) sb[c] = __float_as_uint(-INFINITY);
-        }
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 32; ++c) mx = fmaxf(mx, fmaxf(__uint_as_float(sa[c]), __uint_as_float(sb[c])));
-      const float m_tile = mx * sl2;
-      // lazy rescale: move the reference only when the tile max is far above it
-      const bool need = m_tile > m_ref + kRescaleThreshold;
-      const float m_new = need ? m_tile : m_ref;
-      const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;  // 0 on the first visible tile
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // rescale O in TMEM: wait for P_{j-1} V_{j-1}, then O *= alpha row-wise
-        if (!mbar_wait(smem_u32(&o_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, 210, abort_flag)) { ok = false; break; }
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++i) {
+      const AttnItem a = attn_item(cu, tiles, chunk, it);
+      const int qa = a.q0 + r;
+      const int lim = chunk > 0 ? min(a.L, (qa / chunk + 1) * chunk) : a.L;  // visible keys [0, lim)
+      const uint32_t o_addr = lane_base + 64 + (i & 1) * kTcOCols;
+      float m_ref = -INFINITY;
+      for (int j = 0; j < a.n_kv; ++j, ++g) {
+        if (!mbar_wait(smem_u32(s_full), g & 1, 231, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        uint32_t oa[32];
+        uint32_t sa[32], sb[32];
+        tmem_ld32(lane_base + 0, sa);
+        tmem_ld32(lane_base + 32, sb);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(s_empty));
+        const int nvis = lim - j * kTcKv;
+        if (nvis < kTcKv) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          tmem_ld32(lane_base + 64 + 32 * h, oa);
+          for (int c = 0; c < 32; ++c) {
+            if (c >= nvis) sa[c] = __float_as_uint(-INFINITY);
+            if (32 + c >= nvis) sb[c] = __float_as_uint(-INFINITY);
+          }
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) mx = fmax3(mx, __uint_as_float(sa[c]), __uint_as_float(sb[c]));
+        const float m_tile = mx * sl2;
+        const bool need = m_tile > m_ref + kRescaleThreshold;
+        const float m_new = need ? m_tile : m_ref;
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // rescale O (and its sum column): wait for P_{g-1} [V|1], then scale row-wise
+          if (!mbar_wait(smem_u32(&o_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, 232, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;
+          uint32_t oa[32];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            tmem_ld32(o_addr + 32 * h, oa);
+            tmem_wait_ld();
+#pragma unroll
+            for (int d = 0; d < 32; ++d) oa[d] = __float_as_uint(__uint_as_float(oa[d]) * alpha);
+            tmem_st32(o_addr + 32 * h, oa);
+          }
+          uint32_t ol[16];
+          tmem_ld16(o_addr + 64, ol);
           tmem_wait_ld();
 #pragma unroll
-          for (int d = 0; d < 32; ++d) oa[d] = __float_as_uint(__uint_as_float(oa[d]) * alpha);
-          tmem_st32(lane_base + 64 + 32 * h, oa);
+          for (int d = 0; d < 16; ++d) ol[d] = __float_as_uint(__uint_as_float(ol[d]) * alpha);
+          tmem_st16(o_addr + 64, ol);
+          tmem_wait_st();
         }
-        tmem_wait_st();
-      }
-      l_run *= alpha;
-      m_ref = m_new;
-      const float mo = m_ref == -INFINITY ? 0.f : m_ref;
-      float rs = 0.f;
-      uint32_t pw[32];
+        m_ref = m_new;
+        const float mo = m_ref == -INFINITY ? 0.f : m_ref;
+        uint32_t pw[32];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sa[2 * c]), sl2, -mo));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sa[2 * c + 1]), sl2, -mo));
-        const float p2 = ex2_approx(fmaf(__uint_as_float(sb[2 * c]), sl2, -mo));
-        const float p3 = ex2_approx(fmaf(__uint_as_float(sb[2 * c + 1]), sl2, -mo));
-        rs += (p0 + p1) + (p2 + p3);
-        pw[c] = pack_bf16x2(p0, p1);
-        pw[16 + c] = pack_bf16x2(p2, p3);
-      }
-      l_run += rs;
-      // P_j -> buffer j&1; the MMA of tile j-2 read it last
-      if (j >= 2 && !mbar_wait(smem_u32(&o_done[j & 1]), ((j - 2) >> 1) & 1, 212, abort_flag)) { ok = false; break; }
-      uint8_t* prow = pP + (j & 1) * kTcSmemP + r * 128;
+        for (int c = 0; c < 16; ++c) {
+          pw[c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(sa[2 * c]), sl2, -mo)),
+                              ex2_approx(fmaf(__uint_as_float(sa[2 * c + 1]), sl2, -mo)));
+          pw[16 + c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(sb[2 * c]), sl2, -mo)),
+                                   ex2_approx(fmaf(__uint_as_float(sb[2 * c + 1]), sl2, -mo)));
+        }
+        // P_g -> buffer g&1, last read by P.V of tile g-2
+        if (g >= 2 && !mbar_wait(smem_u32(&o_done[g & 1]), ((g - 2) >> 1) & 1, 233, abort_flag)) { ok = false; break; }
+        uint8_t* prow = pP + (g & 1) * kTcSmemP + r * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
-            make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
-      fence_proxy_async_smem();
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+              make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&p_full[g & 1]));
+      }
+      if (!ok) break;
+      // item complete: O and its row sum -> normalised bf16 rows
+      if (!mbar_wait(smem_u32(&o_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, 234, abort_flag)) break;
+      tc_fence_after();
+      uint32_t oa[32], ob[32], ol[16];
+      tmem_ld32(o_addr, oa);
+      tmem_ld32(o_addr + 32, ob);
+      tmem_ld16(o_addr + 64, ol);
+      tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&p_full[j & 1]));
-    }
-    if (ok && n_kv > 0 && mbar_wait(smem_u32(&o_done[(n_kv - 1) & 1]), ((n_kv - 1) >> 1) & 1, 211, abort_flag)) {
-      tc_fence_after();
-      uint32_t oa[32], ob[32];
-      tmem_ld32(lane_base + 64, oa);
-      tmem_ld32(lane_base + 96, ob);
-      tmem_wait_ld();
-      if (qa < L) {
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-        bf16* orow = out + (long)(base + qa) * 1024 + head * 64;
+      if (lane == 0) mbar_arrive(smem_u32(&o_empty[i & 1]));
+      if (qa < a.L) {
+        const float l = __uint_as_float(ol[0]);
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        bf16* orow = out + (long)(a.base + qa) * 1024 + a.head * 64;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint4 u;
@@ -511,7 +587,7 @@ __global__ void __launch_bounds__(192, 2)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 256);
   }
 }
 
