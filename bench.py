@@ -203,6 +203,8 @@ def main():
     ap.add_argument("--config", default="2", choices=["2", "3", "4", "5"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--requests", type=int, default=0,
+                    help="use only the first R requests of the config (small cases for profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -211,6 +213,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     req_lengths, chunk, seed = request_lengths(args.config)
+    if args.requests > 0:
+        req_lengths = req_lengths[:args.requests]
     strong = args.config in ("4", "5") and world > 1
     cfg = {"workload": CONFIG_NAMES[args.config], "requests": len(req_lengths), "sequences": 2 * len(req_lengths),
            "packed_rows": 2 * sum(req_lengths), "chunk": chunk, "seed": seed,
