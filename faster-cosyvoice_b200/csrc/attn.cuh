@@ -251,7 +251,9 @@ __global__ void __launch_bounds__(256) attn_bf16_mma_kernel(const bf16* __restri
 //            into a 2-stage ring
 //   warp 1   owns TMEM (S at column 0..63, two O buffers of 80 columns at 64 and
 //            144) and issues tcgen05.mma: S_g = Q K_g^T, then O += P_g [V_g | 1]
-//   warps 2-5 softmax, one query row per thread (TMEM lane = row).
+//   warps 2-9 softmax: TMEM lane quarter = warp % 4 (one query row per lane),
+//            key half = (warp - 2) / 4; the two halves of a row combine their
+//            partial maxima through shared memory (64-thread named barrier).
 // The softmax row sum comes from the tensor core: V is extended by a constant
 // shared block whose first column is 1 (reached through the descriptor's
 // leading byte offset), so O column 64 holds sum_k P[q,k] in the same bf16 P
@@ -271,7 +273,8 @@ constexpr int kTcOffK = 2 * kTcSmemQ;
 constexpr int kTcOffV = kTcOffK + 2 * kTcSmemKV;
 constexpr int kTcOffOnes = kTcOffV + 2 * kTcSmemKV;  // 64 x 64 bf16, column 0 = 1
 constexpr int kTcOffP = kTcOffOnes + kTcSmemKV;
-constexpr int kTcOffBar = kTcOffP + 2 * kTcSmemP;
+constexpr int kTcOffXmax = kTcOffP + 2 * kTcSmemP;  // partial row maxima, 2 tiles x 2 halves x 128 rows
+constexpr int kTcOffBar = kTcOffXmax + 2 * 2 * 128 * 4;
 constexpr int kTcSmemBytes = 1024 + kTcOffBar + 256;
 constexpr int kTcOCols = 80;  // 64 output columns + the row sum + 15 zero columns
 constexpr float kRescaleThreshold = 8.0f;
@@ -310,7 +313,13 @@ __device__ __forceinline__ AttnItem attn_item(const int32_t* cu, const int2* til
   return a;
 }
 
-__global__ void __launch_bounds__(192, 2)
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+constexpr int kTcThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax (two per TMEM lane quarter)
+
+__global__ void __launch_bounds__(kTcThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                    const int32_t* __restrict__ cu, const int2* __restrict__ tiles, int n_tiles, int chunk,
                    bf16* __restrict__ out) {
@@ -332,6 +341,7 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* drain = bars + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* xmax = reinterpret_cast<float*>(smem + kTcOffXmax);  // [2 tiles][2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_items = n_tiles * 16;
@@ -342,12 +352,12 @@ __global__ void __launch_bounds__(192, 2)
       mbar_init(smem_u32(&q_empty[i]), 1);
       mbar_init(smem_u32(&kv_full[i]), 1);
       mbar_init(smem_u32(&kv_empty[i]), 1);
-      mbar_init(smem_u32(&p_full[i]), 4);
+      mbar_init(smem_u32(&p_full[i]), 8);
       mbar_init(smem_u32(&o_done[i]), 1);
-      mbar_init(smem_u32(&o_empty[i]), 4);
+      mbar_init(smem_u32(&o_empty[i]), 8);
     }
     mbar_init(smem_u32(s_full), 1);
-    mbar_init(smem_u32(s_empty), 4);
+    mbar_init(smem_u32(s_empty), 8);
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -468,8 +478,9 @@ __global__ void __launch_bounds__(192, 2)
       mbar_wait(smem_u32(drain), 0, 230, nullptr);
     }
   } else {
-    // ---------------- softmax warps 2..5
+    // ---------------- softmax warps 2..9: lane quarter qd = warp % 4, key half h = (warp - 2) / 4
     const int qd = warp & 3;
+    const int h = (warp - 2) >> 2;
     const int r = qd * 32 + lane;  // row within the tile = TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(qd * 32) << 16);
     const float sl2 = 0.125f * 1.4426950408889634f;  // softmax scale in log2 units
@@ -484,65 +495,66 @@ __global__ void __launch_bounds__(192, 2)
       for (int j = 0; j < a.n_kv; ++j, ++g) {
         if (!mbar_wait(smem_u32(s_full), g & 1, 231, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        uint32_t sa[32], sb[32];
-        tmem_ld32(lane_base + 0, sa);
-        tmem_ld32(lane_base + 32, sb);
+        uint32_t sv[32];
+        tmem_ld32(lane_base + h * 32, sv);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(s_empty));
-        const int nvis = lim - j * kTcKv;
-        if (nvis < kTcKv) {
+        const int nvis = lim - j * kTcKv - h * 32;
+        if (nvis < 32) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            if (c >= nvis) sa[c] = __float_as_uint(-INFINITY);
-            if (32 + c >= nvis) sb[c] = __float_as_uint(-INFINITY);
-          }
+          for (int c = 0; c < 32; ++c)
+            if (c >= nvis) sv[c] = __float_as_uint(-INFINITY);
         }
-        float mx = -INFINITY;
+        // partial row max (tree), then combine with the other key half through shared memory
+        float m4[4];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) mx = fmax3(mx, __uint_as_float(sa[c]), __uint_as_float(sb[c]));
+        for (int t = 0; t < 4; ++t)
+          m4[t] = fmax3(fmax3(__uint_as_float(sv[8 * t]), __uint_as_float(sv[8 * t + 1]), __uint_as_float(sv[8 * t + 2])),
+                        fmax3(__uint_as_float(sv[8 * t + 3]), __uint_as_float(sv[8 * t + 4]), __uint_as_float(sv[8 * t + 5])),
+                        fmaxf(__uint_as_float(sv[8 * t + 6]), __uint_as_float(sv[8 * t + 7])));
+        float* xs = xmax + (g & 1) * 256;
+        xs[h * 128 + r] = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        named_bar_sync(1 + qd, 64);
+        const float mx = fmaxf(xs[r], xs[128 + r]);
         const float m_tile = mx * sl2;
         const bool need = m_tile > m_ref + kRescaleThreshold;
         const float m_new = need ? m_tile : m_ref;
         if (j > 0 && __any_sync(0xffffffffu, need)) {
-          // rescale O (and its sum column): wait for P_{g-1} [V|1], then scale row-wise
+          // rescale this half of O and its sum column: wait for P_{g-1} [V|1], then scale row-wise
           if (!mbar_wait(smem_u32(&o_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, 232, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;
           uint32_t oa[32];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            tmem_ld32(o_addr + 32 * h, oa);
-            tmem_wait_ld();
-#pragma unroll
-            for (int d = 0; d < 32; ++d) oa[d] = __float_as_uint(__uint_as_float(oa[d]) * alpha);
-            tmem_st32(o_addr + 32 * h, oa);
-          }
-          uint32_t ol[16];
-          tmem_ld16(o_addr + 64, ol);
+          tmem_ld32(o_addr + 32 * h, oa);
           tmem_wait_ld();
 #pragma unroll
-          for (int d = 0; d < 16; ++d) ol[d] = __float_as_uint(__uint_as_float(ol[d]) * alpha);
-          tmem_st16(o_addr + 64, ol);
+          for (int d = 0; d < 32; ++d) oa[d] = __float_as_uint(__uint_as_float(oa[d]) * alpha);
+          tmem_st32(o_addr + 32 * h, oa);
+          if (h == 0) {
+            uint32_t ol[16];
+            tmem_ld16(o_addr + 64, ol);
+            tmem_wait_ld();
+#pragma unroll
+            for (int d = 0; d < 16; ++d) ol[d] = __float_as_uint(__uint_as_float(ol[d]) * alpha);
+            tmem_st16(o_addr + 64, ol);
+          }
           tmem_wait_st();
         }
         m_ref = m_new;
         const float mo = m_ref == -INFINITY ? 0.f : m_ref;
-        uint32_t pw[32];
+        uint32_t pw[16];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          pw[c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(sa[2 * c]), sl2, -mo)),
-                              ex2_approx(fmaf(__uint_as_float(sa[2 * c + 1]), sl2, -mo)));
-          pw[16 + c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(sb[2 * c]), sl2, -mo)),
-                                   ex2_approx(fmaf(__uint_as_float(sb[2 * c + 1]), sl2, -mo)));
-        }
-        // P_g -> buffer g&1, last read by P.V of tile g-2
+        for (int c = 0; c < 16; ++c)
+          pw[c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(sv[2 * c]), sl2, -mo)),
+                              ex2_approx(fmaf(__uint_as_float(sv[2 * c + 1]), sl2, -mo)));
+        // P_g -> buffer g&1 (this warp's 64 bytes of the row), last read by P.V of tile g-2
         if (g >= 2 && !mbar_wait(smem_u32(&o_done[g & 1]), ((g - 2) >> 1) & 1, 233, abort_flag)) { ok = false; break; }
         uint8_t* prow = pP + (g & 1) * kTcSmemP + r * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4*>(prow + (((4 * h + c) ^ (r & 7)) << 4)) =
               make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
         fence_proxy_async_smem();
         tc_fence_before();
@@ -550,12 +562,11 @@ __global__ void __launch_bounds__(192, 2)
         if (lane == 0) mbar_arrive(smem_u32(&p_full[g & 1]));
       }
       if (!ok) break;
-      // item complete: O and its row sum -> normalised bf16 rows
+      // item complete: this warp's 32 output columns and the row sum -> normalised bf16
       if (!mbar_wait(smem_u32(&o_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, 234, abort_flag)) break;
       tc_fence_after();
-      uint32_t oa[32], ob[32], ol[16];
-      tmem_ld32(o_addr, oa);
-      tmem_ld32(o_addr + 32, ob);
+      uint32_t oa[32], ol[16];
+      tmem_ld32(o_addr + 32 * h, oa);
       tmem_ld16(o_addr + 64, ol);
       tmem_wait_ld();
       tc_fence_before();
@@ -564,7 +575,7 @@ __global__ void __launch_bounds__(192, 2)
       if (qa < a.L) {
         const float l = __uint_as_float(ol[0]);
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        bf16* orow = out + (long)(a.base + qa) * 1024 + a.head * 64;
+        bf16* orow = out + (long)(a.base + qa) * 1024 + a.head * 64 + 32 * h;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint4 u;
@@ -573,12 +584,6 @@ __global__ void __launch_bounds__(192, 2)
           u.z = pack_bf16x2(__uint_as_float(oa[8 * c + 4]) * inv, __uint_as_float(oa[8 * c + 5]) * inv);
           u.w = pack_bf16x2(__uint_as_float(oa[8 * c + 6]) * inv, __uint_as_float(oa[8 * c + 7]) * inv);
           *reinterpret_cast<uint4*>(orow + 8 * c) = u;
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(ob[8 * c]) * inv, __uint_as_float(ob[8 * c + 1]) * inv);
-          w.y = pack_bf16x2(__uint_as_float(ob[8 * c + 2]) * inv, __uint_as_float(ob[8 * c + 3]) * inv);
-          w.z = pack_bf16x2(__uint_as_float(ob[8 * c + 4]) * inv, __uint_as_float(ob[8 * c + 5]) * inv);
-          w.w = pack_bf16x2(__uint_as_float(ob[8 * c + 6]) * inv, __uint_as_float(ob[8 * c + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + 32 + 8 * c) = w;
         }
       }
     }

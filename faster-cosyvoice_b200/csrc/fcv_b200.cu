@@ -339,7 +339,7 @@ int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, cons
     }
     const int items = n_tiles * FCV_HEADS;
     const int ctas = std::min(items, 2 * num_sms());  // persistent, 2 CTAs per SM
-    attn_tc_kernel<<<ctas, 192, kTcSmemBytes, s>>>(tq, tkv, cu, t2, n_tiles, chunk, static_cast<bf16*>(out));
+    attn_tc_kernel<<<ctas, kTcThreads, kTcSmemBytes, s>>>(tq, tkv, cu, t2, n_tiles, chunk, static_cast<bf16*>(out));
     FCV_LAUNCH_CHECK("attn_tc_kernel");
   } else {
     attn_f32_kernel<<<grid, 128, 0, s>>>(static_cast<const float*>(qkv), cu, t2, chunk,
