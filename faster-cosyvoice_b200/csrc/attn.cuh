@@ -248,7 +248,7 @@ __global__ void __launch_bounds__(256) attn_bf16_mma_kernel(const bf16* __restri
 // Persistent: each CTA walks work items (128-row query tile, head) c, c+grid, ...
 // (tiles arrive most expensive first).  6 warps per CTA, 2 CTAs per SM:
 //   warp 0   TMA: Q of each item into one of two buffers, K/V tiles of 64 keys
-//            into a 2-stage ring
+//            into a 3-stage ring (a load starts as soon as P.V two tiles back is done)
 //   warp 1   owns TMEM (S at column 0..63, two O buffers of 80 columns at 64 and
 //            144) and issues tcgen05.mma: S_g = Q K_g^T, then O += P_g [V_g | 1]
 //   warps 2-9 softmax: TMEM lane quarter = warp % 4 (one query row per lane),
@@ -263,17 +263,19 @@ __global__ void __launch_bounds__(256) attn_bf16_mma_kernel(const bf16* __restri
 // first tile -- is issued as soon as S_g has been read, and the next item's Q is
 // loaded while the current item finishes, so items overlap.
 // Barrier invariant: every mbarrier is waited on with a parity that its
-// producer cannot have advanced past by two phases (per-buffer barriers for Q,
-// P, P.V completion and O), so parity waits never alias.
+// producer cannot have advanced past by two phases (per-buffer barriers for Q
+// and O; P is written only after the previous P.V is done), so parity waits
+// never alias.
 constexpr int kTcKv = 64;
 constexpr int kTcSmemQ = 128 * 128;      // 16 KB per Q buffer
 constexpr int kTcSmemKV = kTcKv * 128;   // 8 KB per K or V tile
 constexpr int kTcSmemP = 128 * 128;      // 16 KB per P buffer (128 rows x 64 keys)
+constexpr int kTcKvStages = 3;
 constexpr int kTcOffK = 2 * kTcSmemQ;
-constexpr int kTcOffV = kTcOffK + 2 * kTcSmemKV;
-constexpr int kTcOffOnes = kTcOffV + 2 * kTcSmemKV;  // 64 x 64 bf16, column 0 = 1
+constexpr int kTcOffV = kTcOffK + kTcKvStages * kTcSmemKV;
+constexpr int kTcOffOnes = kTcOffV + kTcKvStages * kTcSmemKV;  // 64 x 64 bf16, column 0 = 1
 constexpr int kTcOffP = kTcOffOnes + kTcSmemKV;
-constexpr int kTcOffXmax = kTcOffP + 2 * kTcSmemP;  // partial row maxima, 2 tiles x 2 halves x 128 rows
+constexpr int kTcOffXmax = kTcOffP + kTcSmemP;  // partial row maxima, 2 tiles x 2 halves x 128 rows
 constexpr int kTcOffBar = kTcOffXmax + 2 * 2 * 128 * 4;
 constexpr int kTcSmemBytes = 1024 + kTcOffBar + 256;
 constexpr int kTcOCols = 80;  // 64 output columns + the row sum + 15 zero columns
@@ -331,12 +333,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcOffBar);
   uint64_t* q_full = bars + 0;    // [2]
   uint64_t* q_empty = bars + 2;   // [2]
-  uint64_t* kv_full = bars + 4;   // [2]
-  uint64_t* kv_empty = bars + 6;  // [2]
-  uint64_t* s_full = bars + 8;
-  uint64_t* s_empty = bars + 9;
-  uint64_t* p_full = bars + 10;   // [2]
-  uint64_t* o_done = bars + 12;   // [2] P_g [V_g|1] complete, per P buffer
+  uint64_t* kv_full = bars + 4;   // [3]
+  uint64_t* kv_empty = bars + 7;  // [3]
+  uint64_t* s_full = bars + 10;
+  uint64_t* s_empty = bars + 11;
+  uint64_t* p_full = bars + 12;   // P_g written
+  uint64_t* o_done = bars + 13;   // P_g [V_g|1] complete (P buffer free, O updated)
   uint64_t* o_empty = bars + 14;  // [2] final O of an item read, per O buffer
   uint64_t* drain = bars + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
@@ -350,12 +352,14 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&q_full[i]), 1);
       mbar_init(smem_u32(&q_empty[i]), 1);
-      mbar_init(smem_u32(&kv_full[i]), 1);
-      mbar_init(smem_u32(&kv_empty[i]), 1);
-      mbar_init(smem_u32(&p_full[i]), 8);
-      mbar_init(smem_u32(&o_done[i]), 1);
       mbar_init(smem_u32(&o_empty[i]), 8);
     }
+    for (int i = 0; i < kTcKvStages; ++i) {
+      mbar_init(smem_u32(&kv_full[i]), 1);
+      mbar_init(smem_u32(&kv_empty[i]), 1);
+    }
+    mbar_init(smem_u32(p_full), 8);
+    mbar_init(smem_u32(o_done), 1);
     mbar_init(smem_u32(s_full), 1);
     mbar_init(smem_u32(s_empty), 8);
     mbar_init(smem_u32(drain), 1);
@@ -394,8 +398,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         mbar_arrive_expect_tx(smem_u32(&q_full[qb]), kTcSmemQ);
         tma_load_2d(sQ + qb * kTcSmemQ, &tmQ, smem_u32(&q_full[qb]), a.head * 64, a.base + a.q0);
         for (int j = 0; j < a.n_kv; ++j, ++g) {
-          const int st = g & 1;
-          if (!mbar_wait(smem_u32(&kv_empty[st]), ((g >> 1) & 1) ^ 1, 222, abort_flag)) { ok = false; break; }
+          const int st = g % kTcKvStages;
+          if (!mbar_wait(smem_u32(&kv_empty[st]), ((g / kTcKvStages) & 1) ^ 1, 222, abort_flag)) { ok = false; break; }
           const uint32_t fb = smem_u32(&kv_full[st]);
           mbar_arrive_expect_tx(fb, 2 * kTcSmemKV);
           tma_load_2d(sK + st * kTcSmemKV, &tmKV, fb, 1024 + a.head * 64, a.base + j * kTcKv);
@@ -403,7 +407,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         }
       }
       // wait for our own copies before the CTA may exit (all phases already issued)
-      for (int k = (g > 2 ? g - 2 : 0); k < g; ++k) mbar_wait(smem_u32(&kv_full[k & 1]), (k >> 1) & 1, 223, nullptr);
+      for (int k = (g > kTcKvStages ? g - kTcKvStages : 0); k < g; ++k)
+        mbar_wait(smem_u32(&kv_full[k % kTcKvStages]), (k / kTcKvStages) & 1, 223, nullptr);
       for (int k = (i > 2 ? i - 2 : 0); k < i; ++k) mbar_wait(smem_u32(&q_full[k & 1]), (k >> 1) & 1, 224, nullptr);
     }
   } else if (warp == 1) {
@@ -434,11 +439,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       auto issue_s = [&](const Cur& c, int g) -> bool {
         const int qb = c.i & 1;
         if (c.j == 0 && !mbar_wait(smem_u32(&q_full[qb]), (c.i >> 1) & 1, 225, abort_flag)) return false;
-        if (!mbar_wait(smem_u32(&kv_full[g & 1]), (g >> 1) & 1, 226, abort_flag)) return false;
+        if (!mbar_wait(smem_u32(&kv_full[g % kTcKvStages]), (g / kTcKvStages) & 1, 226, abort_flag)) return false;
         if (g > 0 && !mbar_wait(smem_u32(s_empty), (g - 1) & 1, 227, abort_flag)) return false;
         tc_fence_after();
         const uint64_t dq = sdesc_sw128(sQ + qb * kTcSmemQ);
-        const uint64_t dk = sdesc_sw128(sK + (g & 1) * kTcSmemKV);
+        const uint64_t dk = sdesc_sw128(sK + (g % kTcKvStages) * kTcSmemKV);
 #pragma unroll
         for (int k = 0; k < 4; ++k) umma_bf16(tmem, dq + 2 * k, dk + 2 * k, idesc_s, k != 0);
         umma_commit(smem_u32(s_full));
@@ -447,17 +452,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       };
       auto issue_pv = [&](const Cur& c, int g) -> bool {
         const int ob = c.i & 1;
-        if (!mbar_wait(smem_u32(&p_full[g & 1]), (g >> 1) & 1, 228, abort_flag)) return false;
+        if (!mbar_wait(smem_u32(p_full), g & 1, 228, abort_flag)) return false;
         if (c.j == 0 && !mbar_wait(smem_u32(&o_empty[ob]), ((c.i >> 1) & 1) ^ 1, 229, abort_flag)) return false;
         tc_fence_after();
-        const uint64_t dp = sdesc_sw128(sP + (g & 1) * kTcSmemP);
-        const uint32_t va = sV + (g & 1) * kTcSmemKV;
+        const uint64_t dp = sdesc_sw128(sP);
+        const uint32_t va = sV + (g % kTcKvStages) * kTcSmemKV;
         const uint64_t dv = sdesc_sw128_lbo(va, sOnes - va);
 #pragma unroll
         for (int k = 0; k < 4; ++k)  // 16 keys per step: P +32 B (K-major), V +2048 B (16 rows of 128 B)
           umma_bf16(tmem + 64 + ob * kTcOCols, dp + 2 * k, dv + 128 * k, idesc_o, (c.j | k) != 0);
-        umma_commit(smem_u32(&o_done[g & 1]));
-        umma_commit(smem_u32(&kv_empty[g & 1]));
+        umma_commit(smem_u32(o_done));
+        umma_commit(smem_u32(&kv_empty[g % kTcKvStages]));
         return true;
       };
       Cur pc, sc;
@@ -523,7 +528,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         const float m_new = need ? m_tile : m_ref;
         if (j > 0 && __any_sync(0xffffffffu, need)) {
           // rescale this half of O and its sum column: wait for P_{g-1} [V|1], then scale row-wise
-          if (!mbar_wait(smem_u32(&o_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, 232, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(smem_u32(o_done), (g - 1) & 1, 232, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;
           uint32_t oa[32];
@@ -549,9 +554,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         for (int c = 0; c < 16; ++c)
           pw[c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(sv[2 * c]), sl2, -mo)),
                               ex2_approx(fmaf(__uint_as_float(sv[2 * c + 1]), sl2, -mo)));
-        // P_g -> buffer g&1 (this warp's 64 bytes of the row), last read by P.V of tile g-2
-        if (g >= 2 && !mbar_wait(smem_u32(&o_done[g & 1]), ((g - 2) >> 1) & 1, 233, abort_flag)) { ok = false; break; }
-        uint8_t* prow = pP + (g & 1) * kTcSmemP + r * 128;
+        // P_g (this warp's 64 bytes of the row) -> the P buffer, last read by P.V of tile g-1
+        if (g >= 1 && !mbar_wait(smem_u32(o_done), (g - 1) & 1, 233, abort_flag)) { ok = false; break; }
+        uint8_t* prow = pP + r * 128;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           *reinterpret_cast<uint4*>(prow + (((4 * h + c) ^ (r & 7)) << 4)) =
@@ -559,11 +564,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&p_full[g & 1]));
+        if (lane == 0) mbar_arrive(smem_u32(p_full));
       }
       if (!ok) break;
       // item complete: this warp's 32 output columns and the row sum -> normalised bf16
-      if (!mbar_wait(smem_u32(&o_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, 234, abort_flag)) break;
+      if (!mbar_wait(smem_u32(o_done), (g - 1) & 1, 234, abort_flag)) break;
       tc_fence_after();
       uint32_t oa[32], ol[16];
       tmem_ld32(o_addr + 32 * h, oa);
