@@ -248,9 +248,10 @@ __global__ void __launch_bounds__(256) attn_bf16_mma_kernel(const bf16* __restri
 // Persistent: each CTA walks work items (128-row query tile, head) c, c+grid, ...
 // (tiles arrive most expensive first).  6 warps per CTA, 2 CTAs per SM:
 //   warp 0   TMA: Q of each item into one of two buffers, K/V tiles of 64 keys
-//            into a 3-stage ring (a load starts as soon as P.V two tiles back is done)
-//   warp 1   owns TMEM (S at column 0..63, two O buffers of 80 columns at 64 and
-//            144) and issues tcgen05.mma: S_g = Q K_g^T, then O += P_g [V_g | 1]
+//            into a 4-stage ring
+//   warp 1   owns TMEM (S at columns 0..63, P at 64..95, two O buffers of 80
+//            columns at 96 and 176) and issues tcgen05.mma: S_g = Q K_g^T, then
+//            O += P_g [V_g | 1] with P_g read from TMEM
 //   warps 2-9 softmax: TMEM lane quarter = warp % 4 (one query row per lane),
 //            key half = (warp - 2) / 4; the two halves of a row combine their
 //            partial maxima through shared memory (64-thread named barrier).
@@ -265,17 +266,19 @@ __global__ void __launch_bounds__(256) attn_bf16_mma_kernel(const bf16* __restri
 // Barrier invariant: every mbarrier is waited on with a parity that its
 // producer cannot have advanced past by two phases (per-buffer barriers for Q
 // and O; P is written only after the previous P.V is done), so parity waits
-// never alias.
+// never alias.  P lives in TMEM, so no shared-memory round trip per tile.
 constexpr int kTcKv = 64;
 constexpr int kTcSmemQ = 128 * 128;      // 16 KB per Q buffer
 constexpr int kTcSmemKV = kTcKv * 128;   // 8 KB per K or V tile
 constexpr int kTcSmemP = 128 * 128;      // 16 KB per P buffer (128 rows x 64 keys)
-constexpr int kTcKvStages = 3;
+constexpr int kTcKvStages = 4;
 constexpr int kTcOffK = 2 * kTcSmemQ;
 constexpr int kTcOffV = kTcOffK + kTcKvStages * kTcSmemKV;
 constexpr int kTcOffOnes = kTcOffV + kTcKvStages * kTcSmemKV;  // 64 x 64 bf16, column 0 = 1
-constexpr int kTcOffP = kTcOffOnes + kTcSmemKV;
-constexpr int kTcOffXmax = kTcOffP + kTcSmemP;  // partial row maxima, 2 tiles x 2 halves x 128 rows
+constexpr int kTcOffXmax = kTcOffOnes + kTcSmemKV;  // partial row maxima, 2 tiles x 2 halves x 128 rows
+// TMEM columns: S [0, 64), P [64, 96) (bf16 pairs), O buffers [96, 176) and [176, 256)
+constexpr int kTcColP = 64;
+constexpr int kTcColO = 96;
 constexpr int kTcOffBar = kTcOffXmax + 2 * 2 * 128 * 4;
 constexpr int kTcSmemBytes = 1024 + kTcOffBar + 256;
 constexpr int kTcOCols = 80;  // 64 output columns + the row sum + 15 zero columns
@@ -328,8 +331,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t s0 = smem_u32(smem);
-  const uint32_t sQ = s0, sK = s0 + kTcOffK, sV = s0 + kTcOffV, sOnes = s0 + kTcOffOnes, sP = s0 + kTcOffP;
-  uint8_t* pP = smem + kTcOffP;
+  const uint32_t sQ = s0, sK = s0 + kTcOffK, sV = s0 + kTcOffV, sOnes = s0 + kTcOffOnes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcOffBar);
   uint64_t* q_full = bars + 0;    // [2]
   uint64_t* q_empty = bars + 2;   // [2]
@@ -455,12 +457,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         if (!mbar_wait(smem_u32(p_full), g & 1, 228, abort_flag)) return false;
         if (c.j == 0 && !mbar_wait(smem_u32(&o_empty[ob]), ((c.i >> 1) & 1) ^ 1, 229, abort_flag)) return false;
         tc_fence_after();
-        const uint64_t dp = sdesc_sw128(sP);
         const uint32_t va = sV + (g % kTcKvStages) * kTcSmemKV;
         const uint64_t dv = sdesc_sw128_lbo(va, sOnes - va);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)  // 16 keys per step: P +32 B (K-major), V +2048 B (16 rows of 128 B)
-          umma_bf16(tmem + 64 + ob * kTcOCols, dp + 2 * k, dv + 128 * k, idesc_o, (c.j | k) != 0);
+        for (int k = 0; k < 4; ++k)  // 16 keys per step: P +8 TMEM columns, V +2048 B (16 rows of 128 B)
+          umma_bf16_ts(tmem + kTcColO + ob * kTcOCols, tmem + kTcColP + 8 * k, dv + 128 * k, idesc_o,
+                       (c.j | k) != 0);
         umma_commit(smem_u32(o_done));
         umma_commit(smem_u32(&kv_empty[g % kTcKvStages]));
         return true;
@@ -495,7 +497,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       const AttnItem a = attn_item(cu, tiles, chunk, it);
       const int qa = a.q0 + r;
       const int lim = chunk > 0 ? min(a.L, (qa / chunk + 1) * chunk) : a.L;  // visible keys [0, lim)
-      const uint32_t o_addr = lane_base + 64 + (i & 1) * kTcOCols;
+      const uint32_t o_addr = lane_base + kTcColO + (i & 1) * kTcOCols;
       float m_ref = -INFINITY;
       for (int j = 0; j < a.n_kv; ++j, ++g) {
         if (!mbar_wait(smem_u32(s_full), g & 1, 231, abort_flag)) { ok = false; break; }
@@ -554,14 +556,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         for (int c = 0; c < 16; ++c)
           pw[c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(sv[2 * c]), sl2, -mo)),
                               ex2_approx(fmaf(__uint_as_float(sv[2 * c + 1]), sl2, -mo)));
-        // P_g (this warp's 64 bytes of the row) -> the P buffer, last read by P.V of tile g-1
+        // P_g (this warp's 32 keys = 16 columns of the row) -> TMEM, last read by P.V of tile g-1
         if (g >= 1 && !mbar_wait(smem_u32(o_done), (g - 1) & 1, 233, abort_flag)) { ok = false; break; }
-        uint8_t* prow = pP + r * 128;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          *reinterpret_cast<uint4*>(prow + (((4 * h + c) ^ (r & 7)) << 4)) =
-              make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
-        fence_proxy_async_smem();
+        tc_fence_after();
+        tmem_st16(lane_base + kTcColP + 16 * h, pw);
+        tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(p_full));
