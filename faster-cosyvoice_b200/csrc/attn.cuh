@@ -280,7 +280,21 @@ constexpr int kTcOffXmax = kTcOffOnes + kTcSmemKV;  // partial row maxima, 2 til
 constexpr int kTcColP = 64;
 constexpr int kTcColO = 96;
 constexpr int kTcOffBar = kTcOffXmax + 2 * 2 * 128 * 4;
-constexpr int kTcSmemBytes = 1024 + kTcOffBar + 256;
+// mbarrier slots (8 bytes each), derived from the stage count
+constexpr int kBarQFull = 0;
+constexpr int kBarQEmpty = kBarQFull + 2;
+constexpr int kBarKvFull = kBarQEmpty + 2;
+constexpr int kBarKvEmpty = kBarKvFull + kTcKvStages;
+constexpr int kBarSFull = kBarKvEmpty + kTcKvStages;
+constexpr int kBarSEmpty = kBarSFull + 1;
+constexpr int kBarPFull = kBarSEmpty + 1;
+constexpr int kBarODone = kBarPFull + 1;
+constexpr int kBarOEmpty = kBarODone + 1;
+constexpr int kBarDrain = kBarOEmpty + 2;
+constexpr int kBarCount = kBarDrain + 1;
+constexpr int kTcBarBytes = 256;
+static_assert(kBarCount * 8 + 8 <= kTcBarBytes, "attention barrier area too small");
+constexpr int kTcSmemBytes = 1024 + kTcOffBar + kTcBarBytes;
 constexpr int kTcOCols = 80;  // 64 output columns + the row sum + 15 zero columns
 constexpr float kRescaleThreshold = 8.0f;
 
@@ -333,17 +347,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const uint32_t s0 = smem_u32(smem);
   const uint32_t sQ = s0, sK = s0 + kTcOffK, sV = s0 + kTcOffV, sOnes = s0 + kTcOffOnes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcOffBar);
-  uint64_t* q_full = bars + 0;    // [2]
-  uint64_t* q_empty = bars + 2;   // [2]
-  uint64_t* kv_full = bars + 4;   // [3]
-  uint64_t* kv_empty = bars + 7;  // [3]
-  uint64_t* s_full = bars + 10;
-  uint64_t* s_empty = bars + 11;
-  uint64_t* p_full = bars + 12;   // P_g written
-  uint64_t* o_done = bars + 13;   // P_g [V_g|1] complete (P buffer free, O updated)
-  uint64_t* o_empty = bars + 14;  // [2] final O of an item read, per O buffer
-  uint64_t* drain = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* q_full = bars + kBarQFull;     // [2]
+  uint64_t* q_empty = bars + kBarQEmpty;   // [2]
+  uint64_t* kv_full = bars + kBarKvFull;   // [kTcKvStages]
+  uint64_t* kv_empty = bars + kBarKvEmpty; // [kTcKvStages]
+  uint64_t* s_full = bars + kBarSFull;
+  uint64_t* s_empty = bars + kBarSEmpty;
+  uint64_t* p_full = bars + kBarPFull;     // P_g written
+  uint64_t* o_done = bars + kBarODone;     // P_g [V_g|1] complete (P free, O updated)
+  uint64_t* o_empty = bars + kBarOEmpty;   // [2] final O of an item read, per O buffer
+  uint64_t* drain = bars + kBarDrain;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBarCount);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* xmax = reinterpret_cast<float*>(smem + kTcOffXmax);  // [2 tiles][2 halves][128 rows]
 
