@@ -188,19 +188,60 @@ __device__ __forceinline__ void ln_modulate32(float (&v)[32], int lane, const fl
   }
 }
 
-// One warp per packed row (flashinfer_kernels.py:83-108).
+// One warp per packed row, 8 rows per block (flashinfer_kernels.py:83-108).  The
+// block stages the shift/scale rows of its first row's document in shared
+// memory while the warps load their rows, so both loads are in flight together;
+// a warp whose row belongs to another document reads its rows from global memory.
 template <typename Th, typename To>
 __global__ void __launch_bounds__(256) ln_modulate_kernel(const Th* __restrict__ h, const float* __restrict__ shift,
                                                           const float* __restrict__ scale,
                                                           const int32_t* __restrict__ doc_ids, long mod_stride,
                                                           int N, To* __restrict__ out) {
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  __shared__ __align__(16) float s_mod[2][1024];
+  const int row0 = blockIdx.x * 8;
+  const int row = row0 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row >= N) return;
-  const long doc = doc_ids[row];
+  const long doc0 = doc_ids[row0];
+  {
+    const int c = threadIdx.x * 4;  // 256 threads x 4 floats = one 1024-float row
+    *reinterpret_cast<float4*>(&s_mod[0][c]) = __ldg(reinterpret_cast<const float4*>(shift + doc0 * mod_stride + c));
+    *reinterpret_cast<float4*>(&s_mod[1][c]) = __ldg(reinterpret_cast<const float4*>(scale + doc0 * mod_stride + c));
+  }
   float v[32];
-  load_row32<Th>(h + (long)row * 1024, lane, v);
-  ln_modulate32(v, lane, shift + doc * mod_stride, scale + doc * mod_stride);
+  long doc = doc0;
+  if (row < N) {
+    doc = doc_ids[row];
+    load_row32<Th>(h + (long)row * 1024, lane, v);
+  }
+  __syncthreads();
+  if (row >= N) return;
+  // modulation rows: the block's staged copy, or this row's document rows in global memory
+  const float* shp = doc == doc0 ? s_mod[0] : shift + doc * mod_stride;
+  const float* scp = doc == doc0 ? s_mod[1] : scale + doc * mod_stride;
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) s += v[j];
+  const float mean = warp_sum(s) * (1.0f / 1024.0f);
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    v[j] -= mean;
+    q += v[j] * v[j];
+  }
+  const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / 1024.0f) + 1e-6f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = i * 256 + lane * 8;
+#pragma unroll
+    for (int k = 0; k < 8; k += 4) {
+      const float4 a = *reinterpret_cast<const float4*>(shp + c + k);
+      const float4 b = *reinterpret_cast<const float4*>(scp + c + k);
+      v[i * 8 + k] = v[i * 8 + k] * inv * b.x + a.x;
+      v[i * 8 + k + 1] = v[i * 8 + k + 1] * inv * b.y + a.y;
+      v[i * 8 + k + 2] = v[i * 8 + k + 2] * inv * b.z + a.z;
+      v[i * 8 + k + 3] = v[i * 8 + k + 3] * inv * b.w + a.w;
+    }
+  }
   store_row32<To>(out + (long)row * 1024, lane, v);
 }
 

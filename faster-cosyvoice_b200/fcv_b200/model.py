@@ -20,7 +20,7 @@ from __future__ import annotations
 
 import ctypes
 from collections import OrderedDict
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import Sequence
 
 import torch
@@ -124,7 +124,6 @@ class PackedLayout:
     gap_rows: torch.Tensor
     attn_tiles: torch.Tensor
     n_attn_tiles: int
-    graphs: dict = field(default_factory=dict)
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -148,7 +147,8 @@ class B200DiT(nn.Module):
 
     def __init__(self, dim: int = DIM, depth: int = 22, heads: int = HEADS, dim_head: int = DIM_HEAD,
                  ff_mult: int = 2, mel_dim: int = MEL, mu_dim: int = MEL, spk_dim: int = MEL,
-                 out_channels: int = MEL, static_chunk_size: int = 50, dropout: float = 0.1):
+                 out_channels: int = MEL, static_chunk_size: int = 50, dropout: float = 0.1,
+                 use_cuda_graph: bool = False):
         super().__init__()
         if (dim, heads, dim_head, ff_mult, mel_dim, mu_dim, spk_dim) != (DIM, HEADS, DIM_HEAD, 2, MEL, MEL, MEL):
             raise ValueError("the kernels implement the CosyVoice3 geometry "
@@ -169,8 +169,10 @@ class B200DiT(nn.Module):
         self.norm_out = _AdaLNZero(dim, 2)
         self.proj_out = nn.Linear(dim, mel_dim)
 
+        self.use_cuda_graph = use_cuda_graph
         self._finalized = False
         self._derived: dict[str, torch.Tensor] = {}
+        self._graphs: OrderedDict = OrderedDict()
         self._weights: DitWeights | None = None
         self._layouts: OrderedDict = OrderedDict()
         self._workspace: torch.Tensor | None = None
@@ -312,6 +314,7 @@ class B200DiT(nn.Module):
     def _workspace_for(self, N: int, B: int, device: torch.device) -> torch.Tensor:
         need = int(lib().fcv_dit_workspace_bytes(N, B, self.depth, _dtype_code(self.weight_dtype)))
         if self._workspace is None or self._workspace.numel() < need or self._workspace.device != device:
+            self._graphs.clear()  # captured graphs reference the old workspace
             self._workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
         return self._workspace
 
@@ -338,19 +341,58 @@ class B200DiT(nn.Module):
             raise ValueError(f"output must be float32 or {self.weight_dtype}")
         return b
 
-    def forward_layout(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor | None = None):
-        """One estimator call on a prepared layout.  Inputs must already be
-        contiguous tensors of the weight dtype on the module's device; ``out``
-        may be float32 (the solver keeps the flow field unrounded)."""
-        B = len(layout.lengths)
-        T = layout.padded_length
-        if out is None:
-            out = torch.empty(B, MEL, T, dtype=self.weight_dtype, device=x.device)
-        ws = self._workspace_for(layout.N, B, x.device)
+    def _launch(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor) -> None:
+        ws = self._workspace_for(layout.N, len(layout.lengths), x.device)
         bs = self.batch_struct(layout, x, mu, t, spks, cond, out)
         call("fcv_dit_forward", ctypes.byref(self.weights_struct()), ctypes.byref(bs), ws.data_ptr(),
              ws.numel(), _stream(x.device))
-        return out
+
+    def forward_layout(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor | None = None,
+                       graph: bool = False):
+        """One estimator call on a prepared layout.  Inputs must already be
+        contiguous tensors of the weight dtype on the module's device; ``out``
+        may be float32 (the solver keeps the flow field unrounded).
+
+        With ``graph=True`` the call is captured once into a CUDA graph per
+        (layout, buffer addresses) and replayed afterwards; without ``out`` the
+        result is then a view of the graph's static output buffer, valid until
+        the next replay of that graph (the reference's graph path,
+        ``flashinfer_dit.py:806-826``, returns such views too)."""
+        B = len(layout.lengths)
+        T = layout.padded_length
+        if not graph:
+            if out is None:
+                out = torch.empty(B, MEL, T, dtype=self.weight_dtype, device=x.device)
+            self._launch(layout, x, mu, t, spks, cond, out)
+            return out
+        entry = self.capture_graph(layout, x, mu, t, spks, cond, out)
+        entry[0].replay()
+        return entry[1]
+
+    def capture_graph(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor | None = None,
+                      warmup: bool = True):
+        """CUDA graph of one estimator call for this layout and these buffers
+        (cached, FIFO of 16).  Returns ``(graph, output buffer, layout)``.  With
+        ``warmup=False`` the caller guarantees an eager call already ran."""
+        B = len(layout.lengths)
+        T = layout.padded_length
+        self._workspace_for(layout.N, B, x.device)  # settle the workspace before capturing
+        key = (id(layout), x.data_ptr(), mu.data_ptr(), t.data_ptr(), spks.data_ptr(), cond.data_ptr(),
+               None if out is None else (out.data_ptr(), out.dtype))
+        entry = self._graphs.get(key)
+        if entry is None:
+            static_out = out if out is not None else torch.empty(B, MEL, T, dtype=self.weight_dtype,
+                                                                 device=x.device)
+            if warmup:
+                self._launch(layout, x, mu, t, spks, cond, static_out)  # first launches outside the capture
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._launch(layout, x, mu, t, spks, cond, static_out)
+            if len(self._graphs) >= 16:
+                self._graphs.popitem(last=False)
+            entry = (g, static_out, layout)  # the layout is kept alive with its graph
+            self._graphs[key] = entry
+        return entry
 
     def forward(self, x: torch.Tensor, mask: torch.Tensor, mu: torch.Tensor, t: torch.Tensor,
                 spks: torch.Tensor | None = None, cond: torch.Tensor | None = None,
@@ -375,16 +417,16 @@ class B200DiT(nn.Module):
                 t = t.repeat(B)
             t = t.reshape(B).contiguous()
             layout = self.layout_from_mask(mask.to(dev), streaming)
-            return self.forward_layout(layout, x, mu, t, spks, cond)
+            return self.forward_layout(layout, x, mu, t, spks, cond, graph=self.use_cuda_graph)
 
 
-def apply_b200(model, dtype: torch.dtype = torch.bfloat16):
+def apply_b200(model, dtype: torch.dtype = torch.bfloat16, enable_cuda_graph: bool = False):
     """Replace a Token2Wav model's estimator with :class:`B200DiT`
     (mirror of ``apply_flashinfer``, ``flashinfer_dit.py:951-988``)."""
     reference = model.flow.decoder.estimator
     device = next(reference.parameters()).device
     est = B200DiT(static_chunk_size=getattr(reference, "static_chunk_size", 50),
-                  depth=len(reference.transformer_blocks))
+                  depth=len(reference.transformer_blocks), use_cuda_graph=enable_cuda_graph)
     missing, unexpected = est.load_state_dict(reference.state_dict(), strict=False)
     missing = [k for k in missing if "rope" not in k and "rotary" not in k]
     if missing or unexpected:

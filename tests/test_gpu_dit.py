@@ -149,3 +149,35 @@ def test_forward_rejects_missing_conditions():
         model(x, torch.ones(1, 1, 10, device=DEV), x, torch.zeros(1, device=DEV), None, x)
     with pytest.raises(RuntimeError):
         model.finalize_weights()
+
+
+def test_cuda_graph_path_matches_eager_and_follows_new_inputs():
+    """use_cuda_graph=True (the reference's enable_cuda_graph) replays a captured
+    estimator call; results equal the eager path bit for bit, and a replay with
+    new values in the same buffers follows the new inputs."""
+    model = _model(4, 2, torch.bfloat16)
+    rng = np.random.default_rng(9)
+    lengths = [150, 77, 150, 77]
+    T = 150
+    B = len(lengths)
+
+    def batch():
+        a = lambda *s: torch.tensor(rng.standard_normal(s), device=DEV, dtype=torch.bfloat16)  # noqa: E731
+        return a(B, 80, T), a(B, 80, T), a(B, 80, T), a(B, 80), torch.tensor(rng.uniform(size=B), device=DEV,
+                                                                           dtype=torch.bfloat16)
+
+    mask = torch.zeros(B, 1, T, device=DEV, dtype=torch.bfloat16)
+    for b, L in enumerate(lengths):
+        mask[b, 0, :L] = 1
+    x, mu, cond, spks, t = batch()
+    with torch.inference_mode():
+        eager = model(x, mask, mu, t, spks, cond, streaming=True).clone()
+        model.use_cuda_graph = True
+        g1 = model(x, mask, mu, t, spks, cond, streaming=True).clone()
+        assert torch.equal(g1, eager)
+        x2, mu2, cond2, spks2, t2 = batch()
+        x.copy_(x2), mu.copy_(mu2), cond.copy_(cond2), spks.copy_(spks2), t.copy_(t2)
+        g2 = model(x, mask, mu, t, spks, cond, streaming=True).clone()
+        model.use_cuda_graph = False
+        e2 = model(x, mask, mu, t, spks, cond, streaming=True)
+    assert torch.equal(g2, e2) and not torch.equal(g2, g1)
