@@ -94,12 +94,21 @@ cudaEvent_t prof_event() {
   if (g_prof.next >= g_prof.pool.size()) return nullptr;
   return g_prof.pool[g_prof.next++];
 }
+// Record an event; inside a stream capture it becomes an external event node, so
+// every replay of the graph records it where host code can read it.
+void prof_record(cudaEvent_t e, cudaStream_t s) {
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &st) == cudaSuccess && st == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(e, s, cudaEventRecordExternal);
+  else
+    cudaEventRecord(e, s);
+}
 void prof_begin(int cat, cudaStream_t s) {
   if (!g_prof.on) return;
   std::lock_guard<std::mutex> lk(g_prof_mu);
   cudaEvent_t e = prof_event();
   if (!e) return;
-  cudaEventRecord(e, s);
+  prof_record(e, s);
   g_prof.open_cat = cat;
   g_prof.open_ev = e;
 }
@@ -112,7 +121,7 @@ void prof_end(cudaStream_t s) {
     g_prof.open_ev = nullptr;
     return;
   }
-  cudaEventRecord(e, s);
+  prof_record(e, s);
   g_prof.marks.push_back({g_prof.open_cat, {g_prof.open_ev, e}});
   g_prof.open_ev = nullptr;
 }
