@@ -10,8 +10,8 @@
 // document's result depends only on its own rows (no split-KV), so outputs
 // are invariant to batch composition.
 //
-// Work list: one CTA per (128-row query tile, head); tiles come from the host
-// as (doc, q0) pairs ordered by cost, most expensive first.
+// Work list: (128-row query tile, head) items; tiles come from the host as
+// (doc, q0) pairs ordered by cost, most expensive first.
 #pragma once
 
 #include "fcv_common.cuh"
@@ -21,42 +21,6 @@ namespace fcv {
 constexpr int kQkvStride = 3072;
 constexpr int kAttnQTile = 128;
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                        uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
-                                          uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
-                                               uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-      "{%8, %9}, {%0, %1, %2, %3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Byte offset of element (row, col) in a 64-column bf16 tile with the 16-byte
-// chunk index XOR-swizzled by (row % 8) (conflict-free ldmatrix).
-__device__ __forceinline__ uint32_t swz64(int row, int col) {
-  return static_cast<uint32_t>(row * 128 + ((((col >> 3) ^ (row & 7)) << 4)) + ((col & 7) << 1));
-}
-
 // Last visible key (exclusive) for the query rows [q0, q0+rows) of a document of length L.
 __device__ __forceinline__ int kv_limit(int q0, int rows, int L, int chunk) {
   const int q_last = min(q0 + rows - 1, L - 1);
@@ -64,189 +28,9 @@ __device__ __forceinline__ int kv_limit(int q0, int rows, int L, int chunk) {
   return min(L, (q_last / chunk + 1) * chunk);
 }
 
-// ------------------------------------------------------------------ bf16 (mma.sync)
-// 8 warps x 16 query rows, 64-key tiles double-buffered with cp.async.
-__global__ void __launch_bounds__(256) attn_bf16_mma_kernel(const bf16* __restrict__ qkv,
-                                                            const int32_t* __restrict__ cu,
-                                                            const int2* __restrict__ tiles,
-                                                            int chunk, bf16* __restrict__ out) {
-  extern __shared__ __align__(128) uint8_t sm[];
-  const uint32_t sQ = smem_u32(sm);
-  const uint32_t sK = sQ + 128 * 128;        // 2 x 64 rows x 128 B
-  const uint32_t sV = sK + 2 * 64 * 128;
-
-  const int2 tl = tiles[blockIdx.x];
-  const int doc = tl.x, q0 = tl.y;
-  const int head = blockIdx.y;
-  const int base = cu[doc];
-  const int L = cu[doc + 1] - base;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kv_end = kv_limit(q0, kAttnQTile, L, chunk);
-  const int n_kv = (kv_end + 63) / 64;
-
-  const bf16* qbase = qkv + (long)base * kQkvStride + head * 64;
-  const bf16* kbase = qbase + 1024;
-  const bf16* vbase = qbase + 2048;
-
-  // Q tile: 128 rows x 8 chunks
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int idx = tid + i * 256;
-    const int r = idx >> 3, c = (idx & 7) * 8;
-    const int q = q0 + r;
-    const bool v = q < L;
-    cp_async16(sQ + swz64(r, c), qbase + (long)(v ? q : 0) * kQkvStride + c, v ? 16 : 0);
-  }
-  auto load_kv = [&](int j, int buf) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int idx = tid + i * 256;
-      const int r = idx >> 3, c = (idx & 7) * 8;
-      const int k = j * 64 + r;
-      const bool v = k < L;
-      const long off = (long)(v ? k : 0) * kQkvStride + c;
-      cp_async16(sK + buf * 8192 + swz64(r, c), kbase + off, v ? 16 : 0);
-      cp_async16(sV + buf * 8192 + swz64(r, c), vbase + off, v ? 16 : 0);
-    }
-  };
-  if (n_kv > 0) load_kv(0, 0);
-  cp_async_commit();
-
-  const float scale_log2 = 0.125f * 1.4426950408889634f;
-  const int g = lane >> 2, tig = lane & 3;
-  const int qr0 = q0 + warp * 16 + g;  // rows qr0 and qr0 + 8
-  float m_r[2] = {-INFINITY, -INFINITY};
-  float l_r[2] = {0.f, 0.f};
-  float o[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  uint32_t qf[4][4];
-  bool q_loaded = false;
-
-  for (int j = 0; j < n_kv; ++j) {
-    const int buf = j & 1;
-    if (j + 1 < n_kv) load_kv(j + 1, buf ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    if (!q_loaded) {
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const int r = warp * 16 + (lane & 15);
-        const int c = ks * 16 + (lane >> 4) * 8;
-        ldsm_x4(sQ + swz64(r, c), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
-      }
-      q_loaded = true;
-    }
-    // S = Q K^T  (16 x 64 per warp)
-    float s[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-    const uint32_t kb = sK + buf * 8192;
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-      for (int nb = 0; nb < 4; ++nb) {
-        const int mi = lane >> 3;
-        const int r = nb * 16 + (mi >> 1) * 8 + (lane & 7);
-        const int c = ks * 16 + (mi & 1) * 8;
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kb + swz64(r, c), b0, b1, b2, b3);
-        mma_bf16_16816(s[2 * nb], qf[ks], b0, b1);
-        mma_bf16_16816(s[2 * nb + 1], qf[ks], b2, b3);
-      }
-    }
-    // mask + online softmax
-    const int kv0 = j * 64;
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = kv0 + nb * 8 + 2 * tig + (e & 1);
-        const int q = qr0 + (e >> 1) * 8;
-        const bool vis = key < L && (chunk <= 0 || (key / chunk) <= (q / chunk));
-        const float val = vis ? s[nb][e] * scale_log2 : -INFINITY;
-        s[nb][e] = val;
-        mx[e >> 1] = fmaxf(mx[e >> 1], val);
-      }
-    }
-    float alpha[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
-      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
-      const float m_new = fmaxf(m_r[h], mx[h]);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      alpha[h] = exp2f(m_r[h] - m_use);
-      m_r[h] = m_new;
-      mx[h] = m_use;
-    }
-    float rs[2] = {0.f, 0.f};
-    uint32_t pf[4][4];
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      const float p0 = exp2f(s[nb][0] - mx[0]);
-      const float p1 = exp2f(s[nb][1] - mx[0]);
-      const float p2 = exp2f(s[nb][2] - mx[1]);
-      const float p3 = exp2f(s[nb][3] - mx[1]);
-      rs[0] += p0 + p1;
-      rs[1] += p2 + p3;
-      const int ks = nb >> 1, hi = nb & 1;
-      pf[ks][hi * 2 + 0] = pack_bf16x2(p0, p1);
-      pf[ks][hi * 2 + 1] = pack_bf16x2(p2, p3);
-    }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) l_r[h] = l_r[h] * alpha[h] + rs[h];
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      o[nb][0] *= alpha[0];
-      o[nb][1] *= alpha[0];
-      o[nb][2] *= alpha[1];
-      o[nb][3] *= alpha[1];
-    }
-    // O += P V
-    const uint32_t vb = sV + buf * 8192;
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      // A fragment layout: a0a1 = (g, k 2tig), a2a3 = (g+8, k 2tig), a4a5 = (g, k 8+2tig), a6a7 = (g+8, k 8+2tig)
-      uint32_t a[4] = {pf[ks][0], pf[ks][1], pf[ks][2], pf[ks][3]};
-#pragma unroll
-      for (int nb = 0; nb < 4; ++nb) {
-        const int mi = lane >> 3;
-        const int r = ks * 16 + (mi & 1) * 8 + (lane & 7);
-        const int c = nb * 16 + (mi >> 1) * 8;
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(vb + swz64(r, c), b0, b1, b2, b3);
-        mma_bf16_16816(o[2 * nb], a, b0, b1);
-        mma_bf16_16816(o[2 * nb + 1], a, b2, b3);
-      }
-    }
-    __syncthreads();
-  }
-  // normalise + store
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    float l = l_r[h];
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    const int q = qr0 + h * 8;
-    if (q < L) {
-      bf16* orow = out + (long)(base + q) * 1024 + head * 64;
-#pragma unroll
-      for (int nb = 0; nb < 8; ++nb) {
-        const int c = nb * 8 + 2 * tig;
-        *reinterpret_cast<uint32_t*>(orow + c) =
-            pack_bf16x2(o[nb][h * 2] * inv, o[nb][h * 2 + 1] * inv);
-      }
-    }
-  }
-}
-
 // ------------------------------------------------------------------ bf16 (tcgen05)
 // Persistent: each CTA walks work items (128-row query tile, head) c, c+grid, ...
-// (tiles arrive most expensive first).  6 warps per CTA, 2 CTAs per SM:
+// (tiles arrive most expensive first).  10 warps per CTA, 2 CTAs per SM:
 //   warp 0   TMA: Q of each item into one of two buffers, K/V tiles of 64 keys
 //            into a 4-stage ring
 //   warp 1   owns TMEM (S at columns 0..63, P at 64..95, two O buffers of 80
@@ -270,7 +54,6 @@ __global__ void __launch_bounds__(256) attn_bf16_mma_kernel(const bf16* __restri
 constexpr int kTcKv = 64;
 constexpr int kTcSmemQ = 128 * 128;      // 16 KB per Q buffer
 constexpr int kTcSmemKV = kTcKv * 128;   // 8 KB per K or V tile
-constexpr int kTcSmemP = 128 * 128;      // 16 KB per P buffer (128 rows x 64 keys)
 constexpr int kTcKvStages = 4;
 constexpr int kTcOffK = 2 * kTcSmemQ;
 constexpr int kTcOffV = kTcOffK + kTcKvStages * kTcSmemKV;
