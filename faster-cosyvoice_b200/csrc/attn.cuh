@@ -184,6 +184,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -403,6 +405,8 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__
                                                        const int32_t* __restrict__ cu,
                                                        const int2* __restrict__ tiles, int chunk,
                                                        float* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   __shared__ float sK[32][64];
   __shared__ float sV[32][64];
   const int2 tl = tiles[blockIdx.x];

@@ -11,6 +11,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -59,6 +60,8 @@ int fail(int code, const char* fmt, ...) {
     if (s_ != FCV_OK) return s_; \
   } while (0)
 
+
+
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 int num_sms() {
@@ -89,6 +92,47 @@ ProfState g_prof;
 std::mutex g_prof_mu;
 
 inline void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+// Programmatic dependent launch: kernels on one stream may start their
+// prologue while the previous kernel finishes (every kernel opens with
+// griddepcontrol.wait before touching memory).  FCV_PDL=0 in the environment
+// launches them with plain stream serialisation instead.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("FCV_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+int launch_k_opt(bool pdl, const char* name, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                 cudaStream_t s, Args... args) {
+  count_launch();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = (pdl && pdl_enabled()) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess) return fail(FCV_ECUDA, "launch of %s failed: %s", name, cudaGetErrorString(e));
+  return FCV_OK;
+}
+template <typename... KArgs, typename... Args>
+int launch_k(const char* name, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+             Args... args) {
+  return launch_k_opt(true, name, kernel, grid, block, smem, s, args...);
+}
+#define FCV_LAUNCH(...)                        \
+  do {                                         \
+    const int rc_ = launch_k(__VA_ARGS__);     \
+    if (rc_ != FCV_OK) return rc_;             \
+  } while (0)
 
 cudaEvent_t prof_event() {
   if (g_prof.next >= g_prof.pool.size()) return nullptr;
@@ -213,8 +257,7 @@ int launch_tc(const GemmCall& g, cudaStream_t s) {
                                   Cfg::SMEM_BYTES));
     attr_set[dev & 63] = true;
   }
-  tc_gemm_kernel<BN, Tact><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, tc, args);
-  FCV_LAUNCH_CHECK("tc_gemm_kernel");
+  FCV_LAUNCH("tc_gemm_kernel", tc_gemm_kernel<BN, Tact>, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM_BYTES, s, ta, tb, tc, args);
   return FCV_OK;
 }
 
@@ -281,8 +324,7 @@ int launch_tc_pair(const GemmCall& g, cudaStream_t s) {
   }
   const int tiles = args.m_blocks * args.n_blocks;
   const int pairs = std::max(1, std::min(tiles, max_pairs()));
-  tc_gemm_pair_kernel<Tact><<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, tc, args);
-  FCV_LAUNCH_CHECK("tc_gemm_pair_kernel");
+  FCV_LAUNCH("tc_gemm_pair_kernel", tc_gemm_pair_kernel<Tact>, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::SMEM_BYTES, s, ta, tb, tc, args);
   return FCV_OK;
 }
 
@@ -311,8 +353,7 @@ int run_gemm(const GemmCall& g, int dtype, cudaStream_t s, int force_bn = 0) {
   a.conv = g.conv;
   a.epi = g.epi;
   dim3 grid((g.N + 63) / 64, (g.M + 63) / 64);
-  simt_gemm_f32_kernel<<<grid, 256, 0, s>>>(a);
-  FCV_LAUNCH_CHECK("simt_gemm_f32_kernel");
+  FCV_LAUNCH("simt_gemm_f32_kernel", simt_gemm_f32_kernel, dim3(grid), dim3(256), 0, s, a);
   return FCV_OK;
 }
 
@@ -348,12 +389,14 @@ int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, cons
     }
     const int items = n_tiles * FCV_HEADS;
     const int ctas = std::min(items, 2 * num_sms());  // persistent, 2 CTAs per SM
-    attn_tc_kernel<<<ctas, kTcThreads, kTcSmemBytes, s>>>(tq, tkv, cu, t2, n_tiles, chunk, static_cast<bf16*>(out));
-    FCV_LAUNCH_CHECK("attn_tc_kernel");
+    // Plain stream order: the work items are dealt to CTAs by index, and CTAs that
+    // start early on the SMs freed first by the previous kernel would unbalance it.
+    const int rc = launch_k_opt(false, "attn_tc_kernel", attn_tc_kernel, dim3(ctas), dim3(kTcThreads), kTcSmemBytes, s, tq, tkv, cu, t2, n_tiles, chunk,
+                                 static_cast<bf16*>(out));
+    if (rc != FCV_OK) return rc;
   } else {
-    attn_f32_kernel<<<grid, 128, 0, s>>>(static_cast<const float*>(qkv), cu, t2, chunk,
+    FCV_LAUNCH("attn_f32_kernel", attn_f32_kernel, dim3(grid), dim3(128), 0, s, static_cast<const float*>(qkv), cu, t2, chunk,
                                          static_cast<float*>(out));
-    FCV_LAUNCH_CHECK("attn_f32_kernel");
   }
   return FCV_OK;
 }
@@ -362,9 +405,18 @@ template <typename Th, typename To>
 int launch_ln(const void* h, const float* shift, const float* scale, const int32_t* doc_ids, long stride,
               int N, void* out, cudaStream_t s) {
   if (N <= 0) return FCV_OK;
-  ln_modulate_kernel<Th, To><<<(N + 7) / 8, 256, 0, s>>>(static_cast<const Th*>(h), shift, scale, doc_ids,
-                                                        stride, N, static_cast<To*>(out));
-  FCV_LAUNCH_CHECK("ln_modulate_kernel");
+  if (reinterpret_cast<uintptr_t>(h) & 15) return fail(FCV_EINVAL, "layer norm: h must be 16-byte aligned");
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    FCV_CUDA(cudaFuncSetAttribute(ln_modulate_kernel<Th, To>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  ln_smem_bytes<Th>()));
+    attr[dev & 63] = true;
+  }
+  const int grid = std::min(num_sms(), (N + kLnWarps - 1) / kLnWarps);
+  FCV_LAUNCH("ln_modulate_kernel", ln_modulate_kernel<Th, To>, dim3(grid), dim3(kLnWarps * 32), ln_smem_bytes<Th>(), s, 
+      static_cast<const Th*>(h), shift, scale, doc_ids, stride, N, static_cast<To*>(out));
   return FCV_OK;
 }
 
@@ -436,9 +488,8 @@ template <typename T>
 int run_time_embed(const fcv_dit_weights* w, const void* t, int B, void* tsin, void* th1, float* temb,
                    void* silu_act, cudaStream_t s) {
   const int dtype = w->dtype;
-  time_sinusoid_kernel<T><<<B, 128, 0, s>>>(static_cast<const T*>(t), dtype == FCV_DTYPE_BF16 ? 1 : 0,
+  FCV_LAUNCH("time_sinusoid_kernel", time_sinusoid_kernel<T>, dim3(B), dim3(128), 0, s, static_cast<const T*>(t), dtype == FCV_DTYPE_BF16 ? 1 : 0,
                                             static_cast<T*>(tsin));
-  FCV_LAUNCH_CHECK("time_sinusoid_kernel");
   GemmCall g1{};
   g1.A = tsin; g1.lda = 256; g1.a_rows = B; g1.W = w->time_w1; g1.M = B; g1.N = 1024; g1.K = 256;
   g1.epi = make_epi(EPI_SILU, B, 1024, th1, 1024, w->time_b1);
@@ -475,13 +526,11 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   {
     ProfScope ps(FCV_CAT_EMBED, s);
     dim3 grid((bt->T + 31) / 32, B);
-    embed_gather_kernel<T><<<grid, 256, 0, s>>>(static_cast<const T*>(bt->x), static_cast<const T*>(bt->cond),
+    FCV_LAUNCH("embed_gather_kernel", embed_gather_kernel<T>, dim3(grid), dim3(256), 0, s, static_cast<const T*>(bt->x), static_cast<const T*>(bt->cond),
                                                 static_cast<const T*>(bt->mu), static_cast<const T*>(bt->spks),
                                                 bt->cu_seqlens, bt->T, static_cast<T*>(ws.a_in));
-    FCV_LAUNCH_CHECK("embed_gather_kernel");
-    zero_gap_rows_kernel<T><<<(unsigned)G, 128, 0, s>>>(bt->gap_rows, (int)G, static_cast<T*>(ws.gap0),
+    FCV_LAUNCH("zero_gap_rows_kernel", zero_gap_rows_kernel<T>, dim3((unsigned)G), dim3(128), 0, s, bt->gap_rows, (int)G, static_cast<T*>(ws.gap0),
                                                        static_cast<T*>(ws.gap1));
-    FCV_LAUNCH_CHECK("zero_gap_rows_kernel");
     GemmCall g{};
     g.A = ws.a_in; g.lda = 320; g.a_rows = N; g.W = w->in_w; g.M = N; g.N = 1024; g.K = 320;
     g.epi = make_epi(EPI_EMBED_GAP, N, 1024, ws.gap0, 1024, w->in_b);
@@ -567,10 +616,9 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mf + 1024, mf + 0, bt->doc_ids, MS, N, ws.norm, dtype, s));
   const int zgrid = std::max(1, std::min(4096, (int)(((long)B * 80 * bt->T + 255) / 256)));
   if (bt->out_f32)
-    zero_padding_kernel<float><<<zgrid, 256, 0, s>>>(bt->cu_seqlens, B, bt->T, static_cast<float*>(bt->out));
+    FCV_LAUNCH("zero_padding_kernel", zero_padding_kernel<float>, dim3(zgrid), dim3(256), 0, s, bt->cu_seqlens, B, bt->T, static_cast<float*>(bt->out));
   else
-    zero_padding_kernel<T><<<zgrid, 256, 0, s>>>(bt->cu_seqlens, B, bt->T, static_cast<T*>(bt->out));
-  FCV_LAUNCH_CHECK("zero_padding_kernel");
+    FCV_LAUNCH("zero_padding_kernel", zero_padding_kernel<T>, dim3(zgrid), dim3(256), 0, s, bt->cu_seqlens, B, bt->T, static_cast<T*>(bt->out));
   GemmCall po{};
   po.A = ws.norm; po.lda = 1024; po.a_rows = N; po.M = N; po.N = 80; po.K = 1024; po.W = w->out_w;
   po.epi = make_epi(EPI_UNPACK, N, 80, bt->out, 0, w->out_b);
@@ -637,10 +685,9 @@ int fcv_mask_lengths(const void* mask, int dtype, int B, int T, int32_t* lengths
   if (!valid_dtype(dtype)) return fail(FCV_EINVAL, "fcv_mask_lengths: bad dtype");
   if (B == 0) return FCV_OK;
   if (dtype == FCV_DTYPE_BF16)
-    mask_lengths_kernel<bf16><<<B, 256, 0, as_stream(stream)>>>(static_cast<const bf16*>(mask), T, lengths);
+    FCV_LAUNCH("mask_lengths_kernel", mask_lengths_kernel<bf16>, dim3(B), dim3(256), 0, as_stream(stream), static_cast<const bf16*>(mask), T, lengths);
   else
-    mask_lengths_kernel<float><<<B, 256, 0, as_stream(stream)>>>(static_cast<const float*>(mask), T, lengths);
-  FCV_LAUNCH_CHECK("mask_lengths_kernel");
+    FCV_LAUNCH("mask_lengths_kernel", mask_lengths_kernel<float>, dim3(B), dim3(256), 0, as_stream(stream), static_cast<const float*>(mask), T, lengths);
   return FCV_OK;
 }
 
@@ -649,12 +696,10 @@ int fcv_pack_layout(const int32_t* lengths, int B, int T, int max_rows, int64_t*
   if (!lengths || !doc_ids || !positions || !cu_seqlens || B < 1 || T < 0 || max_rows < 0)
     return fail(FCV_EINVAL, "fcv_pack_layout: bad arguments");
   cudaStream_t s = as_stream(stream);
-  lengths_scan_kernel<<<1, 1024, 0, s>>>(lengths, B, cu_seqlens);
-  FCV_LAUNCH_CHECK("lengths_scan_kernel");
+  FCV_LAUNCH("lengths_scan_kernel", lengths_scan_kernel, dim3(1), dim3(1024), 0, s, lengths, B, cu_seqlens);
   const long work = std::max<long>((long)max_rows + 30L * (B + 1), 1);
   const int grid = (int)std::min<long>((work + 255) / 256, 8L * num_sms());
-  layout_fill_kernel<<<grid, 256, 0, s>>>(cu_seqlens, B, T, max_rows, gather, doc_ids, positions, gap_rows);
-  FCV_LAUNCH_CHECK("layout_fill_kernel");
+  FCV_LAUNCH("layout_fill_kernel", layout_fill_kernel, dim3(grid), dim3(256), 0, s, cu_seqlens, B, T, max_rows, gather, doc_ids, positions, gap_rows);
   return FCV_OK;
 }
 
@@ -667,12 +712,11 @@ int fcv_unpack_output(const void* packed, int dtype, const int32_t* cu_seqlens, 
   if (total == 0) return FCV_OK;
   const int grid = (int)std::min<long>((total + 255) / 256, 4096);
   if (dtype == FCV_DTYPE_BF16)
-    unpack_kernel<bf16><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const bf16*>(packed), cu_seqlens, B, T,
+    FCV_LAUNCH("unpack_kernel", unpack_kernel<bf16>, dim3(grid), dim3(256), 0, as_stream(stream), static_cast<const bf16*>(packed), cu_seqlens, B, T,
                                                             static_cast<bf16*>(out));
   else
-    unpack_kernel<float><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const float*>(packed), cu_seqlens, B, T,
+    FCV_LAUNCH("unpack_kernel", unpack_kernel<float>, dim3(grid), dim3(256), 0, as_stream(stream), static_cast<const float*>(packed), cu_seqlens, B, T,
                                                              static_cast<float*>(out));
-  FCV_LAUNCH_CHECK("unpack_kernel");
   return FCV_OK;
 }
 
@@ -696,14 +740,13 @@ int fcv_gate_res_ln_modulate(const void* h, const float* gate, const void* r, co
   if (N == 0) return FCV_OK;
   cudaStream_t s = as_stream(stream);
   if (dtype == FCV_DTYPE_BF16)
-    gate_res_ln_modulate_kernel<bf16><<<(N + 7) / 8, 256, 0, s>>>(
+    FCV_LAUNCH("gate_res_ln_modulate_kernel", gate_res_ln_modulate_kernel<bf16>, dim3((N + 7) / 8), dim3(256), 0, s, 
         static_cast<const bf16*>(h), gate, static_cast<const bf16*>(r), shift, scale, doc_ids, mod_stride, N,
         static_cast<bf16*>(h_out), static_cast<bf16*>(norm));
   else
-    gate_res_ln_modulate_kernel<float><<<(N + 7) / 8, 256, 0, s>>>(
+    FCV_LAUNCH("gate_res_ln_modulate_kernel", gate_res_ln_modulate_kernel<float>, dim3((N + 7) / 8), dim3(256), 0, s, 
         static_cast<const float*>(h), gate, static_cast<const float*>(r), shift, scale, doc_ids, mod_stride, N,
         static_cast<float*>(h_out), static_cast<float*>(norm));
-  FCV_LAUNCH_CHECK("gate_res_ln_modulate_kernel");
   return FCV_OK;
 }
 
@@ -825,18 +868,17 @@ int fcv_cfg_euler(float* x, const void* d, int d_dtype, int R, int T, float dt, 
   cudaStream_t s = as_stream(stream);
   const bool db = d_dtype == FCV_DTYPE_BF16, nb = x_next_dtype == FCV_DTYPE_BF16;
   if (db && nb)
-    cfg_euler_kernel<bf16, bf16><<<grid, 256, 0, s>>>(x, static_cast<const bf16*>(d), R, per, dt, cfg_rate,
+    FCV_LAUNCH("cfg_euler_kernel", cfg_euler_kernel<bf16, bf16>, dim3(grid), dim3(256), 0, s, x, static_cast<const bf16*>(d), R, per, dt, cfg_rate,
                                                       static_cast<bf16*>(x_next));
   else if (db)
-    cfg_euler_kernel<bf16, float><<<grid, 256, 0, s>>>(x, static_cast<const bf16*>(d), R, per, dt, cfg_rate,
+    FCV_LAUNCH("cfg_euler_kernel", cfg_euler_kernel<bf16, float>, dim3(grid), dim3(256), 0, s, x, static_cast<const bf16*>(d), R, per, dt, cfg_rate,
                                                        static_cast<float*>(x_next));
   else if (nb)
-    cfg_euler_kernel<float, bf16><<<grid, 256, 0, s>>>(x, static_cast<const float*>(d), R, per, dt, cfg_rate,
+    FCV_LAUNCH("cfg_euler_kernel", cfg_euler_kernel<float, bf16>, dim3(grid), dim3(256), 0, s, x, static_cast<const float*>(d), R, per, dt, cfg_rate,
                                                        static_cast<bf16*>(x_next));
   else
-    cfg_euler_kernel<float, float><<<grid, 256, 0, s>>>(x, static_cast<const float*>(d), R, per, dt, cfg_rate,
+    FCV_LAUNCH("cfg_euler_kernel", cfg_euler_kernel<float, float>, dim3(grid), dim3(256), 0, s, x, static_cast<const float*>(d), R, per, dt, cfg_rate,
                                                         static_cast<float*>(x_next));
-  FCV_LAUNCH_CHECK("cfg_euler_kernel");
   return FCV_OK;
 }
 

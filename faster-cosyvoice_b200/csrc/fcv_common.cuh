@@ -34,6 +34,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Every kernel of the library executes griddep_wait() in all threads before it
+// reads or writes memory that an earlier kernel on the stream may touch, then
+// griddep_launch() so that the next kernel's CTAs may start their prologue.
+// Both are no-ops for a launch without the programmatic-serialization attribute.
+// Because every CTA waits before it exits, a kernel's completion implies the
+// completion of all kernels before it on the stream.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -107,9 +117,18 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, uint32_t
                "r"(src), "r"(x), "r"(y)
                : "memory");
 }
+// 1-D bulk copy global -> shared (no tensor map), completion counted on `bar` in
+// bytes.  Both addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until every committed bulk store has finished reading its shared source.
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until all but the most recent committed bulk group have finished reading their source.
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // Wait until every committed bulk store is complete.
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA).
@@ -307,17 +326,32 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_ma
 __device__ __forceinline__ float bf16_round_f(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
+// 2^x on the special-function unit (ex2.approx.ftz.f32, relative error ~2^-22).
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+// GELU, tanh form: 0.5 x (1 + tanh(u)) with u = sqrt(2/pi) (x + 0.044715 x^3).
+// Uses the identity 0.5 (1 + tanh(u)) = 1 / (1 + e^(-2u)), so no cancellation
+// for negative x: one exponential and one fast division.
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+  const float u = k0 * (x + k1 * x * x * x);
+  return __fdividef(x, 1.0f + ex2_fast(-2.0f * kLog2e * u));
 }
+// Mish: x tanh(softplus(x)).  With n = e^x, tanh(log(1 + n)) = n (n + 2) / (n (n + 2) + 2).
+// Above 20 softplus is x (torch's threshold) and tanh(x) rounds to 1 in fp32.
 __device__ __forceinline__ float mish(float x) {
-  // x * tanh(softplus(x)); softplus = log1p(exp(x)), linear above 20 (torch threshold)
-  const float sp = x > 20.0f ? x : log1pf(expf(x));
-  return x * tanhf(sp);
+  if (x > 20.0f) return x;
+  const float n = ex2_fast(x * kLog2e);
+  const float w = n * (n + 2.0f);
+  return x * __fdividef(w, w + 2.0f);
 }
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+// SiLU: x / (1 + e^-x).
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + ex2_fast(-x * kLog2e)); }
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v);

@@ -213,8 +213,9 @@ struct TcGemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int EPI_WARPS = 8;
-  static constexpr int STAGING_BYTES = EPI_WARPS * 4096;   // 32 rows x 128 B per epilogue warp
-  static constexpr int BIAS_BYTES = EPI_WARPS * (BN / 2) * 4;
+  // two 32-row x 128-byte staging tiles per epilogue warp (TMA output paths only; BN < 128 stores directly)
+  static constexpr int STAGING_BYTES = BN >= 128 ? EPI_WARPS * 8192 : 0;
+  static constexpr int BIAS_BYTES = 0;
   static constexpr int BAR_BYTES = 256;
   static constexpr int BUDGET = 227 * 1024 - 1024 - STAGING_BYTES - BIAS_BYTES - BAR_BYTES;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
@@ -234,13 +235,29 @@ __device__ __forceinline__ void stage_row128(uint8_t* stage, int r, const uint32
   }
 }
 
+// Bias of output columns col0..col0+31 added to v (warp-uniform loads, served by
+// L1).  Only the TMA output paths use it; they require N % 32 == 0, so a piece
+// with col0 < N lies entirely inside the bias vector.
+__device__ __forceinline__ void add_bias32(const EpiParams& P, int col0, float (&v)[32]) {
+  if (P.bias == nullptr || col0 >= P.N) return;
+  const float4* b4 = reinterpret_cast<const float4*>(P.bias + col0);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 b = __ldg(b4 + j);
+    v[4 * j] += b.x;
+    v[4 * j + 1] += b.y;
+    v[4 * j + 2] += b.z;
+    v[4 * j + 3] += b.w;
+  }
+}
+
 // bf16 epilogue on 32 accumulator columns held as raw bits in r[]: adds the bias,
 // applies GELU / SiLU / partial RoPE and packs bf16 pairs into r[0..15].
-__device__ __forceinline__ void epi_bf16_half(const EpiParams& P, uint32_t (&r)[32], const float* bias,
-                                              int col0, int pos) {
+__device__ __forceinline__ void epi_bf16_half(const EpiParams& P, uint32_t (&r)[32], int col0, int pos) {
   float v[32];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) + bias[j];
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  add_bias32(P, col0, v);
   if (P.epi == EPI_GELU) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
@@ -263,25 +280,14 @@ __device__ __forceinline__ void epi_bf16_half(const EpiParams& P, uint32_t (&r)[
   for (int j = 0; j < 16; ++j) r[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
 }
 
-// Stage this warp's bias slice (HALF columns starting at n0) in shared memory.
-template <int HALF>
-__device__ __forceinline__ void stage_bias(const EpiParams& P, int n0, int lane, float* bias_w) {
-  for (int c = lane * 4; c < HALF; c += 128) {
-    float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (P.bias != nullptr && n0 + c + 3 < P.N) b4 = __ldg(reinterpret_cast<const float4*>(P.bias + n0 + c));
-    *reinterpret_cast<float4*>(bias_w + c) = b4;
-  }
-  __syncwarp();
-}
-
 // Drain one accumulator slab through the epilogue: TMEM lanes q*32..q*32+31
 // (output rows row_base + q*32 + lane) and HALF columns starting at TMEM
 // address taddr (output columns n0..).  Direct stores, TMA stores of 32-row x
 // 128-byte tiles, or TMA reduce-add, as args.tma_out says.
 template <int HALF, typename Tact>
 __device__ __forceinline__ void epilogue_slab(const TcGemmArgs& args, const CUtensorMap* tmC, uint32_t taddr,
-                                              int row_base, int q, int lane, int n0, const float* bias_w,
-                                              uint8_t* stage_buf, uint32_t stage_u32) {
+                                              int row_base, int q, int lane, int n0, uint8_t* stage_buf,
+                                              int& sbuf) {
   const EpiParams& P = args.epi;
   const int row = row_base + q * 32 + lane;
   if (args.tma_out == 0) {
@@ -307,22 +313,28 @@ __device__ __forceinline__ void epilogue_slab(const TcGemmArgs& args, const CUte
       tmem_wait_ld();
       const int col0 = n0 + c * 64;
       // in place: bits -> float (+ bias, activation) -> packed bf16 pairs in r0[0..15], r1[0..15]
-      epi_bf16_half(P, r0, bias_w + c * 64, col0, pos);
-      epi_bf16_half(P, r1, bias_w + c * 64 + 32, col0 + 32, pos);
+      epi_bf16_half(P, r0, col0, pos);
+      epi_bf16_half(P, r1, col0 + 32, pos);
       uint32_t w[32];
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         w[j] = r0[j];
         w[16 + j] = r1[j];
       }
-      if (lane == 0) bulk_wait_read0();
-      __syncwarp();
-      stage_row128(stage_buf, lane, w);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0 && col0 < P.N && row_base + q * 32 < P.M) {
-        tma_store_2d(tmC, stage_u32, col0, row_base + q * 32);
-        bulk_commit();
+      if (col0 < P.N && row_base + q * 32 < P.M) {  // warp-uniform
+        // staging tiles alternate per issued store: the group before the most
+        // recent one read this tile, and wait_group.read 1 covers it
+        uint8_t* sb = stage_buf + (sbuf & 1) * 4096;
+        ++sbuf;
+        if (lane == 0) bulk_wait_read1();
+        __syncwarp();
+        stage_row128(sb, lane, w);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tmC, smem_u32(sb), col0, row_base + q * 32);
+          bulk_commit();
+        }
       }
     }
   } else {
@@ -346,22 +358,26 @@ __device__ __forceinline__ void epilogue_slab(const TcGemmArgs& args, const CUte
         }
       }
       tmem_wait_ld();
+      float x[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(r[j]);
+      add_bias32(P, col0, x);
       uint32_t w[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        float x = __uint_as_float(r[j]) + bias_w[c * 32 + j];
-        if (grow != nullptr) x *= g[j];
-        w[j] = __float_as_uint(x);
-      }
-      if (lane == 0) bulk_wait_read0();
-      __syncwarp();
-      stage_row128(stage_buf, lane, w);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0 && col0 < P.N && row_base + q * 32 < P.M) {
-        if (args.tma_out == 2) tma_reduce_add_2d(tmC, stage_u32, col0, row_base + q * 32);
-        else tma_store_2d(tmC, stage_u32, col0, row_base + q * 32);
-        bulk_commit();
+      for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(grow != nullptr ? x[j] * g[j] : x[j]);
+      if (col0 < P.N && row_base + q * 32 < P.M) {  // warp-uniform
+        uint8_t* sb = stage_buf + (sbuf & 1) * 4096;
+        ++sbuf;
+        if (lane == 0) bulk_wait_read1();
+        __syncwarp();
+        stage_row128(sb, lane, w);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (args.tma_out == 2) tma_reduce_add_2d(tmC, smem_u32(sb), col0, row_base + q * 32);
+          else tma_store_2d(tmC, smem_u32(sb), col0, row_base + q * 32);
+          bulk_commit();
+        }
       }
     }
   }
@@ -377,8 +393,7 @@ __global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * Cfg::STAGE_BYTES;
-  float* bias_s = reinterpret_cast<float*>(staging + Cfg::STAGING_BYTES);
-  uint8_t* bar_area = reinterpret_cast<uint8_t*>(bias_s) + Cfg::BIAS_BYTES;
+  uint8_t* bar_area = staging + Cfg::STAGING_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -414,6 +429,10 @@ __global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x != 0) {  // thread 0 (the producer) waits after its weight prefetch
+    griddep_wait();
+    griddep_launch();
+  }
 
   const int num_tiles = args.m_blocks * args.n_blocks;
   const uint32_t smem_base = smem_u32(smem);
@@ -425,6 +444,20 @@ __global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
       uint32_t phase = 0;
       long issued = 0;
       bool ok = true;
+      // The weights are not written by earlier kernels: load the first tile's B
+      // stages before waiting for the previous kernel (overlaps its tail).
+      int pre = 0;
+      if (static_cast<int>(blockIdx.x) < num_tiles) {
+        const int n_blk0 = blockIdx.x % args.n_blocks;
+        pre = min(STAGES, args.num_kb);
+        for (int kb = 0; kb < pre; ++kb) {
+          const uint32_t fb = smem_u32(&full[kb]);
+          mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+          tma_load_2d(smem_base + kb * Cfg::STAGE_BYTES + Cfg::A_BYTES, &tmB, fb, kb * 64, n_blk0 * BN);
+        }
+      }
+      griddep_wait();
+      griddep_launch();
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int m_blk = tile / args.n_blocks;
         const int n_blk = tile - m_blk * args.n_blocks;
@@ -436,7 +469,7 @@ __global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
           const uint32_t sa = smem_base + stage * Cfg::STAGE_BYTES;
           const uint32_t sb = sa + Cfg::A_BYTES;
           const uint32_t fb = smem_u32(&full[stage]);
-          mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+          if (issued >= pre) mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
           int ax, ay;
           if (args.conv) {
             ax = n_blk * 64;
@@ -446,7 +479,7 @@ __global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
             ay = m_blk * 128;
           }
           tma_load_2d(sa, &tmA, fb, ax, ay);
-          tma_load_2d(sb, &tmB, fb, kb * 64, n_blk * BN);
+          if (issued >= pre) tma_load_2d(sb, &tmB, fb, kb * 64, n_blk * BN);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -518,9 +551,8 @@ __global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
     const int ew = warp - 2;
     const int q = warp & 3;
     const int col_begin = (ew >> 2) * HALF;
-    uint8_t* stage_buf = staging + ew * 4096;
-    const uint32_t stage_u32 = smem_u32(stage_buf);
-    float* bias_w = bias_s + ew * HALF;
+    uint8_t* stage_buf = staging + ew * 8192;
+    int sbuf = 0;
     const EpiParams& P = args.epi;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -528,11 +560,10 @@ __global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
       const int m_blk = tile / args.n_blocks;
       const int n_blk = tile - m_blk * args.n_blocks;
       const int n0 = n_blk * BN + col_begin;  // first output column of this warp
-      if (args.tma_out) stage_bias<HALF>(P, n0, lane, bias_w);
       if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, 106, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + col_begin;
-      epilogue_slab<HALF, Tact>(args, &tmC, taddr, m_blk * 128, q, lane, n0, bias_w, stage_buf, stage_u32);
+      epilogue_slab<HALF, Tact>(args, &tmC, taddr, m_blk * 128, q, lane, n0, stage_buf, sbuf);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
@@ -567,8 +598,8 @@ struct TcPairCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int EPI_WARPS = 8;
   static constexpr int HALF = 128;  // columns per epilogue warp
-  static constexpr int STAGING_BYTES = EPI_WARPS * 4096;
-  static constexpr int BIAS_BYTES = EPI_WARPS * HALF * 4;
+  static constexpr int STAGING_BYTES = EPI_WARPS * 8192;  // two 32-row x 128-byte tiles per epilogue warp
+  static constexpr int BIAS_BYTES = 0;
   static constexpr int BAR_BYTES = 256;
   static constexpr int BUDGET = 227 * 1024 - 1024 - STAGING_BYTES - BIAS_BYTES - BAR_BYTES;
   static constexpr int STAGES = BUDGET / STAGE_BYTES > 8 ? 8 : BUDGET / STAGE_BYTES;
@@ -587,8 +618,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * Cfg::STAGE_BYTES;
-  float* bias_s = reinterpret_cast<float*>(staging + Cfg::STAGING_BYTES);
-  uint8_t* bar_area = reinterpret_cast<uint8_t*>(bias_s) + Cfg::BIAS_BYTES;
+  uint8_t* bar_area = staging + Cfg::STAGING_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -626,6 +656,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
   cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x != 0) {  // thread 0 (the producer) waits after its weight prefetch
+    griddep_wait();
+    griddep_launch();
+  }
 
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
@@ -639,6 +673,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
       uint32_t phase = 0;
       long issued = 0;
       bool ok = true;
+      // weight (B) stages of the first tile before waiting for the previous kernel
+      int pre = 0;
+      if (pair < num_tiles) {
+        const int n_blk0 = pair % args.n_blocks;
+        pre = min(STAGES, args.num_kb);
+        for (int kb = 0; kb < pre; ++kb) {
+          const uint32_t fb = smem_u32(&full[kb]);
+          if (leader) mbar_arrive_expect_tx(fb, 2 * Cfg::STAGE_BYTES);
+          tma_load_2d_pair(smem_base + kb * Cfg::STAGE_BYTES + Cfg::A_BYTES, &tmB, to_leader(fb), kb * 64,
+                           n_blk0 * 256 + rank * 128);
+        }
+      }
+      griddep_wait();
+      griddep_launch();
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
         const int m_blk = tile / args.n_blocks;
         const int n_blk = tile - m_blk * args.n_blocks;
@@ -650,9 +698,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
           const uint32_t sa = smem_base + stage * Cfg::STAGE_BYTES;
           const uint32_t sb = sa + Cfg::A_BYTES;
           const uint32_t fb = smem_u32(&full[stage]);
-          if (leader) mbar_arrive_expect_tx(fb, 2 * Cfg::STAGE_BYTES);
+          if (leader && issued >= pre) mbar_arrive_expect_tx(fb, 2 * Cfg::STAGE_BYTES);
           tma_load_2d_pair(sa, &tmA, to_leader(fb), kb * 64, m_blk * 256 + rank * 128);
-          tma_load_2d_pair(sb, &tmB, to_leader(fb), kb * 64, n_blk * 256 + rank * 128);
+          if (issued >= pre) tma_load_2d_pair(sb, &tmB, to_leader(fb), kb * 64, n_blk * 256 + rank * 128);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -720,9 +768,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
     const int ew = warp - 2;
     const int q = warp & 3;
     const int col_begin = (ew >> 2) * HALF;
-    uint8_t* stage_buf = staging + ew * 4096;
-    const uint32_t stage_u32 = smem_u32(stage_buf);
-    float* bias_w = bias_s + ew * HALF;
+    uint8_t* stage_buf = staging + ew * 8192;
+    int sbuf = 0;
     const EpiParams& P = args.epi;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -730,12 +777,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
       const int m_blk = tile / args.n_blocks;
       const int n_blk = tile - m_blk * args.n_blocks;
       const int n0 = n_blk * 256 + col_begin;
-      if (args.tma_out) stage_bias<HALF>(P, n0, lane, bias_w);
       if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, 126, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256 + col_begin;
-      epilogue_slab<HALF, Tact>(args, &tmC, taddr, m_blk * 256 + rank * 128, q, lane, n0, bias_w, stage_buf,
-                                stage_u32);
+      epilogue_slab<HALF, Tact>(args, &tmC, taddr, m_blk * 256 + rank * 128, q, lane, n0, stage_buf, sbuf);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(to_leader(smem_u32(&tempty[acc])));
@@ -768,6 +813,8 @@ struct SimtGemmArgs {
 
 // 64x64 tile, 256 threads, 4x4 outputs per thread (4 consecutive columns).
 __global__ void __launch_bounds__(256) simt_gemm_f32_kernel(const SimtGemmArgs a) {
+  griddep_wait();
+  griddep_launch();
   __shared__ float As[16][64 + 4];
   __shared__ float Bs[16][64 + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;

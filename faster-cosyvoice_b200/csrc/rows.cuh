@@ -12,6 +12,8 @@ namespace fcv {
 
 template <typename T>
 __global__ void mask_lengths_kernel(const T* __restrict__ mask, int T_, int32_t* __restrict__ lengths) {
+  griddep_wait();
+  griddep_launch();
   const int b = blockIdx.x;
   int cnt = 0;
   for (int i = threadIdx.x; i < T_; i += blockDim.x) cnt += to_f<T>(mask[(long)b * T_ + i]) > 0.5f;
@@ -30,6 +32,8 @@ __global__ void mask_lengths_kernel(const T* __restrict__ mask, int T_, int32_t*
 // cu_seqlens = [0, cumsum(lengths)] with one CTA of 1024 threads.
 __global__ void __launch_bounds__(1024) lengths_scan_kernel(const int32_t* __restrict__ lengths, int B,
                                                             int32_t* __restrict__ cu) {
+  griddep_wait();
+  griddep_launch();
   __shared__ int part[1024];
   const int per = (B + 1023) / 1024;
   const int b0 = threadIdx.x * per;
@@ -71,6 +75,8 @@ __device__ __forceinline__ int upper_doc(int B, int v, F key) {
 __global__ void layout_fill_kernel(const int32_t* __restrict__ cu, int B, int T_, int max_rows,
                                    int64_t* __restrict__ gather, int32_t* __restrict__ doc_ids,
                                    int32_t* __restrict__ positions, int32_t* __restrict__ gap_rows) {
+  griddep_wait();
+  griddep_launch();
   const int N = cu[B];
   const int G = N + 30 * (B + 1);
   const int stride = gridDim.x * blockDim.x;
@@ -101,6 +107,8 @@ __global__ void layout_fill_kernel(const int32_t* __restrict__ cu, int B, int T_
 template <typename T>
 __global__ void zero_gap_rows_kernel(const int32_t* __restrict__ gap_rows, int G, T* __restrict__ buf0,
                                      T* __restrict__ buf1) {
+  griddep_wait();
+  griddep_launch();
   const int g = blockIdx.x;
   if (g >= G || gap_rows[g] >= 0) return;
   for (int c = threadIdx.x; c < 1024; c += blockDim.x) {
@@ -188,61 +196,110 @@ __device__ __forceinline__ void ln_modulate32(float (&v)[32], int lane, const fl
   }
 }
 
-// One warp per packed row, 8 rows per block (flashinfer_kernels.py:83-108).  The
-// block stages the shift/scale rows of its first row's document in shared
-// memory while the warps load their rows, so both loads are in flight together;
-// a warp whose row belongs to another document reads its rows from global memory.
+// LayerNorm (eps 1e-6, no affine) + AdaLN modulation, one warp per packed row
+// (flashinfer_kernels.py:83-108): out = LN(h) * scale[doc] + shift[doc], where
+// scale already holds 1 + scale_msa.  Persistent: one CTA of 16 warps per SM;
+// warp w of the grid takes rows w, w + W, w + 2W, ... (W = 16 x grid) and
+// streams them through a ring of kLnStages row buffers in shared memory filled
+// by 1-D bulk copies, so up to 48 rows per SM are in flight without holding
+// registers (at N = 6578 every row is requested in the first round trip).
+// Lane l owns columns 128 i + 4 l .. + 3 (i = 0..7): conflict-free shared reads,
+// 256-byte coalesced global stores.  h rows must be 16-byte aligned.
+constexpr int kLnWarps = 16;
+constexpr int kLnStages = 3;
+template <typename Th>
+constexpr int ln_smem_bytes() {
+  return kLnWarps * kLnStages * 1024 * static_cast<int>(sizeof(Th));
+}
+
 template <typename Th, typename To>
-__global__ void __launch_bounds__(256) ln_modulate_kernel(const Th* __restrict__ h, const float* __restrict__ shift,
-                                                          const float* __restrict__ scale,
-                                                          const int32_t* __restrict__ doc_ids, long mod_stride,
-                                                          int N, To* __restrict__ out) {
-  __shared__ __align__(16) float s_mod[2][1024];
-  const int row0 = blockIdx.x * 8;
-  const int row = row0 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const long doc0 = doc_ids[row0];
-  {
-    const int c = threadIdx.x * 4;  // 256 threads x 4 floats = one 1024-float row
-    *reinterpret_cast<float4*>(&s_mod[0][c]) = __ldg(reinterpret_cast<const float4*>(shift + doc0 * mod_stride + c));
-    *reinterpret_cast<float4*>(&s_mod[1][c]) = __ldg(reinterpret_cast<const float4*>(scale + doc0 * mod_stride + c));
-  }
-  float v[32];
-  long doc = doc0;
-  if (row < N) {
-    doc = doc_ids[row];
-    load_row32<Th>(h + (long)row * 1024, lane, v);
-  }
-  __syncthreads();
-  if (row >= N) return;
-  // modulation rows: the block's staged copy, or this row's document rows in global memory
-  const float* shp = doc == doc0 ? s_mod[0] : shift + doc * mod_stride;
-  const float* scp = doc == doc0 ? s_mod[1] : scale + doc * mod_stride;
-  float s = 0.f;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) s += v[j];
-  const float mean = warp_sum(s) * (1.0f / 1024.0f);
-  float q = 0.f;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    v[j] -= mean;
-    q += v[j] * v[j];
-  }
-  const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / 1024.0f) + 1e-6f);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int c = i * 256 + lane * 8;
-#pragma unroll
-    for (int k = 0; k < 8; k += 4) {
-      const float4 a = *reinterpret_cast<const float4*>(shp + c + k);
-      const float4 b = *reinterpret_cast<const float4*>(scp + c + k);
-      v[i * 8 + k] = v[i * 8 + k] * inv * b.x + a.x;
-      v[i * 8 + k + 1] = v[i * 8 + k + 1] * inv * b.y + a.y;
-      v[i * 8 + k + 2] = v[i * 8 + k + 2] * inv * b.z + a.z;
-      v[i * 8 + k + 3] = v[i * 8 + k + 3] * inv * b.w + a.w;
+__global__ void __launch_bounds__(kLnWarps * 32, 1) ln_modulate_kernel(const Th* __restrict__ h, const float* __restrict__ shift,
+                                                                      const float* __restrict__ scale,
+                                                                      const int32_t* __restrict__ doc_ids, long mod_stride,
+                                                                      int N, To* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
+  extern __shared__ __align__(128) uint8_t ln_rows[];
+  __shared__ __align__(8) uint64_t ln_bars[kLnWarps][kLnStages];
+  constexpr uint32_t kRowBytes = 1024 * sizeof(Th);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = gridDim.x * kLnWarps;
+  const int first = blockIdx.x * kLnWarps + warp;
+  const uint8_t* wrows = ln_rows + warp * kLnStages * kRowBytes;
+  const uint32_t buf = smem_u32(wrows);
+  const uint32_t bar0 = smem_u32(&ln_bars[warp][0]);
+  if (lane == 0) {
+    for (int s = 0; s < kLnStages; ++s) mbar_init(bar0 + 8 * s, 1);
+    fence_mbar_init();
+    for (int s = 0; s < kLnStages; ++s) {
+      const int row = first + s * W;
+      if (row < N) {
+        mbar_arrive_expect_tx(bar0 + 8 * s, kRowBytes);
+        bulk_load(buf + s * kRowBytes, h + (long)row * 1024, kRowBytes, bar0 + 8 * s);
+      }
     }
   }
-  store_row32<To>(out + (long)row * 1024, lane, v);
+  __syncwarp();
+  int k = 0;
+  for (int row = first; row < N; row += W, ++k) {
+    const int s = k % kLnStages;
+    const long doc = doc_ids[row];
+    if (!mbar_wait(bar0 + 8 * s, (k / kLnStages) & 1, 241, nullptr)) {
+      // give up on this warp's rows; let its other copies land before the CTA exits
+      for (int k2 = k + 1; k2 < k + kLnStages && row + (k2 - k) * W < N; ++k2)
+        mbar_wait(bar0 + 8 * (k2 % kLnStages), (k2 / kLnStages) & 1, 242, nullptr);
+      return;
+    }
+    float v[32];
+    const uint8_t* src = wrows + s * kRowBytes;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = i * 128 + lane * 4;
+      if constexpr (sizeof(Th) == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(src + c * 4);
+        v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
+      } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(src + c * 2);
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = b.x; v[4 * i + 3] = b.y;
+      }
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sum += v[j];
+    const float mean = warp_sum(sum) * (1.0f / 1024.0f);
+    // every lane's reads of this buffer have produced `mean`: refill it with row + 3W
+    __syncwarp();
+    if (lane == 0 && row + kLnStages * W < N) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(bar0 + 8 * s, kRowBytes);
+      bulk_load(buf + s * kRowBytes, h + (long)(row + kLnStages * W) * 1024, kRowBytes, bar0 + 8 * s);
+    }
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      v[j] -= mean;
+      q += v[j] * v[j];
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(q) * (1.0f / 1024.0f) + 1e-6f);
+    const float* shp = shift + doc * mod_stride;
+    const float* scp = scale + doc * mod_stride;
+    To* orow = out + (long)row * 1024;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = i * 128 + lane * 4;
+      const float4 a = __ldg(reinterpret_cast<const float4*>(shp + c));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(scp + c));
+      const float o0 = v[4 * i] * inv * b.x + a.x, o1 = v[4 * i + 1] * inv * b.y + a.y;
+      const float o2 = v[4 * i + 2] * inv * b.z + a.z, o3 = v[4 * i + 3] * inv * b.w + a.w;
+      if constexpr (sizeof(To) == 4) {
+        *reinterpret_cast<float4*>(orow + c) = make_float4(o0, o1, o2, o3);
+      } else {
+        *reinterpret_cast<uint2*>(orow + c) = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
+      }
+    }
+  }
 }
 
 // h_out = h + gate*r ; norm = LN(h_out)*scale + shift (flashinfer_kernels.py:110-145).
@@ -251,6 +308,8 @@ __global__ void __launch_bounds__(256) gate_res_ln_modulate_kernel(
     const T* __restrict__ h, const float* __restrict__ gate, const T* __restrict__ r,
     const float* __restrict__ shift, const float* __restrict__ scale, const int32_t* __restrict__ doc_ids,
     long mod_stride, int N, T* __restrict__ h_out, T* __restrict__ norm) {
+  griddep_wait();
+  griddep_launch();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= N) return;
@@ -278,6 +337,8 @@ __global__ void __launch_bounds__(256) embed_gather_kernel(const T* __restrict__
                                                            const T* __restrict__ mu, const T* __restrict__ spks,
                                                            const int32_t* __restrict__ cu, int T_,
                                                            T* __restrict__ a_in) {
+  griddep_wait();
+  griddep_launch();
   __shared__ float tile[240][33];
   const int b = blockIdx.y;
   const int p0 = blockIdx.x * 32;
@@ -311,6 +372,8 @@ __global__ void __launch_bounds__(256) embed_gather_kernel(const T* __restrict__
 template <typename T>
 __global__ void __launch_bounds__(128) time_sinusoid_kernel(const T* __restrict__ t, int round_bf16,
                                                             T* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   const int b = blockIdx.x;
   const int i = threadIdx.x;  // 0..127
   float st = 1000.0f * to_f<T>(t[b]);
@@ -326,6 +389,8 @@ __global__ void __launch_bounds__(128) time_sinusoid_kernel(const T* __restrict_
 // Zero the padding frames p >= L_b of a (B, 80, T) tensor.
 template <typename T>
 __global__ void zero_padding_kernel(const int32_t* __restrict__ cu, int B, int T_, T* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   const long total = (long)B * 80 * T_;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const int p = static_cast<int>(i % T_);
@@ -338,6 +403,8 @@ __global__ void zero_padding_kernel(const int32_t* __restrict__ cu, int B, int T
 template <typename T>
 __global__ void unpack_kernel(const T* __restrict__ packed, const int32_t* __restrict__ cu, int B, int T_,
                               T* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   const long total = (long)B * 80 * T_;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const int p = static_cast<int>(i % T_);
@@ -353,6 +420,8 @@ __global__ void unpack_kernel(const T* __restrict__ packed, const int32_t* __res
 template <typename Td, typename Tn>
 __global__ void cfg_euler_kernel(float* __restrict__ x, const Td* __restrict__ d, int R, long per, float dt,
                                  float rate, Tn* __restrict__ x_next) {
+  griddep_wait();
+  griddep_launch();
   const long total = (long)R * per;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const float dc = to_f<Td>(d[i]);
