@@ -30,15 +30,16 @@ __device__ __forceinline__ int kv_limit(int q0, int rows, int L, int chunk) {
 
 // ------------------------------------------------------------------ bf16 (tcgen05)
 // Persistent: each CTA walks work items (128-row query tile, head) c, c+grid, ...
-// (tiles arrive most expensive first).  10 warps per CTA, 2 CTAs per SM:
+// (tiles arrive most expensive first).  6 warps per CTA, 2 CTAs per SM:
 //   warp 0   TMA: Q of each item into one of two buffers, K/V tiles of 64 keys
 //            into a 4-stage ring
 //   warp 1   owns TMEM (S at columns 0..63, P at 64..95, two O buffers of 80
 //            columns at 96 and 176) and issues tcgen05.mma: S_g = Q K_g^T, then
 //            O += P_g [V_g | 1] with P_g read from TMEM
-//   warps 2-9 softmax: TMEM lane quarter = warp % 4 (one query row per lane),
-//            key half = (warp - 2) / 4; the two halves of a row combine their
-//            partial maxima through shared memory (64-thread named barrier).
+//   warps 2-5 softmax: TMEM lane quarter = warp % 4, one query row per lane and
+//            all 64 keys of a tile per thread, so row maxima stay in registers.
+//            A 32-key half that no row of the warp can see (past the document
+//            or the chunk limit) is neither loaded nor exponentiated: its P is 0.
 // The softmax row sum comes from the tensor core: V is extended by a constant
 // shared block whose first column is 1 (reached through the descriptor's
 // leading byte offset), so O column 64 holds sum_k P[q,k] in the same bf16 P
@@ -58,11 +59,10 @@ constexpr int kTcKvStages = 4;
 constexpr int kTcOffK = 2 * kTcSmemQ;
 constexpr int kTcOffV = kTcOffK + kTcKvStages * kTcSmemKV;
 constexpr int kTcOffOnes = kTcOffV + kTcKvStages * kTcSmemKV;  // 64 x 64 bf16, column 0 = 1
-constexpr int kTcOffXmax = kTcOffOnes + kTcSmemKV;  // partial row maxima, 2 tiles x 2 halves x 128 rows
 // TMEM columns: S [0, 64), P [64, 96) (bf16 pairs), O buffers [96, 176) and [176, 256)
 constexpr int kTcColP = 64;
 constexpr int kTcColO = 96;
-constexpr int kTcOffBar = kTcOffXmax + 2 * 2 * 128 * 4;
+constexpr int kTcOffBar = kTcOffOnes + kTcSmemKV;
 // mbarrier slots (8 bytes each), derived from the stage count
 constexpr int kBarQFull = 0;
 constexpr int kBarQEmpty = kBarQFull + 2;
@@ -73,7 +73,8 @@ constexpr int kBarSEmpty = kBarSFull + 1;
 constexpr int kBarPFull = kBarSEmpty + 1;
 constexpr int kBarODone = kBarPFull + 1;
 constexpr int kBarOEmpty = kBarODone + 1;
-constexpr int kBarDrain = kBarOEmpty + 2;
+constexpr int kBarOFinal = kBarOEmpty + 2;  // [2] last P.V of an item done, per O buffer
+constexpr int kBarDrain = kBarOFinal + 2;
 constexpr int kBarCount = kBarDrain + 1;
 constexpr int kTcBarBytes = 256;
 static_assert(kBarCount * 8 + 8 <= kTcBarBytes, "attention barrier area too small");
@@ -115,11 +116,57 @@ __device__ __forceinline__ AttnItem attn_item(const int32_t* cu, const int2* til
   return a;
 }
 
+// Item `it` from its work-list entry tl (already loaded).
+__device__ __forceinline__ AttnItem attn_item_at(const int32_t* cu, int2 tl, int chunk, int it) {
+  AttnItem a;
+  a.head = it & 15;
+  a.q0 = tl.y;
+  a.base = cu[tl.x];
+  a.L = cu[tl.x + 1] - a.base;
+  a.n_kv = (kv_limit(a.q0, kAttnQTile, a.L, chunk) + kTcKv - 1) / kTcKv;
+  return a;
+}
+
+// A CTA's items it, it + stride, ... with the descriptor lookups run ahead: while
+// item `it` is processed, the item after it is already resolved (its cu loads in
+// flight) and the work-list entry of the one after that is loading, so no role
+// waits on a dependent global load at an item boundary.
+struct ItemFeed {
+  const int32_t* cu;
+  const int2* tiles;
+  int chunk, n_items, stride, it;
+  AttnItem cur, nxt;
+  int2 tl2;
+  __device__ __forceinline__ bool init(const int32_t* cu_, const int2* tiles_, int chunk_, int n_items_,
+                                       int first, int stride_) {
+    cu = cu_;
+    tiles = tiles_;
+    chunk = chunk_;
+    n_items = n_items_;
+    stride = stride_;
+    it = first;
+    if (it >= n_items) return false;
+    cur = attn_item(cu, tiles, chunk, it);
+    if (it + stride < n_items) nxt = attn_item(cu, tiles, chunk, it + stride);
+    if (it + 2 * stride < n_items) tl2 = tiles[(it + 2 * stride) >> 4];
+    return true;
+  }
+  __device__ __forceinline__ bool advance() {
+    it += stride;
+    if (it >= n_items) return false;
+    cur = nxt;
+    if (it + stride < n_items) nxt = attn_item_at(cu, tl2, chunk, it + stride);
+    if (it + 2 * stride < n_items) tl2 = tiles[(it + 2 * stride) >> 4];
+    return true;
+  }
+};
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-constexpr int kTcThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax (two per TMEM lane quarter)
+constexpr int kTcThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax (one per TMEM lane quarter)
+constexpr int kTcSoftmaxWarps = 4;
 
 __global__ void __launch_bounds__(kTcThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
@@ -139,10 +186,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint64_t* p_full = bars + kBarPFull;     // P_g written
   uint64_t* o_done = bars + kBarODone;     // P_g [V_g|1] complete (P free, O updated)
   uint64_t* o_empty = bars + kBarOEmpty;   // [2] final O of an item read, per O buffer
+  uint64_t* o_final = bars + kBarOFinal;   // [2] final O of an item complete, per O buffer
   uint64_t* drain = bars + kBarDrain;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBarCount);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* xmax = reinterpret_cast<float*>(smem + kTcOffXmax);  // [2 tiles][2 halves][128 rows]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_items = n_tiles * 16;
@@ -151,16 +198,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&q_full[i]), 1);
       mbar_init(smem_u32(&q_empty[i]), 1);
-      mbar_init(smem_u32(&o_empty[i]), 8);
+      mbar_init(smem_u32(&o_empty[i]), kTcSoftmaxWarps);
+      mbar_init(smem_u32(&o_final[i]), 1);
     }
     for (int i = 0; i < kTcKvStages; ++i) {
       mbar_init(smem_u32(&kv_full[i]), 1);
       mbar_init(smem_u32(&kv_empty[i]), 1);
     }
-    mbar_init(smem_u32(p_full), 8);
+    mbar_init(smem_u32(p_full), kTcSoftmaxWarps);
     mbar_init(smem_u32(o_done), 1);
     mbar_init(smem_u32(s_full), 1);
-    mbar_init(smem_u32(s_empty), 8);
+    mbar_init(smem_u32(s_empty), kTcSoftmaxWarps);
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -192,8 +240,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       // ---------------- TMA producer
       int g = 0, i = 0;
       bool ok = true;
-      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++i) {
-        const AttnItem a = attn_item(cu, tiles, chunk, it);
+      ItemFeed feed;
+      for (bool have = feed.init(cu, tiles, chunk, n_items, blockIdx.x, gridDim.x); have && ok;
+           have = feed.advance(), ++i) {
+        const AttnItem a = feed.cur;
         const int qb = i & 1;
         if (!mbar_wait(smem_u32(&q_empty[qb]), ((i >> 1) & 1) ^ 1, 221, abort_flag)) { ok = false; break; }
         mbar_arrive_expect_tx(smem_u32(&q_full[qb]), kTcSmemQ);
@@ -220,21 +270,24 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       struct Cur {
         int it, i, j, n_kv;
       };
+      // the S cursor runs at most one tile ahead of the P.V cursor, and the feed
+      // follows the S cursor's item
+      ItemFeed feed;
       auto first = [&](Cur& c) -> bool {
         c.it = blockIdx.x;
         c.i = 0;
         c.j = 0;
-        if (c.it >= n_items) return false;
-        c.n_kv = attn_item(cu, tiles, chunk, c.it).n_kv;
+        if (!feed.init(cu, tiles, chunk, n_items, blockIdx.x, gridDim.x)) return false;
+        c.n_kv = feed.cur.n_kv;
         return true;
       };
       auto next = [&](Cur& c) -> bool {
         if (++c.j < c.n_kv) return true;
-        c.it += gridDim.x;
+        if (!feed.advance()) return false;
+        c.it = feed.it;
         c.i += 1;
         c.j = 0;
-        if (c.it >= n_items) return false;
-        c.n_kv = attn_item(cu, tiles, chunk, c.it).n_kv;
+        c.n_kv = feed.cur.n_kv;
         return true;
       };
       auto issue_s = [&](const Cur& c, int g) -> bool {
@@ -264,6 +317,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                        (c.j | k) != 0);
         umma_commit(smem_u32(o_done));
         umma_commit(smem_u32(&kv_empty[g % kTcKvStages]));
+        if (c.j == c.n_kv - 1) umma_commit(smem_u32(&o_final[ob]));  // the item's O is complete
         return true;
       };
       Cur pc, sc;
@@ -284,101 +338,33 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       mbar_wait(smem_u32(drain), 0, 230, nullptr);
     }
   } else {
-    // ---------------- softmax warps 2..9: lane quarter qd = warp % 4, key half h = (warp - 2) / 4
+    // ---------------- softmax warps 2..5: TMEM lane quarter qd = warp % 4, one query row per lane
     const int qd = warp & 3;
-    const int h = (warp - 2) >> 2;
     const int r = qd * 32 + lane;  // row within the tile = TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-    const float sl2 = 0.125f * 1.4426950408889634f;  // softmax scale in log2 units
+    const float sl2 = 0.125f * kLog2e;  // softmax scale in log2 units
     int g = 0, i = 0;
     bool ok = true;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++i) {
-      const AttnItem a = attn_item(cu, tiles, chunk, it);
-      const int qa = a.q0 + r;
-      const int lim = chunk > 0 ? min(a.L, (qa / chunk + 1) * chunk) : a.L;  // visible keys [0, lim)
-      const uint32_t o_addr = lane_base + kTcColO + (i & 1) * kTcOCols;
-      float m_ref = -INFINITY;
-      for (int j = 0; j < a.n_kv; ++j, ++g) {
-        if (!mbar_wait(smem_u32(s_full), g & 1, 231, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        uint32_t sv[32];
-        tmem_ld32(lane_base + h * 32, sv);
-        tmem_wait_ld();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(s_empty));
-        const int nvis = lim - j * kTcKv - h * 32;
-        if (nvis < 32) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (c >= nvis) sv[c] = __float_as_uint(-INFINITY);
-        }
-        // partial row max (tree), then combine with the other key half through shared memory
-        float m4[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          m4[t] = fmax3(fmax3(__uint_as_float(sv[8 * t]), __uint_as_float(sv[8 * t + 1]), __uint_as_float(sv[8 * t + 2])),
-                        fmax3(__uint_as_float(sv[8 * t + 3]), __uint_as_float(sv[8 * t + 4]), __uint_as_float(sv[8 * t + 5])),
-                        fmaxf(__uint_as_float(sv[8 * t + 6]), __uint_as_float(sv[8 * t + 7])));
-        float* xs = xmax + (g & 1) * 256;
-        xs[h * 128 + r] = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-        named_bar_sync(1 + qd, 64);
-        const float mx = fmaxf(xs[r], xs[128 + r]);
-        const float m_tile = mx * sl2;
-        const bool need = m_tile > m_ref + kRescaleThreshold;
-        const float m_new = need ? m_tile : m_ref;
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
-          // rescale this half of O and its sum column: wait for P_{g-1} [V|1], then scale row-wise
-          if (!mbar_wait(smem_u32(o_done), (g - 1) & 1, 232, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;
-          uint32_t oa[32];
-          tmem_ld32(o_addr + 32 * h, oa);
-          tmem_wait_ld();
-#pragma unroll
-          for (int d = 0; d < 32; ++d) oa[d] = __float_as_uint(__uint_as_float(oa[d]) * alpha);
-          tmem_st32(o_addr + 32 * h, oa);
-          if (h == 0) {
-            uint32_t ol[16];
-            tmem_ld16(o_addr + 64, ol);
-            tmem_wait_ld();
-#pragma unroll
-            for (int d = 0; d < 16; ++d) ol[d] = __float_as_uint(__uint_as_float(ol[d]) * alpha);
-            tmem_st16(o_addr + 64, ol);
-          }
-          tmem_wait_st();
-        }
-        m_ref = m_new;
-        const float mo = m_ref == -INFINITY ? 0.f : m_ref;
-        uint32_t pw[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c)
-          pw[c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(sv[2 * c]), sl2, -mo)),
-                              ex2_approx(fmaf(__uint_as_float(sv[2 * c + 1]), sl2, -mo)));
-        // P_g (this warp's 32 keys = 16 columns of the row) -> TMEM, last read by P.V of tile g-1
-        if (g >= 1 && !mbar_wait(smem_u32(o_done), (g - 1) & 1, 233, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        tmem_st16(lane_base + kTcColP + 16 * h, pw);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(p_full));
-      }
-      if (!ok) break;
-      // item complete: this warp's 32 output columns and the row sum -> normalised bf16
-      if (!mbar_wait(smem_u32(o_done), (g - 1) & 1, 234, abort_flag)) break;
+    // An item's output is read from TMEM after the next item's first tile: by
+    // then its last P.V has long finished (o_final), so that wait is off the
+    // critical path.  The pending item's O buffer is not written again before
+    // that read (its next user is two items later and waits for o_empty).
+    bool pend = false;
+    int p_i = 0, p_row = 0;
+    long p_out = 0;
+    auto epilogue = [&]() -> bool {
+      if (!mbar_wait(smem_u32(&o_final[p_i & 1]), (p_i >> 1) & 1, 234, abort_flag)) return false;
       tc_fence_after();
-      uint32_t oa[32], ol[16];
-      tmem_ld32(o_addr + 32 * h, oa);
-      tmem_ld16(o_addr + 64, ol);
+      const uint32_t po = lane_base + kTcColO + (p_i & 1) * kTcOCols;
+      // two 32-column halves, then the row sum (column 64); O is released after the last read
+      uint32_t oa[32];
+      const uint32_t lsum = tmem_ld1(po + 64);
+      tmem_ld32(po, oa);
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&o_empty[i & 1]));
-      if (qa < a.L) {
-        const float l = __uint_as_float(ol[0]);
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        bf16* orow = out + (long)(a.base + qa) * 1024 + a.head * 64 + 32 * h;
+      const float l = __uint_as_float(lsum);
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      bf16* orow = out + p_out;
+      if (p_row) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint4 u;
@@ -389,7 +375,128 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           *reinterpret_cast<uint4*>(orow + 8 * c) = u;
         }
       }
+      tmem_ld32(po + 32, oa);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&o_empty[p_i & 1]));
+      if (p_row) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint4 u;
+          u.x = pack_bf16x2(__uint_as_float(oa[8 * c]) * inv, __uint_as_float(oa[8 * c + 1]) * inv);
+          u.y = pack_bf16x2(__uint_as_float(oa[8 * c + 2]) * inv, __uint_as_float(oa[8 * c + 3]) * inv);
+          u.z = pack_bf16x2(__uint_as_float(oa[8 * c + 4]) * inv, __uint_as_float(oa[8 * c + 5]) * inv);
+          u.w = pack_bf16x2(__uint_as_float(oa[8 * c + 6]) * inv, __uint_as_float(oa[8 * c + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + 32 + 8 * c) = u;
+        }
+      }
+      pend = false;
+      return true;
+    };
+    ItemFeed feed;
+    for (bool have = feed.init(cu, tiles, chunk, n_items, blockIdx.x, gridDim.x); have && ok;
+         have = feed.advance(), ++i) {
+      const AttnItem a = feed.cur;
+      const int qa = a.q0 + r;
+      const int lim = chunk > 0 ? min(a.L, (qa / chunk + 1) * chunk) : a.L;  // visible keys [0, lim)
+      const int wlim = __reduce_max_sync(0xffffffffu, lim);                    // any row of this warp
+      const uint32_t o_addr = lane_base + kTcColO + (i & 1) * kTcOCols;
+      float m_ref = -INFINITY;
+      for (int j = 0; j < a.n_kv; ++j, ++g) {
+        if (!mbar_wait(smem_u32(s_full), g & 1, 231, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const int k0 = j * kTcKv;
+        const bool hi = wlim > k0 + 32;  // warp-uniform: keys k0+32.. visible to some row
+        uint32_t s0[32], s1[32];
+        tmem_ld32(lane_base, s0);
+        if (hi) tmem_ld32(lane_base + 32, s1);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(s_empty));
+        const int nvis = lim - k0;
+        if (nvis < 64) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (c >= nvis) s0[c] = __float_as_uint(-INFINITY);
+          if (hi) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (c + 32 >= nvis) s1[c] = __float_as_uint(-INFINITY);
+          }
+        }
+        float m4[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          m4[t] = fmax3(fmax3(__uint_as_float(s0[8 * t]), __uint_as_float(s0[8 * t + 1]), __uint_as_float(s0[8 * t + 2])),
+                        fmax3(__uint_as_float(s0[8 * t + 3]), __uint_as_float(s0[8 * t + 4]), __uint_as_float(s0[8 * t + 5])),
+                        fmaxf(__uint_as_float(s0[8 * t + 6]), __uint_as_float(s0[8 * t + 7])));
+        if (hi) {
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            m4[t] = fmax3(m4[t],
+                          fmax3(__uint_as_float(s1[8 * t]), __uint_as_float(s1[8 * t + 1]), __uint_as_float(s1[8 * t + 2])),
+                          fmax3(fmax3(__uint_as_float(s1[8 * t + 3]), __uint_as_float(s1[8 * t + 4]),
+                                      __uint_as_float(s1[8 * t + 5])),
+                                __uint_as_float(s1[8 * t + 6]), __uint_as_float(s1[8 * t + 7])));
+        }
+        const float m_tile = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+        const bool need = m_tile > m_ref + kRescaleThreshold;
+        const float m_new = need ? m_tile : m_ref;
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // rescale this row of O and its sum column: wait for P_{g-1} [V|1], then scale
+          if (!mbar_wait(smem_u32(o_done), (g - 1) & 1, 232, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;
+          // O columns 0..63 in two pieces, then the sum column (rare path: one buffer)
+#pragma unroll 1
+          for (int piece = 0; piece < 2; ++piece) {
+            uint32_t oa[32];
+            tmem_ld32(o_addr + 32 * piece, oa);
+            tmem_wait_ld();
+#pragma unroll
+            for (int d = 0; d < 32; ++d) oa[d] = __float_as_uint(__uint_as_float(oa[d]) * alpha);
+            tmem_st32(o_addr + 32 * piece, oa);
+          }
+          const uint32_t lsum = tmem_ld1(o_addr + 64);
+          tmem_wait_ld();
+          tmem_st1(o_addr + 64, __float_as_uint(__uint_as_float(lsum) * alpha));
+          tmem_wait_st();
+        }
+        m_ref = m_new;
+        const float mo = m_ref == -INFINITY ? 0.f : m_ref;
+        uint32_t pw[32];  // P_g of this row: 64 keys as bf16 pairs
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          pw[c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(s0[2 * c]), sl2, -mo)),
+                              ex2_approx(fmaf(__uint_as_float(s0[2 * c + 1]), sl2, -mo)));
+        if (hi) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            pw[16 + c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(s1[2 * c]), sl2, -mo)),
+                                     ex2_approx(fmaf(__uint_as_float(s1[2 * c + 1]), sl2, -mo)));
+        } else {
+#pragma unroll
+          for (int c = 16; c < 32; ++c) pw[c] = 0u;
+        }
+        // P_g -> TMEM; its columns were last read by P.V of tile g-1
+        if (g >= 1 && !mbar_wait(smem_u32(o_done), (g - 1) & 1, 233, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        tmem_st32(lane_base + kTcColP, pw);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(p_full));
+        if (pend && !epilogue()) { ok = false; break; }
+      }
+      if (!ok) break;
+      pend = true;
+      p_i = i;
+      p_row = qa < a.L;
+      p_out = (long)(a.base + qa) * 1024 + a.head * 64;
     }
+    if (ok && pend) epilogue();
   }
   tc_fence_before();
   __syncthreads();

@@ -261,6 +261,16 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
 }
 
 // 32 TMEM lanes x 16 consecutive 32-bit columns -> 16 registers per thread.
+// 1 register per thread -> 32 TMEM lanes x 1 column.
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+}
+// 32 TMEM lanes x 1 column -> 1 register per thread.
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr) : "memory");
+  return r;
+}
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "

@@ -200,6 +200,12 @@ struct TcGemmArgs {
   int num_kb;      // k-blocks of 64
   int m_blocks;
   int n_blocks;
+  // pair kernel: tiles [0, full_tiles) are 256 x 256; the remaining m_blocks*n_blocks
+  // - full_tiles tiles (the last, partial wave) are each split into `split` (1 or 2)
+  // pieces of 256 x (256/split), spread over more CTA pairs; num_tiles counts pieces
+  int full_tiles;
+  int split;
+  int num_tiles;
   int conv;        // implicit-conv A addressing
   int tma_out;     // 0: direct stores; 1: TMA store of act/f32 tiles; 2: TMA reduce-add into f32 h
   EpiParams epi;
@@ -265,15 +271,22 @@ __device__ __forceinline__ void epi_bf16_half(const EpiParams& P, uint32_t (&r)[
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = silu(v[j]);
   } else if (P.epi == EPI_ROPE && col0 < 2048 && (col0 & 1023) < 64) {
-    const int i0 = (col0 & 1023) >> 1;  // first rotary pair of this 32-column piece
-    const float* cs = P.rope_cos + (long)pos * 32 + i0;
-    const float* sn = P.rope_sin + (long)pos * 32 + i0;
+    const int i0 = (col0 & 1023) >> 1;  // first rotary pair of this 32-column piece (0 or 16)
+    // 16 consecutive table entries per row, 64-byte aligned: four 16-byte loads each
+    const float4* cs = reinterpret_cast<const float4*>(P.rope_cos + (long)pos * 32 + i0);
+    const float4* sn = reinterpret_cast<const float4*>(P.rope_sin + (long)pos * 32 + i0);
+    float cv[16], sv[16];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4 c4 = __ldg(cs + k), s4 = __ldg(sn + k);
+      cv[4 * k] = c4.x; cv[4 * k + 1] = c4.y; cv[4 * k + 2] = c4.z; cv[4 * k + 3] = c4.w;
+      sv[4 * k] = s4.x; sv[4 * k + 1] = s4.y; sv[4 * k + 2] = s4.z; sv[4 * k + 3] = s4.w;
+    }
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float cv = __ldg(cs + i), sv = __ldg(sn + i);
       const float a = v[2 * i], b = v[2 * i + 1];
-      v[2 * i] = a * cv - b * sv;
-      v[2 * i + 1] = b * cv + a * sv;
+      v[2 * i] = a * cv[i] - b * sv[i];
+      v[2 * i + 1] = b * cv[i] + a * sv[i];
     }
   }
 #pragma unroll
@@ -608,13 +621,34 @@ struct TcPairCfg {
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
 };
 
-template <typename Tact>
+// Tile `v` of the pair kernel: output rows m_blk*256.., columns n0..n0+nt-1.
+struct PairTile {
+  int m_blk, n0, nt;
+};
+template <bool SPLIT>
+__device__ __forceinline__ PairTile pair_tile(const TcGemmArgs& a, int v) {
+  PairTile t;
+  int f = v, part = 0;
+  t.nt = 256;
+  if (SPLIT && v >= a.full_tiles) {
+    const int u = v - a.full_tiles;
+    f = a.full_tiles + u / a.split;
+    part = u - (u / a.split) * a.split;
+    t.nt = 256 / a.split;
+  }
+  t.m_blk = f / a.n_blocks;
+  t.n0 = (f - t.m_blk * a.n_blocks) * 256 + part * t.nt;
+  return t;
+}
+
+// SPLIT: the launch splits its last wave's tiles (pieces of 256 x 128 or 256 x 64).
+template <typename Tact, bool SPLIT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmC, const TcGemmArgs args) {
+                        const __grid_constant__ CUtensorMap tmB64, const __grid_constant__ CUtensorMap tmC,
+                        const TcGemmArgs args) {
   using Cfg = TcPairCfg;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr int HALF = Cfg::HALF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* staging = smem + STAGES * Cfg::STAGE_BYTES;
@@ -646,6 +680,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (SPLIT) tma_prefetch_desc(&tmB64);
     if (args.tma_out) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
@@ -663,8 +698,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
 
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
-  const int num_tiles = args.m_blocks * args.n_blocks;  // 256 x 256 tiles
+  const int num_tiles = args.num_tiles;  // 256 x 256 tiles, then the split pieces of the last wave
   const uint32_t smem_base = smem_u32(smem);
+  // B rows per CTA (nt / 2) for a piece of width nt, through the map whose box has that height
+  auto b_map = [&](int nt) -> const CUtensorMap* { return (!SPLIT || nt == 256) ? &tmB : &tmB64; };
+  auto stage_bytes = [&](int nt) -> uint32_t { return SPLIT ? Cfg::A_BYTES + (nt / 2) * Cfg::BK * 2 : Cfg::STAGE_BYTES; };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -676,20 +714,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
       // weight (B) stages of the first tile before waiting for the previous kernel
       int pre = 0;
       if (pair < num_tiles) {
-        const int n_blk0 = pair % args.n_blocks;
+        const PairTile t0 = pair_tile<SPLIT>(args, pair);
         pre = min(STAGES, args.num_kb);
         for (int kb = 0; kb < pre; ++kb) {
           const uint32_t fb = smem_u32(&full[kb]);
-          if (leader) mbar_arrive_expect_tx(fb, 2 * Cfg::STAGE_BYTES);
-          tma_load_2d_pair(smem_base + kb * Cfg::STAGE_BYTES + Cfg::A_BYTES, &tmB, to_leader(fb), kb * 64,
-                           n_blk0 * 256 + rank * 128);
+          if (leader) mbar_arrive_expect_tx(fb, 2 * stage_bytes(t0.nt));
+          tma_load_2d_pair(smem_base + kb * Cfg::STAGE_BYTES + Cfg::A_BYTES, b_map(t0.nt), to_leader(fb), kb * 64,
+                           t0.n0 + rank * (t0.nt / 2));
         }
       }
       griddep_wait();
       griddep_launch();
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        const int m_blk = tile / args.n_blocks;
-        const int n_blk = tile - m_blk * args.n_blocks;
+        const PairTile pt = pair_tile<SPLIT>(args, tile);
         for (int kb = 0; kb < args.num_kb; ++kb) {
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, 121, abort_flag)) {
             ok = false;
@@ -698,9 +735,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
           const uint32_t sa = smem_base + stage * Cfg::STAGE_BYTES;
           const uint32_t sb = sa + Cfg::A_BYTES;
           const uint32_t fb = smem_u32(&full[stage]);
-          if (leader && issued >= pre) mbar_arrive_expect_tx(fb, 2 * Cfg::STAGE_BYTES);
-          tma_load_2d_pair(sa, &tmA, to_leader(fb), kb * 64, m_blk * 256 + rank * 128);
-          if (issued >= pre) tma_load_2d_pair(sb, &tmB, to_leader(fb), kb * 64, n_blk * 256 + rank * 128);
+          if (leader && issued >= pre) mbar_arrive_expect_tx(fb, 2 * stage_bytes(pt.nt));
+          tma_load_2d_pair(sa, &tmA, to_leader(fb), kb * 64, pt.m_blk * 256 + rank * 128);
+          if (issued >= pre) tma_load_2d_pair(sb, b_map(pt.nt), to_leader(fb), kb * 64, pt.n0 + rank * (pt.nt / 2));
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -725,13 +762,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---------------- MMA issuer (leader only)
-      constexpr uint32_t idesc = idesc_bf16_f32(256, 256, false, false);
+      constexpr uint32_t idesc256 = idesc_bf16_f32(256, 256, false, false);
+      constexpr uint32_t idesc128 = idesc_bf16_f32(256, 128, false, false);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const int nt = pair_tile<SPLIT>(args, tile).nt;
+        const uint32_t idesc = (!SPLIT || nt == 256) ? idesc256 : idesc128;
         if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, 123, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * 256;
@@ -767,20 +807,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
     // ---------------- epilogue warps 2..9 (both CTAs): this CTA's 128 rows of each tile
     const int ew = warp - 2;
     const int q = warp & 3;
-    const int col_begin = (ew >> 2) * HALF;
     uint8_t* stage_buf = staging + ew * 8192;
     int sbuf = 0;
-    const EpiParams& P = args.epi;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs) {
-      const int m_blk = tile / args.n_blocks;
-      const int n_blk = tile - m_blk * args.n_blocks;
-      const int n0 = n_blk * 256 + col_begin;
+      const PairTile pt = pair_tile<SPLIT>(args, tile);
+      // the two warps of a TMEM lane quarter split the tile's columns
+      const int width = pt.nt / 2;
+      const int col_begin = (ew >> 2) * width;
       if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, 126, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256 + col_begin;
-      epilogue_slab<HALF, Tact>(args, &tmC, taddr, m_blk * 256 + rank * 128, q, lane, n0, stage_buf, sbuf);
+      if (!SPLIT || width == 128)
+        epilogue_slab<128, Tact>(args, &tmC, taddr, pt.m_blk * 256 + rank * 128, q, lane, pt.n0 + col_begin,
+                                 stage_buf, sbuf);
+      else
+        epilogue_slab<64, Tact>(args, &tmC, taddr, pt.m_blk * 256 + rank * 128, q, lane, pt.n0 + col_begin,
+                                stage_buf, sbuf);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(to_leader(smem_u32(&tempty[acc])));

@@ -150,7 +150,8 @@ def _close(out, ref, dtype):
 @pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
 @pytest.mark.parametrize("M,N,K", [(1, 3072, 1024), (129, 1024, 1024), (300, 2048, 1024),
                                    (257, 1024, 2048), (1000, 80, 1024), (200, 1024, 320),
-                                   (6000, 1024, 1024), (40000, 1024, 1024), (16, 137216, 1024)])
+                                   (6000, 1024, 1024), (40000, 1024, 1024), (16, 137216, 1024),
+                                   (6578, 3072, 1024)])
 def test_gemm_bias(dtype, M, N, K):
     ops = _ops()
     dt = getattr(torch, dtype)
@@ -195,13 +196,15 @@ def test_gemm_rope_epilogue(dtype):
     _close(out, torch.tensor(ref, device=DEV), dt)
 
 
-@pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
-def test_gemm_gate_residual_epilogue(dtype):
+@pytest.mark.parametrize("dtype,lengths", [("bfloat16", [64, 200, 1]), ("float32", [64, 200, 1]),
+                                           ("bfloat16", [3000, 1, 3577])])
+def test_gemm_gate_residual_epilogue(dtype, lengths):
+    """Gated residual into fp32 h; the 6578-row case runs several full waves of
+    256 x 256 tiles and splits the last wave's tiles into 256 x 128 pieces."""
     from fcv_b200 import _lib as L
 
     ops = _ops()
     dt = getattr(torch, dtype)
-    lengths = [64, 200, 1]
     N = sum(lengths)
     A, W, b = _gemm_inputs(N, 1024, 2048, dt, 3)
     doc = torch.tensor(np.repeat(np.arange(3), lengths).astype(np.int32), device=DEV)
