@@ -349,10 +349,37 @@ int launch_tc_pair(const GemmCall& g, cudaStream_t s) {
   return FCV_OK;
 }
 
+// Causal grouped convolution (bf16): A = gapped buffer (a_rows x 1024, 160-row
+// windows), B = (1024, 31*64) weights, one 64-channel group per tile column.
+template <typename Tact>
+int launch_conv(const GemmCall& g, cudaStream_t s) {
+  using Cfg = ConvCfg;
+  CUtensorMap ta, tb;
+  FCV_TRY(make_tmap_bf16(&ta, g.A, g.a_rows, 1024, g.lda, Cfg::A_ROWS));
+  FCV_TRY(make_tmap_bf16(&tb, g.W, g.N, g.K, g.K, 64));
+  TcGemmArgs args{};
+  args.num_kb = Cfg::TAPS;
+  args.m_blocks = (g.M + 127) / 128;
+  args.n_blocks = g.N / 64;
+  args.conv = 1;
+  args.epi = g.epi;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    FCV_CUDA(cudaFuncSetAttribute(tc_conv_kernel<Tact>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    attr_set[dev & 63] = true;
+  }
+  const int tiles = args.m_blocks * args.n_blocks;
+  FCV_LAUNCH("tc_conv_kernel", tc_conv_kernel<Tact>, dim3(std::min(tiles, num_sms())), dim3(Cfg::THREADS),
+             Cfg::SMEM_BYTES, s, ta, tb, args);
+  return FCV_OK;
+}
+
 int run_gemm(const GemmCall& g, int dtype, cudaStream_t s, int force_bn = 0) {
   if (g.M <= 0 || g.N <= 0) return FCV_OK;
   if (dtype == FCV_DTYPE_BF16) {
-    if (g.conv) return launch_tc<64, bf16>(g, s);
+    if (g.conv) return launch_conv<bf16>(g, s);
     if (g.K % 64 != 0) return fail(FCV_EUNSUPPORTED, "bf16 GEMM needs K %% 64 == 0 (K=%d)", g.K);
     if (force_bn == 0 && g.N >= 256) return launch_tc_pair<bf16>(g, s);
     int bn = force_bn;

@@ -320,6 +320,14 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
   return d;
 }
 
+// The matrix that starts `row` 128-byte rows into a 128B-swizzled tile written by
+// TMA.  Both TMA and the MMA apply the swizzle to absolute shared-memory address
+// bits, so moving the start address by whole rows is enough (base offset 0;
+// checked bit-exact against per-tap TMA loads of the shifted rows on B200).
+__device__ __forceinline__ uint64_t sdesc_sw128_row(uint32_t tile_base, int row) {
+  return sdesc_sw128(tile_base + static_cast<uint32_t>(row) * 128u);
+}
+
 // Instruction descriptor: kind::f16, A = B = bf16, D = f32, dense.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_major,
                                                       bool b_mn_major) {

@@ -143,8 +143,28 @@ __device__ __forceinline__ void epilogue_apply(const EpiParams& p, int row, int 
       if (pr < 0) return;
       const Tact* r = reinterpret_cast<const Tact*>(p.res) + (long)row * 1024 + col0;
       float* h = reinterpret_cast<float*>(p.C) + (long)pr * p.ldc + col0;
+      if constexpr (sizeof(Tact) == 2 && W % 8 == 0) {
+        // 16-byte residual loads and stores (rows of 1024, col0 a multiple of W)
 #pragma unroll
-      for (int j = 0; j < W; ++j) h[j] = mish(v[j]) + to_f<Tact>(r[j]);
+        for (int j = 0; j < W; j += 8) {
+          const uint4 u = *reinterpret_cast<const uint4*>(r + j);
+          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+          float rr[8];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[k]));
+            rr[2 * k] = f.x;
+            rr[2 * k + 1] = f.y;
+          }
+          *reinterpret_cast<float4*>(h + j) = make_float4(mish(v[j]) + rr[0], mish(v[j + 1]) + rr[1],
+                                                          mish(v[j + 2]) + rr[2], mish(v[j + 3]) + rr[3]);
+          *reinterpret_cast<float4*>(h + j + 4) = make_float4(mish(v[j + 4]) + rr[4], mish(v[j + 5]) + rr[5],
+                                                              mish(v[j + 6]) + rr[6], mish(v[j + 7]) + rr[7]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < W; ++j) h[j] = mish(v[j]) + to_f<Tact>(r[j]);
+      }
       return;
     }
     case EPI_UNPACK: {
@@ -841,6 +861,227 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TcPairCfg::THREADS, 
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ============================================================== tcgen05 causal grouped convolution
+// Implicit GEMM of the grouped causal convolutions of the input embedding
+// (CausalConvPositionEmbedding, kernel 31, 16 groups of 64 channels;
+// flashinfer_dit.py:615-654) on the gapped buffer: for group n,
+//   out[g, n*64 + c] = bias + sum_t sum_i A[g + t - 30, n*64 + i] * W[n*64 + c, t*64 + i].
+// The 128 output rows of a tile need input rows g0-30 .. g0+127; they are loaded
+// ONCE (160 rows, TMA zero-fills rows before the buffer) and tap t is the MMA on
+// rows t .. t+127 of that tile (descriptor moved by t rows).  The group's
+// weights stream through a ring of stages of 4 taps (4 x 64 x 64), so the MMA
+// thread waits and commits once per 16 MMAs.
+// Persistent, one CTA per SM: warp 0 TMA, warp 1 MMA, warps 2-9 epilogue, two
+// per TMEM lane quarter with 32 columns each (direct stores through
+// epilogue_apply: Mish into the gapped buffer, or Mish plus residual into the
+// packed fp32 stream).
+struct ConvCfg {
+  static constexpr int A_ROWS = 160;
+  static constexpr int A_BYTES = A_ROWS * 128;  // 20 KB, a multiple of 1024
+  static constexpr int B_BYTES = 64 * 128;      // one tap of one group
+  static constexpr int UNIT_TAPS = 4;           // taps per ring stage
+  static constexpr int UNIT_BYTES = UNIT_TAPS * B_BYTES;
+  static constexpr int B_STAGES = 4;
+  static constexpr int TAPS = 31;
+  static constexpr int UNITS = (TAPS + UNIT_TAPS - 1) / UNIT_TAPS;  // 8 per tile, the last with 3 taps
+  static constexpr int THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+  static constexpr int OFF_B = 2 * A_BYTES;
+  static constexpr int OFF_BAR = OFF_B + B_STAGES * UNIT_BYTES;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SMEM_BYTES = 1024 + OFF_BAR + BAR_BYTES;
+  static constexpr int TMEM_COLS = 128;  // two 64-column accumulators
+  static constexpr int EPI_WARPS = 8;
+};
+static_assert((2 + 2 + 2 * ConvCfg::B_STAGES + 2 + 2 + 1) * 8 + 8 <= ConvCfg::BAR_BYTES, "conv barrier area");
+
+template <typename Tact>
+__global__ void __launch_bounds__(ConvCfg::THREADS, 1)
+    tc_conv_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const TcGemmArgs args) {
+  using Cfg = ConvCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t s0 = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
+  uint64_t* a_full = bars;                      // [2]
+  uint64_t* a_empty = bars + 2;                 // [2]
+  uint64_t* b_full = bars + 4;                  // [B_STAGES]
+  uint64_t* b_empty = b_full + Cfg::B_STAGES;   // [B_STAGES]
+  uint64_t* tfull = b_empty + Cfg::B_STAGES;    // [2]
+  uint64_t* tempty = tfull + 2;                 // [2]
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&a_full[i]), 1);
+      mbar_init(smem_u32(&a_empty[i]), 1);
+      mbar_init(smem_u32(&tfull[i]), 1);
+      mbar_init(smem_u32(&tempty[i]), Cfg::EPI_WARPS);
+    }
+    for (int i = 0; i < Cfg::B_STAGES; ++i) {
+      mbar_init(smem_u32(&b_full[i]), 1);
+      mbar_init(smem_u32(&b_empty[i]), 1);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x != 0) {  // thread 0 (the producer) waits after its weight prefetch
+    griddep_wait();
+    griddep_launch();
+  }
+  const int n_groups = args.n_blocks;
+  const int num_tiles = args.m_blocks * n_groups;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      long bi = 0;  // weight stages in ring order
+      long b_issued = 0;
+      int ti = 0, a_issued = 0;
+      bool ok = true;
+      auto load_unit = [&](int st, int u, int grp) {
+        const int taps = min(Cfg::UNIT_TAPS, Cfg::TAPS - u * Cfg::UNIT_TAPS);
+        const uint32_t fb = smem_u32(&b_full[st]);
+        mbar_arrive_expect_tx(fb, taps * Cfg::B_BYTES);
+        for (int j = 0; j < taps; ++j)
+          tma_load_2d(s0 + Cfg::OFF_B + st * Cfg::UNIT_BYTES + j * Cfg::B_BYTES, &tmB, fb,
+                      (u * Cfg::UNIT_TAPS + j) * 64, grp * 64);
+      };
+      int pre = 0;
+      if (static_cast<int>(blockIdx.x) < num_tiles) {
+        pre = Cfg::B_STAGES < Cfg::UNITS ? Cfg::B_STAGES : Cfg::UNITS;
+        for (int u = 0; u < pre; ++u) load_unit(u, u, blockIdx.x % n_groups);
+        b_issued = pre;
+      }
+      griddep_wait();
+      griddep_launch();
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++ti) {
+        const int m_blk = tile / n_groups;
+        const int grp = tile - m_blk * n_groups;
+        const int ab = ti & 1;
+        if (!mbar_wait(smem_u32(&a_empty[ab]), ((ti >> 1) & 1) ^ 1, 141, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(smem_u32(&a_full[ab]), Cfg::A_BYTES);
+        tma_load_2d(s0 + ab * Cfg::A_BYTES, &tmA, smem_u32(&a_full[ab]), grp * 64, m_blk * 128 - kConvPad);
+        ++a_issued;
+        for (int u = 0; u < Cfg::UNITS; ++u, ++bi) {
+          if (bi < pre) continue;  // loaded before the wait on the previous kernel
+          const int st = static_cast<int>(bi % Cfg::B_STAGES);
+          if (!mbar_wait(smem_u32(&b_empty[st]), ((bi / Cfg::B_STAGES) & 1) ^ 1, 142, abort_flag)) {
+            ok = false;
+            break;
+          }
+          load_unit(st, u, grp);
+          ++b_issued;
+        }
+      }
+      if (!ok) {
+        // let the copies that may still be in flight land before the CTA exits
+        for (long k = (b_issued > Cfg::B_STAGES ? b_issued - Cfg::B_STAGES : 0); k < b_issued; ++k)
+          mbar_wait(smem_u32(&b_full[k % Cfg::B_STAGES]), (k / Cfg::B_STAGES) & 1, 147, nullptr);
+        for (int k = (a_issued > 2 ? a_issued - 2 : 0); k < a_issued; ++k)
+          mbar_wait(smem_u32(&a_full[k & 1]), (k >> 1) & 1, 148, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer: 31 taps of 4 K-steps per tile
+      constexpr uint32_t idesc = idesc_bf16_f32(128, 64, false, false);
+      long bi = 0;
+      int ti = 0, acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++ti) {
+        const int ab = ti & 1;
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, 143, abort_flag)) break;
+        if (!mbar_wait(smem_u32(&a_full[ab]), (ti >> 1) & 1, 144, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * 64;
+        const uint32_t sa = s0 + ab * Cfg::A_BYTES;
+        for (int u = 0; u < Cfg::UNITS; ++u, ++bi) {
+          const int st = static_cast<int>(bi % Cfg::B_STAGES);
+          if (!mbar_wait(smem_u32(&b_full[st]), (bi / Cfg::B_STAGES) & 1, 145, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int taps = min(Cfg::UNIT_TAPS, Cfg::TAPS - u * Cfg::UNIT_TAPS);
+          for (int j = 0; j < taps; ++j) {
+            const int tap = u * Cfg::UNIT_TAPS + j;
+            const uint64_t da = sdesc_sw128_row(sa, tap);
+            const uint64_t db = sdesc_sw128(s0 + Cfg::OFF_B + st * Cfg::UNIT_BYTES + j * Cfg::B_BYTES);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) umma_bf16(d_tmem, da + 2 * k, db + 2 * k, idesc, (tap | k) != 0);
+          }
+          umma_commit(smem_u32(&b_empty[st]));
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&tfull[acc]));
+        umma_commit(smem_u32(&a_empty[ab]));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      umma_commit(smem_u32(drain));
+      mbar_wait(smem_u32(drain), 0, 146, nullptr);
+    }
+  } else {
+    // ---------------- epilogue warps 2..9: lane quarter q, 32 columns (half ch) of the tile
+    const int q = warp & 3;
+    const int ch = (warp - 2) >> 2;
+    const EpiParams& P = args.epi;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m_blk = tile / n_groups;
+      const int grp = tile - m_blk * n_groups;
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, 149, abort_flag)) break;
+      tc_fence_after();
+      const int row = m_blk * 128 + q * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 64 + ch * 32;
+      {
+        uint32_t r[32];
+        tmem_ld32(taddr, r);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        epilogue_apply<Tact, 32>(P, row, grp * 64 + ch * 32, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 

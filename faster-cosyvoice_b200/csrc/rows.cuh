@@ -344,15 +344,19 @@ __global__ void __launch_bounds__(256) embed_gather_kernel(const T* __restrict__
   const int p0 = blockIdx.x * 32;
   const int L = cu[b + 1] - cu[b];
   if (p0 >= L) return;
-  for (int i = threadIdx.x; i < 240 * 32; i += blockDim.x) {
-    const int c = i >> 5, pp = i & 31;
+  {
+    // warp w reads channels w, w + 8, ... at positions p0 + lane: all 30 loads in flight
+    const int w = threadIdx.x >> 5, pp = threadIdx.x & 31;
     const int p = p0 + pp;
-    float v = 0.f;
-    if (p < L) {
+    float v[30];
+#pragma unroll
+    for (int k = 0; k < 30; ++k) {
+      const int c = w + 8 * k;
       const T* src = c < 80 ? x : (c < 160 ? cond : mu);
-      v = to_f<T>(src[((long)b * 80 + (c % 80)) * T_ + p]);
+      v[k] = p < L ? to_f<T>(src[((long)b * 80 + (c % 80)) * T_ + p]) : 0.f;
     }
-    tile[c][pp] = v;
+#pragma unroll
+    for (int k = 0; k < 30; ++k) tile[w + 8 * k][pp] = v[k];
   }
   __syncthreads();
   const long row0 = cu[b] + p0;
