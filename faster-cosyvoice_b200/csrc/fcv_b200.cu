@@ -381,7 +381,10 @@ int run_gemm(const GemmCall& g, int dtype, cudaStream_t s, int force_bn = 0) {
   if (dtype == FCV_DTYPE_BF16) {
     if (g.conv) return launch_conv<bf16>(g, s);
     if (g.K % 64 != 0) return fail(FCV_EUNSUPPORTED, "bf16 GEMM needs K %% 64 == 0 (K=%d)", g.K);
-    if (force_bn == 0 && g.N >= 256) return launch_tc_pair<bf16>(g, s);
+    // CTA pairs (256-row tiles) once there are rows to fill them; a GEMM of at most
+    // 128 rows (time MLP, AdaLN modulation) issues half the MMA work per output
+    // column on single-SM 128-row tiles and is bound by streaming its weights
+    if (force_bn == 0 && g.N >= 256 && g.M > 128) return launch_tc_pair<bf16>(g, s);
     int bn = force_bn;
     if (bn == 0) {
       const long mb = (g.M + 127) / 128;
@@ -577,8 +580,8 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     FCV_LAUNCH("embed_gather_kernel", embed_gather_kernel<T>, dim3(grid), dim3(256), 0, s, static_cast<const T*>(bt->x), static_cast<const T*>(bt->cond),
                                                 static_cast<const T*>(bt->mu), static_cast<const T*>(bt->spks),
                                                 bt->cu_seqlens, bt->T, static_cast<T*>(ws.a_in));
-    FCV_LAUNCH("zero_gap_rows_kernel", zero_gap_rows_kernel<T>, dim3((unsigned)G), dim3(128), 0, s, bt->gap_rows, (int)G, static_cast<T*>(ws.gap0),
-                                                       static_cast<T*>(ws.gap1));
+    FCV_LAUNCH("zero_gap_rows_kernel", zero_gap_rows_kernel<T>, dim3(30, B + 1), dim3(128), 0, s, bt->cu_seqlens,
+               static_cast<T*>(ws.gap0), static_cast<T*>(ws.gap1));
     GemmCall g{};
     g.A = ws.a_in; g.lda = 320; g.a_rows = N; g.W = w->in_w; g.M = N; g.N = 1024; g.K = 320;
     g.epi = make_epi(EPI_EMBED_GAP, N, 1024, ws.gap0, 1024, w->in_b);
@@ -662,11 +665,11 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   const float* mf = ws.mods + (long)depth * 6144;
   ProfScope ps_out(FCV_CAT_OUTPUT, s);
   FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mf + 1024, mf + 0, bt->doc_ids, MS, N, ws.norm, dtype, s));
-  const int zgrid = std::max(1, std::min(4096, (int)(((long)B * 80 * bt->T + 255) / 256)));
+  const dim3 zgrid(80, B);
   if (bt->out_f32)
-    FCV_LAUNCH("zero_padding_kernel", zero_padding_kernel<float>, dim3(zgrid), dim3(256), 0, s, bt->cu_seqlens, B, bt->T, static_cast<float*>(bt->out));
+    FCV_LAUNCH("zero_padding_kernel", zero_padding_kernel<float>, zgrid, dim3(128), 0, s, bt->cu_seqlens, B, bt->T, static_cast<float*>(bt->out));
   else
-    FCV_LAUNCH("zero_padding_kernel", zero_padding_kernel<T>, dim3(zgrid), dim3(256), 0, s, bt->cu_seqlens, B, bt->T, static_cast<T*>(bt->out));
+    FCV_LAUNCH("zero_padding_kernel", zero_padding_kernel<T>, zgrid, dim3(128), 0, s, bt->cu_seqlens, B, bt->T, static_cast<T*>(bt->out));
   GemmCall po{};
   po.A = ws.norm; po.lda = 1024; po.a_rows = N; po.M = N; po.N = 80; po.K = 1024; po.W = w->out_w;
   po.epi = make_epi(EPI_UNPACK, N, 80, bt->out, 0, w->out_b);

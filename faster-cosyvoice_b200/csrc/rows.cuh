@@ -105,15 +105,19 @@ __global__ void layout_fill_kernel(const int32_t* __restrict__ cu, int B, int T_
 
 // Zero the gap rows (gap_rows[g] < 0) of a gapped activation buffer.
 template <typename T>
-__global__ void zero_gap_rows_kernel(const int32_t* __restrict__ gap_rows, int G, T* __restrict__ buf0,
-                                     T* __restrict__ buf1) {
+// Zero the 30 gap rows in front of every document (segment d = 0..B-1) and after
+// the last one (d = B) of both gapped buffers: rows cu[d] + 30 d + r, r < 30.
+// Grid (30, B + 1), 128 threads x 8 elements = one 1024-wide row each.
+__global__ void zero_gap_rows_kernel(const int32_t* __restrict__ cu, T* __restrict__ buf0, T* __restrict__ buf1) {
   griddep_wait();
   griddep_launch();
-  const int g = blockIdx.x;
-  if (g >= G || gap_rows[g] >= 0) return;
-  for (int c = threadIdx.x; c < 1024; c += blockDim.x) {
-    buf0[(long)g * 1024 + c] = from_f<T>(0.f);
-    if (buf1) buf1[(long)g * 1024 + c] = from_f<T>(0.f);
+  const int d = blockIdx.y;
+  const long g = (long)cu[d] + 30L * d + blockIdx.x;
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  constexpr int kVec = 16 / sizeof(T);
+  for (int c = threadIdx.x * kVec; c < 1024; c += blockDim.x * kVec) {
+    *reinterpret_cast<uint4*>(buf0 + g * 1024 + c) = z;
+    if (buf1) *reinterpret_cast<uint4*>(buf1 + g * 1024 + c) = z;
   }
 }
 
@@ -390,17 +394,16 @@ __global__ void __launch_bounds__(128) time_sinusoid_kernel(const T* __restrict_
 }
 
 // ------------------------------------------------------------------ output
-// Zero the padding frames p >= L_b of a (B, 80, T) tensor.
+// Zero the padding frames p >= L_b of a (B, 80, T) tensor: block (c, b) clears
+// row (b, c) from L_b on.
 template <typename T>
 __global__ void zero_padding_kernel(const int32_t* __restrict__ cu, int B, int T_, T* __restrict__ out) {
   griddep_wait();
   griddep_launch();
-  const long total = (long)B * 80 * T_;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
-    const int p = static_cast<int>(i % T_);
-    const int b = static_cast<int>(i / ((long)80 * T_));
-    if (p >= cu[b + 1] - cu[b]) out[i] = from_f<T>(0.f);
-  }
+  const int b = blockIdx.y, c = blockIdx.x;
+  const int L = cu[b + 1] - cu[b];
+  T* row = out + ((long)b * 80 + c) * T_;
+  for (int p = L + threadIdx.x; p < T_; p += blockDim.x) row[p] = from_f<T>(0.f);
 }
 
 // out[b, c, p] = packed[cu[b] + p, c] for p < L_b (flashinfer_dit.py:536-543).
