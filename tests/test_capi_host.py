@@ -61,6 +61,21 @@ def test_version_and_error_paths_without_gpu(lib):
     assert lib.fcv_pack_layout(None, 0, 0, 0, None, None, None, None, None, None) == -1
 
 
+def test_alignment_rules_rejected_before_any_launch(lib):
+    """Operands read with 16-byte vector or bulk copies are checked on the host
+    (the pointers below are never dereferenced: the calls return first)."""
+    a16, odd = 0x10000, 0x10004
+    # LayerNorm-modulate streams h rows with 1-D bulk copies: h must be 16-byte aligned
+    rc = lib.fcv_ln_modulate(odd, 0, a16, a16, a16, 4096, 8, a16, 1, None)
+    assert rc == -1 and b"16-byte aligned" in lib.fcv_last_error()
+    # modulation rows are read as float4
+    rc = lib.fcv_ln_modulate(a16, 0, odd, a16, a16, 4096, 8, a16, 1, None)
+    assert rc == -1 and b"16-byte aligned" in lib.fcv_last_error()
+    # RoPE tables are read as float4 in the QKV epilogue
+    rc = lib.fcv_gemm(a16, a16, None, 8, 3072, 1024, 1, 2, a16, a16, None, 0, odd, a16, None)
+    assert rc == -1 and b"RoPE tables must be 16-byte aligned" in lib.fcv_last_error()
+
+
 def test_workspace_bytes_grows_with_rows(lib):
     a = lib.fcv_dit_workspace_bytes(1000, 4, 22, 1)
     b = lib.fcv_dit_workspace_bytes(2000, 4, 22, 1)
