@@ -236,14 +236,12 @@ template <int BN, typename Tact>
 int launch_tc(const GemmCall& g, cudaStream_t s) {
   using Cfg = TcGemmCfg<BN>;
   CUtensorMap ta, tb, tc;
-  const long a_cols = g.conv ? 1024 : g.K;
-  FCV_TRY(make_tmap_bf16(&ta, g.A, g.a_rows, a_cols, g.lda, 128));
+  FCV_TRY(make_tmap_bf16(&ta, g.A, g.a_rows, g.K, g.lda, 128));
   FCV_TRY(make_tmap_bf16(&tb, g.W, g.N, g.K, g.K, BN));
   TcGemmArgs args{};
-  args.num_kb = g.conv ? 31 : (g.K + 63) / 64;
+  args.num_kb = (g.K + 63) / 64;
   args.m_blocks = (g.M + 127) / 128;
   args.n_blocks = (g.N + BN - 1) / BN;
-  args.conv = g.conv;
   args.epi = g.epi;
   args.tma_out = choose_tma_out(g, BN);
   FCV_TRY(make_out_map(&tc, g, args.tma_out, ta));
@@ -265,7 +263,7 @@ int launch_tc(const GemmCall& g, cudaStream_t s) {
 // epilogue writes a plain row-major tile; direct per-thread stores otherwise.
 int choose_tma_out(const GemmCall& g, int bn) {
   const int e = g.epi.epi;
-  if (g.conv || bn < 128) return 0;
+  if (bn < 128) return 0;
   if ((e == EPI_BIAS || e == EPI_GELU || e == EPI_ROPE || e == EPI_SILU) && g.N % 64 == 0) return 1;
   if (e == EPI_F32 && g.epi.C2 == nullptr && g.N % 32 == 0) return 1;
   if (e == EPI_GATE_RES && g.N % 32 == 0) return 2;

@@ -226,7 +226,7 @@ struct TcGemmArgs {
   int full_tiles;
   int split;
   int num_tiles;
-  int conv;        // implicit-conv A addressing
+  int conv;        // tc_conv_kernel: set for the causal grouped convolution
   int tma_out;     // 0: direct stores; 1: TMA store of act/f32 tiles; 2: TMA reduce-add into f32 h
   EpiParams epi;
 };
@@ -503,15 +503,7 @@ __global__ void __launch_bounds__(TcGemmCfg<BN>::THREADS, 1)
           const uint32_t sb = sa + Cfg::A_BYTES;
           const uint32_t fb = smem_u32(&full[stage]);
           if (issued >= pre) mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
-          int ax, ay;
-          if (args.conv) {
-            ax = n_blk * 64;
-            ay = m_blk * 128 + kb - kConvPad;
-          } else {
-            ax = kb * 64;
-            ay = m_blk * 128;
-          }
-          tma_load_2d(sa, &tmA, fb, ax, ay);
+          tma_load_2d(sa, &tmA, fb, kb * 64, m_blk * 128);
           if (issued >= pre) tma_load_2d(sb, &tmB, fb, kb * 64, n_blk * BN);
           ++issued;
           if (++stage == STAGES) {
