@@ -16,6 +16,13 @@ instead shard one fixed request set across the ranks by LPT bins (strong).
 ``--impl reference`` times the reference's CPU path (the oracle port of its
 torch DiT, float32, all host threads) on a bounded sample of the same
 workload; under torchrun only rank 0 runs it.
+
+``--impl reference-gpu`` times the reference's own GPU estimator
+(``FlashInferDiT``: Triton row kernels, FlashInfer ragged prefill, cuBLAS; in
+float16 as ``apply_flashinfer`` deploys it, ``--ref-dtype bf16`` for bfloat16)
+on the same weights and inputs, when the reference has been installed offline
+into ``baseline/_ref``; otherwise it prints an ``unavailable`` line.  A
+comparison bar only: nothing of it is on the B200 path.
 """
 
 from __future__ import annotations
@@ -195,13 +202,111 @@ def cpu_oracle_rate(params, req_lengths, seed, budget_s: float):
 
 
 # ---------------------------------------------------------------------------- main
+def reference_gpu_arm(args, req_lengths, chunk, seed, cfg, strong):
+    """The reference's FlashInferDiT (flashinfer_dit.py:98-543, loaded as apply_flashinfer does at
+    :951-988) on the B200 with this run's weights and inputs; one JSON line."""
+    import torch
+
+    ref_root = os.path.join(ROOT, "baseline", "_ref")
+    base = {"metric": METRIC, "unit": UNIT, "impl": "reference-gpu", "config": cfg}
+    if not os.path.isdir(os.path.join(ref_root, "faster_cosyvoice")):
+        print(json.dumps({**base, "unavailable": "reference not installed in baseline/_ref"}), flush=True)
+        return
+    if not torch.cuda.is_available():
+        print(json.dumps({**base, "unavailable": "no CUDA device"}), flush=True)
+        return
+    # x-transformers==2.23.5 (the reference's RoPE dependency) is not installed: the RoPE tables come
+    # from the test shim that restates them (interleaved pairs, base 10000, rotary dim 64)
+    for p in (ref_root, os.path.join(ROOT, "tests", "golden", "_xt_shim")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    try:
+        from faster_cosyvoice.token2wav.flashinfer_dit import FlashInferDiT
+    except Exception as exc:  # missing flashinfer / triton on this box
+        print(json.dumps({**base, "unavailable": f"reference import failed: {type(exc).__name__}: {exc}"}),
+              flush=True)
+        return
+    from fcv_b200.model import B200DiT
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    rdt = torch.float16 if args.ref_dtype == "fp16" else torch.bfloat16
+    torch.manual_seed(seed)
+    sd = B200DiT(depth=22).eval().state_dict()
+    ref = FlashInferDiT(device=device, static_chunk_size=50)
+    missing, unexpected = ref.load_state_dict(sd, strict=False)
+    missing = [k for k in missing if "rope" not in k]
+    if missing or unexpected:
+        raise RuntimeError(f"state-dict mismatch: missing={missing}, unexpected={unexpected}")
+    ref = ref.to(device=device, dtype=rdt).eval()
+    ref.finalize_weights()
+    lengths, T, host, dev = make_batch(req_lengths, seed, device, rdt)
+    streaming = chunk > 0
+    N = sum(lengths)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step(inp):
+        with torch.inference_mode():
+            return ref(inp["x"], inp["mask"], inp["mu"], inp["t"], inp["spks"], inp["cond"], streaming=streaming)
+
+    for _ in range(args.warmup):
+        step(dev)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(0) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            step(dev)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    ms = float(np.mean(step_ms))
+
+    pin = {k: v.to(rdt).pin_memory() for k, v in host.items()}
+    dev2 = {k: torch.empty_like(v, device=device) for k, v in pin.items()}
+    out_h = torch.empty(len(lengths), 80, T, dtype=rdt).pin_memory()
+
+    def e2e_step():
+        for k in pin:
+            dev2[k].copy_(pin[k], non_blocking=True)
+        out_h.copy_(step(dev2), non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    line = {**base, "value": N / (ms / 1000.0), "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong" if strong else "weak",
+            "vs_baseline": None, "dtype": "f16" if rdt == torch.float16 else "bf16",
+            "data": "synthetic (seeded N(0,1) inputs, random-init weights of the 22-layer DiT)",
+            "e2e": {"value": N / (e2e_ms / 1000.0), "unit": UNIT,
+                    "h2d_bytes_per_step": int(sum(v.numel() * v.element_size() for v in pin.values())),
+                    "d2h_bytes_per_step": int(out_h.numel() * out_h.element_size()),
+                    "api": "FlashInferDiT.forward(x, mask, mu, t, spks, cond, streaming) with pinned host buffers"},
+            "step_ms_min": min(step_ms), "step_ms_median": float(statistics.median(step_ms)),
+            "clocks": clocks.summary(),
+            "note": "the reference's own GPU estimator path (packed Triton/FlashInfer path), "
+                    "L2 flushed between steps, device-resident inputs for value"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="2", choices=["2", "3", "4", "5"])
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-gpu"])
+    ap.add_argument("--ref-dtype", default="fp16", choices=["fp16", "bf16"],
+                    help="element type of the reference GPU estimator (--impl reference-gpu)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--requests", type=int, default=0,
                     help="use only the first R requests of the config (small cases for profiling)")
@@ -247,6 +352,11 @@ def main():
                 "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
                 "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
+        return
+
+    if args.impl == "reference-gpu":
+        if rank == 0:
+            reference_gpu_arm(args, req_lengths, chunk, seed, cfg, strong)
         return
 
     import torch

@@ -70,6 +70,42 @@ def test_bf16_matches_reference_within_1e2(name):
             assert e <= 1e-2, (name, streaming, b, e)
 
 
+@pytest.mark.parametrize("dtype,tol,modes", [("bfloat16", 1e-2, (False, True)), ("float32", 1e-5, (False,))])
+def test_long_documents_match_oracle(dtype, tol, modes):
+    """The gates at the benchmark's document lengths: two requests of 600 and
+    257 frames under CFG (second half with mu, spks and cond zeroed, as
+    flashinfer_flow.py:45-51 stacks them), 22 blocks, so every query tile sees
+    up to ten key tiles.  The oracle runs on the same bf16-rounded weights and
+    inputs; in bf16 mode with the reference's bf16 time-argument rounding."""
+    dt = getattr(torch, dtype)
+    model = _model(11, 22, dt)
+    params = numpy_params(model)  # the weights exactly as the model holds them (bf16 values in bf16 mode)
+    rng = np.random.default_rng(12)
+    req = [600, 257]
+    lengths = req + req
+    B, T = len(lengths), max(lengths)
+    z = {k: np.zeros((B, 80, T), np.float32) for k in ("x", "mu", "cond")}
+    z["spks"] = np.zeros((B, 80), np.float32)
+    for r, L in enumerate(req):
+        z["x"][r, :, :L] = z["x"][r + 2, :, :L] = rng.standard_normal((80, L))
+        z["mu"][r, :, :L] = rng.standard_normal((80, L))
+        z["cond"][r, :, :L] = rng.standard_normal((80, L))
+        z["spks"][r] = rng.standard_normal(80)
+    z["t"] = rng.uniform(size=2).astype(np.float32)[[0, 1, 0, 1]]
+    z["mask"] = np.zeros((B, 1, T), np.float32)
+    for b, L in enumerate(lengths):
+        z["mask"][b, 0, :L] = 1
+    z = {k: O.bf16_round(v) for k, v in z.items()}
+    for streaming in modes:
+        y = _run(model, z, streaming, dt)
+        ref = O.dit_forward_padded(params, z["x"], z["mask"], z["mu"], z["t"], z["spks"], z["cond"],
+                                   streaming=streaming, emulate_bf16_time=dt == torch.bfloat16)
+        for b, L in enumerate(lengths):
+            e = rel_l2(y[b, :, :L], ref[b, :, :L])
+            assert e <= tol, (dtype, streaming, b, e)
+            assert not np.any(y[b, :, L:]), "padding frames must be zero"
+
+
 def test_batch_composition_invariance_bit_exact():
     """A document's output does not depend on its neighbours in the packed
     batch (reference invariant: flashinfer_attention.py:104-107,
