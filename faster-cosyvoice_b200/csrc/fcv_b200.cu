@@ -22,6 +22,7 @@
 #include "gemm.cuh"
 #include "attn.cuh"
 #include "rows.cuh"
+#include "flow.cuh"
 
 using namespace fcv;
 
@@ -264,7 +265,7 @@ int launch_tc(const GemmCall& g, cudaStream_t s) {
 int choose_tma_out(const GemmCall& g, int bn) {
   const int e = g.epi.epi;
   if (bn < 128) return 0;
-  if ((e == EPI_BIAS || e == EPI_GELU || e == EPI_ROPE || e == EPI_SILU) && g.N % 64 == 0) return 1;
+  if ((e == EPI_BIAS || e == EPI_GELU || e == EPI_ROPE || e == EPI_SILU || e == EPI_LRELU) && g.N % 64 == 0) return 1;
   if (e == EPI_F32 && g.epi.C2 == nullptr && g.N % 32 == 0) return 1;
   if (e == EPI_GATE_RES && g.N % 32 == 0) return 2;
   return 0;
@@ -572,10 +573,17 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   // 2. input embedding: gather, proj (K=320), causal grouped conv x2 + Mish + residual
   {
     ProfScope ps(FCV_CAT_EMBED, s);
-    dim3 grid((bt->T + 31) / 32, B);
-    FCV_LAUNCH("embed_gather_kernel", embed_gather_kernel<T>, dim3(grid), dim3(256), 0, s, static_cast<const T*>(bt->x), static_cast<const T*>(bt->cond),
-                                                static_cast<const T*>(bt->mu), static_cast<const T*>(bt->spks),
-                                                bt->cu_seqlens, bt->T, static_cast<T*>(ws.a_in));
+    if (bt->packed) {
+      const int grid = (int)std::min<long>((N + 7) / 8, 16L * num_sms());
+      FCV_LAUNCH("embed_rows_kernel", embed_rows_kernel<T>, dim3(grid), dim3(256), 0, s, static_cast<const T*>(bt->x),
+                 static_cast<const T*>(bt->cond), static_cast<const T*>(bt->mu), static_cast<const T*>(bt->spks),
+                 bt->doc_ids, (long)N, static_cast<T*>(ws.a_in));
+    } else {
+      dim3 grid((bt->T + 31) / 32, B);
+      FCV_LAUNCH("embed_gather_kernel", embed_gather_kernel<T>, dim3(grid), dim3(256), 0, s, static_cast<const T*>(bt->x), static_cast<const T*>(bt->cond),
+                                                  static_cast<const T*>(bt->mu), static_cast<const T*>(bt->spks),
+                                                  bt->cu_seqlens, bt->T, static_cast<T*>(ws.a_in));
+    }
     FCV_LAUNCH("zero_gap_rows_kernel", zero_gap_rows_kernel<T>, dim3(30, B + 1), dim3(128), 0, s, bt->cu_seqlens,
                static_cast<T*>(ws.gap0), static_cast<T*>(ws.gap1));
     GemmCall g{};
@@ -661,6 +669,14 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   const float* mf = ws.mods + (long)depth * 6144;
   ProfScope ps_out(FCV_CAT_OUTPUT, s);
   FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mf + 1024, mf + 0, bt->doc_ids, MS, N, ws.norm, dtype, s));
+  if (bt->packed) {
+    // packed output rows (N, 80): a plain row-major store, nothing to unpack or zero
+    GemmCall po{};
+    po.A = ws.norm; po.lda = 1024; po.a_rows = N; po.M = N; po.N = 80; po.K = 1024; po.W = w->out_w;
+    po.epi = make_epi(bt->out_f32 ? EPI_F32 : EPI_BIAS, N, 80, bt->out, 80, w->out_b);
+    FCV_TRY(run_gemm(po, dtype, s));
+    return FCV_OK;
+  }
   const dim3 zgrid(80, B);
   if (bt->out_f32)
     FCV_LAUNCH("zero_padding_kernel", zero_padding_kernel<float>, zgrid, dim3(128), 0, s, bt->cu_seqlens, B, bt->T, static_cast<float*>(bt->out));
@@ -975,8 +991,14 @@ int fcv_dit_forward(const fcv_dit_weights* w, const fcv_dit_batch* bt, void* wor
   if (!w || !bt || !workspace) return fail(FCV_EINVAL, "fcv_dit_forward: null argument");
   if (!valid_dtype(w->dtype)) return fail(FCV_EINVAL, "fcv_dit_forward: bad dtype");
   if (w->depth < 1) return fail(FCV_EINVAL, "fcv_dit_forward: depth must be >= 1");
-  if (bt->B < 1 || bt->T < 1 || bt->N < 0 || bt->N > bt->B * bt->T || bt->chunk < 0)
+  if (bt->B < 1 || bt->N < 0 || bt->chunk < 0 || (!bt->packed && (bt->T < 1 || bt->N > (long)bt->B * bt->T)))
     return fail(FCV_EINVAL, "fcv_dit_forward: bad batch geometry B=%d T=%d N=%d", bt->B, bt->T, bt->N);
+  if (bt->packed) {
+    const void* rows[5] = {bt->x, bt->mu, bt->cond, bt->spks, bt->out};
+    for (const void* r : rows)
+      if (reinterpret_cast<uintptr_t>(r) & 15)
+        return fail(FCV_EINVAL, "fcv_dit_forward: packed rows and spks must be 16-byte aligned");
+  }
   if ((reinterpret_cast<uintptr_t>(w->rope_cos) & 15) || (reinterpret_cast<uintptr_t>(w->rope_sin) & 15))
     return fail(FCV_EINVAL, "fcv_dit_forward: RoPE tables must be 16-byte aligned");
   if (bt->max_len > w->rope_max_len)
@@ -989,6 +1011,137 @@ int fcv_dit_forward(const fcv_dit_weights* w, const fcv_dit_batch* bt, void* wor
   cudaStream_t s = as_stream(stream);
   if (w->dtype == FCV_DTYPE_BF16) return forward_impl<bf16>(w, bt, ws, s);
   return forward_impl<float>(w, bt, ws, s);
+}
+
+
+// ====================================================================== packed flow front end
+size_t fcv_flow_workspace_bytes(int n_out_tokens, int dtype) {
+  if (n_out_tokens < 0 || !valid_dtype(dtype)) return 0;
+  const size_t es = dtype == FCV_DTYPE_BF16 ? 2 : 4;
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  const size_t n = (size_t)n_out_tokens;
+  return up(n * kLookK * kFlowIn * es) + up(n * kFlowHid * es) + up(n * kCausalK * kFlowHid * es) +
+         up(n * kFlowIn * 4);
+}
+
+int fcv_flow_frontend(const fcv_flow_weights* w, const int32_t* tokens, const int32_t* token_cu, const int32_t* out_cu,
+                      int B, int n_out_tokens, int max_out_len, int ratio, void* workspace, size_t workspace_bytes,
+                      void* mu_rows, void* stream) {
+  if (!w || !tokens || !token_cu || !out_cu || !mu_rows || B < 0 || n_out_tokens < 0 || max_out_len < 0 || ratio < 1)
+    return fail(FCV_EINVAL, "fcv_flow_frontend: bad arguments");
+  if (!valid_dtype(w->dtype) || w->vocab < 1 || !w->embed || !w->conv1_w || !w->conv2_w)
+    return fail(FCV_EINVAL, "fcv_flow_frontend: bad weights");
+  if (B == 0 || n_out_tokens == 0) return FCV_OK;
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(FCV_EINVAL, "fcv_flow_frontend: workspace must be 256-byte aligned");
+  const size_t need = fcv_flow_workspace_bytes(n_out_tokens, w->dtype);
+  if (workspace_bytes < need)
+    return fail(FCV_EINVAL, "fcv_flow_frontend: workspace of %zu bytes < %zu needed", workspace_bytes, need);
+  const int dtype = w->dtype;
+  const size_t es = dtype == FCV_DTYPE_BF16 ? 2 : 4;
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  const size_t n = (size_t)n_out_tokens;
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  void* a1 = base;
+  void* h1 = base + up(n * kLookK * kFlowIn * es);
+  void* a2 = static_cast<uint8_t*>(h1) + up(n * kFlowHid * es);
+  float* c2 = reinterpret_cast<float*>(static_cast<uint8_t*>(a2) + up(n * kCausalK * kFlowHid * es));
+  cudaStream_t s = as_stream(stream);
+  const dim3 tgrid((max_out_len + 7) / 8, B);
+  const dim3 mgrid(((long)max_out_len * ratio + 7) / 8, B);
+  // conv1 (kernel 4, right lookahead) + LeakyReLU, conv2 (kernel 3, causal) as GEMMs on windows
+  GemmCall g1{};
+  g1.A = a1; g1.lda = kLookK * kFlowIn; g1.a_rows = n_out_tokens; g1.W = w->conv1_w;
+  g1.M = n_out_tokens; g1.N = kFlowHid; g1.K = kLookK * kFlowIn;
+  g1.epi = make_epi(EPI_LRELU, n_out_tokens, kFlowHid, h1, kFlowHid, w->conv1_b);
+  GemmCall g2{};
+  g2.A = a2; g2.lda = kCausalK * kFlowHid; g2.a_rows = n_out_tokens; g2.W = w->conv2_w;
+  g2.M = n_out_tokens; g2.N = kFlowIn; g2.K = kCausalK * kFlowHid;
+  g2.epi = make_epi(EPI_F32, n_out_tokens, kFlowIn, c2, kFlowIn, w->conv2_b);
+  if (dtype == FCV_DTYPE_BF16) {
+    FCV_LAUNCH("token_window_kernel", token_window_kernel<bf16>, tgrid, dim3(256), 0, s, tokens, token_cu, out_cu,
+               static_cast<const bf16*>(w->embed), w->vocab, static_cast<bf16*>(a1));
+    FCV_TRY(run_gemm(g1, dtype, s));
+    FCV_LAUNCH("causal_window_kernel", causal_window_kernel<bf16>, tgrid, dim3(256), 0, s, out_cu,
+               static_cast<const bf16*>(h1), static_cast<bf16*>(a2));
+    FCV_TRY(run_gemm(g2, dtype, s));
+    FCV_LAUNCH("mu_rows_kernel", mu_rows_kernel<bf16>, mgrid, dim3(256), 0, s, tokens, token_cu, out_cu,
+               static_cast<const bf16*>(w->embed), w->vocab, c2, ratio, static_cast<bf16*>(mu_rows));
+  } else {
+    FCV_LAUNCH("token_window_kernel", token_window_kernel<float>, tgrid, dim3(256), 0, s, tokens, token_cu, out_cu,
+               static_cast<const float*>(w->embed), w->vocab, static_cast<float*>(a1));
+    FCV_TRY(run_gemm(g1, dtype, s));
+    FCV_LAUNCH("causal_window_kernel", causal_window_kernel<float>, tgrid, dim3(256), 0, s, out_cu,
+               static_cast<const float*>(h1), static_cast<float*>(a2));
+    FCV_TRY(run_gemm(g2, dtype, s));
+    FCV_LAUNCH("mu_rows_kernel", mu_rows_kernel<float>, mgrid, dim3(256), 0, s, tokens, token_cu, out_cu,
+               static_cast<const float*>(w->embed), w->vocab, c2, ratio, static_cast<float*>(mu_rows));
+  }
+  return FCV_OK;
+}
+
+int fcv_speaker_projection(const void* spk, int spk_dtype, int B, int dim, const void* w, const float* b, int n_out,
+                           void* out, int dtype, void* stream) {
+  if (!spk || !w || !out || B < 0 || dim < 1 || dim > 4096 || n_out < 1)
+    return fail(FCV_EINVAL, "fcv_speaker_projection: bad arguments");
+  if (!valid_dtype(spk_dtype) || !valid_dtype(dtype)) return fail(FCV_EINVAL, "fcv_speaker_projection: bad dtype");
+  if (B == 0) return FCV_OK;
+  cudaStream_t s = as_stream(stream);
+  const size_t smem = (size_t)dim * sizeof(float);
+  const bool sb = spk_dtype == FCV_DTYPE_BF16, ob = dtype == FCV_DTYPE_BF16;
+  if (sb && ob)
+    FCV_LAUNCH("speaker_projection_kernel", speaker_projection_kernel<bf16, bf16>, dim3(B), dim3(128), smem, s,
+               static_cast<const bf16*>(spk), dim, static_cast<const bf16*>(w), b, n_out, static_cast<bf16*>(out));
+  else if (ob)
+    FCV_LAUNCH("speaker_projection_kernel", speaker_projection_kernel<float, bf16>, dim3(B), dim3(128), smem, s,
+               static_cast<const float*>(spk), dim, static_cast<const bf16*>(w), b, n_out, static_cast<bf16*>(out));
+  else if (sb)
+    FCV_LAUNCH("speaker_projection_kernel", speaker_projection_kernel<bf16, float>, dim3(B), dim3(128), smem, s,
+               static_cast<const bf16*>(spk), dim, static_cast<const float*>(w), b, n_out, static_cast<float*>(out));
+  else
+    FCV_LAUNCH("speaker_projection_kernel", speaker_projection_kernel<float, float>, dim3(B), dim3(128), smem, s,
+               static_cast<const float*>(spk), dim, static_cast<const float*>(w), b, n_out, static_cast<float*>(out));
+  return FCV_OK;
+}
+
+int fcv_prompt_rows(const void* prompt, const int32_t* prompt_cu, const int32_t* mel_cu, int B, int max_mel_len,
+                    void* cond, int dtype, void* stream) {
+  if (!prompt_cu || !mel_cu || !cond || B < 0 || max_mel_len < 0) return fail(FCV_EINVAL, "fcv_prompt_rows: bad arguments");
+  if (!valid_dtype(dtype)) return fail(FCV_EINVAL, "fcv_prompt_rows: bad dtype");
+  if (B == 0 || max_mel_len == 0) return FCV_OK;
+  const dim3 grid((max_mel_len + 7) / 8, B);
+  cudaStream_t s = as_stream(stream);
+  if (dtype == FCV_DTYPE_BF16)
+    FCV_LAUNCH("prompt_rows_kernel", prompt_rows_kernel<bf16>, grid, dim3(256), 0, s, static_cast<const bf16*>(prompt),
+               prompt_cu, mel_cu, static_cast<bf16*>(cond));
+  else
+    FCV_LAUNCH("prompt_rows_kernel", prompt_rows_kernel<float>, grid, dim3(256), 0, s, static_cast<const float*>(prompt),
+               prompt_cu, mel_cu, static_cast<float*>(cond));
+  return FCV_OK;
+}
+
+int fcv_pack_rows(const void* src, int src_dtype, long batch_stride, int T, const int32_t* cu, int B, int max_len,
+                  void* dst, int dst_dtype, void* stream) {
+  if (!src || !cu || !dst || B < 0 || max_len < 0 || T < max_len || batch_stride < 0)
+    return fail(FCV_EINVAL, "fcv_pack_rows: bad arguments");
+  if (!valid_dtype(src_dtype) || !valid_dtype(dst_dtype)) return fail(FCV_EINVAL, "fcv_pack_rows: bad dtype");
+  if (B == 0 || max_len == 0) return FCV_OK;
+  const dim3 grid((max_len + 31) / 32, B);
+  cudaStream_t s = as_stream(stream);
+  const bool sb = src_dtype == FCV_DTYPE_BF16, db = dst_dtype == FCV_DTYPE_BF16;
+  if (sb && db)
+    FCV_LAUNCH("pack_rows_kernel", pack_rows_kernel<bf16, bf16>, grid, dim3(256), 0, s, static_cast<const bf16*>(src),
+               batch_stride, T, cu, static_cast<bf16*>(dst));
+  else if (sb)
+    FCV_LAUNCH("pack_rows_kernel", pack_rows_kernel<bf16, float>, grid, dim3(256), 0, s, static_cast<const bf16*>(src),
+               batch_stride, T, cu, static_cast<float*>(dst));
+  else if (db)
+    FCV_LAUNCH("pack_rows_kernel", pack_rows_kernel<float, bf16>, grid, dim3(256), 0, s, static_cast<const float*>(src),
+               batch_stride, T, cu, static_cast<bf16*>(dst));
+  else
+    FCV_LAUNCH("pack_rows_kernel", pack_rows_kernel<float, float>, grid, dim3(256), 0, s, static_cast<const float*>(src),
+               batch_stride, T, cu, static_cast<float*>(dst));
+  return FCV_OK;
 }
 
 }  // extern "C"

@@ -370,6 +370,8 @@ __device__ __forceinline__ float mish(float x) {
 }
 // SiLU: x / (1 + e^-x).
 __device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + ex2_fast(-x * kLog2e)); }
+// F.leaky_relu with its default slope 0.01 (upsample_encoder.py:84)
+__device__ __forceinline__ float leaky_relu(float x) { return x >= 0.f ? x : 0.01f * x; }
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v);

@@ -31,6 +31,7 @@ enum Epi : int {
   EPI_MISH_RES = 7,   // gapped row g, packed p = gap_rows[g] >= 0: h(f32)[p] = mish(acc+b) + res[g]
   EPI_UNPACK = 8,     // out(act)[doc, col, pos] = acc + b   (proj_out -> (B, 80, T))
   EPI_SILU = 9,       // C(act) = silu(acc + b)
+  EPI_LRELU = 10,     // C(act) = leaky_relu(acc + b, 0.01)   (pre-lookahead conv1)
 };
 
 constexpr int kConvPad = 30;  // kernel_size - 1 zero rows before every document
@@ -112,6 +113,10 @@ __device__ __forceinline__ void epilogue_apply(const EpiParams& p, int row, int 
     case EPI_SILU:
 #pragma unroll
       for (int j = 0; j < W; ++j) v[j] = silu(v[j]);
+      break;
+    case EPI_LRELU:
+#pragma unroll
+      for (int j = 0; j < W; ++j) v[j] = leaky_relu(v[j]);
       break;
     case EPI_F32: {
       if (p.C2 != nullptr) {
@@ -290,6 +295,9 @@ __device__ __forceinline__ void epi_bf16_half(const EpiParams& P, uint32_t (&r)[
   } else if (P.epi == EPI_SILU) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = silu(v[j]);
+  } else if (P.epi == EPI_LRELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = leaky_relu(v[j]);
   } else if (P.epi == EPI_ROPE && col0 < 2048 && (col0 & 1023) < 64) {
     const int i0 = (col0 & 1023) >> 1;  // first rotary pair of this 32-column piece (0 or 16)
     // 16 consecutive table entries per row, 64-byte aligned: four 16-byte loads each

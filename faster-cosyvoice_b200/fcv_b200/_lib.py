@@ -55,6 +55,11 @@ EXPORTS = (
     "fcv_launch_count",
     "fcv_dit_workspace_bytes",
     "fcv_dit_forward",
+    "fcv_flow_workspace_bytes",
+    "fcv_flow_frontend",
+    "fcv_speaker_projection",
+    "fcv_prompt_rows",
+    "fcv_pack_rows",
 )
 
 
@@ -118,6 +123,19 @@ class DitBatch(ctypes.Structure):
         ("n_attn_tiles", ctypes.c_int),
         ("out", ctypes.c_void_p),
         ("out_f32", ctypes.c_int),
+        ("packed", ctypes.c_int),
+    ]
+
+
+class FlowWeights(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_int),
+        ("vocab", ctypes.c_int),
+        ("embed", ctypes.c_void_p),
+        ("conv1_w", ctypes.c_void_p),
+        ("conv1_b", ctypes.c_void_p),
+        ("conv2_w", ctypes.c_void_p),
+        ("conv2_b", ctypes.c_void_p),
     ]
 
 
@@ -148,6 +166,12 @@ _SIGNATURES = {
     "fcv_launch_count": (ctypes.c_long, []),
     "fcv_dit_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i]),
     "fcv_dit_forward": (_i, [ctypes.POINTER(DitWeights), ctypes.POINTER(DitBatch), _vp, ctypes.c_size_t, _vp]),
+    "fcv_flow_workspace_bytes": (ctypes.c_size_t, [_i, _i]),
+    "fcv_flow_frontend": (_i, [ctypes.POINTER(FlowWeights), _vp, _vp, _vp, _i, _i, _i, _i, _vp, ctypes.c_size_t,
+                               _vp, _vp]),
+    "fcv_speaker_projection": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _vp, _i, _vp]),
+    "fcv_prompt_rows": (_i, [_vp, _vp, _vp, _i, _i, _vp, _i, _vp]),
+    "fcv_pack_rows": (_i, [_vp, _i, _l, _i, _vp, _i, _i, _vp, _i, _vp]),
 }
 
 

@@ -318,7 +318,9 @@ class B200DiT(nn.Module):
             self._workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
         return self._workspace
 
-    def batch_struct(self, layout: PackedLayout, x, mu, t, spks, cond, out) -> DitBatch:
+    def batch_struct(self, layout: PackedLayout, x, mu, t, spks, cond, out, packed: bool = False) -> DitBatch:
+        """C-ABI batch descriptor.  ``packed``: x, mu, cond and out are (N, 80)
+        rows in document order instead of (B, 80, T)."""
         b = DitBatch()
         b.B = len(layout.lengths)
         b.T = layout.padded_length
@@ -333,6 +335,7 @@ class B200DiT(nn.Module):
         b.attn_tiles = layout.attn_tiles.data_ptr()
         b.n_attn_tiles = layout.n_attn_tiles
         b.out = out.data_ptr()
+        b.packed = 1 if packed else 0
         if out.dtype == torch.float32:
             b.out_f32 = 1
         elif out.dtype == self.weight_dtype:
@@ -341,14 +344,14 @@ class B200DiT(nn.Module):
             raise ValueError(f"output must be float32 or {self.weight_dtype}")
         return b
 
-    def _launch(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor) -> None:
+    def _launch(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor, packed: bool = False) -> None:
         ws = self._workspace_for(layout.N, len(layout.lengths), x.device)
-        bs = self.batch_struct(layout, x, mu, t, spks, cond, out)
+        bs = self.batch_struct(layout, x, mu, t, spks, cond, out, packed)
         call("fcv_dit_forward", ctypes.byref(self.weights_struct()), ctypes.byref(bs), ws.data_ptr(),
              ws.numel(), _stream(x.device))
 
     def forward_layout(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor | None = None,
-                       graph: bool = False):
+                       graph: bool = False, packed: bool = False):
         """One estimator call on a prepared layout.  Inputs must already be
         contiguous tensors of the weight dtype on the module's device; ``out``
         may be float32 (the solver keeps the flow field unrounded).
@@ -357,37 +360,41 @@ class B200DiT(nn.Module):
         (layout, buffer addresses) and replayed afterwards; without ``out`` the
         result is then a view of the graph's static output buffer, valid until
         the next replay of that graph (the reference's graph path,
-        ``flashinfer_dit.py:806-826``, returns such views too)."""
-        B = len(layout.lengths)
-        T = layout.padded_length
+        ``flashinfer_dit.py:806-826``, returns such views too).
+
+        ``packed=True``: x, mu, cond are (N, 80) rows in document order and the
+        result is (N, 80) rows (the device-packed flow, no padded layout)."""
         if not graph:
             if out is None:
-                out = torch.empty(B, MEL, T, dtype=self.weight_dtype, device=x.device)
-            self._launch(layout, x, mu, t, spks, cond, out)
+                out = self._new_out(layout, x.device, packed)
+            self._launch(layout, x, mu, t, spks, cond, out, packed)
             return out
-        entry = self.capture_graph(layout, x, mu, t, spks, cond, out)
+        entry = self.capture_graph(layout, x, mu, t, spks, cond, out, packed=packed)
         entry[0].replay()
         return entry[1]
 
+    def _new_out(self, layout: PackedLayout, device: torch.device, packed: bool) -> torch.Tensor:
+        if packed:
+            return torch.empty(max(layout.N, 1), MEL, dtype=self.weight_dtype, device=device)[:layout.N]
+        return torch.empty(len(layout.lengths), MEL, layout.padded_length, dtype=self.weight_dtype, device=device)
+
     def capture_graph(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor | None = None,
-                      warmup: bool = True):
+                      warmup: bool = True, packed: bool = False):
         """CUDA graph of one estimator call for this layout and these buffers
         (cached, FIFO of 16).  Returns ``(graph, output buffer, layout)``.  With
         ``warmup=False`` the caller guarantees an eager call already ran."""
         B = len(layout.lengths)
-        T = layout.padded_length
         self._workspace_for(layout.N, B, x.device)  # settle the workspace before capturing
         key = (id(layout), x.data_ptr(), mu.data_ptr(), t.data_ptr(), spks.data_ptr(), cond.data_ptr(),
-               None if out is None else (out.data_ptr(), out.dtype))
+               None if out is None else (out.data_ptr(), out.dtype), packed)
         entry = self._graphs.get(key)
         if entry is None:
-            static_out = out if out is not None else torch.empty(B, MEL, T, dtype=self.weight_dtype,
-                                                                 device=x.device)
+            static_out = out if out is not None else self._new_out(layout, x.device, packed)
             if warmup:
-                self._launch(layout, x, mu, t, spks, cond, static_out)  # first launches outside the capture
+                self._launch(layout, x, mu, t, spks, cond, static_out, packed)  # first launches outside the capture
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self._launch(layout, x, mu, t, spks, cond, static_out)
+                self._launch(layout, x, mu, t, spks, cond, static_out, packed)
             if len(self._graphs) >= 16:
                 self._graphs.popitem(last=False)
             entry = (g, static_out, layout)  # the layout is kept alive with its graph

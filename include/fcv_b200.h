@@ -129,6 +129,12 @@ typedef struct fcv_dit_batch {
   int n_attn_tiles;
   void* out;         /* (B, 80, T); padding frames zeroed                      */
   int out_f32;       /* 0: out has element type dtype; 1: out is float32       */
+  int packed;        /* 1: x, mu, cond and out are packed rows (N, 80) in
+                      * document order (cu_seqlens), T is unused and nothing
+                      * is padded; rows and spks 16-byte aligned.  0: the
+                      * padded (B, 80, T) layout above.  The packed form
+                      * serves the device-packed flow (flashinfer_flow.py
+                      * 118-281 without its padded intermediate tensors).   */
 } fcv_dit_batch;
 
 /* Layout ------------------------------------------------------------------ */
@@ -273,6 +279,57 @@ size_t fcv_dit_workspace_bytes(int N, int B, int depth, int dtype);
  * proj_out, unpack into batch->out.  `workspace` must be 256-byte aligned. */
 int fcv_dit_forward(const fcv_dit_weights* w, const fcv_dit_batch* batch, void* workspace,
                     size_t workspace_bytes, void* stream);
+
+/* Packed flow front end ----------------------------------------------------
+ * Device-packed replacement of the per-request Python front end of
+ * flow_inference_batched / flow_inference_batched_streaming
+ * (flashinfer_flow.py:118-281; CausalMaskedDiffWithDiT.inference, flow.py:365-409).
+ * Token rows are packed per request: request b owns input tokens
+ * [token_cu[b], token_cu[b+1]) -- for a non-final stream the last 3 of them
+ * are lookahead context -- and output token rows [out_cu[b], out_cu[b+1]),
+ * out_len = in_len (final / offline) or in_len - 3 (non-final).  Its mel rows
+ * are [ratio*out_cu[b], ratio*out_cu[b+1]). */
+typedef struct fcv_flow_weights {
+  int dtype;             /* FCV_DTYPE_*: element type of the tables and rows    */
+  int vocab;             /* rows of the token table (6561)                      */
+  const void* embed;     /* (vocab, 80) input_embedding.weight                  */
+  const void* conv1_w;   /* (1024, 4*80): conv1.weight[o, c, k] at [o, k*80+c]  */
+  const float* conv1_b;  /* (1024)                                              */
+  const void* conv2_w;   /* (80, 3*1024): conv2.weight[o, c, k] at [o, k*1024+c] */
+  const float* conv2_b;  /* (80)                                                */
+} fcv_flow_weights;
+
+/* Workspace bytes of fcv_flow_frontend for n_out_tokens output token rows. */
+size_t fcv_flow_workspace_bytes(int n_out_tokens, int dtype);
+
+/* mu_rows (ratio*n_out_tokens, 80), element type w->dtype, = the
+ * PreLookaheadLayer (upsample_encoder.py:55-92) over every request's embedded
+ * tokens (flashinfer_flow.py:148-149, 171-182), repeat-interleaved to the mel
+ * rate (:150, 183).  Token ids are clamped at 0 (:148); ids >= vocab must be
+ * rejected by the caller.  max_out_len = longest out_len. */
+int fcv_flow_frontend(const fcv_flow_weights* w, const int32_t* tokens, const int32_t* token_cu,
+                      const int32_t* out_cu, int B, int n_out_tokens, int max_out_len, int ratio,
+                      void* workspace, size_t workspace_bytes, void* mu_rows, void* stream);
+
+/* out (B, n_out) = W normalize(spk) + b: F.normalize then spk_embed_affine_layer
+ * (flashinfer_flow.py:145-146, 219-220).  spk (B, dim) of spk_dtype; W (n_out,
+ * dim) and out of dtype; the normalised vector is rounded to dtype as the
+ * reference's module computes in its own dtype. */
+int fcv_speaker_projection(const void* spk, int spk_dtype, int B, int dim, const void* w, const float* b,
+                           int n_out, void* out, int dtype, void* stream);
+
+/* cond rows (mel_cu[B], 80) of dtype: the prompt Mel of request b in its first
+ * prompt_cu[b+1]-prompt_cu[b] rows, zeros after (_copy_prompt_features,
+ * flashinfer_flow.py:95-115).  prompt (prompt_cu[B], 80) of dtype; every prompt
+ * must fit its request (checked on the host by the caller). */
+int fcv_prompt_rows(const void* prompt, const int32_t* prompt_cu, const int32_t* mel_cu, int B,
+                    int max_mel_len, void* cond, int dtype, void* stream);
+
+/* Channel-major padded (B, 80, T) -> packed rows: dst[cu[b]+p, c] =
+ * src[b*batch_stride + c*T + p] for p < cu[b+1]-cu[b].  batch_stride 0
+ * broadcasts one sequence (the fixed noise prefix, flashinfer_flow.py:266). */
+int fcv_pack_rows(const void* src, int src_dtype, long batch_stride, int T, const int32_t* cu, int B,
+                  int max_len, void* dst, int dst_dtype, void* stream);
 
 #ifdef __cplusplus
 }

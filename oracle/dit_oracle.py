@@ -381,28 +381,35 @@ def cosine_time_span(num_steps: int = 10, emulate_bf16=False):
 
 
 def solve_euler_docs(params, noise_docs, mu_docs, cond_docs, spks, num_steps=10,
-                     streaming=False, chunk=50, cfg_rate=CFG_RATE):
+                     streaming=False, chunk=50, cfg_rate=CFG_RATE, emulate_bf16=False):
     """CFG-doubled Euler solver over documents (``flashinfer_flow.py:16-74``):
     the unconditional half has mu, spks and cond zeroed (``:45-51``), the
     sample is repeated (``:55``), ``d = (1+r) d_c - r d_u`` (``:66-69``),
-    ``x += dt d`` with the cosine schedule (``:34-43, 70-73``).  fp32."""
-    ts = cosine_time_span(num_steps)
+    ``x += dt d`` with the cosine schedule (``:34-43, 70-73``).  fp32.
+
+    ``emulate_bf16=True`` reproduces the semantics of a bf16 solver call: the
+    schedule, t and dt are computed in bf16 (the solver works in
+    ``speaker_embeddings.dtype``, ``:34-43, 70-73``), the estimator sees
+    bf16-rounded inputs and ``bf16(1000 t)``; the sample itself stays float32."""
+    ts = cosine_time_span(num_steps, emulate_bf16)
+    rnd = (lambda v: np.float32(bf16_round(np.asarray(v, np.float32)))) if emulate_bf16 else np.float32
+    inp = bf16_round if emulate_bf16 else (lambda a: a)
     R = len(noise_docs)
     xs = [np.asarray(n, np.float32).copy() for n in noise_docs]
     t = ts[0]
-    dt = ts[1] - ts[0]
+    dt = rnd(ts[1] - ts[0])
     for step in range(1, num_steps + 1):
-        docs = [(xs[i], mu_docs[i], cond_docs[i], spks[i]) for i in range(R)]
-        docs += [(xs[i], np.zeros_like(mu_docs[i]), np.zeros_like(cond_docs[i]),
+        docs = [(inp(xs[i]), inp(mu_docs[i]), inp(cond_docs[i]), inp(spks[i])) for i in range(R)]
+        docs += [(inp(xs[i]), np.zeros_like(mu_docs[i]), np.zeros_like(cond_docs[i]),
                   np.zeros_like(spks[i])) for i in range(R)]
         tt = np.full(2 * R, t, np.float32)
-        d = dit_forward_docs(params, docs, tt, chunk if streaming else None)
+        d = dit_forward_docs(params, docs, tt, chunk if streaming else None, emulate_bf16_time=emulate_bf16)
         for i in range(R):
             der = (np.float32(1.0 + cfg_rate) * d[i] - np.float32(cfg_rate) * d[R + i]).astype(np.float32)
             xs[i] = (xs[i] + dt * der).astype(np.float32)
-        t = np.float32(t + dt)
+        t = rnd(t + dt)
         if step < num_steps:
-            dt = np.float32(ts[step + 1] - t)
+            dt = rnd(ts[step + 1] - t)
     return xs
 
 

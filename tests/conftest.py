@@ -40,6 +40,36 @@ def make_model(seed: int, depth: int):
     return B200DiT(depth=depth).eval()
 
 
+def make_flow(dit_seed: int, depth: int):
+    """B200Flow with the reference's random initialisation: the DiT from
+    ``dit_seed``, then the CFM reseed and the front-end modules (CPU, fp32)."""
+    import torch
+    from fcv_b200.flow import B200Flow
+
+    torch.manual_seed(dit_seed)
+    return B200Flow(depth=depth).eval()
+
+
+def flow_case(z: dict, mode: str) -> dict:
+    """Per-request inputs of one mode of ``flow_frontend.npz``."""
+    tl = [int(v) for v in z[f"{mode}_token_lengths"]]
+    tok = z[f"{mode}_tokens"]
+    cu = np.concatenate([[0], np.cumsum(tl)])
+    pcu = z[f"{mode}_prompt_cu"]
+    ocu = z[f"{mode}_out_cu"]
+    mcu = z[f"{mode}_mu_cu"]
+    R = len(tl)
+    return {
+        "tokens": [tok[cu[i]:cu[i + 1]] for i in range(R)],
+        "prompts": [z[f"{mode}_prompt"][pcu[i]:pcu[i + 1]] for i in range(R)],
+        "spk": z[f"{mode}_spk"],
+        "spk_proj": z[f"{mode}_spk_proj"],
+        "mu": [z[f"{mode}_mu"][mcu[i]:mcu[i + 1]] for i in range(R)],
+        "out": [z[f"{mode}_out"][ocu[i]:ocu[i + 1]] for i in range(R)],
+        "finalize": [bool(v) for v in z[f"{mode}_finalize"]] if f"{mode}_finalize" in z else None,
+    }
+
+
 def numpy_params(model) -> dict:
     return {k: v.detach().float().cpu().numpy() for k, v in model.state_dict().items()}
 

@@ -14,12 +14,16 @@ The reference's own code is imported and executed on the CPU in float32:
 * ``flashinfer_kernels.layer_norm_modulate_torch`` (``flashinfer_kernels.py:288-296``);
 * ``flashinfer_flow.solve_euler_batched`` (``flashinfer_flow.py:16-74``) with
   ``CausalConditionalCFM`` (``flow_matching.py:196-200``);
-* ``modules.TimestepEmbedding`` in bf16 (``modules.py:71-83, 606-616``).
+* ``modules.TimestepEmbedding`` in bf16 (``modules.py:71-83, 606-616``);
+* ``flashinfer_flow.flow_inference_batched`` / ``flow_inference_batched_streaming``
+  (``flashinfer_flow.py:118-281``) on a ``CausalMaskedDiffWithDiT`` built as
+  ``builders.py:16-45`` does (``python tests/golden/make_golden.py flow`` regenerates
+  only this fixture).
 
 ``x_transformers`` (pinned 2.23.5, absent here) is replaced by the restatement in
 ``_xt_shim``; ``omegaconf`` is bypassed by passing a ``SimpleNamespace`` as
-``cfm_params``.  Weights come from ``torch.manual_seed(seed)`` followed by the
-reference constructor; their SHA-256 fingerprints are stored so the tests can
+``cfm_params`` (and stubbed for ``flow.py``'s default-argument import).  Weights come
+from ``torch.manual_seed(seed)`` followed by the reference constructor; their SHA-256 fingerprints are stored so the tests can
 check that the framework's own module tree reproduces the same initialisation.
 
 None of the tests import this script or the reference; they read the ``.npz`` /
@@ -188,7 +192,120 @@ def ode_case():
                         rand_noise_head=decoder.rand_noise[0, :, :8].numpy(), **out)
 
 
+def build_ref_flow(dit_seed: int, depth: int):
+    """``builders.py:16-45`` (DiT depth reduced), random init.  The DiT draws from
+    ``dit_seed``; the CFM constructor then reseeds 0 and draws ``rand_noise``
+    (``flow_matching.py:199-200``); the front-end modules draw next: the
+    ``PreLookaheadLayer`` argument (conv1, conv2), then ``nn.Embedding`` and the
+    speaker ``nn.Linear`` inside ``CausalMaskedDiffWithDiT.__init__`` (``flow.py:306-307``).
+    ``omegaconf`` (imported by ``flow.py:20`` for a default argument only) is stubbed."""
+    if "omegaconf" not in sys.modules:
+        stub = types.ModuleType("omegaconf")
+        stub.DictConfig = dict
+        sys.modules["omegaconf"] = stub
+    from faster_cosyvoice.token2wav.cosyvoice.flow.flow import CausalMaskedDiffWithDiT
+    from faster_cosyvoice.token2wav.cosyvoice.transformer.upsample_encoder import PreLookaheadLayer
+
+    est = build_ref_dit(dit_seed, depth)
+    cfm = types.SimpleNamespace(sigma_min=1e-6, solver="euler", t_scheduler="cosine",
+                                training_cfg_rate=0.2, inference_cfg_rate=0.7, reg_loss_type="l1")
+    decoder = CausalConditionalCFM(in_channels=240, cfm_params=cfm, n_spks=1, spk_emb_dim=80,
+                                   estimator=est)
+    flow = CausalMaskedDiffWithDiT(
+        input_size=80, output_size=80, spk_embed_dim=192, output_type="mel", vocab_size=6561,
+        input_frame_rate=25, only_mask_loss=True, token_mel_ratio=2, pre_lookahead_len=3,
+        pre_lookahead_layer=PreLookaheadLayer(in_channels=80, channels=1024, pre_lookahead_len=3),
+        decoder=decoder)
+    return flow.eval()
+
+
+def _concat_rows(mats):
+    """(L_i, C) matrices -> one (sum L_i, C) array + cu offsets."""
+    cu = np.zeros(len(mats) + 1, np.int64)
+    for i, m in enumerate(mats):
+        cu[i + 1] = cu[i] + m.shape[0]
+    return np.concatenate(mats, 0).astype(np.float32), cu
+
+
+@torch.no_grad()
+def flow_case():
+    """``flashinfer_flow.flow_inference_batched`` (``flashinfer_flow.py:118-184``) and
+    ``flow_inference_batched_streaming`` (``:187-281``) on a depth-2 flow, plus their
+    front-end intermediates (speaker projection, repeat-interleaved mu)."""
+    flow = build_ref_flow(4, 2)
+    rng = np.random.default_rng(31)
+    out = {}
+    front = {"input_embedding.weight": flow.input_embedding.weight,
+             "spk_embed_affine_layer.weight": flow.spk_embed_affine_layer.weight,
+             "spk_embed_affine_layer.bias": flow.spk_embed_affine_layer.bias,
+             "pre_lookahead_layer.conv1.weight": flow.pre_lookahead_layer.conv1.weight,
+             "pre_lookahead_layer.conv1.bias": flow.pre_lookahead_layer.conv1.bias,
+             "pre_lookahead_layer.conv2.weight": flow.pre_lookahead_layer.conv2.weight,
+             "pre_lookahead_layer.conv2.bias": flow.pre_lookahead_layer.conv2.bias}
+    fps = {k: {"shape": list(v.shape), "dtype": "float32",
+               "sha256": hashlib.sha256(v.detach().contiguous().numpy().tobytes()).hexdigest()}
+           for k, v in front.items()}
+    for mode, tok_lens, prompt_lens, finalize in (
+            ("offline", [37, 61, 20], [24, 40, 10], None),
+            ("streaming", [30, 45, 23], [20, 16, 12], [True, False, False])):
+        tokens = [rng.integers(0, 6561, size=L).astype(np.int64) for L in tok_lens]
+        tokens[0][5] = -1  # clamp(min=0) path (flashinfer_flow.py:148)
+        prompts = [rng.standard_normal((L, 80)).astype(np.float32) for L in prompt_lens]
+        spk = rng.standard_normal((len(tok_lens), 192)).astype(np.float32)
+        prompt_t = [torch.from_numpy(p).unsqueeze(0) for p in prompts]
+        spk_t = torch.from_numpy(spk)
+        token_list = [t.tolist() for t in tokens]
+        captured = {}
+        if mode == "offline":
+            orig = torch.randn
+
+            def rec(*a, **k):
+                r = orig(*a, **k)
+                captured["noise"] = r.clone()
+                return r
+
+            torch.manual_seed(2024)
+            torch.randn = rec
+            try:
+                gen = ref_flow.flow_inference_batched(flow, token_list, prompt_t, spk_t)
+            finally:
+                torch.randn = orig
+            # front-end intermediates exactly as flashinfer_flow.py:144-153 forms them
+            tok, tok_len = ref_flow._pack_tokens(token_list, torch.device("cpu"))
+            mask = (~ref_flow.make_pad_mask(tok_len)).unsqueeze(-1).float()
+            feats = flow.input_embedding(torch.clamp(tok, min=0)) * mask
+            mu = flow.pre_lookahead_layer(feats).repeat_interleave(2, dim=1)
+            mu_docs = [mu[i, :2 * L].numpy() for i, L in enumerate(tok_lens)]
+            spk_proj = flow.spk_embed_affine_layer(torch.nn.functional.normalize(spk_t, dim=1)).numpy()
+            out[f"{mode}_noise"] = captured["noise"].numpy()
+        else:
+            gen = ref_flow.flow_inference_batched_streaming(flow, token_list, prompt_t, spk_t, finalize)
+            mu_docs = [ref_flow._streaming_token_features(flow, tl, finalize=f, device=torch.device("cpu"))[0].numpy()
+                       for tl, f in zip(token_list, finalize)]
+            spk_proj = flow.spk_embed_affine_layer(torch.nn.functional.normalize(spk_t, dim=1)).numpy()
+            out[f"{mode}_finalize"] = np.asarray(finalize, np.int64)
+        tok_cat = np.concatenate(tokens).astype(np.int64)
+        out[f"{mode}_tokens"] = tok_cat
+        out[f"{mode}_token_lengths"] = np.asarray(tok_lens, np.int64)
+        out[f"{mode}_prompt"], out[f"{mode}_prompt_cu"] = _concat_rows(prompts)
+        out[f"{mode}_spk"] = spk
+        out[f"{mode}_spk_proj"] = spk_proj.astype(np.float32)
+        out[f"{mode}_mu"], out[f"{mode}_mu_cu"] = _concat_rows(mu_docs)
+        gens = [g[0].float().numpy().T for g in gen]  # (G_i, 80)
+        out[f"{mode}_out"], out[f"{mode}_out_cu"] = _concat_rows(gens)
+    out["rand_noise_head"] = flow.decoder.rand_noise[0, :, :8].numpy()
+    np.savez_compressed(HERE / "flow_frontend.npz", **out)
+    return fps
+
+
 def main():
+    if sys.argv[1:] == ["flow"]:
+        fps = json.loads((HERE / "weights_fingerprint.json").read_text())
+        fps["flow_seed4_depth2_frontend"] = flow_case()
+        fps["seed4_depth2"] = fingerprint(build_ref_dit(4, 2))
+        (HERE / "weights_fingerprint.json").write_text(json.dumps(fps, indent=0, sort_keys=True))
+        print("flow golden vectors written to", HERE)
+        return
     fps = {}
     m = dit_case("dit_block_fp32", seed=0, depth=1, lengths=[300], T=300, cfg_pairs=False, in_seed=100)
     fps["seed0_depth1"] = fingerprint(m)
@@ -199,6 +316,8 @@ def main():
                  cfg_pairs=False, in_seed=102)
     fps["seed2_depth2"] = fingerprint(m)
     fps["seed3_depth2"] = fingerprint(build_ref_dit(3, 2))
+    fps["seed4_depth2"] = fingerprint(build_ref_dit(4, 2))
+    fps["flow_seed4_depth2_frontend"] = flow_case()
     (HERE / "weights_fingerprint.json").write_text(json.dumps(fps, indent=0, sort_keys=True))
     pack_cases()
     rownorm_case()

@@ -9,8 +9,9 @@ import hashlib
 import numpy as np
 import pytest
 
-from conftest import golden_fingerprints, load_golden, make_model, numpy_params, rel_l2
+from conftest import flow_case, golden_fingerprints, load_golden, make_flow, make_model, numpy_params, rel_l2
 from oracle import dit_oracle as O
+from oracle import flow_oracle as F
 
 
 def test_pack_layout_matches_reference_bit_exact():
@@ -54,7 +55,8 @@ def test_time_sinusoid_matches_reference_fp32_and_bf16():
 
 
 @pytest.mark.parametrize("key,seed,depth", [("seed0_depth1", 0, 1), ("seed2_depth2", 2, 2),
-                                            ("seed3_depth2", 3, 2), ("seed1_depth22", 1, 22)])
+                                            ("seed3_depth2", 3, 2), ("seed4_depth2", 4, 2),
+                                            ("seed1_depth22", 1, 22)])
 def test_module_tree_reproduces_reference_init(key, seed, depth):
     fp = golden_fingerprints()[key]
     sd = make_model(seed, depth).state_dict()
@@ -106,3 +108,60 @@ def test_flop_model_matches_survey_formula():
     per_seq = 2 * 1024 * 137216 + 2 * (256 * 1024 + 1024 * 1024)
     assert f1 == 378044416 + 22 * 4096 * 1 + per_seq
     assert O.visible_pairs([100], 50) == 50 * 50 + 50 * 100
+
+
+# ---------------------------------------------------------------- packed flow front end
+
+def _flow_params():
+    flow = make_flow(4, 2)
+    sd = {k: v.detach().float().numpy() for k, v in flow.state_dict().items()}
+    fe = {k: v for k, v in sd.items() if not k.startswith("decoder.")}
+    dit = {k[len("decoder.estimator."):]: v for k, v in sd.items() if k.startswith("decoder.estimator.")}
+    return flow, fe, dit
+
+
+def test_flow_module_reproduces_reference_init():
+    """B200Flow's front-end parameters and noise prefix equal the reference's
+    CausalMaskedDiffWithDiT built as builders.py:16-45 does (same RNG order)."""
+    flow, fe, _ = _flow_params()
+    fp = golden_fingerprints()["flow_seed4_depth2_frontend"]
+    assert sorted(fe.keys()) == sorted(fp.keys())
+    for k, meta in fp.items():
+        assert list(fe[k].shape) == meta["shape"], k
+        assert hashlib.sha256(np.ascontiguousarray(fe[k]).tobytes()).hexdigest() == meta["sha256"], k
+    z = load_golden("flow_frontend")
+    assert np.array_equal(flow.decoder.rand_noise[0, :, :8].numpy(), z["rand_noise_head"])
+
+
+@pytest.mark.parametrize("mode", ["offline", "streaming"])
+def test_flow_frontend_oracle_matches_reference(mode):
+    """Token embedding + PreLookaheadLayer + repeat-interleave and the speaker
+    projection vs the reference's own modules (flashinfer_flow.py:144-153, 167-184)."""
+    _, fe, _ = _flow_params()
+    c = flow_case(load_golden("flow_frontend"), mode)
+    fin = c["finalize"] or [True] * len(c["tokens"])
+    for i, toks in enumerate(c["tokens"]):
+        mu = F.frontend_mu(fe, toks, fin[i])
+        assert mu.shape == c["mu"][i].shape, (mode, i)
+        np.testing.assert_allclose(mu, c["mu"][i], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(F.speaker_projection(fe, c["spk"]), c["spk_proj"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("mode", ["offline", "streaming"])
+def test_flow_inference_oracle_matches_reference(mode):
+    """The whole batched flow inference (flashinfer_flow.py:118-281) on a
+    depth-2 flow: the generated Mel of every request."""
+    flow, fe, dit = _flow_params()
+    z = load_golden("flow_frontend")
+    c = flow_case(z, mode)
+    fin = c["finalize"] or [True] * len(c["tokens"])
+    n_mel = [m.shape[0] for m in c["mu"]]
+    if mode == "offline":
+        noise = [z["offline_noise"][i, :, :n] for i, n in enumerate(n_mel)]
+    else:
+        noise = [flow.decoder.rand_noise[0, :, :n].numpy() for n in n_mel]
+    outs = F.flow_inference_docs(fe, dit, c["tokens"], c["prompts"], c["spk"], noise, finalize=fin,
+                                 streaming=mode == "streaming")
+    for i, o in enumerate(outs):
+        assert o.shape == c["out"][i].T.shape, (mode, i)
+        assert np.abs(o - c["out"][i].T).max() < 1e-4, (mode, i)
