@@ -23,6 +23,11 @@ float16 as ``apply_flashinfer`` deploys it, ``--ref-dtype bf16`` for bfloat16)
 on the same weights and inputs, when the reference has been installed offline
 into ``baseline/_ref``; otherwise it prints an ``unavailable`` line.  A
 comparison bar only: nothing of it is on the B200 path.
+
+``--flow`` (configs 2 and 3) times the whole flow inference instead -- token
+front end and the 10-step CFG ODE -- through ``flow_inference_batched`` (offline)
+or ``flow_inference_batched_streaming`` (streaming); with ``--impl
+reference-gpu`` the reference's own functions over ``FlashInferDiT``.
 """
 
 from __future__ import annotations
@@ -201,6 +206,130 @@ def cpu_oracle_rate(params, req_lengths, seed, budget_s: float):
     return L / dt, dt, L, cores, sample
 
 
+# ---------------------------------------------------------------------------- flow inference
+def flow_requests(config: str, seed: int):
+    """Token, prompt and speaker inputs of the flow workload of a config.  A
+    request of L mel frames carries L // 2 speech tokens (token_mel_ratio 2).
+    Offline (config 2): its prompt Mel is the first 40 % of its frames.
+    Streaming (config 3): the prompt part of L is the prompt Mel, every stream
+    is non-final with 3 lookahead tokens of context."""
+    import torch
+
+    req, chunk, _ = request_lengths(config)
+    rng = np.random.default_rng(500 + seed)
+    streaming = chunk > 0
+    tokens, prompts = [], []
+    if streaming:
+        prng = np.random.default_rng(2)
+        prompt_mel = prng.integers(100, 401, size=32)
+    for i, L in enumerate(req):
+        n_tok = L // 2
+        lp = int(prompt_mel[i]) if streaming else int(0.4 * 2 * n_tok)
+        lp = min(lp, 2 * n_tok)
+        tokens.append(rng.integers(0, 6561, size=n_tok + (3 if streaming else 0)).tolist())
+        prompts.append(torch.from_numpy(rng.standard_normal((1, lp, 80)).astype(np.float32)))
+    spk = torch.from_numpy(rng.standard_normal((len(req), 192)).astype(np.float32))
+    finalize = [False] * len(req) if streaming else None
+    mel = sum(2 * (len(t) - (3 if streaming else 0)) for t in tokens)
+    return tokens, prompts, spk, finalize, mel
+
+
+def flow_arm(args, impl: str):
+    """One JSON line: the whole flow inference (front end + 10-step CFG ODE) of a
+    config's requests, this build's device-packed flow or the reference's
+    flow_inference_batched[_streaming] over FlashInferDiT (flashinfer_flow.py:118-281)."""
+    import types
+
+    import torch
+
+    from fcv_b200.flow import B200Flow, flow_inference_batched, flow_inference_batched_streaming
+
+    req, chunk, seed = request_lengths(args.config)
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    tokens, prompts, spk, finalize, mel = flow_requests(args.config, seed)
+    streaming = finalize is not None
+    torch.manual_seed(seed)
+    ours = B200Flow(depth=22).eval()
+    base = {"metric": "flow mel-frames/s (front end + 10-step CFG ODE)", "unit": UNIT,
+            "config": {"workload": f"flow inference, {CONFIG_NAMES[args.config]}", "requests": len(req),
+                       "mel_frames": mel, "streaming": streaming}}
+    if impl == "b200":
+        flow = ours.to(device, torch.bfloat16)
+        flow.decoder.estimator.finalize_weights()
+        dtype = "bf16"
+
+        def run(p, s):
+            if streaming:
+                return flow_inference_batched_streaming(flow, tokens, p, s, finalize)
+            return flow_inference_batched(flow, tokens, p, s)
+    else:
+        ref_root = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref_root, "faster_cosyvoice")):
+            print(json.dumps({**base, "impl": "reference-gpu", "unavailable": "reference not installed in baseline/_ref"}))
+            return
+        for p in (ref_root, os.path.join(ROOT, "tests", "golden", "_xt_shim")):
+            if p not in sys.path:
+                sys.path.insert(0, p)
+        if "omegaconf" not in sys.modules:  # imported by flow.py for a default argument only
+            stub = types.ModuleType("omegaconf")
+            stub.DictConfig = dict
+            sys.modules["omegaconf"] = stub
+        from faster_cosyvoice.token2wav import flashinfer_flow as ref_flow
+        from faster_cosyvoice.token2wav.cosyvoice.flow.flow import CausalMaskedDiffWithDiT
+        from faster_cosyvoice.token2wav.cosyvoice.flow.flow_matching import CausalConditionalCFM
+        from faster_cosyvoice.token2wav.cosyvoice.transformer.upsample_encoder import PreLookaheadLayer
+        from faster_cosyvoice.token2wav.flashinfer_dit import FlashInferDiT
+
+        est = FlashInferDiT(device=device, static_chunk_size=50)
+        est.load_state_dict(ours.decoder.estimator.state_dict(), strict=False)
+        rdt = torch.float16 if args.ref_dtype == "fp16" else torch.bfloat16
+        est = est.to(device=device, dtype=rdt).eval()
+        est.finalize_weights()
+        cfm = types.SimpleNamespace(sigma_min=1e-6, solver="euler", t_scheduler="cosine", training_cfg_rate=0.2,
+                                    inference_cfg_rate=0.7, reg_loss_type="l1")
+        decoder = CausalConditionalCFM(in_channels=240, cfm_params=cfm, n_spks=1, spk_emb_dim=80, estimator=est)
+        flow = CausalMaskedDiffWithDiT(input_size=80, output_size=80, spk_embed_dim=192, output_type="mel",
+                                       vocab_size=6561, input_frame_rate=25, only_mask_loss=True, token_mel_ratio=2,
+                                       pre_lookahead_len=3,
+                                       pre_lookahead_layer=PreLookaheadLayer(in_channels=80, channels=1024,
+                                                                             pre_lookahead_len=3),
+                                       decoder=decoder)
+        front = {k: v for k, v in ours.state_dict().items() if not k.startswith("decoder.")}
+        flow.load_state_dict(front, strict=False)
+        flow = flow.to(device).to(rdt).eval()
+        dtype = "f16" if rdt == torch.float16 else "bf16"
+
+        def run(p, s):
+            if streaming:
+                return ref_flow.flow_inference_batched_streaming(flow, tokens, p, s, finalize)
+            return ref_flow.flow_inference_batched(flow, tokens, p, s)
+
+    p_dev = [p.to(device) for p in prompts]
+    s_dev = spk.to(device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        run(p_dev, s_dev)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(0) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            out = run(p_dev, s_dev)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    ms = [a.elapsed_time(b) for a, b in ev]
+    t = float(np.mean(ms))
+    line = {**base, "impl": impl if impl == "b200" else "reference-gpu", "value": mel / (t / 1000.0),
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t,
+            "higher_is_better": True, "dtype": dtype, "data": "synthetic (seeded tokens, prompts, speakers; "
+            "random-init 22-layer DiT and front end)", "step_ms_min": min(ms), "clocks": clocks.summary(),
+            "generated_frames": int(sum(o.shape[2] for o in out))}
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------------------- main
 def reference_gpu_arm(args, req_lengths, chunk, seed, cfg, strong):
     """The reference's FlashInferDiT (flashinfer_dit.py:98-543, loaded as apply_flashinfer does at
@@ -308,6 +437,9 @@ def main():
     ap.add_argument("--ref-dtype", default="fp16", choices=["fp16", "bf16"],
                     help="element type of the reference GPU estimator (--impl reference-gpu)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--flow", action="store_true",
+                    help="time the whole flow inference (front end + 10-step ODE) of --config 2 (offline) "
+                         "or 3 (streaming) instead of one estimator call")
     ap.add_argument("--requests", type=int, default=0,
                     help="use only the first R requests of the config (small cases for profiling)")
     args = ap.parse_args()
@@ -325,6 +457,13 @@ def main():
            "packed_rows": 2 * sum(req_lengths), "chunk": chunk, "seed": seed,
            "parallelism": f"dp{world} (request bins, no collective)",
            "l2": "working set (662 MB of weights per NFE) exceeds the 126 MB L2; L2 also flushed between steps"}
+
+    if args.flow:
+        if args.config not in ("2", "3"):
+            raise SystemExit("--flow runs configs 2 (offline) and 3 (streaming)")
+        if rank == 0 and args.impl != "reference":
+            flow_arm(args, args.impl)
+        return
 
     if args.impl == "reference":
         if rank != 0:
