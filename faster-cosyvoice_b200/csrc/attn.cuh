@@ -170,8 +170,8 @@ constexpr int kTcSoftmaxWarps = 4;
 
 __global__ void __launch_bounds__(kTcThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
-                   const int32_t* __restrict__ cu, const int2* __restrict__ tiles, int n_tiles, int chunk,
-                   bf16* __restrict__ out) {
+                   const int32_t* __restrict__ cu, const int2* __restrict__ tiles, int n_tiles,
+                   const int32_t* __restrict__ n_tiles_dev, int chunk, bf16* __restrict__ out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t s0 = smem_u32(smem);
@@ -192,7 +192,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_items = n_tiles * 16;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -234,6 +233,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const uint32_t tmem = *tmem_slot;
   griddep_wait();
   griddep_launch();
+  // work-list length: a launch parameter, or (CUDA-graph buckets) read from the
+  // device and clamped to the capacity the launch was sized for
+  const int n_items = (n_tiles_dev ? min(max(__ldg(n_tiles_dev), 0), n_tiles) : n_tiles) * 16;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -510,10 +512,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 // One thread per query row (128 per CTA), 32-key tiles in shared memory.
 __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__ qkv,
                                                        const int32_t* __restrict__ cu,
-                                                       const int2* __restrict__ tiles, int chunk,
+                                                       const int2* __restrict__ tiles,
+                                                       const int32_t* __restrict__ n_tiles_dev, int chunk,
                                                        float* __restrict__ out) {
   griddep_wait();
   griddep_launch();
+  if (n_tiles_dev && (int)blockIdx.x >= __ldg(n_tiles_dev)) return;  // grid sized for the capacity
   __shared__ float sK[32][64];
   __shared__ float sV[32][64];
   const int2 tl = tiles[blockIdx.x];

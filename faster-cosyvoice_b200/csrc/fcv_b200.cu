@@ -419,7 +419,7 @@ EpiParams make_epi(int epi, int M, int N, void* C, long ldc, const float* bias) 
 
 // ------------------------------------------------------------------ attention launch
 int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, const int32_t* tiles,
-                  int n_tiles, void* out, long n_rows, cudaStream_t s) {
+                  int n_tiles, void* out, long n_rows, cudaStream_t s, const int32_t* n_tiles_dev = nullptr) {
   if (n_tiles <= 0) return FCV_OK;
   dim3 grid(n_tiles, FCV_HEADS);
   const int2* t2 = reinterpret_cast<const int2*>(tiles);
@@ -439,11 +439,11 @@ int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, cons
     const int ctas = std::min(items, 2 * num_sms());  // persistent, 2 CTAs per SM
     // Plain stream order: the work items are dealt to CTAs by index, and CTAs that
     // start early on the SMs freed first by the previous kernel would unbalance it.
-    const int rc = launch_k_opt(false, "attn_tc_kernel", attn_tc_kernel, dim3(ctas), dim3(kTcThreads), kTcSmemBytes, s, tq, tkv, cu, t2, n_tiles, chunk,
+    const int rc = launch_k_opt(false, "attn_tc_kernel", attn_tc_kernel, dim3(ctas), dim3(kTcThreads), kTcSmemBytes, s, tq, tkv, cu, t2, n_tiles, n_tiles_dev, chunk,
                                  static_cast<bf16*>(out));
     if (rc != FCV_OK) return rc;
   } else {
-    FCV_LAUNCH("attn_f32_kernel", attn_f32_kernel, dim3(grid), dim3(128), 0, s, static_cast<const float*>(qkv), cu, t2, chunk,
+    FCV_LAUNCH("attn_f32_kernel", attn_f32_kernel, dim3(grid), dim3(128), 0, s, static_cast<const float*>(qkv), cu, t2, n_tiles_dev, chunk,
                                          static_cast<float*>(out));
   }
   return FCV_OK;
@@ -627,7 +627,7 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     {
       ProfScope ps(FCV_CAT_ATTENTION, s);
       FCV_TRY(run_attention(ws.qkv, dtype, bt->cu_seqlens, bt->chunk, bt->attn_tiles, bt->n_attn_tiles,
-                            ws.attn, N, s));
+                            ws.attn, N, s, bt->n_attn_tiles_dev));
     }
     GemmCall o{};
     o.A = ws.attn; o.lda = 1024; o.a_rows = N; o.M = N; o.N = 1024; o.K = 1024;

@@ -124,6 +124,7 @@ class DitBatch(ctypes.Structure):
         ("out", ctypes.c_void_p),
         ("out_f32", ctypes.c_int),
         ("packed", ctypes.c_int),
+        ("n_attn_tiles_dev", ctypes.c_void_p),
     ]
 
 

@@ -148,7 +148,7 @@ class B200DiT(nn.Module):
     def __init__(self, dim: int = DIM, depth: int = 22, heads: int = HEADS, dim_head: int = DIM_HEAD,
                  ff_mult: int = 2, mel_dim: int = MEL, mu_dim: int = MEL, spk_dim: int = MEL,
                  out_channels: int = MEL, static_chunk_size: int = 50, dropout: float = 0.1,
-                 use_cuda_graph: bool = False):
+                 use_cuda_graph: bool = False, graph_buckets: Sequence[int] | None = None):
         super().__init__()
         if (dim, heads, dim_head, ff_mult, mel_dim, mu_dim, spk_dim) != (DIM, HEADS, DIM_HEAD, 2, MEL, MEL, MEL):
             raise ValueError("the kernels implement the CosyVoice3 geometry "
@@ -170,6 +170,10 @@ class B200DiT(nn.Module):
         self.proj_out = nn.Linear(dim, mel_dim)
 
         self.use_cuda_graph = use_cuda_graph
+        # row capacities of the bucketed graphs (None: one graph per exact layout)
+        self.graph_buckets = tuple(sorted({int(b) for b in graph_buckets})) if graph_buckets else None
+        self._bucket_graphs: OrderedDict = OrderedDict()
+        self.bucket_captures = 0
         self._finalized = False
         self._derived: dict[str, torch.Tensor] = {}
         self._graphs: OrderedDict = OrderedDict()
@@ -423,17 +427,98 @@ class B200DiT(nn.Module):
             if t.ndim == 0:
                 t = t.repeat(B)
             t = t.reshape(B).contiguous()
+            if self.use_cuda_graph and self.graph_buckets:
+                m = mask.to(device=dev, dtype=dt).contiguous()
+                lengths_dev = torch.empty(B, dtype=torch.int32, device=dev)
+                call("fcv_mask_lengths", m.data_ptr(), _dtype_code(dt), B, T, lengths_dev.data_ptr(), _stream(dev))
+                lengths = lengths_dev.cpu().tolist()
+                y = self.forward_bucketed(lengths, x, mu, t, spks, cond, streaming)
+                if y is not None:
+                    return y
+                layout = self.prepare_layout(lengths, T, streaming, dev, lengths_dev)
+                return self.forward_layout(layout, x, mu, t, spks, cond)
             layout = self.layout_from_mask(mask.to(dev), streaming)
             return self.forward_layout(layout, x, mu, t, spks, cond, graph=self.use_cuda_graph)
 
+    # ------------------------------------------------------------------ bucketed graphs
+    def bucket_for(self, lengths: Sequence[int]) -> tuple[int, int] | None:
+        """(row capacity, document capacity) of the graph serving this batch, or
+        None when no bucket holds it (or a document exceeds the RoPE table)."""
+        if not self.graph_buckets:
+            return None
+        N = sum(lengths)
+        if max(lengths, default=0) > ROPE_TABLE_LEN:
+            return None
+        rows = next((b for b in self.graph_buckets if b >= N), None)
+        if rows is None:
+            return None
+        docs = 2
+        while docs < len(lengths):
+            docs *= 2
+        return rows, docs
 
-def apply_b200(model, dtype: torch.dtype = torch.bfloat16, enable_cuda_graph: bool = False):
+    def forward_bucketed(self, lengths: Sequence[int], x, mu, t, spks, cond, streaming: bool,
+                         out: torch.Tensor | None = None) -> torch.Tensor | None:
+        """Replay the bucket graph that holds this batch (the packed counterpart of
+        ``_forward_graph_bucketed`` / ``_forward_graph_bucketed_stream``,
+        ``flashinfer_dit.py:742-826``): one captured estimator call serves every
+        composition of up to ``docs`` documents and ``rows`` packed rows, so a new
+        composition costs a few copies, not a capture.  x, mu, cond are padded
+        (B, 80, T) of the weight dtype on the module's device.  Returns the
+        (B, 80, T) flow field (padding frames zero), or None when no bucket holds
+        the batch."""
+        key = self.bucket_for(lengths)
+        if key is None:
+            return None
+        chunk = self._chunk_size if streaming else 0
+        gkey = key + (chunk,)
+        g = self._bucket_graphs.get(gkey)
+        if g is None:
+            if len(self._bucket_graphs) >= 16:
+                self._bucket_graphs.popitem(last=False)
+            g = _BucketGraph(self, key[0], key[1], chunk, x.device)
+            self._bucket_graphs[gkey] = g
+            self.bucket_captures += 1
+        else:
+            self._bucket_graphs.move_to_end(gkey)
+        return g.run(lengths, x, mu, t, spks, cond, out)
+
+
+def graph_row_buckets(cuda_graph_buckets: Sequence[float] | None = None,
+                      stream_graph_buckets: Sequence[int] | None = None) -> tuple[int, ...] | None:
+    """Row capacities for the bucketed graphs from the reference's presets:
+    offline buckets in seconds (50 Mel frames per second,
+    ``flashinfer_dit.py:154-158``), streaming buckets in frames; each holds one
+    CFG pair, so a bucket of F frames is 2F packed rows."""
+    rows = set()
+    for s in cuda_graph_buckets or ():
+        rows.add(2 * round(float(s) * 50))
+    for f in stream_graph_buckets or ():
+        rows.add(2 * int(f))
+    return tuple(sorted(rows)) or None
+
+
+# Default row ladder for packed batches: steps of 512 rows to 4096, then 1.25x.
+DEFAULT_GRAPH_BUCKETS = (512, 1024, 1536, 2048, 2560, 3072, 3584, 4096, 5120, 6144, 7168, 8192, 10240,
+                         12288, 14336, 16384, 20480, 24576, 28672, 32768)
+
+
+def apply_b200(model, dtype: torch.dtype = torch.bfloat16, enable_cuda_graph: bool = False,
+               cuda_graph_buckets: Sequence[float] | None = None,
+               stream_graph_buckets: Sequence[int] | None = None):
     """Replace a Token2Wav model's estimator with :class:`B200DiT`
-    (mirror of ``apply_flashinfer``, ``flashinfer_dit.py:951-988``)."""
+    (mirror of ``apply_flashinfer``, ``flashinfer_dit.py:951-988``).  With
+    ``enable_cuda_graph`` every call replays a bucketed graph: the reference's
+    bucket presets (seconds offline, frames streaming) become row capacities,
+    else :data:`DEFAULT_GRAPH_BUCKETS`."""
     reference = model.flow.decoder.estimator
     device = next(reference.parameters()).device
+    buckets = None
+    if enable_cuda_graph:
+        buckets = graph_row_buckets(cuda_graph_buckets, stream_graph_buckets) or DEFAULT_GRAPH_BUCKETS
     est = B200DiT(static_chunk_size=getattr(reference, "static_chunk_size", 50),
-                  depth=len(reference.transformer_blocks), use_cuda_graph=enable_cuda_graph)
+                  depth=len(reference.transformer_blocks), use_cuda_graph=enable_cuda_graph,
+                  graph_buckets=buckets)
     missing, unexpected = est.load_state_dict(reference.state_dict(), strict=False)
     missing = [k for k in missing if "rope" not in k and "rotary" not in k]
     if missing or unexpected:
@@ -442,3 +527,126 @@ def apply_b200(model, dtype: torch.dtype = torch.bfloat16, enable_cuda_graph: bo
     est.finalize_weights()
     model.flow.decoder.estimator = est
     return model
+
+
+class _BucketGraph:
+    """One estimator call captured for ``rows`` packed rows and ``docs`` real
+    document slots, serving every batch that fits.
+
+    The graph holds the packed layout computation (``fcv_pack_layout`` from a
+    device lengths buffer) and the packed-row estimator call.  Per replay the
+    host uploads one small block -- lengths, cu_seqlens, the attention work
+    list and its length -- and packs the inputs into the static rows.  Rows
+    past the batch belong to filler documents (at most ``ROPE_TABLE_LEN`` rows
+    each, after the unused zero-length slots): every kernel but attention is
+    row-local or document-local, so they never touch real rows, and the work
+    list leaves them out of attention.  Results are bit-identical to the eager
+    call (no kernel's per-element reduction order depends on the row count)."""
+
+    def __init__(self, model: B200DiT, rows: int, docs: int, chunk: int, device: torch.device):
+        self.model, self.rows, self.docs, self.chunk, self.device = model, rows, docs, chunk, device
+        dt = model.weight_dtype
+        self.n_fill = max(1, -(-rows // ROPE_TABLE_LEN))
+        self.n_docs = docs + self.n_fill
+        self.tile_cap = -(-rows // 128) + docs
+        nd = self.n_docs
+        # device block: lengths (nd) | cu (nd + 1) | n_tiles (1) | pad | tiles (2 * cap), int32
+        self.off_cu = nd
+        self.off_nt = 2 * nd + 1
+        self.off_tiles = (self.off_nt + 2) // 2 * 2
+        size = self.off_tiles + 2 * self.tile_cap
+        self.meta = torch.zeros(size, dtype=torch.int32, device=device)
+        self.host = torch.zeros(size, dtype=torch.int32).pin_memory()
+        self.copied = torch.cuda.Event()
+        self.x = torch.zeros(rows, MEL, dtype=dt, device=device)
+        self.mu = torch.zeros_like(self.x)
+        self.cond = torch.zeros_like(self.x)
+        self.spks = torch.zeros(nd, MEL, dtype=dt, device=device)
+        self.t = torch.zeros(nd, dtype=dt, device=device)
+        self.out = torch.zeros(rows, MEL, dtype=dt, device=device)
+        self.gather = torch.empty(rows, dtype=torch.int64, device=device)
+        self.doc_ids = torch.empty(rows, dtype=torch.int32, device=device)
+        self.positions = torch.empty(rows, dtype=torch.int32, device=device)
+        self.cu = torch.empty(nd + 1, dtype=torch.int32, device=device)
+        self.gap_rows = torch.empty(rows + 30 * (nd + 1), dtype=torch.int32, device=device)
+        need = int(lib().fcv_dit_workspace_bytes(rows, nd, model.depth, _dtype_code(dt)))
+        # zeroed once: rows no kernel writes for a batch stay finite
+        self.workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
+        self.batch = DitBatch()
+        b = self.batch
+        b.B, b.T, b.N, b.max_len, b.chunk = nd, rows, rows, min(rows, ROPE_TABLE_LEN), chunk
+        b.x, b.mu, b.cond, b.spks, b.t = (self.x.data_ptr(), self.mu.data_ptr(), self.cond.data_ptr(),
+                                          self.spks.data_ptr(), self.t.data_ptr())
+        b.cu_seqlens, b.doc_ids, b.positions = self.cu.data_ptr(), self.doc_ids.data_ptr(), self.positions.data_ptr()
+        b.gap_rows = self.gap_rows.data_ptr()
+        b.attn_tiles = self.meta.data_ptr() + 4 * self.off_tiles
+        b.n_attn_tiles = self.tile_cap
+        b.n_attn_tiles_dev = self.meta.data_ptr() + 4 * self.off_nt
+        b.out, b.out_f32, b.packed = self.out.data_ptr(), 0, 1
+        self._fill_host([])  # an empty batch: everything is filler
+        self.meta.copy_(self.host)
+        stream = _stream(device)
+        self._body(stream)  # first launches (function attributes) outside the capture
+        torch.cuda.synchronize(device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._body(_stream(device))
+
+    def _body(self, stream: int) -> None:
+        call("fcv_pack_layout", self.meta.data_ptr(), self.n_docs, self.rows, self.rows, self.gather.data_ptr(),
+             self.doc_ids.data_ptr(), self.positions.data_ptr(), self.cu.data_ptr(), self.gap_rows.data_ptr(),
+             stream)
+        call("fcv_dit_forward", ctypes.byref(self.model.weights_struct()), ctypes.byref(self.batch),
+             self.workspace.data_ptr(), self.workspace.numel(), stream)
+
+    def _fill_host(self, lengths: Sequence[int]) -> int:
+        """Lengths (real, zero slots, filler), cu_seqlens and the work list into
+        the pinned block; returns the real row count."""
+        B, N = len(lengths), sum(lengths)
+        fill, rest = [], self.rows - N
+        for _ in range(self.n_fill):
+            f = min(rest, ROPE_TABLE_LEN)
+            fill.append(f)
+            rest -= f
+        ext = list(lengths) + [0] * (self.docs - B) + fill
+        h = self.host
+        h[:self.n_docs] = torch.tensor(ext, dtype=torch.int32)
+        cu = [0]
+        for v in ext:
+            cu.append(cu[-1] + v)
+        h[self.off_cu:self.off_cu + self.n_docs + 1] = torch.tensor(cu, dtype=torch.int32)
+        n_tiles = 0
+        if B:
+            cap = sum((L + 127) // 128 for L in lengths)
+            buf = (ctypes.c_int32 * (2 * max(cap, 1)))()
+            lens = (ctypes.c_int32 * B)(*lengths)
+            n_tiles = call("fcv_attn_tiles", ctypes.addressof(lens), B, self.chunk, ctypes.addressof(buf), cap)
+            if n_tiles:
+                h[self.off_tiles:self.off_tiles + 2 * n_tiles] = torch.frombuffer(buf, dtype=torch.int32)[:2 * n_tiles]
+        h[self.off_nt] = n_tiles
+        return N
+
+    def run(self, lengths: Sequence[int], x, mu, t, spks, cond, out: torch.Tensor | None = None) -> torch.Tensor:
+        lengths = [int(v) for v in lengths]
+        B, T = len(lengths), int(x.shape[2])
+        dev, stream = self.device, _stream(self.device)
+        self.copied.synchronize()  # the previous upload has left the pinned block
+        N = self._fill_host(lengths)
+        self.meta.copy_(self.host, non_blocking=True)
+        self.copied.record()
+        cu_real = self.meta[self.off_cu:self.off_cu + B + 1]
+        dcode = _dtype_code(self.model.weight_dtype)
+        max_len = max(lengths, default=0)
+        for src, dst in ((x, self.x), (mu, self.mu), (cond, self.cond)):
+            call("fcv_pack_rows", src.data_ptr(), dcode, MEL * T, T, cu_real.data_ptr(), B, max_len,
+                 dst.data_ptr(), dcode, stream)
+        self.spks[:B].copy_(spks)
+        self.spks[B:].zero_()
+        self.t[:B].copy_(t)
+        self.t[B:].zero_()
+        self.graph.replay()
+        if out is None:
+            out = torch.empty(B, MEL, T, dtype=self.model.weight_dtype, device=dev)
+        # rows -> (B, 80, T), padding frames written as zeros
+        call("fcv_unpack_output", self.out.data_ptr(), dcode, cu_real.data_ptr(), B, T, N, out.data_ptr(), stream)
+        return out

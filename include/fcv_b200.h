@@ -135,6 +135,12 @@ typedef struct fcv_dit_batch {
                       * padded (B, 80, T) layout above.  The packed form
                       * serves the device-packed flow (flashinfer_flow.py
                       * 118-281 without its padded intermediate tensors).   */
+  const int32_t* n_attn_tiles_dev; /* optional (device int): the work list's
+                      * length, read on the device at run time; n_attn_tiles
+                      * is then only its capacity.  Lets one captured CUDA
+                      * graph serve every batch composition of a bucket
+                      * (the packed counterpart of the reference's graph
+                      * buckets, flashinfer_dit.py:742-826).               */
 } fcv_dit_batch;
 
 /* Layout ------------------------------------------------------------------ */

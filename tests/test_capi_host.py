@@ -149,3 +149,13 @@ def test_layout_cache_fifo_and_no_replan(monkeypatch, lib):
     assert dit.prepare_layout([100, 100], 100, True, cpu) is not a  # evicted, re-planned
     with pytest.raises(ValueError):
         dit.prepare_layout([5, 300], 100, True, cpu)
+
+
+def test_graph_bucket_presets_become_row_capacities():
+    """The reference's presets (seconds offline at 50 frames/s, frames streaming;
+    config/settings.py:9-10) hold one CFG pair: F frames -> 2F packed rows."""
+    from fcv_b200.model import DEFAULT_GRAPH_BUCKETS, graph_row_buckets
+
+    assert graph_row_buckets((8.0, 12.0), (512, 640)) == (800, 1024, 1200, 1280)
+    assert graph_row_buckets(None, None) is None
+    assert list(DEFAULT_GRAPH_BUCKETS) == sorted(DEFAULT_GRAPH_BUCKETS)

@@ -217,3 +217,34 @@ def test_cuda_graph_path_matches_eager_and_follows_new_inputs():
         model.use_cuda_graph = False
         e2 = model(x, mask, mu, t, spks, cond, streaming=True)
     assert torch.equal(g2, e2) and not torch.equal(g2, g1)
+
+
+@pytest.mark.parametrize("streaming", [False, True])
+def test_bucketed_graph_serves_many_compositions_bit_exact(streaming):
+    """One captured graph per (row bucket, document bucket, mask) serves every
+    batch composition that fits it (the packed counterpart of the reference's
+    graph buckets, flashinfer_dit.py:742-826); results equal the eager call bit
+    for bit, and batches beyond the largest bucket run eagerly."""
+    model = _model(5, 2, torch.bfloat16)
+    model.graph_buckets = (512, 1024)
+    rng = np.random.default_rng(17)
+    compositions = [[150, 77, 150, 77], [100, 20, 100, 20], [300, 300], [33, 1, 200, 33, 1, 200],
+                    [1, 1], [700, 700]]
+    for lengths in compositions:
+        B, T = len(lengths), max(lengths) + 3
+        x, mu, cond = (torch.tensor(rng.standard_normal((B, 80, T)), device=DEV, dtype=torch.bfloat16)
+                       for _ in range(3))
+        spks = torch.tensor(rng.standard_normal((B, 80)), device=DEV, dtype=torch.bfloat16)
+        t = torch.tensor(rng.uniform(size=B), device=DEV, dtype=torch.bfloat16)
+        mask = torch.zeros(B, 1, T, device=DEV, dtype=torch.bfloat16)
+        for b, L in enumerate(lengths):
+            mask[b, 0, :L] = 1
+        with torch.inference_mode():
+            model.use_cuda_graph = False
+            ref = model(x, mask, mu, t, spks, cond, streaming=streaming)
+            model.use_cuda_graph = True
+            got = model(x, mask, mu, t, spks, cond, streaming=streaming)
+        assert torch.equal(got, ref), (lengths, streaming)
+    # (512 rows, 4 docs), (1024, 2), (512, 8), (512, 2); [700, 700] exceeds every bucket
+    assert model.bucket_captures == 4
+    assert len(model._bucket_graphs) == 4
