@@ -24,6 +24,11 @@ on the same weights and inputs, when the reference has been installed offline
 into ``baseline/_ref``; otherwise it prints an ``unavailable`` line.  A
 comparison bar only: nothing of it is on the B200 path.
 
+``--latency`` times one estimator call for a single CFG pair (B = 2, 200 / 400 /
+800 frames), eager and through the bucketed CUDA graphs, for this build or (with
+``--impl reference-gpu``) the reference's ``FlashInferDiT`` with and without its
+own graph buckets.
+
 ``--flow`` (configs 2 and 3) times the whole flow inference instead -- token
 front end and the 10-step CFG ODE -- through ``flow_inference_batched`` (offline)
 or ``flow_inference_batched_streaming`` (streaming); with ``--impl
@@ -330,6 +335,98 @@ def flow_arm(args, impl: str):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------- single-request latency
+def latency_arm(args, impl: str):
+    """One JSON line: latency of one estimator call for one CFG pair (B = 2),
+    the case the reference's CUDA-graph buckets serve (flashinfer_dit.py:742-826):
+    eager and graph-bucketed, through the module's forward on device-resident
+    inputs.  ``wall`` = host time from call to synchronised result (launch cost
+    included), ``device`` = CUDA-event time on the stream."""
+    import torch
+
+    from fcv_b200.model import DEFAULT_GRAPH_BUCKETS, B200DiT
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    streaming = args.config == "3"
+    torch.manual_seed(1)
+    ours = B200DiT(depth=22).eval()
+    if impl == "b200":
+        model = ours.to(device, torch.bfloat16)
+        model.finalize_weights()
+        model.graph_buckets = DEFAULT_GRAPH_BUCKETS
+        dt = torch.bfloat16
+
+        def set_graph(on):
+            model.use_cuda_graph = on
+    else:
+        ref_root = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref_root, "faster_cosyvoice")):
+            print(json.dumps({"impl": "reference-gpu", "unavailable": "reference not installed in baseline/_ref"}))
+            return
+        for p in (ref_root, os.path.join(ROOT, "tests", "golden", "_xt_shim")):
+            if p not in sys.path:
+                sys.path.insert(0, p)
+        from faster_cosyvoice.token2wav.flashinfer_dit import FlashInferDiT
+
+        dt = torch.float16 if args.ref_dtype == "fp16" else torch.bfloat16
+        models = {}
+        for on in (False, True):
+            # offline presets in seconds, streaming presets in frames (config/settings.py:9-10)
+            m = FlashInferDiT(device=device, static_chunk_size=50, enable_cuda_graph=on and not streaming,
+                              cuda_graph_buckets=(8.0, 12.0, 16.0, 20.0, 24.0) if on and not streaming else None,
+                              stream_graph_buckets=(512, 640, 768, 896, 1024, 1280) if on and streaming else None)
+            m.load_state_dict(ours.state_dict(), strict=False)
+            m = m.to(device=device, dtype=dt).eval()
+            m.finalize_weights()
+            models[on] = m
+        holder = {}
+
+        def set_graph(on):
+            holder["m"] = models[on]
+
+        def model(*a, **k):
+            return holder["m"](*a, **k)
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    results = {}
+    for L in (200, 400, 800):
+        g = torch.Generator().manual_seed(L)
+        x = torch.randn(1, 80, L, generator=g).repeat(2, 1, 1)
+        mu = torch.cat([torch.randn(1, 80, L, generator=g), torch.zeros(1, 80, L)])
+        cond = torch.cat([torch.randn(1, 80, L, generator=g), torch.zeros(1, 80, L)])
+        spks = torch.cat([torch.randn(1, 80, generator=g), torch.zeros(1, 80)])
+        t = torch.rand(1, generator=g).repeat(2)
+        inp = [v.to(device, dt).contiguous() for v in (x, torch.ones(2, 1, L), mu, t, spks, cond)]
+        res = {}
+        for on in (False, True):
+            set_graph(on)
+            with torch.inference_mode():
+                for _ in range(args.warmup):
+                    model(*inp, streaming=streaming)
+                torch.cuda.synchronize()
+                wall, dev_ms = [], []
+                for _ in range(args.steps):
+                    flush.zero_()
+                    torch.cuda.synchronize()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    t0 = time.perf_counter()
+                    e0.record(stream)
+                    model(*inp, streaming=streaming)
+                    e1.record(stream)
+                    torch.cuda.synchronize()
+                    wall.append(1000 * (time.perf_counter() - t0))
+                    dev_ms.append(e0.elapsed_time(e1))
+            res["graph" if on else "eager"] = {"wall_ms": float(statistics.median(wall)),
+                                               "device_ms": float(statistics.median(dev_ms))}
+        results[f"L={L}"] = res
+    print(json.dumps({"metric": "estimator call latency, one CFG pair (B=2)", "unit": "ms",
+                      "higher_is_better": False, "impl": impl, "dtype": "bf16" if dt == torch.bfloat16 else "f16",
+                      "streaming": streaming, "steps": args.steps, "warmup": args.warmup,
+                      "results": results}), flush=True)
+
+
 # ---------------------------------------------------------------------------- main
 def reference_gpu_arm(args, req_lengths, chunk, seed, cfg, strong):
     """The reference's FlashInferDiT (flashinfer_dit.py:98-543, loaded as apply_flashinfer does at
@@ -440,6 +537,9 @@ def main():
     ap.add_argument("--flow", action="store_true",
                     help="time the whole flow inference (front end + 10-step ODE) of --config 2 (offline) "
                          "or 3 (streaming) instead of one estimator call")
+    ap.add_argument("--latency", action="store_true",
+                    help="latency of one estimator call for one CFG pair, eager and graph-bucketed "
+                         "(--config 3 for the streaming mask)")
     ap.add_argument("--requests", type=int, default=0,
                     help="use only the first R requests of the config (small cases for profiling)")
     args = ap.parse_args()
@@ -457,6 +557,11 @@ def main():
            "packed_rows": 2 * sum(req_lengths), "chunk": chunk, "seed": seed,
            "parallelism": f"dp{world} (request bins, no collective)",
            "l2": "working set (662 MB of weights per NFE) exceeds the 126 MB L2; L2 also flushed between steps"}
+
+    if args.latency:
+        if rank == 0 and args.impl != "reference":
+            latency_arm(args, args.impl)
+        return
 
     if args.flow:
         if args.config not in ("2", "3"):
