@@ -719,7 +719,7 @@ def main():
     def attn_layers():
         for i in range(22):
             ops.ragged_attention(gO, layout.cu_seqlens, layout.attn_tiles, layout.n_attn_tiles, layout.chunk,
-                                 layout.max_len)
+                                 layout.max_len, layout.attn_sched, layout.attn_ctas)
 
     def time_graph(fn, reps):
         fn()  # eager warm-up (first-launch attributes)

@@ -127,36 +127,63 @@ __device__ __forceinline__ AttnItem attn_item_at(const int32_t* cu, int2 tl, int
   return a;
 }
 
-// A CTA's items it, it + stride, ... with the descriptor lookups run ahead: while
-// item `it` is processed, the item after it is already resolved (its cu loads in
-// flight) and the work-list entry of the one after that is loading, so no role
-// waits on a dependent global load at an item boundary.
+// A CTA's items with the descriptor lookups run ahead: while item `it` is
+// processed, the item after it is already resolved (its cu loads in flight)
+// and the work-list entry of the one after that is loading, so no role waits
+// on a dependent global load at an item boundary.  Items come either round
+// robin (positions first, first + stride, ... of the work list) or from a
+// host-built schedule: positions [beg, end) of a per-CTA item list.
 struct ItemFeed {
   const int32_t* cu;
   const int2* tiles;
-  int chunk, n_items, stride, it;
+  const int32_t* list;  // schedule items, or null for round robin
+  int chunk, end, stride, pos, it, it1, it2;
   AttnItem cur, nxt;
   int2 tl2;
-  __device__ __forceinline__ bool init(const int32_t* cu_, const int2* tiles_, int chunk_, int n_items_,
-                                       int first, int stride_) {
+  __device__ __forceinline__ int item_at(int p) const { return list ? __ldg(list + p) : p; }
+  // Round robin when sched is null; else sched = [offsets (gridDim + 1) | items].
+  __device__ __forceinline__ bool init(const int32_t* cu_, const int2* tiles_, int chunk_, int n_items,
+                                       const int32_t* sched) {
     cu = cu_;
     tiles = tiles_;
     chunk = chunk_;
-    n_items = n_items_;
-    stride = stride_;
-    it = first;
-    if (it >= n_items) return false;
+    if (sched) {
+      list = sched + gridDim.x + 1;
+      pos = __ldg(sched + blockIdx.x);
+      end = __ldg(sched + blockIdx.x + 1);
+      stride = 1;
+    } else {
+      list = nullptr;
+      pos = blockIdx.x;
+      end = n_items;
+      stride = gridDim.x;
+    }
+    if (pos >= end) return false;
+    it = item_at(pos);
     cur = attn_item(cu, tiles, chunk, it);
-    if (it + stride < n_items) nxt = attn_item(cu, tiles, chunk, it + stride);
-    if (it + 2 * stride < n_items) tl2 = tiles[(it + 2 * stride) >> 4];
+    if (pos + stride < end) {
+      it1 = item_at(pos + stride);
+      nxt = attn_item(cu, tiles, chunk, it1);
+    }
+    if (pos + 2 * stride < end) {
+      it2 = item_at(pos + 2 * stride);
+      tl2 = tiles[it2 >> 4];
+    }
     return true;
   }
   __device__ __forceinline__ bool advance() {
-    it += stride;
-    if (it >= n_items) return false;
+    pos += stride;
+    if (pos >= end) return false;
+    it = it1;
     cur = nxt;
-    if (it + stride < n_items) nxt = attn_item_at(cu, tl2, chunk, it + stride);
-    if (it + 2 * stride < n_items) tl2 = tiles[(it + 2 * stride) >> 4];
+    if (pos + stride < end) {
+      it1 = it2;
+      nxt = attn_item_at(cu, tl2, chunk, it1);
+    }
+    if (pos + 2 * stride < end) {
+      it2 = item_at(pos + 2 * stride);
+      tl2 = tiles[it2 >> 4];
+    }
     return true;
   }
 };
@@ -171,7 +198,8 @@ constexpr int kTcSoftmaxWarps = 4;
 __global__ void __launch_bounds__(kTcThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                    const int32_t* __restrict__ cu, const int2* __restrict__ tiles, int n_tiles,
-                   const int32_t* __restrict__ n_tiles_dev, int chunk, bf16* __restrict__ out) {
+                   const int32_t* __restrict__ n_tiles_dev, const int32_t* __restrict__ sched, int chunk,
+                   bf16* __restrict__ out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t s0 = smem_u32(smem);
@@ -243,7 +271,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       int g = 0, i = 0;
       bool ok = true;
       ItemFeed feed;
-      for (bool have = feed.init(cu, tiles, chunk, n_items, blockIdx.x, gridDim.x); have && ok;
+      for (bool have = feed.init(cu, tiles, chunk, n_items, sched); have && ok;
            have = feed.advance(), ++i) {
         const AttnItem a = feed.cur;
         const int qb = i & 1;
@@ -276,10 +304,10 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       // follows the S cursor's item
       ItemFeed feed;
       auto first = [&](Cur& c) -> bool {
-        c.it = blockIdx.x;
         c.i = 0;
         c.j = 0;
-        if (!feed.init(cu, tiles, chunk, n_items, blockIdx.x, gridDim.x)) return false;
+        if (!feed.init(cu, tiles, chunk, n_items, sched)) return false;
+        c.it = feed.it;
         c.n_kv = feed.cur.n_kv;
         return true;
       };
@@ -397,7 +425,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       return true;
     };
     ItemFeed feed;
-    for (bool have = feed.init(cu, tiles, chunk, n_items, blockIdx.x, gridDim.x); have && ok;
+    for (bool have = feed.init(cu, tiles, chunk, n_items, sched); have && ok;
          have = feed.advance(), ++i) {
       const AttnItem a = feed.cur;
       const int qa = a.q0 + r;

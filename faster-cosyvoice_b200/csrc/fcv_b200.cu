@@ -419,7 +419,8 @@ EpiParams make_epi(int epi, int M, int N, void* C, long ldc, const float* bias) 
 
 // ------------------------------------------------------------------ attention launch
 int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, const int32_t* tiles,
-                  int n_tiles, void* out, long n_rows, cudaStream_t s, const int32_t* n_tiles_dev = nullptr) {
+                  int n_tiles, void* out, long n_rows, cudaStream_t s, const int32_t* n_tiles_dev = nullptr,
+                  const int32_t* sched = nullptr, int sched_ctas = 0) {
   if (n_tiles <= 0) return FCV_OK;
   dim3 grid(n_tiles, FCV_HEADS);
   const int2* t2 = reinterpret_cast<const int2*>(tiles);
@@ -436,10 +437,13 @@ int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, cons
       attr[dev & 63] = true;
     }
     const int items = n_tiles * FCV_HEADS;
-    const int ctas = std::min(items, 2 * num_sms());  // persistent, 2 CTAs per SM
+    // persistent, 2 CTAs per SM; a host schedule fixes the CTA count it was built for
+    const int ctas = sched ? sched_ctas : std::min(items, 2 * num_sms());
+    if (sched && (sched_ctas < 1 || sched_ctas > 2 * num_sms()))
+      return fail(FCV_EINVAL, "attention schedule built for %d CTAs", sched_ctas);
     // Plain stream order: the work items are dealt to CTAs by index, and CTAs that
     // start early on the SMs freed first by the previous kernel would unbalance it.
-    const int rc = launch_k_opt(false, "attn_tc_kernel", attn_tc_kernel, dim3(ctas), dim3(kTcThreads), kTcSmemBytes, s, tq, tkv, cu, t2, n_tiles, n_tiles_dev, chunk,
+    const int rc = launch_k_opt(false, "attn_tc_kernel", attn_tc_kernel, dim3(ctas), dim3(kTcThreads), kTcSmemBytes, s, tq, tkv, cu, t2, n_tiles, n_tiles_dev, sched, chunk,
                                  static_cast<bf16*>(out));
     if (rc != FCV_OK) return rc;
   } else {
@@ -627,7 +631,7 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     {
       ProfScope ps(FCV_CAT_ATTENTION, s);
       FCV_TRY(run_attention(ws.qkv, dtype, bt->cu_seqlens, bt->chunk, bt->attn_tiles, bt->n_attn_tiles,
-                            ws.attn, N, s, bt->n_attn_tiles_dev));
+                            ws.attn, N, s, bt->n_attn_tiles_dev, bt->attn_sched, bt->attn_sched_ctas));
     }
     GemmCall o{};
     o.A = ws.attn; o.lda = 1024; o.a_rows = N; o.M = N; o.N = 1024; o.K = 1024;
@@ -854,14 +858,15 @@ int fcv_gemm(const void* A, const void* W, const float* bias, int M, int Nout, i
 }
 
 int fcv_attention(const void* qkv, int dtype, const int32_t* cu_seqlens, int B, int N, int max_len, int chunk,
-                  const int32_t* tiles, int n_tiles, void* out, void* stream) {
+                  const int32_t* tiles, int n_tiles, const int32_t* sched, int sched_ctas, void* out, void* stream) {
   (void)B;
   (void)max_len;
   if (!qkv || !cu_seqlens || !out || (n_tiles > 0 && !tiles) || chunk < 0 || N < 0)
     return fail(FCV_EINVAL, "fcv_attention: bad arguments");
   if (!valid_dtype(dtype)) return fail(FCV_EINVAL, "fcv_attention: bad dtype");
   if (N == 0) return FCV_OK;
-  return run_attention(qkv, dtype, cu_seqlens, chunk, tiles, n_tiles, out, N, as_stream(stream));
+  return run_attention(qkv, dtype, cu_seqlens, chunk, tiles, n_tiles, out, N, as_stream(stream), nullptr, sched,
+                       sched_ctas);
 }
 
 int fcv_attn_tiles(const int32_t* lengths_host, int B, int chunk, int32_t* tiles, int cap) {
@@ -888,6 +893,56 @@ int fcv_attn_tiles(const int32_t* lengths_host, int B, int chunk, int32_t* tiles
     tiles[2 * i + 1] = items[i].q0;
   }
   return (int)items.size();
+}
+
+int fcv_attn_ctas(int n_tiles) {
+  if (n_tiles < 0) return fail(FCV_EINVAL, "fcv_attn_ctas: negative tile count");
+  return std::max(1, std::min(n_tiles * FCV_HEADS, 2 * num_sms()));
+}
+
+int fcv_attn_schedule(const int32_t* lengths_host, int B, int chunk, const int32_t* tiles, int n_tiles, int n_ctas,
+                      int32_t* sched, int cap) {
+  if (!lengths_host || (n_tiles > 0 && !tiles) || !sched || B < 0 || chunk < 0 || n_tiles < 0 || n_ctas < 1)
+    return fail(FCV_EINVAL, "fcv_attn_schedule: bad arguments");
+  const long items = (long)n_tiles * FCV_HEADS;
+  const long need = n_ctas + 1 + items;
+  if (need > cap) return fail(FCV_EINVAL, "fcv_attn_schedule: capacity %d < %ld", cap, need);
+  // item cost: its key tiles plus one for the per-item work (Q load, first S, output)
+  std::vector<std::pair<long, int>> order;  // (cost, item), most expensive first
+  order.reserve(items);
+  for (int t = 0; t < n_tiles; ++t) {
+    const int d = tiles[2 * t], q0 = tiles[2 * t + 1];
+    if (d < 0 || d >= B) return fail(FCV_EINVAL, "fcv_attn_schedule: tile %d names document %d", t, d);
+    const int L = lengths_host[d];
+    const int q_last = std::min(q0 + kAttnQTile, L) - 1;
+    const int kv = chunk > 0 ? std::min(L, (q_last / chunk + 1) * chunk) : L;
+    const long cost = (kv + kTcKv - 1) / kTcKv + 1;
+    for (int h = 0; h < FCV_HEADS; ++h) order.push_back({cost, t * FCV_HEADS + h});
+  }
+  std::stable_sort(order.begin(), order.end(), [](const auto& a, const auto& b) { return a.first > b.first; });
+  // longest processing time first: each item to the least loaded CTA
+  std::vector<std::vector<int>> per(n_ctas);
+  std::vector<std::pair<long, int>> heap;  // (load, cta), min-heap
+  heap.reserve(n_ctas);
+  for (int c = 0; c < n_ctas; ++c) heap.push_back({0, c});
+  auto cmp = [](const auto& a, const auto& b) { return a.first != b.first ? a.first > b.first : a.second > b.second; };
+  std::make_heap(heap.begin(), heap.end(), cmp);
+  for (const auto& it : order) {
+    std::pop_heap(heap.begin(), heap.end(), cmp);
+    auto& slot = heap.back();
+    per[slot.second].push_back(it.second);
+    slot.first += it.first;
+    std::push_heap(heap.begin(), heap.end(), cmp);
+  }
+  int32_t* off = sched;
+  int32_t* list = sched + n_ctas + 1;
+  long k = 0;
+  for (int c = 0; c < n_ctas; ++c) {
+    off[c] = (int32_t)k;
+    for (int v : per[c]) list[k++] = v;
+  }
+  off[n_ctas] = (int32_t)k;
+  return (int)need;
 }
 
 int fcv_time_embed(const fcv_dit_weights* w, const void* t, int B, float* temb, void* silu_act, void* stream) {

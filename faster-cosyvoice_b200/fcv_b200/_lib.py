@@ -47,6 +47,8 @@ EXPORTS = (
     "fcv_gemm",
     "fcv_attention",
     "fcv_attn_tiles",
+    "fcv_attn_ctas",
+    "fcv_attn_schedule",
     "fcv_time_embed",
     "fcv_time_embed_noalloc",
     "fcv_cfg_euler",
@@ -125,6 +127,8 @@ class DitBatch(ctypes.Structure):
         ("out_f32", ctypes.c_int),
         ("packed", ctypes.c_int),
         ("n_attn_tiles_dev", ctypes.c_void_p),
+        ("attn_sched", ctypes.c_void_p),
+        ("attn_sched_ctas", ctypes.c_int),
     ]
 
 
@@ -157,8 +161,10 @@ _SIGNATURES = {
     "fcv_ln_modulate": (_i, [_vp, _i, _vp, _vp, _vp, _l, _i, _vp, _i, _vp]),
     "fcv_gate_res_ln_modulate": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _l, _i, _vp, _vp, _i, _vp]),
     "fcv_gemm": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _l, _vp, _vp, _vp]),
-    "fcv_attention": (_i, [_vp, _i, _vp, _i, _i, _i, _i, _vp, _i, _vp, _vp]),
+    "fcv_attention": (_i, [_vp, _i, _vp, _i, _i, _i, _i, _vp, _i, _vp, _i, _vp, _vp]),
     "fcv_attn_tiles": (_i, [_vp, _i, _i, _vp, _i]),
+    "fcv_attn_ctas": (_i, [_i]),
+    "fcv_attn_schedule": (_i, [_vp, _i, _i, _vp, _i, _i, _vp, _i]),
     "fcv_time_embed": (_i, [ctypes.POINTER(DitWeights), _vp, _i, _vp, _vp, _vp]),
     "fcv_time_embed_noalloc": (_i, [ctypes.POINTER(DitWeights), _vp, _i, _vp, _vp, _vp]),
     "fcv_cfg_euler": (_i, [_vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _vp, _i, _vp]),

@@ -124,6 +124,8 @@ class PackedLayout:
     gap_rows: torch.Tensor
     attn_tiles: torch.Tensor
     n_attn_tiles: int
+    attn_sched: torch.Tensor | None = None  # per-CTA items (fcv_attn_schedule)
+    attn_ctas: int = 0
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -174,6 +176,8 @@ class B200DiT(nn.Module):
         self.graph_buckets = tuple(sorted({int(b) for b in graph_buckets})) if graph_buckets else None
         self._bucket_graphs: OrderedDict = OrderedDict()
         self.bucket_captures = 0
+        # balanced (LPT) attention schedule per batch composition; False deals items round robin
+        self.use_attn_schedule = True
         self._finalized = False
         self._derived: dict[str, torch.Tensor] = {}
         self._graphs: OrderedDict = OrderedDict()
@@ -291,12 +295,19 @@ class B200DiT(nn.Module):
         call("fcv_pack_layout", lengths_dev.data_ptr(), B, int(padded_length), N, gather.data_ptr(),
              doc_ids.data_ptr(), positions.data_ptr(), cu.data_ptr(), gap_rows.data_ptr(), stream)
         cap = sum((L + 127) // 128 for L in lengths)
-        tiles_host = (ctypes.c_int32 * (2 * max(cap, 1)))()
+        ctas = int(lib().fcv_attn_ctas(cap))
+        # one host block, one upload: work list (2 * cap) then the balanced schedule
+        host = (ctypes.c_int32 * (2 * max(cap, 1) + ctas + 1 + 16 * cap))()
         lens_host = (ctypes.c_int32 * B)(*lengths)
-        n_tiles = call("fcv_attn_tiles", ctypes.addressof(lens_host), B, chunk, ctypes.addressof(tiles_host), cap)
-        tiles = torch.tensor(list(tiles_host)[:2 * max(n_tiles, 1)], dtype=torch.int32).to(device)
+        n_tiles = call("fcv_attn_tiles", ctypes.addressof(lens_host), B, chunk, ctypes.addressof(host), cap)
+        ctas = int(call("fcv_attn_ctas", n_tiles))
+        s_off = 2 * max(n_tiles, 1)
+        n_sched = call("fcv_attn_schedule", ctypes.addressof(lens_host), B, chunk, ctypes.addressof(host), n_tiles,
+                       ctas, ctypes.addressof(host) + 4 * s_off, len(host) - s_off)
+        block = torch.frombuffer(host, dtype=torch.int32)[:s_off + n_sched].clone().to(device)
+        tiles, sched = block[:s_off], block[s_off:]
         lay = PackedLayout(lengths, int(padded_length), chunk, N, max(lengths) if lengths else 0, lengths_dev,
-                           cu, gather[:N], doc_ids[:N], positions[:N], gap_rows, tiles, n_tiles)
+                           cu, gather[:N], doc_ids[:N], positions[:N], gap_rows, tiles, n_tiles, sched, ctas)
         if len(self._layouts) >= MAX_LAYOUT_CACHE:
             self._layouts.popitem(last=False)
         self._layouts[key] = lay
@@ -338,6 +349,9 @@ class B200DiT(nn.Module):
         b.gap_rows = layout.gap_rows.data_ptr()
         b.attn_tiles = layout.attn_tiles.data_ptr()
         b.n_attn_tiles = layout.n_attn_tiles
+        if layout.attn_sched is not None and self.use_attn_schedule:
+            b.attn_sched = layout.attn_sched.data_ptr()
+            b.attn_sched_ctas = layout.attn_ctas
         b.out = out.data_ptr()
         b.packed = 1 if packed else 0
         if out.dtype == torch.float32:
@@ -549,12 +563,15 @@ class _BucketGraph:
         self.n_fill = max(1, -(-rows // ROPE_TABLE_LEN))
         self.n_docs = docs + self.n_fill
         self.tile_cap = -(-rows // 128) + docs
+        self.ctas = int(lib().fcv_attn_ctas(self.tile_cap))
         nd = self.n_docs
-        # device block: lengths (nd) | cu (nd + 1) | n_tiles (1) | pad | tiles (2 * cap), int32
+        # device block: lengths (nd) | cu (nd + 1) | n_tiles (1) | pad | tiles (2 * cap) | schedule, int32
         self.off_cu = nd
         self.off_nt = 2 * nd + 1
         self.off_tiles = (self.off_nt + 2) // 2 * 2
-        size = self.off_tiles + 2 * self.tile_cap
+        self.off_sched = self.off_tiles + 2 * self.tile_cap
+        self.sched_cap = self.ctas + 1 + 16 * self.tile_cap
+        size = self.off_sched + self.sched_cap
         self.meta = torch.zeros(size, dtype=torch.int32, device=device)
         self.host = torch.zeros(size, dtype=torch.int32).pin_memory()
         self.copied = torch.cuda.Event()
@@ -582,6 +599,8 @@ class _BucketGraph:
         b.attn_tiles = self.meta.data_ptr() + 4 * self.off_tiles
         b.n_attn_tiles = self.tile_cap
         b.n_attn_tiles_dev = self.meta.data_ptr() + 4 * self.off_nt
+        b.attn_sched = self.meta.data_ptr() + 4 * self.off_sched
+        b.attn_sched_ctas = self.ctas
         b.out, b.out_f32, b.packed = self.out.data_ptr(), 0, 1
         self._fill_host([])  # an empty batch: everything is filler
         self.meta.copy_(self.host)
@@ -616,14 +635,14 @@ class _BucketGraph:
             cu.append(cu[-1] + v)
         h[self.off_cu:self.off_cu + self.n_docs + 1] = torch.tensor(cu, dtype=torch.int32)
         n_tiles = 0
+        lens = (ctypes.c_int32 * max(B, 1))(*lengths)
+        base = h.data_ptr()
         if B:
             cap = sum((L + 127) // 128 for L in lengths)
-            buf = (ctypes.c_int32 * (2 * max(cap, 1)))()
-            lens = (ctypes.c_int32 * B)(*lengths)
-            n_tiles = call("fcv_attn_tiles", ctypes.addressof(lens), B, self.chunk, ctypes.addressof(buf), cap)
-            if n_tiles:
-                h[self.off_tiles:self.off_tiles + 2 * n_tiles] = torch.frombuffer(buf, dtype=torch.int32)[:2 * n_tiles]
+            n_tiles = call("fcv_attn_tiles", ctypes.addressof(lens), B, self.chunk, base + 4 * self.off_tiles, cap)
         h[self.off_nt] = n_tiles
+        call("fcv_attn_schedule", ctypes.addressof(lens), B, self.chunk, base + 4 * self.off_tiles, n_tiles,
+             self.ctas, base + 4 * self.off_sched, self.sched_cap)
         return N
 
     def run(self, lengths: Sequence[int], x, mu, t, spks, cond, out: torch.Tensor | None = None) -> torch.Tensor:

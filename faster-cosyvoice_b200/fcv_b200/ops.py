@@ -127,15 +127,19 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
 
 
 def ragged_attention(qkv: torch.Tensor, cu_seqlens: torch.Tensor, tiles: torch.Tensor, n_tiles: int,
-                     chunk: int = 0, max_len: int = 0) -> torch.Tensor:
+                     chunk: int = 0, max_len: int = 0, sched: torch.Tensor | None = None,
+                     sched_ctas: int = 0) -> torch.Tensor:
     """Packed ragged attention over (N, 3072) [Q|K|V] rows (replaces
     ``RaggedAttentionRunner.wrapper.run``, ``flashinfer_dit.py:501``); chunk > 0
-    applies the chunk-causal streaming mask (``flashinfer_attention.py:16-33``)."""
+    applies the chunk-causal streaming mask (``flashinfer_attention.py:16-33``).
+    ``sched``/``sched_ctas``: the balanced item schedule of a prepared layout
+    (``PackedLayout.attn_sched``/``attn_ctas``); results do not depend on it."""
     _check_rows(qkv, cu_seqlens, tiles)
     N = qkv.shape[0]
     out = torch.empty(N, 1024, dtype=qkv.dtype, device=qkv.device)
     call("fcv_attention", qkv.data_ptr(), _dt(qkv), cu_seqlens.data_ptr(), cu_seqlens.numel() - 1, N,
-         int(max_len), int(chunk), tiles.data_ptr(), int(n_tiles), out.data_ptr(), _s(qkv))
+         int(max_len), int(chunk), tiles.data_ptr(), int(n_tiles), None if sched is None else sched.data_ptr(),
+         int(sched_ctas), out.data_ptr(), _s(qkv))
     return out
 
 

@@ -141,6 +141,10 @@ typedef struct fcv_dit_batch {
                       * graph serve every batch composition of a bucket
                       * (the packed counterpart of the reference's graph
                       * buckets, flashinfer_dit.py:742-826).               */
+  const int32_t* attn_sched;  /* optional (device): per-CTA attention items from
+                      * fcv_attn_schedule, for attn_sched_ctas CTAs; null:
+                      * items dealt round robin.  Results do not depend on it. */
+  int attn_sched_ctas;
 } fcv_dit_batch;
 
 /* Layout ------------------------------------------------------------------ */
@@ -204,16 +208,30 @@ int fcv_gemm(const void* A, const void* W, const float* bias, int M, int Nout, i
  * keys k < L_d, and, when chunk > 0, only k // chunk <= q // chunk.
  * qkv: (N, 3072) [Q|K|V] element type dtype; out: (N, 1024); N = cu_seqlens[B].
  * tiles: (n_tiles, 2) int32 (doc, q0) list of 128-row query tiles, built by
- * fcv_attn_tiles().  Replaces the FlashInfer ragged prefill of
- * flashinfer_attention.py:36-142 + flashinfer_dit.py:501. */
+ * fcv_attn_tiles().  sched (device, optional): the balanced per-CTA item
+ * list of fcv_attn_schedule for sched_ctas CTAs; null deals items round
+ * robin (the result is the same either way).  Replaces the FlashInfer ragged
+ * prefill of flashinfer_attention.py:36-142 + flashinfer_dit.py:501. */
 int fcv_attention(const void* qkv, int dtype, const int32_t* cu_seqlens, int B, int N,
-                  int max_len, int chunk, const int32_t* tiles, int n_tiles, void* out,
-                  void* stream);
+                  int max_len, int chunk, const int32_t* tiles, int n_tiles,
+                  const int32_t* sched, int sched_ctas, void* out, void* stream);
 
 /* Host helper: fill `tiles` (capacity `cap` pairs, host memory) with the
  * 128-row query tiles of the documents, most expensive first.  Returns the
  * number of tiles or a negative status. */
 int fcv_attn_tiles(const int32_t* lengths_host, int B, int chunk, int32_t* tiles, int cap);
+
+/* Host helpers for a balanced attention launch (the FlashInfer plan's load
+ * balancing, flashinfer_attention.py:110-120, done once per batch
+ * composition).  fcv_attn_ctas: the CTA count of the persistent attention
+ * launch for n_tiles work-list entries on the current device.
+ * fcv_attn_schedule: assign the 16 * n_tiles items (tile t, head h) = t*16+h
+ * to n_ctas CTAs, longest first to the least loaded (cost = key tiles + 1);
+ * writes offsets (n_ctas + 1) then the items grouped by CTA into `sched`
+ * (capacity cap ints).  Returns the ints written or a negative status. */
+int fcv_attn_ctas(int n_tiles);
+int fcv_attn_schedule(const int32_t* lengths_host, int B, int chunk, const int32_t* tiles, int n_tiles,
+                      int n_ctas, int32_t* sched, int cap);
 
 /* Time embedding + AdaLN ---------------------------------------------------- */
 /* temb (B,1024) f32 = TimestepEmbedding(t) (modules.py:606-616); silu_act

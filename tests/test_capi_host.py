@@ -56,7 +56,7 @@ def test_version_and_error_paths_without_gpu(lib):
     assert rc == -1
     assert b"fcv_gemm" in lib.fcv_last_error()
     assert lib.fcv_dit_forward(None, None, None, 0, None) == -1
-    assert lib.fcv_attention(None, 1, None, 0, 0, 0, 0, None, 0, None, None) == -1
+    assert lib.fcv_attention(None, 1, None, 0, 0, 0, 0, None, 0, None, 0, None, None) == -1
     assert lib.fcv_ln_modulate(None, 0, None, None, None, 0, 0, None, 0, None) == -1
     assert lib.fcv_pack_layout(None, 0, 0, 0, None, None, None, None, None, None) == -1
 
@@ -159,3 +159,39 @@ def test_graph_bucket_presets_become_row_capacities():
     assert graph_row_buckets((8.0, 12.0), (512, 640)) == (800, 1024, 1200, 1280)
     assert graph_row_buckets(None, None) is None
     assert list(DEFAULT_GRAPH_BUCKETS) == sorted(DEFAULT_GRAPH_BUCKETS)
+
+
+@pytest.mark.parametrize("chunk", [0, 50])
+def test_attention_schedule_assigns_every_item_once_and_balances(lib, chunk):
+    """fcv_attn_schedule: a permutation of the 16 * n_tiles items grouped by CTA,
+    longest first to the least loaded CTA; its worst CTA carries no more work
+    than round robin's (config-2 lengths, 296 CTAs)."""
+    rng = np.random.default_rng(1)
+    req = [int(v) for v in rng.integers(150, 601, size=8)]
+    lengths = req + req + [1, 0, 3000]
+    n, tiles = _tiles(lib, lengths, chunk)
+    ctas = lib.fcv_attn_ctas(n)
+    assert ctas == min(16 * n, 296) or ctas == min(16 * n, 2 * ctas)
+    cap = ctas + 1 + 16 * n
+    buf = (ctypes.c_int32 * cap)()
+    lens = (ctypes.c_int32 * len(lengths))(*lengths)
+    flat = (ctypes.c_int32 * (2 * n))(*tiles.reshape(-1).tolist())
+    assert lib.fcv_attn_schedule(ctypes.addressof(lens), len(lengths), chunk, ctypes.addressof(flat), n, ctas,
+                                 ctypes.addressof(buf), cap) == cap
+    s = np.array(list(buf))
+    off, items = s[:ctas + 1], s[ctas + 1:]
+    assert off[0] == 0 and off[-1] == 16 * n and np.all(np.diff(off) >= 0)
+    assert sorted(items.tolist()) == list(range(16 * n))
+
+    def cost(it):
+        d, q0 = tiles[it // 16]
+        L = lengths[d]
+        q_last = min(q0 + 128, L) - 1
+        kv = min(L, (q_last // chunk + 1) * chunk) if chunk else L
+        return -(-kv // 64) + 1
+
+    lpt = max(sum(cost(i) for i in items[off[c]:off[c + 1]]) for c in range(ctas))
+    rr = max(sum(cost(i) for i in range(c, 16 * n, ctas)) for c in range(ctas))
+    assert lpt <= rr
+    assert lib.fcv_attn_schedule(ctypes.addressof(lens), len(lengths), chunk, ctypes.addressof(flat), n, ctas,
+                                 ctypes.addressof(buf), cap - 1) == -1

@@ -248,3 +248,25 @@ def test_bucketed_graph_serves_many_compositions_bit_exact(streaming):
     # (512 rows, 4 docs), (1024, 2), (512, 8), (512, 2); [700, 700] exceeds every bucket
     assert model.bucket_captures == 4
     assert len(model._bucket_graphs) == 4
+
+
+@pytest.mark.parametrize("streaming", [False, True])
+def test_attention_schedule_does_not_change_results(streaming):
+    """The balanced (LPT) attention schedule only reassigns items to CTAs:
+    estimator outputs are bit-identical to the round-robin deal."""
+    model = _model(6, 2, torch.bfloat16)
+    rng = np.random.default_rng(23)
+    lengths = [int(v) for v in rng.integers(150, 601, size=6)] * 2 + [1, 700]
+    B, T = len(lengths), max(lengths)
+    x, mu, cond = (torch.tensor(rng.standard_normal((B, 80, T)), device=DEV, dtype=torch.bfloat16) for _ in range(3))
+    spks = torch.tensor(rng.standard_normal((B, 80)), device=DEV, dtype=torch.bfloat16)
+    t = torch.tensor(rng.uniform(size=B), device=DEV, dtype=torch.bfloat16)
+    lay = model.prepare_layout(lengths, T, streaming, torch.device(DEV))
+    assert lay.attn_sched is not None and lay.attn_ctas > 0
+    with torch.inference_mode():
+        model.use_attn_schedule = True
+        a = model.forward_layout(lay, x, mu, t, spks, cond)
+        model.use_attn_schedule = False
+        b = model.forward_layout(lay, x, mu, t, spks, cond)
+    model.use_attn_schedule = True
+    assert torch.equal(a, b)
