@@ -174,3 +174,34 @@ def test_pack_rows_bit_exact(src_dtype):
          out.data_ptr(), _lib.DTYPE_F32, stream)
     ref = torch.cat([src[0, :, :L].t() for L in lengths]).float()
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_streaming_prefix_trajectory_is_stable_across_calls(dtype):
+    """Semantics behind streaming prefix reuse (flashinfer_flow.py:215-221 recomputes
+    the whole prefix every call): with the chunk-causal mask, the causal position
+    convolution, lookahead context tokens that are the real next tokens and the
+    fixed noise prefix, a frame in a chunk that was complete in the previous call
+    follows the same 10-step trajectory in the next call, so its output is
+    bit-identical; frames of the previous call's partial chunk change (they now
+    see the rest of their chunk)."""
+    from fcv_b200.flow import flow_inference_batched_streaming
+
+    dt = getattr(torch, dtype)
+    flow = _flow(dt)
+    rng = np.random.default_rng(77)
+    tokens = rng.integers(0, 6561, size=200).tolist()
+    prompt = torch.tensor(rng.standard_normal((1, 30, 80)), device=DEV, dtype=torch.float32)
+    spk = torch.tensor(rng.standard_normal((1, 192)), device=DEV, dtype=torch.float32)
+    prev = None
+    for n_tok in (63, 88, 113):  # 60, 85, 110 tokens + 3 lookahead tokens of context
+        out = flow_inference_batched_streaming(flow, [tokens[:n_tok]], [prompt], spk, [False])[0][0]
+        mel = 2 * (n_tok - 3)
+        assert out.shape[1] == mel - 30
+        if prev is not None:
+            prev_mel = prev.shape[1] + 30
+            stable = (prev_mel // 50) * 50 - 30  # generated frames in the previous call's complete chunks
+            assert torch.equal(out[:, :stable], prev[:, :stable]), (dtype, n_tok)
+            if prev_mel % 50:
+                assert not torch.equal(out[:, stable:prev.shape[1]], prev[:, stable:]), (dtype, n_tok)
+        prev = out
