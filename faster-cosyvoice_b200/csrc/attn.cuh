@@ -28,6 +28,18 @@ __device__ __forceinline__ int kv_limit(int q0, int rows, int L, int chunk) {
   return min(L, (q_last / chunk + 1) * chunk);
 }
 
+// Where a document's queries and keys live.  Queries (and outputs) are rows
+// [cu[d], cu[d+1]) of the packed Q buffer.  A document may continue a cached
+// prefix (streaming prefix reuse): its first query row then sits at absolute
+// position pos0[d], and its keys are rows kv_base[d] .. kv_base[d] + pos0[d] + L
+// of a separate K/V buffer (the cache, prefix keys first).  Without pos0 /
+// kv_base the keys are the document's own rows of the QKV buffer.
+struct AttnSrc {
+  const int32_t* cu;
+  const int32_t* pos0;     // null: 0
+  const int32_t* kv_base;  // null: cu[d]
+};
+
 // ------------------------------------------------------------------ bf16 (tcgen05)
 // Persistent: each CTA walks work items (128-row query tile, head) c, c+grid, ...
 // (tiles arrive most expensive first).  6 warps per CTA, 2 CTAs per SM:
@@ -101,30 +113,32 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+// One work item: query rows [q0, q0 + 128) of a document (local indices), one
+// head.  base / L: the document's query rows; pos0: absolute position of local
+// row 0; kvb / Lkv: its first key row and key count (pos0 + L).
 struct AttnItem {
-  int base, L, q0, head, n_kv;
+  int base, L, q0, head, n_kv, pos0, kvb, Lkv;
 };
 
-__device__ __forceinline__ AttnItem attn_item(const int32_t* cu, const int2* tiles, int chunk, int it) {
-  const int2 tl = tiles[it >> 4];
+// Item `it` from its work-list entry tl (already loaded).
+__device__ __forceinline__ AttnItem attn_item_at(const AttnSrc& src, int2 tl, int chunk, int it) {
   AttnItem a;
   a.head = it & 15;
   a.q0 = tl.y;
-  a.base = cu[tl.x];
-  a.L = cu[tl.x + 1] - a.base;
-  a.n_kv = (kv_limit(a.q0, kAttnQTile, a.L, chunk) + kTcKv - 1) / kTcKv;
+  a.base = src.cu[tl.x];
+  a.L = src.cu[tl.x + 1] - a.base;
+  a.pos0 = src.pos0 ? __ldg(src.pos0 + tl.x) : 0;
+  a.kvb = src.kv_base ? __ldg(src.kv_base + tl.x) : a.base;
+  a.Lkv = a.pos0 + a.L;
+  // the tile's last query row in absolute positions bounds its visible keys
+  const int q_last = a.pos0 + min(a.q0 + kAttnQTile - 1, a.L - 1);
+  const int lim = chunk > 0 ? min(a.Lkv, (q_last / chunk + 1) * chunk) : a.Lkv;
+  a.n_kv = (lim + kTcKv - 1) / kTcKv;
   return a;
 }
 
-// Item `it` from its work-list entry tl (already loaded).
-__device__ __forceinline__ AttnItem attn_item_at(const int32_t* cu, int2 tl, int chunk, int it) {
-  AttnItem a;
-  a.head = it & 15;
-  a.q0 = tl.y;
-  a.base = cu[tl.x];
-  a.L = cu[tl.x + 1] - a.base;
-  a.n_kv = (kv_limit(a.q0, kAttnQTile, a.L, chunk) + kTcKv - 1) / kTcKv;
-  return a;
+__device__ __forceinline__ AttnItem attn_item(const AttnSrc& src, const int2* tiles, int chunk, int it) {
+  return attn_item_at(src, tiles[it >> 4], chunk, it);
 }
 
 // A CTA's items with the descriptor lookups run ahead: while item `it` is
@@ -134,7 +148,7 @@ __device__ __forceinline__ AttnItem attn_item_at(const int32_t* cu, int2 tl, int
 // robin (positions first, first + stride, ... of the work list) or from a
 // host-built schedule: positions [beg, end) of a per-CTA item list.
 struct ItemFeed {
-  const int32_t* cu;
+  AttnSrc cu;
   const int2* tiles;
   const int32_t* list;  // schedule items, or null for round robin
   int chunk, end, stride, pos, it, it1, it2;
@@ -142,7 +156,7 @@ struct ItemFeed {
   int2 tl2;
   __device__ __forceinline__ int item_at(int p) const { return list ? __ldg(list + p) : p; }
   // Round robin when sched is null; else sched = [offsets (gridDim + 1) | items].
-  __device__ __forceinline__ bool init(const int32_t* cu_, const int2* tiles_, int chunk_, int n_items,
+  __device__ __forceinline__ bool init(const AttnSrc& cu_, const int2* tiles_, int chunk_, int n_items,
                                        const int32_t* sched) {
     cu = cu_;
     tiles = tiles_;
@@ -197,9 +211,9 @@ constexpr int kTcSoftmaxWarps = 4;
 
 __global__ void __launch_bounds__(kTcThreads, 2)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
-                   const int32_t* __restrict__ cu, const int2* __restrict__ tiles, int n_tiles,
+                   const AttnSrc src, const int2* __restrict__ tiles, int n_tiles,
                    const int32_t* __restrict__ n_tiles_dev, const int32_t* __restrict__ sched, int chunk,
-                   bf16* __restrict__ out) {
+                   int k_col, int v_col, bf16* __restrict__ out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t s0 = smem_u32(smem);
@@ -271,7 +285,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       int g = 0, i = 0;
       bool ok = true;
       ItemFeed feed;
-      for (bool have = feed.init(cu, tiles, chunk, n_items, sched); have && ok;
+      for (bool have = feed.init(src, tiles, chunk, n_items, sched); have && ok;
            have = feed.advance(), ++i) {
         const AttnItem a = feed.cur;
         const int qb = i & 1;
@@ -283,8 +297,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
           if (!mbar_wait(smem_u32(&kv_empty[st]), ((g / kTcKvStages) & 1) ^ 1, 222, abort_flag)) { ok = false; break; }
           const uint32_t fb = smem_u32(&kv_full[st]);
           mbar_arrive_expect_tx(fb, 2 * kTcSmemKV);
-          tma_load_2d(sK + st * kTcSmemKV, &tmKV, fb, 1024 + a.head * 64, a.base + j * kTcKv);
-          tma_load_2d(sV + st * kTcSmemKV, &tmKV, fb, 2048 + a.head * 64, a.base + j * kTcKv);
+          tma_load_2d(sK + st * kTcSmemKV, &tmKV, fb, k_col + a.head * 64, a.kvb + j * kTcKv);
+          tma_load_2d(sV + st * kTcSmemKV, &tmKV, fb, v_col + a.head * 64, a.kvb + j * kTcKv);
         }
       }
       // wait for our own copies before the CTA may exit (all phases already issued)
@@ -306,7 +320,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       auto first = [&](Cur& c) -> bool {
         c.i = 0;
         c.j = 0;
-        if (!feed.init(cu, tiles, chunk, n_items, sched)) return false;
+        if (!feed.init(src, tiles, chunk, n_items, sched)) return false;
         c.it = feed.it;
         c.n_kv = feed.cur.n_kv;
         return true;
@@ -425,11 +439,12 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       return true;
     };
     ItemFeed feed;
-    for (bool have = feed.init(cu, tiles, chunk, n_items, sched); have && ok;
+    for (bool have = feed.init(src, tiles, chunk, n_items, sched); have && ok;
          have = feed.advance(), ++i) {
       const AttnItem a = feed.cur;
-      const int qa = a.q0 + r;
-      const int lim = chunk > 0 ? min(a.L, (qa / chunk + 1) * chunk) : a.L;  // visible keys [0, lim)
+      const int qa = a.q0 + r;                                   // local query row
+      const int qabs = a.pos0 + qa;                              // its absolute position
+      const int lim = chunk > 0 ? min(a.Lkv, (qabs / chunk + 1) * chunk) : a.Lkv;  // visible keys [0, lim)
       const int wlim = __reduce_max_sync(0xffffffffu, lim);                    // any row of this warp
       const uint32_t o_addr = lane_base + kTcColO + (i & 1) * kTcOCols;
       float m_ref = -INFINITY;
@@ -538,9 +553,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
 
 // ------------------------------------------------------------------ fp32 (CUDA cores)
 // One thread per query row (128 per CTA), 32-key tiles in shared memory.
-__global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__ qkv,
-                                                       const int32_t* __restrict__ cu,
-                                                       const int2* __restrict__ tiles,
+__global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__ qkv, const AttnSrc src,
+                                                       const float* __restrict__ kv, long kv_rows, long kv_stride,
+                                                       int k_col, int v_col, const int2* __restrict__ tiles,
                                                        const int32_t* __restrict__ n_tiles_dev, int chunk,
                                                        float* __restrict__ out) {
   griddep_wait();
@@ -548,31 +563,31 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__
   if (n_tiles_dev && (int)blockIdx.x >= __ldg(n_tiles_dev)) return;  // grid sized for the capacity
   __shared__ float sK[32][64];
   __shared__ float sV[32][64];
-  const int2 tl = tiles[blockIdx.x];
-  const int doc = tl.x, q0 = tl.y;
+  const AttnItem a = attn_item_at(src, tiles[blockIdx.x], chunk, (int)blockIdx.y);
   const int head = blockIdx.y;
-  const int base = cu[doc];
-  const int L = cu[doc + 1] - base;
-  const int q = q0 + threadIdx.x;
-  const bool valid = q < L;
+  const int q = a.q0 + threadIdx.x;  // local query row
+  const bool valid = q < a.L;
   float qv[64], o[64];
-  const float* qrow = qkv + (long)(base + (valid ? q : 0)) * kQkvStride + head * 64;
+  const float* qrow = qkv + (long)(a.base + (valid ? q : 0)) * kQkvStride + head * 64;
 #pragma unroll
   for (int d = 0; d < 64; ++d) {
     qv[d] = qrow[d] * 0.125f;
     o[d] = 0.f;
   }
   float m = -INFINITY, l = 0.f;
-  const int kv_end = kv_limit(q0, kAttnQTile, L, chunk);
-  const int my_end = valid ? (chunk > 0 ? min(L, (q / chunk + 1) * chunk) : L) : 0;
+  const int kv_end = a.n_kv * kTcKv < a.Lkv ? a.n_kv * kTcKv : a.Lkv;
+  const int qabs = a.pos0 + q;
+  const int my_end = valid ? (chunk > 0 ? min(a.Lkv, (qabs / chunk + 1) * chunk) : a.Lkv) : 0;
   for (int k0 = 0; k0 < kv_end; k0 += 32) {
     __syncthreads();
     for (int i = threadIdx.x; i < 32 * 64; i += 128) {
       const int r = i >> 6, c = i & 63;
       const int k = k0 + r;
-      const long off = (long)(base + (k < L ? k : 0)) * kQkvStride + head * 64 + c;
-      sK[r][c] = k < L ? qkv[off + 1024] : 0.f;
-      sV[r][c] = k < L ? qkv[off + 2048] : 0.f;
+      const long row = (long)a.kvb + k;
+      const bool in = k < a.Lkv && row >= 0 && row < kv_rows;  // rows outside the buffer read as 0
+      const long off = (in ? row : 0) * kv_stride + head * 64 + c;
+      sK[r][c] = in ? kv[off + k_col] : 0.f;
+      sV[r][c] = in ? kv[off + v_col] : 0.f;
     }
     __syncthreads();
     const int kmax = min(32, my_end - k0);
@@ -591,7 +606,7 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__
   }
   if (valid) {
     const float inv = 1.f / l;
-    float* orow = out + (long)(base + q) * 1024 + head * 64;
+    float* orow = out + (long)(a.base + q) * 1024 + head * 64;
 #pragma unroll
     for (int d = 0; d < 64; ++d) orow[d] = o[d] * inv;
   }

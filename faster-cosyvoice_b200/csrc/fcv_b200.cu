@@ -418,17 +418,36 @@ EpiParams make_epi(int epi, int M, int N, void* C, long ldc, const float* bias) 
 }
 
 // ------------------------------------------------------------------ attention launch
+// Keys of a launch: by default the documents' own rows of the QKV buffer; for
+// documents continuing a cached prefix, a K/V cache of `rows` x 2048 ([K | V])
+// with per-document first key rows and absolute query offsets.
+struct KvSrc {
+  const void* kv = nullptr;  // null: the QKV buffer itself
+  long rows = 0;
+  const int32_t* pos0 = nullptr;
+  const int32_t* kv_base = nullptr;
+};
+
 int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, const int32_t* tiles,
                   int n_tiles, void* out, long n_rows, cudaStream_t s, const int32_t* n_tiles_dev = nullptr,
-                  const int32_t* sched = nullptr, int sched_ctas = 0) {
+                  const int32_t* sched = nullptr, int sched_ctas = 0, const KvSrc& kvs = KvSrc()) {
   if (n_tiles <= 0) return FCV_OK;
   dim3 grid(n_tiles, FCV_HEADS);
   const int2* t2 = reinterpret_cast<const int2*>(tiles);
+  const bool cached = kvs.kv != nullptr;
+  AttnSrc src;
+  src.cu = cu;
+  src.pos0 = cached ? kvs.pos0 : nullptr;
+  src.kv_base = cached ? kvs.kv_base : nullptr;
+  const int k_col = cached ? 0 : 1024, v_col = cached ? 1024 : 2048;
   if (dtype == FCV_DTYPE_BF16) {
-    // Q tiles of 128 rows and K/V tiles of 64 rows straight from the (N, 3072) [Q|K|V] buffer
+    // Q tiles of 128 rows from the (N, 3072) [Q|K|V] buffer; K/V tiles of 64 rows from it or the cache
     CUtensorMap tq, tkv;
     FCV_TRY(make_tmap(&tq, qkv, false, n_rows, 3072, 3072, 64, 128));
-    FCV_TRY(make_tmap(&tkv, qkv, false, n_rows, 3072, 3072, 64, kTcKv));
+    if (cached)
+      FCV_TRY(make_tmap(&tkv, kvs.kv, false, kvs.rows, 2048, 2048, 64, kTcKv));
+    else
+      FCV_TRY(make_tmap(&tkv, qkv, false, n_rows, 3072, 3072, 64, kTcKv));
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -443,12 +462,16 @@ int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, cons
       return fail(FCV_EINVAL, "attention schedule built for %d CTAs", sched_ctas);
     // Plain stream order: the work items are dealt to CTAs by index, and CTAs that
     // start early on the SMs freed first by the previous kernel would unbalance it.
-    const int rc = launch_k_opt(false, "attn_tc_kernel", attn_tc_kernel, dim3(ctas), dim3(kTcThreads), kTcSmemBytes, s, tq, tkv, cu, t2, n_tiles, n_tiles_dev, sched, chunk,
-                                 static_cast<bf16*>(out));
+    const int rc = launch_k_opt(false, "attn_tc_kernel", attn_tc_kernel, dim3(ctas), dim3(kTcThreads), kTcSmemBytes,
+                                s, tq, tkv, src, t2, n_tiles, n_tiles_dev, sched, chunk, k_col, v_col,
+                                static_cast<bf16*>(out));
     if (rc != FCV_OK) return rc;
   } else {
-    FCV_LAUNCH("attn_f32_kernel", attn_f32_kernel, dim3(grid), dim3(128), 0, s, static_cast<const float*>(qkv), cu, t2, n_tiles_dev, chunk,
-                                         static_cast<float*>(out));
+    const float* kv = cached ? static_cast<const float*>(kvs.kv) : static_cast<const float*>(qkv);
+    const long kv_stride = cached ? 2048 : 3072;
+    const long kv_rows = cached ? kvs.rows : n_rows;
+    FCV_LAUNCH("attn_f32_kernel", attn_f32_kernel, dim3(grid), dim3(128), 0, s, static_cast<const float*>(qkv), src,
+               kv, kv_rows, kv_stride, k_col, v_col, t2, n_tiles_dev, chunk, static_cast<float*>(out));
   }
   return FCV_OK;
 }
@@ -588,8 +611,12 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
                                                   static_cast<const T*>(bt->mu), static_cast<const T*>(bt->spks),
                                                   bt->cu_seqlens, bt->T, static_cast<T*>(ws.a_in));
     }
-    FCV_LAUNCH("zero_gap_rows_kernel", zero_gap_rows_kernel<T>, dim3(30, B + 1), dim3(128), 0, s, bt->cu_seqlens,
-               static_cast<T*>(ws.gap0), static_cast<T*>(ws.gap1));
+    if (bt->conv_ctx)  // continuing documents: the cached rows are the convolutions' left context
+      FCV_LAUNCH("gap_context_kernel", gap_context_kernel<T>, dim3(30, B + 1), dim3(128), 0, s, bt->cu_seqlens, B,
+                 static_cast<const T*>(bt->conv_ctx), static_cast<T*>(ws.gap0), static_cast<T*>(ws.gap1));
+    else
+      FCV_LAUNCH("zero_gap_rows_kernel", zero_gap_rows_kernel<T>, dim3(30, B + 1), dim3(128), 0, s, bt->cu_seqlens,
+                 static_cast<T*>(ws.gap0), static_cast<T*>(ws.gap1));
     GemmCall g{};
     g.A = ws.a_in; g.lda = 320; g.a_rows = N; g.W = w->in_w; g.M = N; g.N = 1024; g.K = 320;
     g.epi = make_epi(EPI_EMBED_GAP, N, 1024, ws.gap0, 1024, w->in_b);
@@ -601,6 +628,10 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     c1.epi = make_epi(EPI_MISH_GAP, G_rows, 1024, ws.gap1, 1024, w->conv1_b);
     c1.epi.aux = bt->gap_rows;
     FCV_TRY(run_gemm(c1, dtype, s));
+    if (bt->conv_ctx_out)  // both convolution inputs are in place: keep the next call's context
+      FCV_LAUNCH("context_save_kernel", context_save_kernel<T>, dim3(30, B), dim3(128), 0, s, bt->cu_seqlens,
+                 bt->ctx_row0, static_cast<const T*>(bt->conv_ctx), static_cast<const T*>(ws.gap0),
+                 static_cast<const T*>(ws.gap1), static_cast<T*>(bt->conv_ctx_out));
     GemmCall c2 = c1;
     c2.A = ws.gap1; c2.W = w->conv2_w;
     c2.epi = make_epi(EPI_MISH_RES, G_rows, 1024, ws.h, 1024, w->conv2_b);
@@ -628,10 +659,22 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
       ProfScope ps(FCV_CAT_GEMM_QKV, s);
       FCV_TRY(run_gemm(q, dtype, s));
     }
+    KvSrc kvs;
+    if (bt->kv_cache) {
+      // this block's cache: the prefix keys of earlier calls, then the new rows' keys appended
+      kvs.kv = static_cast<const uint8_t*>(bt->kv_cache) + (size_t)i * bt->kv_layer_rows * 2048 * es;
+      kvs.rows = bt->kv_layer_rows;
+      kvs.pos0 = bt->doc_pos0;
+      kvs.kv_base = bt->doc_kv_base;
+      const int grid = (int)std::min<long>((N + 7) / 8, 16L * num_sms());
+      FCV_LAUNCH("kv_append_kernel", kv_append_kernel<T>, dim3(grid), dim3(256), 0, s, static_cast<const T*>(ws.qkv),
+                 bt->doc_ids, bt->positions, bt->doc_kv_base, (long)N, bt->kv_layer_rows,
+                 static_cast<T*>(const_cast<void*>(kvs.kv)));
+    }
     {
       ProfScope ps(FCV_CAT_ATTENTION, s);
       FCV_TRY(run_attention(ws.qkv, dtype, bt->cu_seqlens, bt->chunk, bt->attn_tiles, bt->n_attn_tiles,
-                            ws.attn, N, s, bt->n_attn_tiles_dev, bt->attn_sched, bt->attn_sched_ctas));
+                            ws.attn, N, s, bt->n_attn_tiles_dev, bt->attn_sched, bt->attn_sched_ctas, kvs));
     }
     GemmCall o{};
     o.A = ws.attn; o.lda = 1024; o.a_rows = N; o.M = N; o.N = 1024; o.K = 1024;
@@ -1048,6 +1091,16 @@ int fcv_dit_forward(const fcv_dit_weights* w, const fcv_dit_batch* bt, void* wor
   if (w->depth < 1) return fail(FCV_EINVAL, "fcv_dit_forward: depth must be >= 1");
   if (bt->B < 1 || bt->N < 0 || bt->chunk < 0 || (!bt->packed && (bt->T < 1 || bt->N > (long)bt->B * bt->T)))
     return fail(FCV_EINVAL, "fcv_dit_forward: bad batch geometry B=%d T=%d N=%d", bt->B, bt->T, bt->N);
+  if (bt->kv_cache || bt->doc_pos0 || bt->conv_ctx) {
+    // streaming prefix reuse: every piece of the cached state is needed, on packed rows
+    if (!bt->kv_cache || !bt->doc_pos0 || !bt->doc_kv_base || !bt->conv_ctx || !bt->packed || bt->kv_layer_rows < 1)
+      return fail(FCV_EINVAL, "fcv_dit_forward: a cached prefix needs packed rows, kv_cache, kv_layer_rows, "
+                              "doc_pos0, doc_kv_base and conv_ctx");
+    if (bt->conv_ctx_out && (!bt->ctx_row0 || bt->conv_ctx_out == bt->conv_ctx))
+      return fail(FCV_EINVAL, "fcv_dit_forward: conv_ctx_out needs ctx_row0 and a buffer other than conv_ctx");
+    if (reinterpret_cast<uintptr_t>(bt->kv_cache) & 15)
+      return fail(FCV_EINVAL, "fcv_dit_forward: kv_cache must be 16-byte aligned");
+  }
   if (bt->packed) {
     const void* rows[5] = {bt->x, bt->mu, bt->cond, bt->spks, bt->out};
     for (const void* r : rows)
@@ -1068,6 +1121,15 @@ int fcv_dit_forward(const fcv_dit_weights* w, const fcv_dit_batch* bt, void* wor
   return forward_impl<float>(w, bt, ws, s);
 }
 
+
+int fcv_offset_positions(int32_t* positions, const int32_t* doc_ids, const int32_t* doc_pos0, int N, void* stream) {
+  if (!positions || !doc_ids || !doc_pos0 || N < 0) return fail(FCV_EINVAL, "fcv_offset_positions: bad arguments");
+  if (N == 0) return FCV_OK;
+  const int grid = (int)std::min<long>((N + 255) / 256, 8L * num_sms());
+  FCV_LAUNCH("offset_positions_kernel", offset_positions_kernel, dim3(grid), dim3(256), 0, as_stream(stream), doc_ids,
+             doc_pos0, (long)N, positions);
+  return FCV_OK;
+}
 
 // ====================================================================== packed flow front end
 size_t fcv_flow_workspace_bytes(int n_out_tokens, int dtype) {

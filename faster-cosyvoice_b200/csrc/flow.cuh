@@ -198,4 +198,96 @@ __global__ void __launch_bounds__(256) embed_rows_kernel(const T* __restrict__ x
   }
 }
 
+// ------------------------------------------------------------------ streaming prefix reuse
+// A document continuing a cached prefix runs only its rows from absolute
+// position pos0[d] on.  The kernels below give it the cached state of the
+// earlier rows: RoPE positions, the convolutions' left context and the keys.
+
+// positions[n] += pos0[doc[n]] (absolute RoPE positions of the new rows).
+__global__ void offset_positions_kernel(const int32_t* __restrict__ doc, const int32_t* __restrict__ pos0, long N,
+                                        int32_t* __restrict__ positions) {
+  griddep_wait();
+  griddep_launch();
+  for (long n = blockIdx.x * (long)blockDim.x + threadIdx.x; n < N; n += (long)gridDim.x * blockDim.x)
+    positions[n] += __ldg(pos0 + __ldg(doc + n));
+}
+
+// The 30 gap rows in front of document d (rows cu[d] + 30 d + r of both gapped
+// buffers) take the cached left context ctx[d][buffer][r] ((B, 2, 30, 1024));
+// the group after the last document stays zero.  Grid (30, B + 1).
+template <typename T>
+__global__ void gap_context_kernel(const int32_t* __restrict__ cu, int B, const T* __restrict__ ctx,
+                                   T* __restrict__ buf0, T* __restrict__ buf1) {
+  griddep_wait();
+  griddep_launch();
+  const int d = blockIdx.y, r = blockIdx.x;
+  const long g = (long)cu[d] + 30L * d + r;
+  constexpr int kVec = 16 / sizeof(T);
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  const T* c0 = d < B ? ctx + ((long)d * 2 * 30 + r) * kFlowHid : nullptr;
+  const T* c1 = d < B ? ctx + ((long)d * 2 * 30 + 30 + r) * kFlowHid : nullptr;
+  for (int c = threadIdx.x * kVec; c < kFlowHid; c += blockDim.x * kVec) {
+    *reinterpret_cast<uint4*>(buf0 + g * kFlowHid + c) = c0 ? *reinterpret_cast<const uint4*>(c0 + c) : z;
+    *reinterpret_cast<uint4*>(buf1 + g * kFlowHid + c) = c1 ? *reinterpret_cast<const uint4*>(c1 + c) : z;
+  }
+}
+
+// The next call's left context of document d: the 30 rows ending before its
+// local row row0[d] (row0[d] < 0: keep nothing, the caller keeps the old one).
+// Rows before local row 0 come from this call's context ctx_in.  Writes
+// ctx_out[d][buffer][r] from the gapped buffers (document d's local row p is
+// gapped row cu[d] + 30 (d + 1) + p).  Grid (30, B).
+template <typename T>
+__global__ void context_save_kernel(const int32_t* __restrict__ cu, const int32_t* __restrict__ row0,
+                                    const T* __restrict__ ctx_in, const T* __restrict__ buf0,
+                                    const T* __restrict__ buf1, T* __restrict__ ctx_out) {
+  griddep_wait();
+  griddep_launch();
+  const int d = blockIdx.y, r = blockIdx.x;
+  const int start = __ldg(row0 + d);
+  if (start < 0) return;
+  const int p = start - 30 + r;  // local row feeding context row r
+  constexpr int kVec = 16 / sizeof(T);
+  const T* s0;
+  const T* s1;
+  if (p >= 0) {
+    const long g = (long)cu[d] + 30L * (d + 1) + p;
+    s0 = buf0 + g * kFlowHid;
+    s1 = buf1 + g * kFlowHid;
+  } else {
+    s0 = ctx_in + ((long)d * 2 * 30 + 30 + p) * kFlowHid;
+    s1 = ctx_in + ((long)d * 2 * 30 + 60 + p) * kFlowHid;
+  }
+  T* o0 = ctx_out + ((long)d * 2 * 30 + r) * kFlowHid;
+  T* o1 = ctx_out + ((long)d * 2 * 30 + 30 + r) * kFlowHid;
+  for (int c = threadIdx.x * kVec; c < kFlowHid; c += blockDim.x * kVec) {
+    *reinterpret_cast<uint4*>(o0 + c) = *reinterpret_cast<const uint4*>(s0 + c);
+    *reinterpret_cast<uint4*>(o1 + c) = *reinterpret_cast<const uint4*>(s1 + c);
+  }
+}
+
+// Append the new rows' keys and values to the cache: cache[kv_base[d] + pos][0:2048]
+// = qkv[n][1024:3072] with pos the row's absolute position.  One warp per row.
+// A destination outside the cache's `rows` is skipped and reported (code 251).
+template <typename T>
+__global__ void __launch_bounds__(256) kv_append_kernel(const T* __restrict__ qkv, const int32_t* __restrict__ doc,
+                                                        const int32_t* __restrict__ positions,
+                                                        const int32_t* __restrict__ kv_base, long N, long rows,
+                                                        T* __restrict__ cache) {
+  griddep_wait();
+  griddep_launch();
+  constexpr int V = 2048 * (int)sizeof(T) / 16;
+  const int lane = threadIdx.x & 31;
+  for (long n = blockIdx.x * 8L + (threadIdx.x >> 5); n < N; n += gridDim.x * 8L) {
+    const long dst = (long)__ldg(kv_base + __ldg(doc + n)) + __ldg(positions + n);
+    if (dst < 0 || dst >= rows) {
+      if (lane == 0) record_error(251);
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(qkv + n * 3072 + 1024);
+    uint4* out = reinterpret_cast<uint4*>(cache + dst * 2048);
+    for (int v = lane; v < V; v += 32) out[v] = __ldg(src + v);
+  }
+}
+
 }  // namespace fcv

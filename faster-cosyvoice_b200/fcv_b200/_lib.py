@@ -57,6 +57,7 @@ EXPORTS = (
     "fcv_launch_count",
     "fcv_dit_workspace_bytes",
     "fcv_dit_forward",
+    "fcv_offset_positions",
     "fcv_flow_workspace_bytes",
     "fcv_flow_frontend",
     "fcv_speaker_projection",
@@ -129,6 +130,13 @@ class DitBatch(ctypes.Structure):
         ("n_attn_tiles_dev", ctypes.c_void_p),
         ("attn_sched", ctypes.c_void_p),
         ("attn_sched_ctas", ctypes.c_int),
+        ("doc_pos0", ctypes.c_void_p),
+        ("doc_kv_base", ctypes.c_void_p),
+        ("kv_cache", ctypes.c_void_p),
+        ("kv_layer_rows", ctypes.c_long),
+        ("conv_ctx", ctypes.c_void_p),
+        ("conv_ctx_out", ctypes.c_void_p),
+        ("ctx_row0", ctypes.c_void_p),
     ]
 
 
@@ -173,6 +181,7 @@ _SIGNATURES = {
     "fcv_launch_count": (ctypes.c_long, []),
     "fcv_dit_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i]),
     "fcv_dit_forward": (_i, [ctypes.POINTER(DitWeights), ctypes.POINTER(DitBatch), _vp, ctypes.c_size_t, _vp]),
+    "fcv_offset_positions": (_i, [_vp, _vp, _vp, _i, _vp]),
     "fcv_flow_workspace_bytes": (ctypes.c_size_t, [_i, _i]),
     "fcv_flow_frontend": (_i, [ctypes.POINTER(FlowWeights), _vp, _vp, _vp, _i, _i, _i, _i, _vp, ctypes.c_size_t,
                                _vp, _vp]),

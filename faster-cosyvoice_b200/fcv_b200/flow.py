@@ -30,7 +30,7 @@ import torch.nn as nn
 
 from . import _lib
 from ._lib import FlowWeights, call
-from .model import B200DiT, _dtype_code, _stream
+from .model import B200DiT, PrefixState, _dtype_code, _stream
 
 
 def cosine_schedule(num_timesteps: int, dtype: torch.dtype) -> list[float]:
@@ -358,15 +358,137 @@ def flow_inference_batched(flow, token_list: Sequence[Sequence[int]], prompt_fea
         return _split(x, mel_cu, prompt_lens)
 
 
+class PrefixCache:
+    """Cached state of streaming flows for prefix reuse.
+
+    The reference recomputes every frame of a stream at every call
+    (``flashinfer_flow.py:215-221``).  A frame in a chunk that was complete in
+    the previous call keeps a bit-identical trajectory (chunk-causal attention,
+    causal position convolutions, lookahead tokens that are the real next
+    tokens, the fixed noise prefix), so a call only needs its rows from the
+    first incomplete chunk on, given per ODE step and DiT block the earlier
+    frames' keys and values, per step the two position convolutions' 30-row
+    left context, and the final sample of the earlier frames.  This object
+    holds that state for up to ``max_streams`` streams of at most
+    ``max_frames`` Mel frames (prompt included): ``steps x depth x
+    (2 x max_streams x max_frames) x 2048`` K/V values (both CFG documents of a
+    stream), about 0.9 MB per frame and document over 10 steps and 22 blocks."""
+
+    def __init__(self, flow, max_streams: int, max_frames: int, num_timesteps: int = 10):
+        est = flow.decoder.estimator
+        if not isinstance(est, B200DiT):
+            raise TypeError("flow.decoder.estimator must be a B200DiT")
+        self.device, self.dtype = est.proj_out.weight.device, est.weight_dtype
+        self.steps, self.max_streams = int(num_timesteps), int(max_streams)
+        self.cap = -(-int(max_frames) // 64) * 64
+        self.chunk = int(est.static_chunk_size)
+        self.layer_rows = 2 * self.max_streams * self.cap
+        # zeroed once: attention loads whole 64-key tiles, and the rows past a document's
+        # keys must hold finite values (their probabilities are 0, but 0 x NaN is NaN)
+        self.kv = torch.zeros(self.steps, est.depth, self.layer_rows, 2048, dtype=self.dtype, device=self.device)
+        self.ctx = torch.zeros(self.steps, 2 * self.max_streams, 2, 30, 1024, dtype=self.dtype, device=self.device)
+        self.final = torch.zeros(self.max_streams, self.cap, 80, dtype=torch.float32, device=self.device)
+        self._state: dict = {}  # stream id -> [slot, stable frames]
+        self._free = list(range(self.max_streams))[::-1]
+
+    def stable_frames(self, stream_id) -> int:
+        """Frames of a stream whose state is cached (0 for an unknown stream)."""
+        st = self._state.get(stream_id)
+        return 0 if st is None else st[1]
+
+    def release(self, stream_id) -> None:
+        """Forget a stream (its slot is reused)."""
+        st = self._state.pop(stream_id, None)
+        if st is not None:
+            self._free.append(st[0])
+
+    def _acquire(self, stream_id) -> list:
+        st = self._state.get(stream_id)
+        if st is None:
+            if not self._free:
+                raise RuntimeError(f"prefix cache full ({self.max_streams} streams)")
+            slot = self._free.pop()
+            self.ctx[:, 2 * slot:2 * slot + 2].zero_()  # a fresh stream's convolutions see zeros
+            st = self._state[stream_id] = [slot, 0]
+        return st
+
+
+@torch.inference_mode()
+def _solve_euler_prefix(decoder, cache: PrefixCache, x0: torch.Tensor, mu: torch.Tensor, cond: torch.Tensor,
+                        spk: torch.Tensor, new_lens: list[int], pos0: list[int], slots: list[int],
+                        next_stable: list[int], num_timesteps: int) -> torch.Tensor:
+    """The streaming CFG Euler solver on the new rows only (chunk-causal mask),
+    every estimator call continuing the cached prefixes; returns the new rows'
+    final samples (float32)."""
+    est: B200DiT = decoder.estimator
+    rate = float(decoder.inference_cfg_rate)
+    dev, dt_w = cache.device, cache.dtype
+    R, N = len(new_lens), sum(new_lens)
+    x = x0.to(torch.float32).clone()
+    if N == 0:
+        return x
+    span = cosine_schedule(num_timesteps, spk.dtype)
+    t = span[0]
+    step = span[1] - span[0]
+    layout = est.prepare_layout(new_lens + new_lens, max(new_lens), True, dev)
+    # both CFG documents of request r: cache slots 2 slot_r and 2 slot_r + 1
+    docs = [2 * s for s in slots] + [2 * s + 1 for s in slots]
+    meta = torch.tensor(pos0 + pos0 + [d * cache.cap for d in docs] + docs
+                        + [n - p for n, p in zip(next_stable, pos0)] * 2, dtype=torch.int32).to(dev)
+    pos0_d, kvb_d, slot_d, row0_d = meta[:2 * R], meta[2 * R:4 * R], meta[4 * R:6 * R], meta[6 * R:]
+    positions = layout.positions.clone()
+    call("fcv_offset_positions", positions.data_ptr(), layout.document_ids.data_ptr(), pos0_d.data_ptr(), 2 * N,
+         _stream(dev))
+    slot_idx = slot_d.long()
+    max_pos = max(p + n for p, n in zip(pos0, new_lens))
+    mu_in = torch.zeros(2 * N, 80, dtype=dt_w, device=dev)
+    mu_in[:N].copy_(mu)
+    cond_in = torch.zeros(2 * N, 80, dtype=dt_w, device=dev)
+    cond_in[:N].copy_(cond)
+    spk_in = torch.zeros(2 * R, 80, dtype=dt_w, device=dev)
+    spk_in[:R].copy_(spk)
+    x_in = torch.empty(2 * N, 80, dtype=dt_w, device=dev)
+    x_in[:N].copy_(x)
+    x_in[N:].copy_(x)
+    d = torch.empty(2 * N, 80, dtype=torch.float32, device=dev)
+    t_in = torch.empty(2 * R, dtype=dt_w, device=dev)
+    stream = _stream(dev)
+    for k in range(1, num_timesteps + 1):
+        t_in.fill_(float(t))
+        ctx_in = cache.ctx[k - 1].index_select(0, slot_idx)
+        ctx_out = torch.empty_like(ctx_in)
+        prefix = PrefixState(positions, pos0_d, kvb_d, cache.kv[k - 1], cache.layer_rows, ctx_in, ctx_out, row0_d,
+                             max_pos)
+        est.forward_layout(layout, x_in, mu_in, t_in, spk_in, cond_in, out=d, packed=True, prefix=prefix)
+        cache.ctx[k - 1].index_copy_(0, slot_idx, ctx_out)
+        nxt = x_in.data_ptr() if k < num_timesteps else None
+        call("fcv_cfg_euler", x.data_ptr(), d.data_ptr(), _lib.DTYPE_F32, 1, N, float(step), rate, nxt,
+             _dtype_code(dt_w), stream)
+        t = t + step
+        if k < num_timesteps:
+            step = span[k + 1] - t
+    return x
+
+
 @torch.inference_mode()
 def flow_inference_batched_streaming(flow, token_list: Sequence[Sequence[int]],
                                      prompt_features: Sequence[torch.Tensor], speaker_embeddings: torch.Tensor,
-                                     finalize_list: Sequence[bool], num_timesteps: int = 10) -> list[torch.Tensor]:
+                                     finalize_list: Sequence[bool], num_timesteps: int = 10,
+                                     cache: PrefixCache | None = None,
+                                     stream_ids: Sequence | None = None) -> list[torch.Tensor]:
     """Full-prefix streaming flow inference for several streams
     (``flow_inference_batched_streaming``, ``flashinfer_flow.py:187-281``),
     device-packed: a non-final stream's last ``pre_lookahead_len`` tokens are
     lookahead context only, the start is the decoder's fixed noise prefix and
-    the estimator uses the chunk-causal mask."""
+    the estimator uses the chunk-causal mask.
+
+    With a :class:`PrefixCache` and one ``stream_ids`` entry per request (the
+    same id on every call of a stream) only the rows from each stream's first
+    incomplete chunk on are computed; the result is bit-identical to the full
+    recomputation.  A finalised stream is released from the cache."""
+    if cache is not None:
+        return _streaming_with_cache(flow, token_list, prompt_features, speaker_embeddings, finalize_list,
+                                     num_timesteps, cache, stream_ids)
     if len(token_list) != len(finalize_list):
         raise ValueError("token_list and finalize_list must have the same length")
     fe = prepare_frontend(flow)
@@ -390,3 +512,60 @@ def flow_inference_batched_streaming(flow, token_list: Sequence[Sequence[int]],
              mel_cu_d.data_ptr(), R, max_mel, x0.data_ptr(), _lib.DTYPE_F32, _stream(dev))
         x = solve_euler_packed(flow.decoder, x0, mu, mel_lens, spk, cond, num_timesteps, streaming=True)
         return _split(x, mel_cu, prompt_lens)
+
+
+def _streaming_with_cache(flow, token_list, prompt_features, speaker_embeddings, finalize_list, num_timesteps,
+                          cache: PrefixCache, stream_ids) -> list[torch.Tensor]:
+    if len(token_list) != len(finalize_list):
+        raise ValueError("token_list and finalize_list must have the same length")
+    if stream_ids is None or len(stream_ids) != len(token_list) or len(set(stream_ids)) != len(stream_ids):
+        raise ValueError("one distinct stream id per request is required with a prefix cache")
+    if num_timesteps != cache.steps:
+        raise ValueError(f"the cache holds {cache.steps} ODE steps, not {num_timesteps}")
+    fe = prepare_frontend(flow)
+    dev, dt = fe.device, fe.dtype
+    if dev != cache.device or dt != cache.dtype:
+        raise ValueError("the prefix cache belongs to another device or dtype")
+    R = len(token_list)
+    with torch.cuda.device(dev):
+        spk = _speaker_rows(fe, speaker_embeddings.to(device=dev, dtype=torch.float32))
+        out_lens = []
+        for r, (tl, fin) in enumerate(zip(token_list, finalize_list)):
+            if not fin and len(tl) < fe.lookahead:
+                raise ValueError(f"non-final stream {r} has fewer than {fe.lookahead} lookahead tokens")
+            out_lens.append(len(tl) if fin else len(tl) - fe.lookahead)
+        mu, cond, mel_lens, mel_cu, mel_cu_d, prompt_lens = _packed_front(flow, fe, token_list, prompt_features,
+                                                                          out_lens)
+        max_mel = max(mel_lens) if mel_lens else 0
+        if fe.rand_noise is None or fe.rand_noise.shape[2] < max_mel:
+            raise ValueError("the decoder's noise prefix is shorter than the longest stream")
+        states = [cache._acquire(sid) for sid in stream_ids]
+        for r, st in enumerate(states):
+            if mel_lens[r] > cache.cap:
+                raise ValueError(f"stream {stream_ids[r]!r} has {mel_lens[r]} frames, the cache holds {cache.cap}")
+            if mel_lens[r] < st[1]:
+                raise ValueError(f"stream {stream_ids[r]!r} shrank below its cached {st[1]} frames")
+        pos0 = [st[1] for st in states]
+        new_lens = [L - p for L, p in zip(mel_lens, pos0)]
+        nxt = [L if fin else (L // cache.chunk) * cache.chunk for L, fin in zip(mel_lens, finalize_list)]
+        # full noise rows as the non-cached path forms them, then the new rows of every request
+        x0_all = torch.empty(max(mel_cu[-1], 1), 80, dtype=torch.float32, device=dev)[:mel_cu[-1]]
+        call("fcv_pack_rows", fe.rand_noise.data_ptr(), _dtype_code(dt), 0, int(fe.rand_noise.shape[2]),
+             mel_cu_d.data_ptr(), R, max_mel, x0_all.data_ptr(), _lib.DTYPE_F32, _stream(dev))
+        idx = torch.cat([torch.arange(mel_cu[r] + pos0[r], mel_cu[r + 1]) for r in range(R)]).to(dev) \
+            if sum(new_lens) else torch.zeros(0, dtype=torch.long, device=dev)
+        x_new = _solve_euler_prefix(flow.decoder, cache, x0_all.index_select(0, idx), mu.index_select(0, idx),
+                                    cond.index_select(0, idx), spk, new_lens, pos0, [st[0] for st in states], nxt,
+                                    num_timesteps)
+        outs, o = [], 0
+        for r, st in enumerate(states):
+            slot, n = st[0], new_lens[r]
+            rows = torch.cat([cache.final[slot, :pos0[r]], x_new[o:o + n]])
+            cache.final[slot, pos0[r]:nxt[r]].copy_(x_new[o:o + nxt[r] - pos0[r]])
+            st[1] = nxt[r]
+            outs.append(rows[prompt_lens[r]:].t().unsqueeze(0).contiguous())
+            o += n
+        for sid, fin in zip(stream_ids, finalize_list):
+            if fin:
+                cache.release(sid)
+        return outs

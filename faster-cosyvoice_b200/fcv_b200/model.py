@@ -128,6 +128,25 @@ class PackedLayout:
     attn_ctas: int = 0
 
 
+@dataclass
+class PrefixState:
+    """Cached-prefix arguments of one estimator call (streaming prefix reuse,
+    see ``fcv_dit_batch``): absolute positions of the new rows, each document's
+    prefix length and first cache row, this ODE step's K/V cache
+    (depth x layer_rows x 2048) and the convolutions' left context in and out
+    ((B, 2, 30, 1024) each; ctx_row0 = local row where the next call starts)."""
+
+    positions: torch.Tensor
+    doc_pos0: torch.Tensor
+    doc_kv_base: torch.Tensor
+    kv_cache: torch.Tensor
+    layer_rows: int
+    conv_ctx: torch.Tensor
+    conv_ctx_out: torch.Tensor | None = None
+    ctx_row0: torch.Tensor | None = None
+    max_pos: int = 0
+
+
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
@@ -333,7 +352,8 @@ class B200DiT(nn.Module):
             self._workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
         return self._workspace
 
-    def batch_struct(self, layout: PackedLayout, x, mu, t, spks, cond, out, packed: bool = False) -> DitBatch:
+    def batch_struct(self, layout: PackedLayout, x, mu, t, spks, cond, out, packed: bool = False,
+                     prefix: PrefixState | None = None) -> DitBatch:
         """C-ABI batch descriptor.  ``packed``: x, mu, cond and out are (N, 80)
         rows in document order instead of (B, 80, T)."""
         b = DitBatch()
@@ -352,6 +372,19 @@ class B200DiT(nn.Module):
         if layout.attn_sched is not None and self.use_attn_schedule:
             b.attn_sched = layout.attn_sched.data_ptr()
             b.attn_sched_ctas = layout.attn_ctas
+        if prefix is not None:
+            if not packed:
+                raise ValueError("a cached prefix runs on packed rows")
+            b.positions = prefix.positions.data_ptr() if layout.N else b.positions
+            b.max_len = max(b.max_len, prefix.max_pos)
+            b.doc_pos0 = prefix.doc_pos0.data_ptr()
+            b.doc_kv_base = prefix.doc_kv_base.data_ptr()
+            b.kv_cache = prefix.kv_cache.data_ptr()
+            b.kv_layer_rows = prefix.layer_rows
+            b.conv_ctx = prefix.conv_ctx.data_ptr()
+            if prefix.conv_ctx_out is not None:
+                b.conv_ctx_out = prefix.conv_ctx_out.data_ptr()
+                b.ctx_row0 = prefix.ctx_row0.data_ptr()
         b.out = out.data_ptr()
         b.packed = 1 if packed else 0
         if out.dtype == torch.float32:
@@ -362,14 +395,15 @@ class B200DiT(nn.Module):
             raise ValueError(f"output must be float32 or {self.weight_dtype}")
         return b
 
-    def _launch(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor, packed: bool = False) -> None:
+    def _launch(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor, packed: bool = False,
+                prefix: PrefixState | None = None) -> None:
         ws = self._workspace_for(layout.N, len(layout.lengths), x.device)
-        bs = self.batch_struct(layout, x, mu, t, spks, cond, out, packed)
+        bs = self.batch_struct(layout, x, mu, t, spks, cond, out, packed, prefix)
         call("fcv_dit_forward", ctypes.byref(self.weights_struct()), ctypes.byref(bs), ws.data_ptr(),
              ws.numel(), _stream(x.device))
 
     def forward_layout(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor | None = None,
-                       graph: bool = False, packed: bool = False):
+                       graph: bool = False, packed: bool = False, prefix: PrefixState | None = None):
         """One estimator call on a prepared layout.  Inputs must already be
         contiguous tensors of the weight dtype on the module's device; ``out``
         may be float32 (the solver keeps the flow field unrounded).
@@ -381,11 +415,13 @@ class B200DiT(nn.Module):
         ``flashinfer_dit.py:806-826``, returns such views too).
 
         ``packed=True``: x, mu, cond are (N, 80) rows in document order and the
-        result is (N, 80) rows (the device-packed flow, no padded layout)."""
-        if not graph:
+        result is (N, 80) rows (the device-packed flow, no padded layout).
+        ``prefix``: the documents continue cached prefixes (streaming prefix
+        reuse, eager only)."""
+        if not graph or prefix is not None:
             if out is None:
                 out = self._new_out(layout, x.device, packed)
-            self._launch(layout, x, mu, t, spks, cond, out, packed)
+            self._launch(layout, x, mu, t, spks, cond, out, packed, prefix)
             return out
         entry = self.capture_graph(layout, x, mu, t, spks, cond, out, packed=packed)
         entry[0].replay()

@@ -145,6 +145,27 @@ typedef struct fcv_dit_batch {
                       * fcv_attn_schedule, for attn_sched_ctas CTAs; null:
                       * items dealt round robin.  Results do not depend on it. */
   int attn_sched_ctas;
+  /* Streaming prefix reuse (optional; all null = off).  Document d continues
+   * a prefix of doc_pos0[d] frames computed by earlier calls, whose state is
+   * cached: it runs only its new rows, positions must be absolute (see
+   * fcv_offset_positions), and packed must be 1.  Frames of chunks that were
+   * complete in the previous call keep bit-identical trajectories, so the
+   * result equals recomputing the whole prefix (flashinfer_flow.py:215-221). */
+  const int32_t* doc_pos0;    /* (B) device: absolute position of d's first row   */
+  const int32_t* doc_kv_base; /* (B) device: d's first row in a block's K/V cache */
+  void* kv_cache;             /* device: depth consecutive blocks of kv_layer_rows
+                               * x 2048 ([K | V], element type dtype); the new
+                               * rows' K/V are appended at doc_kv_base[d] + their
+                               * absolute positions, attention reads all keys
+                               * [0, doc_pos0[d] + L_d) from it                  */
+  long kv_layer_rows;
+  const void* conv_ctx;       /* (B, 2, 30, 1024) device, dtype: left context of
+                               * the two position convolutions (zeros for a
+                               * fresh document)                                 */
+  void* conv_ctx_out;         /* optional (B, 2, 30, 1024), not conv_ctx: the
+                               * next call's context, the 30 rows before local
+                               * row ctx_row0[d] (< 0: not written)             */
+  const int32_t* ctx_row0;
 } fcv_dit_batch;
 
 /* Layout ------------------------------------------------------------------ */
@@ -303,6 +324,11 @@ size_t fcv_dit_workspace_bytes(int N, int B, int depth, int dtype);
  * proj_out, unpack into batch->out.  `workspace` must be 256-byte aligned. */
 int fcv_dit_forward(const fcv_dit_weights* w, const fcv_dit_batch* batch, void* workspace,
                     size_t workspace_bytes, void* stream);
+
+/* positions[n] += doc_pos0[doc_ids[n]]: absolute positions for documents that
+ * continue a cached prefix (see fcv_dit_batch).  Apply once per layout. */
+int fcv_offset_positions(int32_t* positions, const int32_t* doc_ids, const int32_t* doc_pos0, int N,
+                         void* stream);
 
 /* Packed flow front end ----------------------------------------------------
  * Device-packed replacement of the per-request Python front end of
