@@ -29,6 +29,10 @@ comparison bar only: nothing of it is on the B200 path.
 ``--impl reference-gpu``) the reference's ``FlashInferDiT`` with and without its
 own graph buckets.
 
+``--stream [--prefix-cache]`` times a streaming session: 32 streams that advance by
+25 tokens (50 frames) per call, through ``flow_inference_batched_streaming``,
+recomputing the whole prefix (as the reference does) or reusing the cached one.
+
 ``--flow`` (configs 2 and 3) times the whole flow inference instead -- token
 front end and the 10-step CFG ODE -- through ``flow_inference_batched`` (offline)
 or ``flow_inference_batched_streaming`` (streaming); with ``--impl
@@ -335,6 +339,104 @@ def flow_arm(args, impl: str):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------- streaming calls
+def stream_arm(args, impl: str, cached: bool):
+    """One JSON line: a streaming session of 32 streams (config 3's prompts, 100-400
+    Mel frames) that each advance by 25 speech tokens (50 frames) per call, all
+    calls through flow_inference_batched_streaming (flashinfer_flow.py:187-281).
+    Calls 1..3 warm up (and build the cache); the next ``--steps`` calls are
+    timed.  Metric: new Mel frames per second (50 per stream per call)."""
+    import types
+
+    import torch
+
+    from fcv_b200.flow import B200Flow, PrefixCache, flow_inference_batched_streaming
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    rng = np.random.default_rng(2)
+    prompt_mel = [int(v) for v in rng.integers(100, 401, size=32)]
+    R = len(prompt_mel)
+    calls = 3 + args.steps
+    prng = np.random.default_rng(7)
+    tokens = [prng.integers(0, 6561, size=pm // 2 + 25 * (calls + 1) + 3).tolist() for pm in prompt_mel]
+    prompts = [torch.from_numpy(prng.standard_normal((1, pm, 80)).astype(np.float32)).to(device) for pm in prompt_mel]
+    spk = torch.from_numpy(prng.standard_normal((R, 192)).astype(np.float32)).to(device)
+    torch.manual_seed(2)
+    ours = B200Flow(depth=22).eval()
+    if impl == "b200":
+        flow = ours.to(device, torch.bfloat16)
+        flow.decoder.estimator.finalize_weights()
+        max_frames = max(prompt_mel) + 50 * (calls + 1) + 64
+        cache = PrefixCache(flow, max_streams=R, max_frames=max_frames) if cached else None
+        dtype = "bf16"
+
+        def run(tl):
+            if cache is None:
+                return flow_inference_batched_streaming(flow, tl, prompts, spk, [False] * R)
+            return flow_inference_batched_streaming(flow, tl, prompts, spk, [False] * R, cache=cache,
+                                                    stream_ids=list(range(R)))
+    else:
+        ref_root = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref_root, "faster_cosyvoice")):
+            print(json.dumps({"impl": "reference-gpu", "unavailable": "reference not installed in baseline/_ref"}))
+            return
+        for p in (ref_root, os.path.join(ROOT, "tests", "golden", "_xt_shim")):
+            if p not in sys.path:
+                sys.path.insert(0, p)
+        if "omegaconf" not in sys.modules:
+            stub = types.ModuleType("omegaconf")
+            stub.DictConfig = dict
+            sys.modules["omegaconf"] = stub
+        from faster_cosyvoice.token2wav import flashinfer_flow as ref_flow
+        from faster_cosyvoice.token2wav.cosyvoice.flow.flow import CausalMaskedDiffWithDiT
+        from faster_cosyvoice.token2wav.cosyvoice.flow.flow_matching import CausalConditionalCFM
+        from faster_cosyvoice.token2wav.cosyvoice.transformer.upsample_encoder import PreLookaheadLayer
+        from faster_cosyvoice.token2wav.flashinfer_dit import FlashInferDiT
+
+        rdt = torch.float16 if args.ref_dtype == "fp16" else torch.bfloat16
+        est = FlashInferDiT(device=device, static_chunk_size=50)
+        est.load_state_dict(ours.decoder.estimator.state_dict(), strict=False)
+        est = est.to(device=device, dtype=rdt).eval()
+        est.finalize_weights()
+        cfm = types.SimpleNamespace(sigma_min=1e-6, solver="euler", t_scheduler="cosine", training_cfg_rate=0.2,
+                                    inference_cfg_rate=0.7, reg_loss_type="l1")
+        decoder = CausalConditionalCFM(in_channels=240, cfm_params=cfm, n_spks=1, spk_emb_dim=80, estimator=est)
+        flow = CausalMaskedDiffWithDiT(input_size=80, output_size=80, spk_embed_dim=192, output_type="mel",
+                                       vocab_size=6561, input_frame_rate=25, only_mask_loss=True, token_mel_ratio=2,
+                                       pre_lookahead_len=3,
+                                       pre_lookahead_layer=PreLookaheadLayer(in_channels=80, channels=1024,
+                                                                             pre_lookahead_len=3),
+                                       decoder=decoder)
+        flow.load_state_dict({k: v for k, v in ours.state_dict().items() if not k.startswith("decoder.")},
+                             strict=False)
+        flow = flow.to(device).to(rdt).eval()
+        dtype = "f16" if rdt == torch.float16 else "bf16"
+
+        def run(tl):
+            return ref_flow.flow_inference_batched_streaming(flow, tl, prompts, spk, [False] * R)
+
+    stream = torch.cuda.current_stream(device)
+    times, frames = [], []
+    for c in range(calls):
+        tl = [tokens[r][:prompt_mel[r] // 2 + 25 * (c + 1) + 3] for r in range(R)]
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        run(tl)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if c >= 3:
+            times.append(e0.elapsed_time(e1))
+            frames.append(sum(2 * (len(t) - 3) for t in tl))
+    t = float(np.mean(times))
+    print(json.dumps({"metric": "streaming flow: new mel-frames/s (32 streams, +50 frames per call)",
+                      "unit": UNIT, "value": R * 50 / (t / 1000.0), "impl": impl if impl == "b200" else "reference-gpu",
+                      "prefix_cache": cached, "ms_per_call": t, "calls_timed": len(times),
+                      "frames_per_call_total": float(np.mean(frames)), "dtype": dtype,
+                      "data": "synthetic (config-3 prompt lengths, seeded tokens)"}), flush=True)
+
+
 # ---------------------------------------------------------------------------- single-request latency
 def latency_arm(args, impl: str):
     """One JSON line: latency of one estimator call for one CFG pair (B = 2),
@@ -540,6 +642,10 @@ def main():
     ap.add_argument("--latency", action="store_true",
                     help="latency of one estimator call for one CFG pair, eager and graph-bucketed "
                          "(--config 3 for the streaming mask)")
+    ap.add_argument("--stream", action="store_true",
+                    help="a streaming session: 32 streams advancing 50 frames per call (full prefix recomputed)")
+    ap.add_argument("--prefix-cache", action="store_true",
+                    help="with --stream: reuse the cached prefix (this build only)")
     ap.add_argument("--requests", type=int, default=0,
                     help="use only the first R requests of the config (small cases for profiling)")
     args = ap.parse_args()
@@ -557,6 +663,11 @@ def main():
            "packed_rows": 2 * sum(req_lengths), "chunk": chunk, "seed": seed,
            "parallelism": f"dp{world} (request bins, no collective)",
            "l2": "working set (662 MB of weights per NFE) exceeds the 126 MB L2; L2 also flushed between steps"}
+
+    if args.stream:
+        if rank == 0 and args.impl != "reference":
+            stream_arm(args, args.impl, args.prefix_cache and args.impl == "b200")
+        return
 
     if args.latency:
         if rank == 0 and args.impl != "reference":
