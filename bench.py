@@ -418,22 +418,23 @@ def stream_arm(args, impl: str, cached: bool):
 
     stream = torch.cuda.current_stream(device)
     times, frames = [], []
-    for c in range(calls):
-        tl = [tokens[r][:prompt_mel[r] // 2 + 25 * (c + 1) + 3] for r in range(R)]
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        run(tl)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        if c >= 3:
-            times.append(e0.elapsed_time(e1))
-            frames.append(sum(2 * (len(t) - 3) for t in tl))
+    with ClockSampler(0) as clocks:
+        for c in range(calls):
+            tl = [tokens[r][:prompt_mel[r] // 2 + 25 * (c + 1) + 3] for r in range(R)]
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            run(tl)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            if c >= 3:
+                times.append(e0.elapsed_time(e1))
+                frames.append(sum(2 * (len(t) - 3) for t in tl))
     t = float(np.mean(times))
     print(json.dumps({"metric": "streaming flow: new mel-frames/s (32 streams, +50 frames per call)",
                       "unit": UNIT, "value": R * 50 / (t / 1000.0), "impl": impl if impl == "b200" else "reference-gpu",
                       "prefix_cache": cached, "ms_per_call": t, "calls_timed": len(times),
-                      "frames_per_call_total": float(np.mean(frames)), "dtype": dtype,
+                      "frames_per_call_total": float(np.mean(frames)), "dtype": dtype, "clocks": clocks.summary(),
                       "data": "synthetic (config-3 prompt lengths, seeded tokens)"}), flush=True)
 
 

@@ -584,16 +584,17 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   const long G = (long)N + 30L * (B + 1);
   const int G_rows = N + 30 * B;  // gapped rows that can hold data
 
-  // 1. time embedding + all AdaLN projections (one GEMM, flashinfer_dit.py:430-445)
-  {
-  ProfScope ps(FCV_CAT_ADALN, s);
-  FCV_TRY(run_time_embed<T>(w, bt->t, B, ws.tsin, ws.th1, ws.temb, ws.silu, s));
-  {
+  // 1. time embedding + all AdaLN projections (one GEMM, flashinfer_dit.py:430-445), or one
+  // precomputed row shared by every document (the ODE solver's documents share t): stride 0
+  const float* mods = bt->shared_mods ? bt->shared_mods : ws.mods;
+  const long mstride = bt->shared_mods ? 0 : MS;
+  if (!bt->shared_mods) {
+    ProfScope ps(FCV_CAT_ADALN, s);
+    FCV_TRY(run_time_embed<T>(w, bt->t, B, ws.tsin, ws.th1, ws.temb, ws.silu, s));
     GemmCall g{};
     g.A = ws.silu; g.lda = 1024; g.a_rows = B; g.W = w->ada_w; g.M = B; g.N = (int)MS; g.K = 1024;
     g.epi = make_epi(EPI_F32, B, (int)MS, ws.mods, MS, w->ada_b);
     FCV_TRY(run_gemm(g, dtype, s));
-  }
   }
   if (N == 0) return FCV_OK;
 
@@ -643,10 +644,10 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   // 3. DiT blocks (flashinfer_dit.py:485-533; DiTBlock.forward modules.py:516-530)
   const size_t es = dsize(dtype);
   for (int i = 0; i < depth; ++i) {
-    const float* mi = ws.mods + (long)i * 6144;
+    const float* mi = mods + (long)i * 6144;
     {
       ProfScope ps(FCV_CAT_LN, s);
-      FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mi + 0, mi + 1024, bt->doc_ids, MS, N, ws.norm, dtype, s));
+      FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mi + 0, mi + 1024, bt->doc_ids, mstride, N, ws.norm, dtype, s));
     }
     GemmCall q{};
     q.A = ws.norm; q.lda = 1024; q.a_rows = N; q.M = N; q.N = 3072; q.K = 1024;
@@ -682,14 +683,14 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     o.epi = make_epi(EPI_GATE_RES, N, 1024, ws.h, 1024, w->o_b + (long)i * 1024);
     o.epi.aux = bt->doc_ids;
     o.epi.gate = mi + 2048;
-    o.epi.gate_stride = MS;
+    o.epi.gate_stride = mstride;
     {
       ProfScope ps(FCV_CAT_GEMM_OUT, s);
       FCV_TRY(run_gemm(o, dtype, s));
     }
     {
       ProfScope ps(FCV_CAT_LN, s);
-      FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mi + 3072, mi + 4096, bt->doc_ids, MS, N, ws.norm, dtype, s));
+      FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mi + 3072, mi + 4096, bt->doc_ids, mstride, N, ws.norm, dtype, s));
     }
     GemmCall f1{};
     f1.A = ws.norm; f1.lda = 1024; f1.a_rows = N; f1.M = N; f1.N = 2048; f1.K = 1024;
@@ -705,7 +706,7 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     f2.epi = make_epi(EPI_GATE_RES, N, 1024, ws.h, 1024, w->ff2_b + (long)i * 1024);
     f2.epi.aux = bt->doc_ids;
     f2.epi.gate = mi + 5120;
-    f2.epi.gate_stride = MS;
+    f2.epi.gate_stride = mstride;
     {
       ProfScope ps(FCV_CAT_GEMM_FF2, s);
       FCV_TRY(run_gemm(f2, dtype, s));
@@ -713,9 +714,9 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
   }
 
   // 4. final AdaLN (chunk order scale, shift: modules.py:260-265), proj_out, unpack
-  const float* mf = ws.mods + (long)depth * 6144;
+  const float* mf = mods + (long)depth * 6144;
   ProfScope ps_out(FCV_CAT_OUTPUT, s);
-  FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mf + 1024, mf + 0, bt->doc_ids, MS, N, ws.norm, dtype, s));
+  FCV_TRY(run_ln(ws.h, FCV_DTYPE_F32, mf + 1024, mf + 0, bt->doc_ids, mstride, N, ws.norm, dtype, s));
   if (bt->packed) {
     // packed output rows (N, 80): a plain row-major store, nothing to unpack or zero
     GemmCall po{};
@@ -1121,6 +1122,27 @@ int fcv_dit_forward(const fcv_dit_weights* w, const fcv_dit_batch* bt, void* wor
   return forward_impl<float>(w, bt, ws, s);
 }
 
+
+int fcv_dit_modulations(const fcv_dit_weights* w, const void* t, float* mods, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  if (!w || !t || !mods || !workspace) return fail(FCV_EINVAL, "fcv_dit_modulations: null argument");
+  if (!valid_dtype(w->dtype) || w->depth < 1) return fail(FCV_EINVAL, "fcv_dit_modulations: bad weights");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return fail(FCV_EINVAL, "fcv_dit_modulations: workspace must be 256-byte aligned");
+  Workspace ws = carve(static_cast<uint8_t*>(workspace), 0, 1, w->depth, w->dtype);
+  if (ws.total > workspace_bytes)
+    return fail(FCV_EINVAL, "fcv_dit_modulations: workspace of %zu bytes < %zu needed", workspace_bytes, ws.total);
+  cudaStream_t s = as_stream(stream);
+  const long MS = (long)w->depth * 6144 + 2048;
+  if (w->dtype == FCV_DTYPE_BF16)
+    FCV_TRY(run_time_embed<bf16>(w, t, 1, ws.tsin, ws.th1, ws.temb, ws.silu, s));
+  else
+    FCV_TRY(run_time_embed<float>(w, t, 1, ws.tsin, ws.th1, ws.temb, ws.silu, s));
+  GemmCall g{};
+  g.A = ws.silu; g.lda = 1024; g.a_rows = 1; g.W = w->ada_w; g.M = 1; g.N = (int)MS; g.K = 1024;
+  g.epi = make_epi(EPI_F32, 1, (int)MS, mods, MS, w->ada_b);
+  return run_gemm(g, w->dtype, s);
+}
 
 int fcv_offset_positions(int32_t* positions, const int32_t* doc_ids, const int32_t* doc_pos0, int N, void* stream) {
   if (!positions || !doc_ids || !doc_pos0 || N < 0) return fail(FCV_EINVAL, "fcv_offset_positions: bad arguments");

@@ -58,6 +58,7 @@ EXPORTS = (
     "fcv_dit_workspace_bytes",
     "fcv_dit_forward",
     "fcv_offset_positions",
+    "fcv_dit_modulations",
     "fcv_flow_workspace_bytes",
     "fcv_flow_frontend",
     "fcv_speaker_projection",
@@ -137,6 +138,7 @@ class DitBatch(ctypes.Structure):
         ("conv_ctx", ctypes.c_void_p),
         ("conv_ctx_out", ctypes.c_void_p),
         ("ctx_row0", ctypes.c_void_p),
+        ("shared_mods", ctypes.c_void_p),
     ]
 
 
@@ -182,6 +184,7 @@ _SIGNATURES = {
     "fcv_dit_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i]),
     "fcv_dit_forward": (_i, [ctypes.POINTER(DitWeights), ctypes.POINTER(DitBatch), _vp, ctypes.c_size_t, _vp]),
     "fcv_offset_positions": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "fcv_dit_modulations": (_i, [ctypes.POINTER(DitWeights), _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "fcv_flow_workspace_bytes": (ctypes.c_size_t, [_i, _i]),
     "fcv_flow_frontend": (_i, [ctypes.POINTER(FlowWeights), _vp, _vp, _vp, _i, _i, _i, _i, _vp, ctypes.c_size_t,
                                _vp, _vp]),

@@ -81,7 +81,8 @@ def solve_euler_batched(decoder, noise: torch.Tensor, mu: torch.Tensor, mask: to
         stream = _stream(dev)
         for k in range(1, num_timesteps + 1):
             t_in.fill_(float(t))
-            est.forward_layout(layout, x_in, mu_in, t_in, spk_in, cond_in, out=d)
+            est.forward_layout(layout, x_in, mu_in, t_in, spk_in, cond_in, out=d,
+                               shared_mods=est.shared_modulations(float(t)))
             nxt = x_in.data_ptr() if k < num_timesteps else None
             call("fcv_cfg_euler", x.data_ptr(), d.data_ptr(), _lib.DTYPE_F32, R, T, float(step), rate, nxt,
                  _dtype_code(dt_w), stream)
@@ -255,7 +256,8 @@ def solve_euler_packed(decoder, noise_rows: torch.Tensor, mu_rows: torch.Tensor,
         stream = _stream(dev)
         for k in range(1, num_timesteps + 1):
             t_in.fill_(float(t))
-            est.forward_layout(layout, x_in, mu_in, t_in, spk_in, cond_in, out=d, packed=True)
+            est.forward_layout(layout, x_in, mu_in, t_in, spk_in, cond_in, out=d, packed=True,
+                               shared_mods=est.shared_modulations(float(t)))
             nxt = x_in.data_ptr() if k < num_timesteps else None
             # rows (N, 80) are one flat run of 80*N values: the kernel's (R=1, 80, T=N) view
             call("fcv_cfg_euler", x.data_ptr(), d.data_ptr(), _lib.DTYPE_F32, 1, N, float(step), rate, nxt,
@@ -459,7 +461,8 @@ def _solve_euler_prefix(decoder, cache: PrefixCache, x0: torch.Tensor, mu: torch
         ctx_out = torch.empty_like(ctx_in)
         prefix = PrefixState(positions, pos0_d, kvb_d, cache.kv[k - 1], cache.layer_rows, ctx_in, ctx_out, row0_d,
                              max_pos)
-        est.forward_layout(layout, x_in, mu_in, t_in, spk_in, cond_in, out=d, packed=True, prefix=prefix)
+        est.forward_layout(layout, x_in, mu_in, t_in, spk_in, cond_in, out=d, packed=True, prefix=prefix,
+                           shared_mods=est.shared_modulations(float(t)))
         cache.ctx[k - 1].index_copy_(0, slot_idx, ctx_out)
         nxt = x_in.data_ptr() if k < num_timesteps else None
         call("fcv_cfg_euler", x.data_ptr(), d.data_ptr(), _lib.DTYPE_F32, 1, N, float(step), rate, nxt,

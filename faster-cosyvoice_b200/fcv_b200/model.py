@@ -197,6 +197,9 @@ class B200DiT(nn.Module):
         self.bucket_captures = 0
         # balanced (LPT) attention schedule per batch composition; False deals items round robin
         self.use_attn_schedule = True
+        # AdaLN modulation rows per timestep value (the ODE schedule's t values repeat on every call)
+        self._mod_cache: dict = {}
+        self._mod_ws: torch.Tensor | None = None
         self._finalized = False
         self._derived: dict[str, torch.Tensor] = {}
         self._graphs: OrderedDict = OrderedDict()
@@ -283,6 +286,27 @@ class B200DiT(nn.Module):
             raise RuntimeError("call finalize_weights() first")
         return self._weights
 
+    def shared_modulations(self, t: float) -> torch.Tensor:
+        """The AdaLN modulation row (depth * 6144 + 2048 floats) of timestep ``t``
+        rounded to the weight dtype, computed once per value and kept: the ODE
+        solver's documents share t and its ten schedule values repeat on every
+        call, so the time embedding and the 281 MB modulation GEMM run once per
+        value instead of once per estimator call."""
+        dev, dt = self.proj_out.weight.device, self.weight_dtype
+        tv = torch.tensor([float(t)], dtype=dt)
+        key = float(tv.float().item())
+        row = self._mod_cache.get(key)
+        if row is None:
+            need = int(lib().fcv_dit_workspace_bytes(0, 1, self.depth, _dtype_code(dt)))
+            if self._mod_ws is None or self._mod_ws.numel() < need:
+                self._mod_ws = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+            row = torch.empty(self.depth * 6144 + 2048, dtype=torch.float32, device=dev)
+            t_dev = tv.to(dev)
+            call("fcv_dit_modulations", ctypes.byref(self.weights_struct()), t_dev.data_ptr(), row.data_ptr(),
+                 self._mod_ws.data_ptr(), self._mod_ws.numel(), _stream(dev))
+            self._mod_cache[key] = row
+        return row
+
     # ------------------------------------------------------------------ layout
     def prepare_layout(self, lengths: Sequence[int], padded_length: int, streaming: bool,
                        device: torch.device | None = None, lengths_dev: torch.Tensor | None = None) -> PackedLayout:
@@ -353,7 +377,7 @@ class B200DiT(nn.Module):
         return self._workspace
 
     def batch_struct(self, layout: PackedLayout, x, mu, t, spks, cond, out, packed: bool = False,
-                     prefix: PrefixState | None = None) -> DitBatch:
+                     prefix: PrefixState | None = None, shared_mods: torch.Tensor | None = None) -> DitBatch:
         """C-ABI batch descriptor.  ``packed``: x, mu, cond and out are (N, 80)
         rows in document order instead of (B, 80, T)."""
         b = DitBatch()
@@ -372,6 +396,8 @@ class B200DiT(nn.Module):
         if layout.attn_sched is not None and self.use_attn_schedule:
             b.attn_sched = layout.attn_sched.data_ptr()
             b.attn_sched_ctas = layout.attn_ctas
+        if shared_mods is not None:
+            b.shared_mods = shared_mods.data_ptr()
         if prefix is not None:
             if not packed:
                 raise ValueError("a cached prefix runs on packed rows")
@@ -396,14 +422,15 @@ class B200DiT(nn.Module):
         return b
 
     def _launch(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor, packed: bool = False,
-                prefix: PrefixState | None = None) -> None:
+                prefix: PrefixState | None = None, shared_mods: torch.Tensor | None = None) -> None:
         ws = self._workspace_for(layout.N, len(layout.lengths), x.device)
-        bs = self.batch_struct(layout, x, mu, t, spks, cond, out, packed, prefix)
+        bs = self.batch_struct(layout, x, mu, t, spks, cond, out, packed, prefix, shared_mods)
         call("fcv_dit_forward", ctypes.byref(self.weights_struct()), ctypes.byref(bs), ws.data_ptr(),
              ws.numel(), _stream(x.device))
 
     def forward_layout(self, layout: PackedLayout, x, mu, t, spks, cond, out: torch.Tensor | None = None,
-                       graph: bool = False, packed: bool = False, prefix: PrefixState | None = None):
+                       graph: bool = False, packed: bool = False, prefix: PrefixState | None = None,
+                       shared_mods: torch.Tensor | None = None):
         """One estimator call on a prepared layout.  Inputs must already be
         contiguous tensors of the weight dtype on the module's device; ``out``
         may be float32 (the solver keeps the flow field unrounded).
@@ -417,11 +444,12 @@ class B200DiT(nn.Module):
         ``packed=True``: x, mu, cond are (N, 80) rows in document order and the
         result is (N, 80) rows (the device-packed flow, no padded layout).
         ``prefix``: the documents continue cached prefixes (streaming prefix
-        reuse, eager only)."""
-        if not graph or prefix is not None:
+        reuse, eager only).  ``shared_mods``: every document shares this
+        modulation row (:meth:`shared_modulations`), ``t`` is then unused."""
+        if not graph or prefix is not None or shared_mods is not None:
             if out is None:
                 out = self._new_out(layout, x.device, packed)
-            self._launch(layout, x, mu, t, spks, cond, out, packed, prefix)
+            self._launch(layout, x, mu, t, spks, cond, out, packed, prefix, shared_mods)
             return out
         entry = self.capture_graph(layout, x, mu, t, spks, cond, out, packed=packed)
         entry[0].replay()

@@ -166,6 +166,13 @@ typedef struct fcv_dit_batch {
                                * next call's context, the 30 rows before local
                                * row ctx_row0[d] (< 0: not written)             */
   const int32_t* ctx_row0;
+  const float* shared_mods;   /* optional (device): one modulation row (depth*6144
+                               * + 2048 floats, fcv_dit_modulations) that every
+                               * document uses -- the ODE solver's documents
+                               * share t (flashinfer_flow.py:55-58), and the
+                               * schedule's ten t values repeat on every call --
+                               * so the time embedding and the AdaLN GEMM are
+                               * skipped; t is then unused                       */
 } fcv_dit_batch;
 
 /* Layout ------------------------------------------------------------------ */
@@ -324,6 +331,14 @@ size_t fcv_dit_workspace_bytes(int N, int B, int depth, int dtype);
  * proj_out, unpack into batch->out.  `workspace` must be 256-byte aligned. */
 int fcv_dit_forward(const fcv_dit_weights* w, const fcv_dit_batch* batch, void* workspace,
                     size_t workspace_bytes, void* stream);
+
+/* The AdaLN modulation row of one timestep (TimestepEmbedding + every block's
+ * AdaLayerNormZero and the final norm, flashinfer_dit.py:430-445) for
+ * fcv_dit_batch.shared_mods: t is one value of the weights' dtype on the
+ * device, mods receives depth*6144 + 2048 floats; workspace as
+ * fcv_dit_workspace_bytes(0, 1, depth, dtype). */
+int fcv_dit_modulations(const fcv_dit_weights* w, const void* t, float* mods, void* workspace,
+                        size_t workspace_bytes, void* stream);
 
 /* positions[n] += doc_pos0[doc_ids[n]]: absolute positions for documents that
  * continue a cached prefix (see fcv_dit_batch).  Apply once per layout. */

@@ -270,3 +270,24 @@ def test_attention_schedule_does_not_change_results(streaming):
         b = model.forward_layout(lay, x, mu, t, spks, cond)
     model.use_attn_schedule = True
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_shared_modulation_row_equals_per_document_time_embedding(dtype):
+    """When every document has the same t (the ODE solver's case), the cached
+    modulation row of that t (fcv_dit_modulations, broadcast with stride 0)
+    gives exactly the per-document time embedding + AdaLN GEMM result."""
+    dt = getattr(torch, dtype)
+    model = _model(7, 2, dt)
+    rng = np.random.default_rng(29)
+    lengths = [150, 77, 150, 77]
+    B, T = len(lengths), max(lengths)
+    x, mu, cond = (torch.tensor(rng.standard_normal((B, 80, T)), device=DEV).to(dt) for _ in range(3))
+    spks = torch.tensor(rng.standard_normal((B, 80)), device=DEV).to(dt)
+    t = torch.full((B,), 0.3071, device=DEV, dtype=dt)
+    lay = model.prepare_layout(lengths, T, False, torch.device(DEV))
+    with torch.inference_mode():
+        a = model.forward_layout(lay, x, mu, t, spks, cond)
+        b = model.forward_layout(lay, x, mu, t, spks, cond, shared_mods=model.shared_modulations(0.3071))
+    assert torch.equal(a, b)
+    assert len(model._mod_cache) == 1
