@@ -200,6 +200,8 @@ class B200DiT(nn.Module):
         # AdaLN modulation rows per timestep value (the ODE schedule's t values repeat on every call)
         self._mod_cache: dict = {}
         self._mod_ws: torch.Tensor | None = None
+        self._stage: OrderedDict = OrderedDict()  # device buffers for host inputs
+        self._copy_stream: torch.cuda.Stream | None = None
         self._finalized = False
         self._derived: dict[str, torch.Tensor] = {}
         self._graphs: OrderedDict = OrderedDict()
@@ -494,17 +496,52 @@ class B200DiT(nn.Module):
         dt = self.weight_dtype
         dev = self.proj_out.weight.device
         with torch.cuda.device(dev):
-            x = x.to(device=dev, dtype=dt).contiguous()
-            mu = mu.to(device=dev, dtype=dt).contiguous()
-            cond = cond.to(device=dev, dtype=dt).contiguous()
-            spks = spks.to(device=dev, dtype=dt).contiguous()
             B, C, T = x.shape
             if C != MEL or mu.shape != x.shape or cond.shape != x.shape or spks.shape != (B, MEL):
                 raise ValueError("expected x, mu, cond of shape (B, 80, T) and spks of shape (B, 80)")
-            t = t.to(device=dev, dtype=dt)
             if t.ndim == 0:
                 t = t.repeat(B)
-            t = t.reshape(B).contiguous()
+            t = t.reshape(B)
+            staged = None
+            if x.device.type == "cpu":
+                # host inputs: uploaded on a copy stream into one of two persistent device buffer
+                # sets (stable addresses for graph replay), so the next call's upload overlaps this
+                # call's compute; asynchronous when the host memory is pinned, and the caller keeps
+                # the host tensors unchanged until the upload has run
+                staged = self._staging(B, T, dt, dev)
+                cs = self._copy_stream_for(dev)
+                cs.wait_event(staged["free"])  # the compute that last read this set is done
+                with torch.cuda.stream(cs):
+                    for name, src in (("x", x), ("mu", mu), ("cond", cond), ("spks", spks), ("t", t)):
+                        staged[name].copy_(src, non_blocking=src.is_pinned())
+                    staged["ready"].record(cs)
+                torch.cuda.current_stream(dev).wait_event(staged["ready"])
+                x, mu, cond, spks, t = staged["x"], staged["mu"], staged["cond"], staged["spks"], staged["t"]
+            else:
+                x = x.to(device=dev, dtype=dt).contiguous()
+                mu = mu.to(device=dev, dtype=dt).contiguous()
+                cond = cond.to(device=dev, dtype=dt).contiguous()
+                spks = spks.to(device=dev, dtype=dt).contiguous()
+                t = t.to(device=dev, dtype=dt).contiguous()
+            if mask.device.type == "cpu":
+                # lengths counted on the host (entries > 0.5, exact): no device round trip per call
+                lengths = (mask.reshape(B, -1)[:, :T] > 0.5).sum(-1).tolist()
+                y = None
+                if self.use_cuda_graph and self.graph_buckets:
+                    y = self.forward_bucketed(lengths, x, mu, t, spks, cond, streaming)
+                if y is None:
+                    layout = self.prepare_layout(lengths, T, streaming, dev)
+                    y = self.forward_layout(layout, x, mu, t, spks, cond,
+                                            graph=self.use_cuda_graph and not self.graph_buckets)
+                if staged is not None:
+                    staged["free"].record(torch.cuda.current_stream(dev))
+                return y
+            if staged is not None:  # device mask: every use of the staged set is enqueued below
+                m = mask.to(device=dev, dtype=dt).contiguous()
+                layout = self.layout_from_mask(m, streaming)
+                y = self.forward_layout(layout, x, mu, t, spks, cond, graph=self.use_cuda_graph)
+                staged["free"].record(torch.cuda.current_stream(dev))
+                return y
             if self.use_cuda_graph and self.graph_buckets:
                 m = mask.to(device=dev, dtype=dt).contiguous()
                 lengths_dev = torch.empty(B, dtype=torch.int32, device=dev)
@@ -517,6 +554,33 @@ class B200DiT(nn.Module):
                 return self.forward_layout(layout, x, mu, t, spks, cond)
             layout = self.layout_from_mask(mask.to(dev), streaming)
             return self.forward_layout(layout, x, mu, t, spks, cond, graph=self.use_cuda_graph)
+
+    def _staging(self, B: int, T: int, dt: torch.dtype, dev: torch.device) -> dict:
+        """The next of two persistent device buffer sets for host inputs of one (B, T)
+        shape, with its upload-done and compute-done events (FIFO of 8 shapes)."""
+        key = (B, T)
+        pair = self._stage.get(key)
+        if pair is None:
+            if len(self._stage) >= 8:
+                torch.cuda.synchronize(dev)  # nothing may still read the evicted buffers
+                self._stage.popitem(last=False)
+            pair = [0, []]
+            for _ in range(2):
+                pair[1].append({"x": torch.empty(B, MEL, T, dtype=dt, device=dev),
+                                "mu": torch.empty(B, MEL, T, dtype=dt, device=dev),
+                                "cond": torch.empty(B, MEL, T, dtype=dt, device=dev),
+                                "spks": torch.empty(B, MEL, dtype=dt, device=dev),
+                                "t": torch.empty(B, dtype=dt, device=dev),
+                                "ready": torch.cuda.Event(), "free": torch.cuda.Event()})
+            self._stage[key] = pair
+        st = pair[1][pair[0]]
+        pair[0] ^= 1
+        return st
+
+    def _copy_stream_for(self, dev: torch.device) -> torch.cuda.Stream:
+        if self._copy_stream is None:
+            self._copy_stream = torch.cuda.Stream(dev)
+        return self._copy_stream
 
     # ------------------------------------------------------------------ bucketed graphs
     def bucket_for(self, lengths: Sequence[int]) -> tuple[int, int] | None:

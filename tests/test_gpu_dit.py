@@ -291,3 +291,37 @@ def test_shared_modulation_row_equals_per_document_time_embedding(dtype):
         b = model.forward_layout(lay, x, mu, t, spks, cond, shared_mods=model.shared_modulations(0.3071))
     assert torch.equal(a, b)
     assert len(model._mod_cache) == 1
+
+
+def test_host_inputs_match_device_inputs():
+    """forward() on host tensors (pinned or not; lengths counted from the host
+    mask, inputs staged into persistent device buffers) gives exactly the
+    device-tensor result, eagerly, through the per-layout graph and through the
+    bucketed graph; a replay with new host values follows them."""
+    model = _model(8, 2, torch.bfloat16)
+    rng = np.random.default_rng(33)
+    lengths = [120, 57, 120, 57]
+    B, T = len(lengths), 124
+    host = {k: torch.tensor(rng.standard_normal((B, 80, T)), dtype=torch.bfloat16) for k in ("x", "mu", "cond")}
+    host["spks"] = torch.tensor(rng.standard_normal((B, 80)), dtype=torch.bfloat16)
+    host["t"] = torch.tensor(rng.uniform(size=B), dtype=torch.bfloat16)
+    host["mask"] = torch.zeros(B, 1, T, dtype=torch.bfloat16)
+    for b, L in enumerate(lengths):
+        host["mask"][b, 0, :L] = 1
+    order = ("x", "mask", "mu", "t", "spks", "cond")
+    dev = {k: v.to(DEV) for k, v in host.items()}
+    pinned = {k: v.pin_memory() for k, v in host.items()}
+    with torch.inference_mode():
+        for graph, buckets in ((False, None), (True, None), (True, (512,))):
+            model.use_cuda_graph, model.graph_buckets = graph, buckets
+            ref = model(*(dev[k] for k in order)).clone()
+            for src in (host, pinned):
+                got = model(*(src[k] for k in order))
+                torch.cuda.synchronize()
+                assert torch.equal(got, ref), (graph, buckets, src is pinned)
+        pinned["x"].mul_(0.5)
+        got = model(*(pinned[k] for k in order))
+        torch.cuda.synchronize()
+        ref = model(*(pinned[k].to(DEV) for k in order))
+        assert torch.equal(got, ref)
+    model.use_cuda_graph, model.graph_buckets = False, None
