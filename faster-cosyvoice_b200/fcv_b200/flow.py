@@ -488,7 +488,9 @@ def flow_inference_batched_streaming(flow, token_list: Sequence[Sequence[int]],
     With a :class:`PrefixCache` and one ``stream_ids`` entry per request (the
     same id on every call of a stream) only the rows from each stream's first
     incomplete chunk on are computed; the result is bit-identical to the full
-    recomputation.  A finalised stream is released from the cache."""
+    recomputation.  A stream's tokens may only grow between its calls, and its
+    prompt and speaker embedding must stay the same (the cached state depends on
+    them).  A finalised stream is released from the cache."""
     if cache is not None:
         return _streaming_with_cache(flow, token_list, prompt_features, speaker_embeddings, finalize_list,
                                      num_timesteps, cache, stream_ids)
