@@ -572,6 +572,9 @@ class B200DiT(nn.Module):
                                 "spks": torch.empty(B, MEL, dtype=dt, device=dev),
                                 "t": torch.empty(B, dtype=dt, device=dev),
                                 "ready": torch.cuda.Event(), "free": torch.cuda.Event()})
+                # the allocator may hand out memory that work queued on the compute stream still
+                # reads or writes: the copy stream must not touch it before that work is done
+                pair[1][-1]["free"].record(torch.cuda.current_stream(dev))
             self._stage[key] = pair
         st = pair[1][pair[0]]
         pair[0] ^= 1
