@@ -380,10 +380,12 @@ int run_gemm(const GemmCall& g, int dtype, cudaStream_t s) {
   if (dtype == FCV_DTYPE_BF16) {
     if (g.conv) return launch_conv<bf16>(g, s);
     if (g.K % 64 != 0) return fail(FCV_EUNSUPPORTED, "bf16 GEMM needs K %% 64 == 0 (K=%d)", g.K);
-    // CTA pairs (256-row tiles) once there are rows to fill them; a GEMM of at most
-    // 128 rows (time MLP, AdaLN modulation) issues half the MMA work per output
-    // column on single-SM 128-row tiles and is bound by streaming its weights
-    if (g.N >= 256 && g.M > 128) return launch_tc_pair<bf16>(g, s);
+    // CTA pairs (256-row tiles) once there are rows to fill them.  Up to 1536 rows the
+    // single-SM kernel is faster (a chain of the 88 block GEMMs of one estimator call,
+    // measured on B200: 400 rows 959 vs 1162 us, 800 rows 1071 vs 1186 us, 1400 rows
+    // 1219 vs 1255 us; 1600 rows 1319 vs 1307 us), and a GEMM of at most 128 rows (time
+    // MLP, AdaLN modulation) is bound by streaming its weights either way
+    if (g.N >= 256 && g.M > 1536) return launch_tc_pair<bf16>(g, s);
     const long mb = (g.M + 127) / 128;
     const long t256 = mb * ((g.N + 255) / 256);
     // 128-wide tiles only when 256-wide ones leave SMs idle: the AdaLN weight
