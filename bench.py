@@ -339,6 +339,87 @@ def flow_arm(args, impl: str):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------- vocoder
+def vocoder_arm(args, impl: str):
+    """One JSON line: the HiFT vocoder over a config's request mels (offline
+    finalize=True for config 2, non-final chunks for config 3), this build's one
+    packed ``fcv_hift_forward`` call or the reference's per-request
+    ``CausalHiFTGenerator.inference`` loop (token2wav.py:130-131, 194-195).
+    Synthetic seeded weights and noise table (tests/golden/hift_weights.py), float32."""
+    import types
+
+    import torch
+
+    req, chunk, seed = request_lengths(args.config)
+    if args.requests > 0:
+        req = req[:args.requests]
+    finalize = chunk == 0
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import hift_weights as HW
+
+    sd = HW.hift_state(0)
+    noise = HW.hift_noise(480 * (max(req) + 8), 1)
+    rng = np.random.default_rng(900 + seed)
+    mels = [torch.from_numpy((1.5 * rng.standard_normal((1, 80, L)) - 3).astype(np.float32)).to(device) for L in req]
+    frames = sum(req)
+    base = {"metric": "vocoder mel-frames/s (HiFT decode)", "unit": UNIT,
+            "config": {"workload": f"HiFT vocoder, {CONFIG_NAMES[args.config]}", "requests": len(req),
+                       "mel_frames": frames, "finalize": finalize}}
+    if impl == "b200":
+        from fcv_b200.hift import B200HiFT
+
+        voc = B200HiFT(sd, noise, device)
+
+        def run():
+            return voc.inference_batched(mels, finalize)
+    else:
+        ref_root = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref_root, "faster_cosyvoice")):
+            print(json.dumps({**base, "impl": "reference-gpu", "unavailable": "reference not installed in baseline/_ref"}))
+            return
+        for p in (ref_root, os.path.join(ROOT, "tests", "golden", "_xt_shim")):
+            if p not in sys.path:
+                sys.path.insert(0, p)
+        if "omegaconf" not in sys.modules:  # builders.py imports it for the flow's config only
+            stub = types.ModuleType("omegaconf")
+            stub.DictConfig = dict
+            sys.modules["omegaconf"] = stub
+        from faster_cosyvoice.token2wav.builders import build_hift
+
+        hift = build_hift()
+        hift.load_state_dict(sd, strict=True)
+        hift.m_source.l_sin_gen.sine_waves = noise[None]
+        hift = hift.to(device).eval()
+
+        def run():
+            with torch.inference_mode():
+                return [hift.inference(speech_feat=m, finalize=finalize)[0] for m in mels]
+
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(0) as clocks:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            out = run()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    ms = [a.elapsed_time(b) for a, b in ev]
+    t = float(np.mean(ms))
+    line = {**base, "impl": impl if impl == "b200" else "reference-gpu", "value": frames / (t / 1000.0),
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t, "step_ms_min": min(ms),
+            "higher_is_better": True, "dtype": "f32 (f64 f0 predictor)",
+            "data": "synthetic (seeded mels, weights and noise table)", "clocks": clocks.summary(),
+            "samples": int(sum(o.shape[-1] for o in out))}
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------------------- streaming calls
 def stream_arm(args, impl: str, cached: bool):
     """One JSON line: a streaming session of 32 streams (config 3's prompts, 100-400
@@ -647,6 +728,8 @@ def main():
                     help="a streaming session: 32 streams advancing 50 frames per call (full prefix recomputed)")
     ap.add_argument("--prefix-cache", action="store_true",
                     help="with --stream: reuse the cached prefix (this build only)")
+    ap.add_argument("--vocoder", action="store_true",
+                    help="time the HiFT vocoder over --config 2 (offline) or 3 (non-final chunks) request mels")
     ap.add_argument("--requests", type=int, default=0,
                     help="use only the first R requests of the config (small cases for profiling)")
     args = ap.parse_args()
@@ -664,6 +747,13 @@ def main():
            "packed_rows": 2 * sum(req_lengths), "chunk": chunk, "seed": seed,
            "parallelism": f"dp{world} (request bins, no collective)",
            "l2": "working set (662 MB of weights per NFE) exceeds the 126 MB L2; L2 also flushed between steps"}
+
+    if args.vocoder:
+        if args.config not in ("2", "3"):
+            raise SystemExit("--vocoder runs configs 2 (offline) and 3 (streaming)")
+        if rank == 0 and args.impl != "reference":
+            vocoder_arm(args, args.impl)
+        return
 
     if args.stream:
         if rank == 0 and args.impl != "reference":

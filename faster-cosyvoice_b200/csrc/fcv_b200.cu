@@ -23,6 +23,7 @@
 #include "attn.cuh"
 #include "rows.cuh"
 #include "flow.cuh"
+#include "hift.cuh"
 
 using namespace fcv;
 
@@ -1282,6 +1283,256 @@ int fcv_pack_rows(const void* src, int src_dtype, long batch_stride, int T, cons
   else
     FCV_LAUNCH("pack_rows_kernel", pack_rows_kernel<float, float>, grid, dim3(256), 0, s, static_cast<const float*>(src),
                batch_stride, T, cu, static_cast<float*>(dst));
+  return FCV_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- HiFT vocoder
+namespace {
+
+struct HiftGeom {
+  int cin, cout, k, dil, stride, up, pad;
+};
+
+// Geometry of convolution idx (the index order of fcv_hift_weights), from the
+// module structure of generator.py:616-676 with builders.py:38-50's sizes.
+HiftGeom hift_geom(int idx) {
+  static const int ch[3] = {256, 128, 64}, upr[3] = {8, 5, 3}, upk[3] = {16, 11, 7};
+  static const int sdk[3] = {30, 6, 1}, sds[3] = {15, 3, 1};
+  static const int srk[3] = {7, 7, 11}, rbk[3] = {3, 7, 11}, dil[3] = {1, 3, 5};
+  if (idx == 0) return {80, 512, 5, 1, 1, 1, 0};  // look-ahead 4: reads t .. t + 4
+  if (idx <= 3) {
+    const int i = idx - 1;
+    return {i == 0 ? 512 : ch[i - 1], ch[i], upk[i], 1, 1, upr[i], upk[i] - 1};
+  }
+  if (idx <= 6) {
+    const int i = idx - 4;
+    return {18, ch[i], sdk[i], 1, sds[i], 1, sds[i] - 1};
+  }
+  if (idx <= 78) {
+    const bool src = idx <= 24;
+    const int q = src ? idx - 7 : idx - 25, n = q / 6, s = (q % 6) / 2, second = q % 2;
+    const int level = src ? n : n / 3, k = src ? srk[n] : rbk[n % 3];
+    const int d = second ? 1 : dil[s];
+    return {ch[level], ch[level], k, d, 1, 1, (k - 1) * d};
+  }
+  return {64, 18, 7, 1, 1, 1, 6};
+}
+
+inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+size_t hift_level_floats(const int* rows) {
+  return std::max({(size_t)rows[5] * 256, (size_t)rows[6] * 128, (size_t)rows[7] * 64, (size_t)1});
+}
+
+template <typename Tin, typename T>
+int hift_conv(const hift::ConvArgs<T>& a, cudaStream_t s) {
+  if (a.rows_out == 0) return FCV_OK;
+  const dim3 grid((a.rows_out + 127) / 128, a.cout_pad / 64);
+  FCV_LAUNCH("hift_conv_kernel", hift::conv_kernel<Tin, T>, grid, dim3(256), 0, s, a);
+  return FCV_OK;
+}
+
+// Float32 convolution idx from x (rows on in_off / in_lim) to out (rows on out_cu).
+hift::ConvArgs<float> hift_args(const fcv_hift_weights* w, int idx, const void* x, const int* in_off, const int* in_lim,
+                                const int* out_cu, int n_docs, int rows_out, float* out) {
+  const HiftGeom g = hift_geom(idx);
+  hift::ConvArgs<float> a{};
+  a.x = x;
+  a.x_pitch = g.cin;
+  a.in_off = in_off;
+  a.in_lim = in_lim;
+  a.out_cu = out_cu;
+  a.n_docs = n_docs;
+  a.rows_out = rows_out;
+  a.w = w->conv_w[idx];
+  a.b = w->conv_b[idx];
+  a.cin = g.cin;
+  a.cin_pad = round_up(g.cin, 16);
+  a.cout = g.cout;
+  a.cout_pad = round_up(g.cout, 64);
+  a.k = g.k;
+  a.dil = g.dil;
+  a.stride = g.stride;
+  a.up = g.up;
+  a.pad_left = g.pad;
+  a.out = out;
+  a.out_pitch = g.cout;
+  return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t fcv_hift_workspace_bytes(const int* rows) {
+  if (!rows) return 0;
+  for (int i = 0; i < FCV_HIFT_LAYOUT_ARRAYS; ++i)
+    if (rows[i] < 0) return 0;
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  const size_t lvl = up(hift_level_floats(rows) * 4);
+  return 2 * up((size_t)rows[1] * 512 * 8) + up((size_t)rows[1] * 4) + up((size_t)rows[1] * 9 * 4) +
+         up((size_t)rows[3] * 4) + up((size_t)rows[4] * 18 * 4) + up((size_t)rows[2] * 512 * 4) + 6 * lvl +
+         up((size_t)rows[7] * 18 * 4) + up((size_t)rows[7] * 9 * 8);
+}
+
+int fcv_hift_forward(const fcv_hift_weights* w, const fcv_hift_batch* b, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  using namespace hift;
+  if (!w || !b || b->n_docs < 0) return fail(FCV_EINVAL, "fcv_hift_forward: bad arguments");
+  if (b->n_docs == 0 || b->rows[8] == 0) return FCV_OK;
+  if (!b->mel || !b->layout || !b->audio) return fail(FCV_EINVAL, "fcv_hift_forward: null mel, layout or audio");
+  for (int i = 0; i < FCV_HIFT_CONVS; ++i)
+    if (!w->conv_w[i] || !w->conv_b[i]) return fail(FCV_EINVAL, "fcv_hift_forward: convolution %d has no weights", i);
+  for (int i = 0; i < 5; ++i)
+    if (!w->f0_w[i] || !w->f0_b[i]) return fail(FCV_EINVAL, "fcv_hift_forward: f0 convolution %d has no weights", i);
+  if (!w->f0_cls_w || !w->source_w || !w->noise) return fail(FCV_EINVAL, "fcv_hift_forward: missing weights");
+  if (b->max_src < 0 || (long long)b->max_src > w->noise_rows)
+    return fail(FCV_EINVAL, "fcv_hift_forward: a document needs %d noise rows, the table holds %lld", b->max_src,
+                w->noise_rows);
+  const int* rows = b->rows;
+  for (int i = 0; i < FCV_HIFT_LAYOUT_ARRAYS; ++i)
+    if (rows[i] < 0) return fail(FCV_EINVAL, "fcv_hift_forward: negative row total");
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(FCV_EINVAL, "fcv_hift_forward: workspace must be 256-byte aligned");
+  const size_t need = fcv_hift_workspace_bytes(rows);
+  if (workspace_bytes < need)
+    return fail(FCV_EINVAL, "fcv_hift_forward: workspace of %zu bytes < %zu needed", workspace_bytes, need);
+  const int D = b->n_docs;
+  const int* L = b->layout;
+  const int *mel_cu = L, *f0_cu = L + (D + 1), *x_cu = L + 2 * (D + 1), *src_cu = L + 3 * (D + 1),
+            *stft_cu = L + 4 * (D + 1), *audio_cu = L + 8 * (D + 1);
+  const int* lvl_cu[3] = {L + 5 * (D + 1), L + 6 * (D + 1), L + 7 * (D + 1)};
+  const int lvl_rows[3] = {rows[5], rows[6], rows[7]};
+
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  uint8_t* p = static_cast<uint8_t*>(workspace);
+  auto take = [&](size_t bytes) {
+    void* r = p;
+    p += up(bytes);
+    return r;
+  };
+  double* f0a = static_cast<double*>(take((size_t)rows[1] * 512 * 8));
+  double* f0b = static_cast<double*>(take((size_t)rows[1] * 512 * 8));
+  float* f0 = static_cast<float*>(take((size_t)rows[1] * 4));
+  float* sines = static_cast<float*>(take((size_t)rows[1] * 9 * 4));
+  float* s_src = static_cast<float*>(take((size_t)rows[3] * 4));
+  float* spec_in = static_cast<float*>(take((size_t)rows[4] * 18 * 4));
+  float* x0 = static_cast<float*>(take((size_t)rows[2] * 512 * 4));
+  const size_t lvl = hift_level_floats(rows) * 4;
+  float* xb[2] = {static_cast<float*>(take(lvl)), static_cast<float*>(take(lvl))};
+  float* tmp = static_cast<float*>(take(lvl));
+  float* y = static_cast<float*>(take(lvl));
+  float* xs = static_cast<float*>(take(lvl));
+  float* si = static_cast<float*>(take(lvl));
+  float* post = static_cast<float*>(take((size_t)rows[7] * 18 * 4));
+  float2* spec_out = static_cast<float2*>(take((size_t)rows[7] * 9 * 8));
+  cudaStream_t s = as_stream(stream);
+
+  // ---- f0 predictor (float64): condnet 0 (k 4, look-ahead 3) + 4 x (k 3, causal), ELU after each
+  for (int i = 0; i < 5; ++i) {
+    ConvArgs<double> a{};
+    a.x = i == 0 ? static_cast<const void*>(b->mel) : static_cast<const void*>(i % 2 ? f0a : f0b);
+    a.x_pitch = i == 0 ? 80 : 512;
+    a.in_off = i == 0 ? mel_cu : f0_cu;
+    a.in_lim = a.in_off;
+    a.out_cu = f0_cu;
+    a.n_docs = D;
+    a.rows_out = rows[1];
+    a.w = w->f0_w[i];
+    a.b = w->f0_b[i];
+    a.cin = i == 0 ? 80 : 512;
+    a.cin_pad = a.cin;
+    a.cout = a.cout_pad = 512;
+    a.k = i == 0 ? 4 : 3;
+    a.dil = a.stride = a.up = 1;
+    a.pad_left = i == 0 ? 0 : 2;
+    a.epi = EPI_ELU;
+    a.out = i % 2 ? f0b : f0a;
+    a.out_pitch = 512;
+    if (i == 0) FCV_TRY((hift_conv<float, double>(a, s)));
+    else FCV_TRY((hift_conv<double, double>(a, s)));
+  }
+  if (rows[1] > 0) {
+    FCV_LAUNCH("hift_f0_head_kernel", f0_head_kernel, dim3((rows[1] + 7) / 8), dim3(256), 0, s, f0a, rows[1], 512,
+               w->f0_cls_w, w->f0_cls_b, f0);
+    // ---- source excitation and its STFT
+    FCV_LAUNCH("hift_source_phase_kernel", source_phase_kernel, dim3(D), dim3(256), 0, s, f0, f0_cu, sines);
+  }
+  if (rows[3] > 0)
+    FCV_LAUNCH("hift_source_kernel", source_kernel, dim3((rows[3] + 255) / 256), dim3(256), 0, s, f0, sines, f0_cu,
+               src_cu, D, rows[3], w->noise, w->source_w, w->source_b, s_src);
+  if (rows[4] > 0)
+    FCV_LAUNCH("hift_stft_kernel", stft_kernel, dim3((rows[4] + 127) / 128), dim3(128), 0, s, s_src, src_cu, stft_cu,
+               D, rows[4], spec_in);
+
+  // ---- decode: conv_pre reads the first F0 mel frames of each request (look-ahead 4 of them)
+  FCV_TRY((hift_conv<float, float>(hift_args(w, 0, b->mel, mel_cu, f0_cu, x_cu, D, rows[2], x0), s)));
+  const float* x_prev = x0;
+  const int* prev_cu = x_cu;
+  for (int i = 0; i < 3; ++i) {
+    float* x = xb[i & 1];
+    const int* cu = lvl_cu[i];
+    const int n = lvl_rows[i];
+    auto ca = [&](int idx, const void* in, const int* in_cu, float* out) {
+      return hift_args(w, idx, in, in_cu, in_cu, cu, D, n, out);
+    };
+    ConvArgs<float> a = hift_args(w, 1 + i, x_prev, prev_cu, prev_cu, cu, D, n, x);
+    a.pre = PRE_LEAKY;
+    a.slope = 0.1f;
+    a.reflect_first = i == 2;
+    FCV_TRY((hift_conv<float, float>(a, s)));
+    FCV_TRY((hift_conv<float, float>(ca(4 + i, spec_in, stft_cu, si), s)));
+    // one residual block: per dilation, conv1(snake1(.)) with snake2 fused into its
+    // epilogue, then conv2 + residual; the last conv2 may fold in the sum that follows
+    auto resblock = [&](int first, const float* in, float* work, int last_epi, float* last_out, const float* acc) {
+      const float* cur = in;
+      for (int st = 0; st < 3; ++st) {
+        const int c1 = first + 2 * st;
+        ConvArgs<float> a1 = ca(c1, cur, cu, tmp);
+        a1.pre = PRE_SNAKE;
+        a1.pre_alpha = w->snake_alpha[c1];
+        a1.pre_inv = w->snake_inv[c1];
+        a1.epi = EPI_SNAKE;
+        a1.post_alpha = w->snake2_alpha[c1];
+        a1.post_inv = w->snake2_inv[c1];
+        FCV_TRY((hift_conv<float, float>(a1, s)));
+        ConvArgs<float> a2 = ca(c1 + 1, tmp, cu, work);
+        a2.epi = EPI_RES;
+        a2.res = cur;
+        if (st == 2 && last_epi != EPI_RES) {
+          a2.epi = last_epi;
+          a2.acc = acc;
+          a2.out = last_out;
+        }
+        FCV_TRY((hift_conv<float, float>(a2, s)));
+        cur = work;
+      }
+      return FCV_OK;
+    };
+    // source branch: si = resblock(si); x = x + si folded into its last conv2
+    FCV_TRY(resblock(7 + 6 * i, si, si, EPI_RES_ACC, x, x));
+    // xs = rb0(x); xs += rb1(x); x = (xs + rb2(x)) / 3
+    const int rb0 = 25 + 6 * (3 * i);
+    FCV_TRY(resblock(rb0, x, xs, EPI_RES, xs, nullptr));
+    FCV_TRY(resblock(rb0 + 6, x, y, EPI_RES_ACC, xs, xs));
+    FCV_TRY(resblock(rb0 + 12, x, y, EPI_RES_ACC_AVG, x, xs));
+    x_prev = x;
+    prev_cu = cu;
+  }
+  // ---- conv_post (leaky 0.01 on load), magnitude/phase head, inverse STFT
+  ConvArgs<float> ap = hift_args(w, 79, x_prev, prev_cu, prev_cu, prev_cu, D, rows[7], post);
+  ap.pre = PRE_LEAKY;
+  ap.slope = 0.01f;
+  FCV_TRY((hift_conv<float, float>(ap, s)));
+  FCV_LAUNCH("hift_spectrum_kernel", spectrum_kernel, dim3((rows[7] * 9 + 255) / 256), dim3(256), 0, s, post, rows[7],
+             spec_out);
+  FCV_LAUNCH("hift_istft_kernel", istft_kernel, dim3((rows[8] + 255) / 256), dim3(256), 0, s, spec_out, lvl_cu[2],
+             audio_cu, D, rows[8], b->audio);
+  if (b->source && rows[3] > 0)
+    FCV_CUDA(cudaMemcpyAsync(b->source, s_src, (size_t)rows[3] * 4, cudaMemcpyDeviceToDevice, s));
+  if (b->f0 && rows[1] > 0) FCV_CUDA(cudaMemcpyAsync(b->f0, f0, (size_t)rows[1] * 4, cudaMemcpyDeviceToDevice, s));
   return FCV_OK;
 }
 

@@ -64,6 +64,8 @@ EXPORTS = (
     "fcv_speaker_projection",
     "fcv_prompt_rows",
     "fcv_pack_rows",
+    "fcv_hift_workspace_bytes",
+    "fcv_hift_forward",
 )
 
 
@@ -154,6 +156,42 @@ class FlowWeights(ctypes.Structure):
     ]
 
 
+HIFT_CONVS = 80
+HIFT_LAYOUT_ARRAYS = 9
+
+
+class HiftWeights(ctypes.Structure):
+    _fields_ = [
+        ("conv_w", ctypes.c_void_p * HIFT_CONVS),
+        ("conv_b", ctypes.c_void_p * HIFT_CONVS),
+        ("snake_alpha", ctypes.c_void_p * HIFT_CONVS),
+        ("snake_inv", ctypes.c_void_p * HIFT_CONVS),
+        ("snake2_alpha", ctypes.c_void_p * HIFT_CONVS),
+        ("snake2_inv", ctypes.c_void_p * HIFT_CONVS),
+        ("f0_w", ctypes.c_void_p * 5),
+        ("f0_b", ctypes.c_void_p * 5),
+        ("f0_cls_w", ctypes.c_void_p),
+        ("f0_cls_b", ctypes.c_double),
+        ("source_w", ctypes.c_void_p),
+        ("source_b", ctypes.c_float),
+        ("noise", ctypes.c_void_p),
+        ("noise_rows", ctypes.c_longlong),
+    ]
+
+
+class HiftBatch(ctypes.Structure):
+    _fields_ = [
+        ("n_docs", ctypes.c_int),
+        ("mel", ctypes.c_void_p),
+        ("layout", ctypes.c_void_p),
+        ("rows", ctypes.c_int * HIFT_LAYOUT_ARRAYS),
+        ("max_src", ctypes.c_int),
+        ("audio", ctypes.c_void_p),
+        ("source", ctypes.c_void_p),
+        ("f0", ctypes.c_void_p),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -191,6 +229,8 @@ _SIGNATURES = {
     "fcv_speaker_projection": (_i, [_vp, _i, _i, _i, _vp, _vp, _i, _vp, _i, _vp]),
     "fcv_prompt_rows": (_i, [_vp, _vp, _vp, _i, _i, _vp, _i, _vp]),
     "fcv_pack_rows": (_i, [_vp, _i, _l, _i, _vp, _i, _i, _vp, _i, _vp]),
+    "fcv_hift_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(ctypes.c_int)]),
+    "fcv_hift_forward": (_i, [ctypes.POINTER(HiftWeights), ctypes.POINTER(HiftBatch), _vp, ctypes.c_size_t, _vp]),
 }
 
 

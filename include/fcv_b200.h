@@ -396,6 +396,75 @@ int fcv_prompt_rows(const void* prompt, const int32_t* prompt_cu, const int32_t*
 int fcv_pack_rows(const void* src, int src_dtype, long batch_stride, int T, const int32_t* cu, int B,
                   int max_len, void* dst, int dst_dtype, void* stream);
 
+/* ------------------------------------------------------------------ HiFT vocoder
+ * CausalHiFTGenerator (cosyvoice/hifigan/generator.py:578-740) as built by
+ * builders.py:38-50, over packed requests.  Replaces the per-request
+ * hift.inference(speech_feat=mel, finalize=...) calls of token2wav.py:130-131
+ * and :194-195 with one call for a whole batch.
+ *
+ * Convolutions are indexed 0..79 in this order:
+ *   0            conv_pre                       80 -> 512, k 5, right look-ahead 4
+ *   1..3         ups.{0,1,2}                    nearest x8/x5/x3 then k 16/11/7 causal
+ *   4..6         source_downs.{0,1,2}           18 -> 256/128/64, k 30/6/1, stride 15/3/1
+ *   7 + 6i + 2s  source_resblocks.{i}.convs1.{s} (+1: convs2.{s}), i, s in 0..2
+ *   25 + 6n + 2s resblocks.{n}.convs1.{s}       (+1: convs2.{s}), n = 3 level + kernel, 0..8
+ *   79           conv_post                      64 -> 18, k 7 causal
+ * Weights (weight norm folded) are float32 [k][roundup(C_in, 16)][roundup(C_out, 64)],
+ * zero in the padding; biases float32 [roundup(C_out, 64)].  Snake parameters
+ * are given at the index of the convs1 they surround: snake_alpha / snake_inv
+ * (activations1, applied to convs1's input) and snake2_alpha / snake2_inv
+ * (activations2, applied to convs1's output); inv = 1 / (alpha + 1e-9) in float32.
+ * The f0 predictor (f0_predictor.py:60-103) is float64: condnet convs 0..4 as
+ * [k][C_in][512] (k 4 then 3), classifier (512) + bias. */
+#define FCV_HIFT_CONVS 80
+#define FCV_HIFT_SAMPLES_PER_FRAME 480
+
+typedef struct fcv_hift_weights {
+  const float* conv_w[FCV_HIFT_CONVS];
+  const float* conv_b[FCV_HIFT_CONVS];
+  const float* snake_alpha[FCV_HIFT_CONVS];
+  const float* snake_inv[FCV_HIFT_CONVS];
+  const float* snake2_alpha[FCV_HIFT_CONVS];
+  const float* snake2_inv[FCV_HIFT_CONVS];
+  const double* f0_w[5];
+  const double* f0_b[5];
+  const double* f0_cls_w;
+  double f0_cls_b;
+  const float* source_w;     /* m_source.l_linear.weight (9) */
+  float source_b;            /* m_source.l_linear.bias */
+  const float* noise;        /* (noise_rows, 9) l_sin_gen.sine_waves (generator.py:187) */
+  long long noise_rows;
+} fcv_hift_weights;
+
+/* Per-document row layout, 9 int32 cu arrays of n_docs + 1 entries each, in
+ * this order (L = given mel frames, F0 = L offline or L - 3 non-final, X = F0 or
+ * F0 - 4 non-final):
+ *   mel (L), f0 (F0), x (X), source (480 F0), stft (120 F0 + 1),
+ *   level0 (8 X), level1 (40 X), level2 (120 X + 1), audio (480 X, non-final 480 X - 480). */
+#define FCV_HIFT_LAYOUT_ARRAYS 9
+
+typedef struct fcv_hift_batch {
+  int n_docs;
+  const float* mel;          /* packed mel rows (rows of the mel array, 80) */
+  const int32_t* layout;     /* device, FCV_HIFT_LAYOUT_ARRAYS * (n_docs + 1) int32 */
+  int rows[FCV_HIFT_LAYOUT_ARRAYS]; /* host copy of each array's last entry (totals) */
+  int max_src;               /* longest document's source samples (480 F0): noise rows needed */
+  float* audio;              /* (rows[8]) packed speech samples */
+  float* source;             /* optional (rows[3]) excitation s (generator.py:737) */
+  float* f0;                 /* optional (rows[1]) f0 */
+} fcv_hift_batch;
+
+/* Workspace bytes of fcv_hift_forward for these totals (rows as in fcv_hift_batch). */
+size_t fcv_hift_workspace_bytes(const int* rows);
+
+/* speech = CausalHiFTGenerator.inference(mel, finalize) (generator.py:728-740)
+ * of every document: f0 predictor, source excitation, STFT, decode network,
+ * inverse STFT and clamp, documents independent (causal per document).  The
+ * noise table must hold max_src rows.  float32 like the reference's module
+ * (float64 f0 predictor). */
+int fcv_hift_forward(const fcv_hift_weights* w, const fcv_hift_batch* batch, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,6 +74,18 @@ def numpy_params(model) -> dict:
     return {k: v.detach().float().cpu().numpy() for k, v in model.state_dict().items()}
 
 
+def hift_inputs():
+    """Seeded HiFT test weights (reference state-dict format), the folded numpy
+    weights for the oracle, the noise table and the golden case."""
+    if str(GOLDEN) not in sys.path:
+        sys.path.insert(0, str(GOLDEN))
+    import hift_weights as HW
+
+    z = load_golden("hift_case")
+    sd = HW.hift_state(0)
+    return sd, HW.folded(sd), HW.hift_noise(int(z["noise_rows"]), 1), z
+
+
 def rel_l2(a, b) -> float:
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)

@@ -18,7 +18,10 @@ The reference's own code is imported and executed on the CPU in float32:
 * ``flashinfer_flow.flow_inference_batched`` / ``flow_inference_batched_streaming``
   (``flashinfer_flow.py:118-281``) on a ``CausalMaskedDiffWithDiT`` built as
   ``builders.py:16-45`` does (``python tests/golden/make_golden.py flow`` regenerates
-  only this fixture).
+  only this fixture);
+* ``cosyvoice/hifigan/generator.py`` ``CausalHiFTGenerator.inference`` built by
+  ``builders.py:38-50`` with the seeded weights of ``hift_weights.py``
+  (``python tests/golden/make_golden.py hift`` regenerates only this fixture).
 
 ``x_transformers`` (pinned 2.23.5, absent here) is replaced by the restatement in
 ``_xt_shim``; ``omegaconf`` is bypassed by passing a ``SimpleNamespace`` as
@@ -298,7 +301,50 @@ def flow_case():
     return fps
 
 
+def hift_case():
+    """HiFT vocoder: the reference's ``CausalHiFTGenerator`` as ``builders.py:38-50``
+    builds it, with the seeded weights and noise table of ``hift_weights.py``,
+    run through ``inference`` (``generator.py:728-740``) offline (``finalize=True``)
+    and for a non-final streaming chunk (``finalize=False``)."""
+    if "omegaconf" not in sys.modules:
+        stub = types.ModuleType("omegaconf")
+        stub.DictConfig = dict
+        sys.modules["omegaconf"] = stub
+    from faster_cosyvoice.token2wav.builders import build_hift
+
+    sys.path.insert(0, str(HERE))
+    import hift_weights as HW
+
+    torch.manual_seed(0)
+    hift = build_hift().eval()
+    sd = HW.hift_state(0)
+    hift.load_state_dict(sd, strict=True)
+    noise = HW.hift_noise(480 * 20, 1)
+    hift.m_source.l_sin_gen.sine_waves = noise[None]
+    rng = np.random.default_rng(7)
+    out = {"noise_rows": np.int64(noise.shape[0])}
+    cases = (("off0", 9, True), ("off1", 14, True), ("str0", 17, False))
+    for name, L, fin in cases:
+        mel = (1.5 * rng.standard_normal((1, 80, L)) - 3.0).astype(np.float32)
+        with torch.inference_mode():
+            speech, s = hift.inference(speech_feat=torch.from_numpy(mel), finalize=fin)
+            f0 = hift.f0_predictor(torch.from_numpy(mel).double(), finalize=fin).float()
+        out[f"{name}_mel"] = mel[0]
+        out[f"{name}_finalize"] = np.bool_(fin)
+        out[f"{name}_speech"] = speech[0].numpy()
+        out[f"{name}_s"] = s[0, 0].numpy()
+        out[f"{name}_f0"] = f0[0].numpy()
+    np.savez_compressed(HERE / "hift_case.npz", **out)
+    return HW.fingerprint(sd)
+
+
 def main():
+    if sys.argv[1:] == ["hift"]:
+        fps = json.loads((HERE / "weights_fingerprint.json").read_text())
+        fps["hift_seed0"] = hift_case()
+        (HERE / "weights_fingerprint.json").write_text(json.dumps(fps, indent=0, sort_keys=True))
+        print("hift golden vectors written to", HERE)
+        return
     if sys.argv[1:] == ["flow"]:
         fps = json.loads((HERE / "weights_fingerprint.json").read_text())
         fps["flow_seed4_depth2_frontend"] = flow_case()
@@ -318,6 +364,7 @@ def main():
     fps["seed3_depth2"] = fingerprint(build_ref_dit(3, 2))
     fps["seed4_depth2"] = fingerprint(build_ref_dit(4, 2))
     fps["flow_seed4_depth2_frontend"] = flow_case()
+    fps["hift_seed0"] = hift_case()
     (HERE / "weights_fingerprint.json").write_text(json.dumps(fps, indent=0, sort_keys=True))
     pack_cases()
     rownorm_case()

@@ -9,9 +9,10 @@ import hashlib
 import numpy as np
 import pytest
 
-from conftest import flow_case, golden_fingerprints, load_golden, make_flow, make_model, numpy_params, rel_l2
+from conftest import flow_case, golden_fingerprints, hift_inputs, load_golden, make_flow, make_model, numpy_params, rel_l2
 from oracle import dit_oracle as O
 from oracle import flow_oracle as F
+from oracle import hift_oracle as H
 
 
 def test_pack_layout_matches_reference_bit_exact():
@@ -165,3 +166,23 @@ def test_flow_inference_oracle_matches_reference(mode):
     for i, o in enumerate(outs):
         assert o.shape == c["out"][i].T.shape, (mode, i)
         assert np.abs(o - c["out"][i].T).max() < 1e-4, (mode, i)
+
+
+def test_hift_weights_reproduce_golden_state():
+    """The seeded generator still yields the weights the HiFT fixture was made with."""
+    sd, _, _, _ = hift_inputs()
+    import hift_weights as HW
+    assert HW.fingerprint(sd) == golden_fingerprints()["hift_seed0"]
+
+
+@pytest.mark.parametrize("case", ["off0", "off1", "str0"])
+def test_hift_oracle_matches_reference(case):
+    """The numpy HiFT restatement against the reference's CausalHiFTGenerator.inference
+    (offline and non-final chunks): f0 exact, excitation and speech within float32 noise."""
+    _, W, noise, z = hift_inputs()
+    fin = bool(z[f"{case}_finalize"])
+    speech, s, f0 = H.inference(z[f"{case}_mel"].T.copy(), W, noise.numpy(), fin)
+    np.testing.assert_array_equal(f0, z[f"{case}_f0"])
+    assert speech.shape == z[f"{case}_speech"].shape == (H.out_samples(z[f"{case}_mel"].shape[1], fin),)
+    assert rel_l2(s, z[f"{case}_s"]) <= 1e-6
+    assert rel_l2(speech, z[f"{case}_speech"]) <= 1e-5
