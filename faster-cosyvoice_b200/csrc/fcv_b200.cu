@@ -1330,7 +1330,7 @@ template <typename Tin, typename T>
 int hift_conv(const hift::ConvArgs<T>& a, cudaStream_t s) {
   if (a.rows_out == 0) return FCV_OK;
   const dim3 grid((a.rows_out + 127) / 128, a.cout_pad / 64);
-  FCV_LAUNCH("hift_conv_kernel", hift::conv_kernel<Tin, T>, grid, dim3(256), 0, s, a);
+  FCV_LAUNCH("hift_conv_kernel", hift::conv_kernel<Tin, T>, grid, dim3(128), 0, s, a);
   return FCV_OK;
 }
 
@@ -1357,6 +1357,7 @@ hift::ConvArgs<float> hift_args(const fcv_hift_weights* w, int idx, const void* 
   a.stride = g.stride;
   a.up = g.up;
   a.pad_left = g.pad;
+  a.vec = g.cin % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
   a.out = out;
   a.out_pitch = g.cout;
   return a;
@@ -1373,7 +1374,7 @@ size_t fcv_hift_workspace_bytes(const int* rows) {
   auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
   const size_t lvl = up(hift_level_floats(rows) * 4);
   return 2 * up((size_t)rows[1] * 512 * 8) + up((size_t)rows[1] * 4) + up((size_t)rows[1] * 9 * 4) +
-         up((size_t)rows[3] * 4) + up((size_t)rows[4] * 18 * 4) + up((size_t)rows[2] * 512 * 4) + 6 * lvl +
+         up((size_t)rows[3] * 4) + up((size_t)rows[4] * 18 * 4) + up((size_t)rows[2] * 512 * 4) + 10 * lvl +
          up((size_t)rows[7] * 18 * 4) + up((size_t)rows[7] * 9 * 8);
 }
 
@@ -1426,6 +1427,8 @@ int fcv_hift_forward(const fcv_hift_weights* w, const fcv_hift_batch* b, void* w
   float* y = static_cast<float*>(take(lvl));
   float* xs = static_cast<float*>(take(lvl));
   float* si = static_cast<float*>(take(lvl));
+  float* act = static_cast<float*>(take(lvl));   // Snake input of the next convs1 inside a residual block
+  float* actx[3] = {static_cast<float*>(take(lvl)), static_cast<float*>(take(lvl)), static_cast<float*>(take(lvl))};
   float* post = static_cast<float*>(take((size_t)rows[7] * 18 * 4));
   float2* spec_out = static_cast<float2*>(take((size_t)rows[7] * 9 * 8));
   cudaStream_t s = as_stream(stream);
@@ -1483,17 +1486,27 @@ int fcv_hift_forward(const fcv_hift_weights* w, const fcv_hift_batch* b, void* w
     a.slope = 0.1f;
     a.reflect_first = i == 2;
     FCV_TRY((hift_conv<float, float>(a, s)));
-    FCV_TRY((hift_conv<float, float>(ca(4 + i, spec_in, stft_cu, si), s)));
-    // one residual block: per dilation, conv1(snake1(.)) with snake2 fused into its
-    // epilogue, then conv2 + residual; the last conv2 may fold in the sum that follows
-    auto resblock = [&](int first, const float* in, float* work, int last_epi, float* last_out, const float* acc) {
+    // Every convs1 reads its Snake input (activations1) ready-made: the convolution
+    // producing that input stores it from its epilogue (act_out).
+    auto add_act = [&](ConvArgs<float>& c, float* dst, int c1) {
+      c.act_out[c.n_act] = dst;
+      c.act_alpha[c.n_act] = w->snake_alpha[c1];
+      c.act_inv[c.n_act] = w->snake_inv[c1];
+      ++c.n_act;
+    };
+    const int src_first = 7 + 6 * i, rb0 = 25 + 6 * (3 * i);
+    ConvArgs<float> sd = ca(4 + i, spec_in, stft_cu, si);
+    add_act(sd, act, src_first);
+    FCV_TRY((hift_conv<float, float>(sd, s)));
+    // one residual block: per dilation, conv1 with activations2 in its epilogue, then
+    // conv2 + residual storing the next stage's activations1; the last conv2 may fold
+    // in the sum that follows (last_epi) and store other blocks' first inputs (acts)
+    auto resblock = [&](int first, const float* in, const float* in_act, float* work, int last_epi, float* last_out,
+                        const float* acc, bool acts) {
       const float* cur = in;
       for (int st = 0; st < 3; ++st) {
         const int c1 = first + 2 * st;
-        ConvArgs<float> a1 = ca(c1, cur, cu, tmp);
-        a1.pre = PRE_SNAKE;
-        a1.pre_alpha = w->snake_alpha[c1];
-        a1.pre_inv = w->snake_inv[c1];
+        ConvArgs<float> a1 = ca(c1, st == 0 ? in_act : act, cu, tmp);
         a1.epi = EPI_SNAKE;
         a1.post_alpha = w->snake2_alpha[c1];
         a1.post_inv = w->snake2_inv[c1];
@@ -1501,23 +1514,26 @@ int fcv_hift_forward(const fcv_hift_weights* w, const fcv_hift_batch* b, void* w
         ConvArgs<float> a2 = ca(c1 + 1, tmp, cu, work);
         a2.epi = EPI_RES;
         a2.res = cur;
+        if (st < 2) add_act(a2, act, c1 + 2);
         if (st == 2 && last_epi != EPI_RES) {
           a2.epi = last_epi;
           a2.acc = acc;
           a2.out = last_out;
         }
+        if (st == 2 && acts)
+          for (int j = 0; j < 3; ++j) add_act(a2, actx[j], rb0 + 6 * j);
         FCV_TRY((hift_conv<float, float>(a2, s)));
         cur = work;
       }
       return FCV_OK;
     };
-    // source branch: si = resblock(si); x = x + si folded into its last conv2
-    FCV_TRY(resblock(7 + 6 * i, si, si, EPI_RES_ACC, x, x));
+    // source branch: si = resblock(si); x = x + si folded into its last conv2, which
+    // also stores the three blocks' first Snake inputs
+    FCV_TRY(resblock(src_first, si, act, si, EPI_RES_ACC, x, x, true));
     // xs = rb0(x); xs += rb1(x); x = (xs + rb2(x)) / 3
-    const int rb0 = 25 + 6 * (3 * i);
-    FCV_TRY(resblock(rb0, x, xs, EPI_RES, xs, nullptr));
-    FCV_TRY(resblock(rb0 + 6, x, y, EPI_RES_ACC, xs, xs));
-    FCV_TRY(resblock(rb0 + 12, x, y, EPI_RES_ACC_AVG, x, xs));
+    FCV_TRY(resblock(rb0, x, actx[0], xs, EPI_RES, xs, nullptr, false));
+    FCV_TRY(resblock(rb0 + 6, x, actx[1], y, EPI_RES_ACC, xs, xs, false));
+    FCV_TRY(resblock(rb0 + 12, x, actx[2], y, EPI_RES_ACC_AVG, x, xs, false));
     x_prev = x;
     prev_cu = cu;
   }

@@ -35,6 +35,9 @@ constexpr int kBins = 9;        // n_fft / 2 + 1
 // with up > 1 the input is first repeated up times (nearest upsampling), so idx
 // addresses the repeated sequence and reads input row idx / up.  Positions
 // outside [0, up * lim) are zero padding; lim = in_lim[d + 1] - in_lim[d].
+// Besides out, the epilogue can store up to 3 Snake activations of the final
+// value (act_out[q] = snake(out; act_alpha[q])): the next convolutions' inputs,
+// computed once per element instead of once per tap and channel tile.
 template <typename T>
 struct ConvArgs {
   const void* x;
@@ -46,6 +49,7 @@ struct ConvArgs {
   const T* w;          // [k][cin_pad][cout_pad]
   const T* b;          // [cout_pad]
   int cin, cin_pad, cout, cout_pad, k, dil, stride, up, pad_left, reflect_first;
+  int vec;             // rows load as float4: float input, cin % 16 == 0, x_pitch % 4 == 0, 16-byte base
   int pre;
   float slope;
   const float* pre_alpha;
@@ -57,6 +61,10 @@ struct ConvArgs {
   const T* acc;
   T* out;
   int out_pitch;
+  int n_act;
+  T* act_out[3];
+  const float* act_alpha[3];
+  const float* act_inv[3];
 };
 
 __device__ __forceinline__ int find_doc(const int* __restrict__ cu, int n_docs, int r) {
@@ -88,16 +96,35 @@ __device__ __forceinline__ T add_rn(T a, T b) { return a + b; }
 template <>
 __device__ __forceinline__ float add_rn<float>(float a, float b) { return __fadd_rn(a, b); }
 
-// SIMT implicit-GEMM tile: 128 output rows x 64 output channels, 256 threads,
-// each 8 rows x 4 channels; K = taps x input channels in steps of BK, operands
-// double-buffered in shared memory through registers.
+// Four consecutive shared-memory elements (16-byte aligned for float: one 128-bit load).
+__device__ __forceinline__ void load4(float* d, const float* s) {
+  const float4 v = *reinterpret_cast<const float4*>(s);
+  d[0] = v.x;
+  d[1] = v.y;
+  d[2] = v.z;
+  d[3] = v.w;
+}
+__device__ __forceinline__ void load4(double* d, const double* s) {
+  const double2 v0 = *reinterpret_cast<const double2*>(s), v1 = *reinterpret_cast<const double2*>(s + 2);
+  d[0] = v0.x;
+  d[1] = v0.y;
+  d[2] = v1.x;
+  d[3] = v1.y;
+}
+
+// SIMT implicit-GEMM tile: 128 output rows x 64 output channels, 128 threads,
+// each 8 rows x 8 channels; K = taps x input channels in steps of BK (one row of
+// BK channels loaded per thread), operands double-buffered in shared memory
+// through registers.  The accumulation order over (tap, channel) is the same
+// for every output element whatever its tile, so packed documents give the
+// same bits as single ones.
 template <typename Tin, typename T>
-__global__ void __launch_bounds__(256) conv_kernel(ConvArgs<T> p) {
+__global__ void __launch_bounds__(128, sizeof(T) == 8 ? 2 : 4) conv_kernel(ConvArgs<T> p) {
   griddep_wait();
   griddep_launch();
-  constexpr int BM = 128, BN = 64;
+  constexpr int BM = 128, BN = 64, NT = 128;
   constexpr int BK = sizeof(T) == 8 ? 8 : 16;
-  constexpr int AH = BK / 2;           // input channels one thread loads per row
+  constexpr int NB = BK * BN / NT;     // weights one thread loads per step
   __shared__ __align__(16) T As[2][BK][BM + 4];
   __shared__ __align__(16) T Bs[2][BK][BN];
   const int tid = threadIdx.x;
@@ -105,10 +132,10 @@ __global__ void __launch_bounds__(256) conv_kernel(ConvArgs<T> p) {
   const Tin* __restrict__ x = static_cast<const Tin*>(p.x);
 
   // the A row this thread loads, and its document geometry
-  const int lrow = tid >> 1, lhalf = tid & 1;
-  const int r_ld = m0 + lrow;
+  const int r_ld = m0 + tid;
   int base = 0, pos0 = 0, lim_up = 0;
-  if (r_ld < p.rows_out) {
+  const bool row_ok = r_ld < p.rows_out;
+  if (row_ok) {
     const int d = find_doc(p.out_cu, p.n_docs, r_ld);
     const int t = r_ld - __ldg(p.out_cu + d);
     const int c = p.reflect_first ? (t == 0 ? 1 : t - 1) : t;
@@ -119,63 +146,83 @@ __global__ void __launch_bounds__(256) conv_kernel(ConvArgs<T> p) {
   const int n_ci = p.cin_pad / BK;
   const int n_iter = p.k * n_ci;
 
-  T a_reg[AH];
-  T b_reg[BK * BN / 256];
-  auto load = [&](int it) {
-    const int j = it / n_ci, ci0 = (it - j * n_ci) * BK + lhalf * AH;
-    const int idx = pos0 + j * p.dil;
-    const bool ok = r_ld < p.rows_out && idx >= 0 && idx < lim_up;
-    const Tin* src = x + (size_t)(base + (ok ? idx / p.up : 0)) * p.x_pitch;
+  T a_reg[BK];
+  T b_reg[NB];
+  int ld_j = 0, ld_c = 0;   // tap and channel chunk of the next load
+  auto load = [&]() {
+    const int idx = pos0 + ld_j * p.dil;
+    const bool ok = row_ok && idx >= 0 && idx < lim_up;
+    const int ci0 = ld_c * BK;
+    if (ok) {
+      const Tin* src = x + (size_t)(base + (p.up == 1 ? idx : idx / p.up)) * p.x_pitch + ci0;
+      if (sizeof(Tin) == 4 && p.vec) {
 #pragma unroll
-    for (int q = 0; q < AH; ++q) {
-      const int ci = ci0 + q;
-      T v = T(0);
-      if (ok && ci < p.cin) v = pre_act<T>(T(src[ci]), p.pre, p.slope, p.pre_alpha, p.pre_inv, ci);
-      a_reg[q] = v;
+        for (int q = 0; q < BK; q += 4) {
+          const float4 v4 = __ldg(reinterpret_cast<const float4*>(src) + q / 4);
+          a_reg[q] = T(v4.x);
+          a_reg[q + 1] = T(v4.y);
+          a_reg[q + 2] = T(v4.z);
+          a_reg[q + 3] = T(v4.w);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < BK; ++q) a_reg[q] = ci0 + q < p.cin ? T(src[q]) : T(0);
+      }
+      if (p.pre != PRE_NONE) {
+#pragma unroll
+        for (int q = 0; q < BK; ++q)
+          if (ci0 + q < p.cin) a_reg[q] = pre_act<T>(a_reg[q], p.pre, p.slope, p.pre_alpha, p.pre_inv, ci0 + q);
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < BK; ++q) a_reg[q] = T(0);
     }
-    const T* wsrc = p.w + ((size_t)j * p.cin_pad + (it - j * n_ci) * BK) * p.cout_pad + n0;
+    const T* wsrc = p.w + ((size_t)ld_j * p.cin_pad + ci0) * p.cout_pad + n0;
 #pragma unroll
-    for (int q = 0; q < BK * BN / 256; ++q) {
-      const int e = tid + q * 256;
+    for (int q = 0; q < NB; ++q) {
+      const int e = tid + q * NT;
       b_reg[q] = __ldg(wsrc + (size_t)(e / BN) * p.cout_pad + (e % BN));
+    }
+    if (++ld_c == n_ci) {
+      ld_c = 0;
+      ++ld_j;
     }
   };
   auto store = [&](int buf) {
 #pragma unroll
-    for (int q = 0; q < AH; ++q) As[buf][lhalf * AH + q][lrow] = a_reg[q];
+    for (int q = 0; q < BK; ++q) As[buf][q][tid] = a_reg[q];
 #pragma unroll
-    for (int q = 0; q < BK * BN / 256; ++q) {
-      const int e = tid + q * 256;
+    for (int q = 0; q < NB; ++q) {
+      const int e = tid + q * NT;
       Bs[buf][e / BN][e % BN] = b_reg[q];
     }
   };
 
-  const int tx = tid & 15, ty = tid >> 4;
-  T accum[8][4];
+  const int tx = tid & 15, ty = tid >> 4;   // rows tx*4 (+64), channels ty*4 (+32)
+  T accum[8][8];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) accum[i][jj] = T(0);
+    for (int jj = 0; jj < 8; ++jj) accum[i][jj] = T(0);
 
-  load(0);
+  load();
   store(0);
   __syncthreads();
   for (int it = 0; it < n_iter; ++it) {
     const int buf = it & 1;
-    if (it + 1 < n_iter) load(it + 1);
-#pragma unroll
+    if (it + 1 < n_iter) load();
+    // partial unroll: the fully unrolled step (~1100 instructions) stalled on instruction fetch
+#pragma unroll 4
     for (int kk = 0; kk < BK; ++kk) {
-      T a[8], bv[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        a[q] = As[buf][kk][tx * 4 + q];
-        a[4 + q] = As[buf][kk][64 + tx * 4 + q];
-        bv[q] = Bs[buf][kk][ty * 4 + q];
-      }
+      T a[8], bv[8];
+      load4(a, &As[buf][kk][tx * 4]);
+      load4(a + 4, &As[buf][kk][64 + tx * 4]);
+      load4(bv, &Bs[buf][kk][ty * 4]);
+      load4(bv + 4, &Bs[buf][kk][32 + ty * 4]);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) accum[i][jj] = fma(a[i], bv[jj], accum[i][jj]);
+        for (int jj = 0; jj < 8; ++jj) accum[i][jj] = fma(a[i], bv[jj], accum[i][jj]);
     }
     if (it + 1 < n_iter) store(buf ^ 1);
     __syncthreads();
@@ -187,8 +234,8 @@ __global__ void __launch_bounds__(256) conv_kernel(ConvArgs<T> p) {
     const int r = m0 + (i < 4 ? tx * 4 + i : 64 + tx * 4 + (i - 4));
     if (r >= p.rows_out) continue;
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const int co = n0 + ty * 4 + jj;
+    for (int jj = 0; jj < 8; ++jj) {
+      const int co = n0 + (jj < 4 ? ty * 4 + jj : 32 + ty * 4 + (jj - 4));
       if (co >= p.cout) continue;
       T v = add_rn<T>(accum[i][jj], p.b[co]);
       const size_t o = (size_t)r * p.out_pitch + co;
@@ -201,6 +248,8 @@ __global__ void __launch_bounds__(256) conv_kernel(ConvArgs<T> p) {
         default: break;
       }
       p.out[o] = v;
+      for (int q = 0; q < p.n_act; ++q)
+        p.act_out[q][o] = T(snake(float(v), __ldg(p.act_alpha[q] + co), __ldg(p.act_inv[q] + co)));
     }
   }
 }
