@@ -1326,9 +1326,38 @@ size_t hift_level_floats(const int* rows) {
   return std::max({(size_t)rows[5] * 256, (size_t)rows[6] * 128, (size_t)rows[7] * 64, (size_t)1});
 }
 
+template <int N>
+int hift_res_conv_tc(const hift::ConvArgs<float>& a, cudaStream_t s) {
+  using Cfg = hift::ResConvCfg<N>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    FCV_CUDA(cudaFuncSetAttribute(hift::res_conv_tc_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  Cfg::SMEM_BYTES));
+    attr_set[dev & 63] = true;
+  }
+  FCV_LAUNCH("hift_res_conv_tc_kernel", hift::res_conv_tc_kernel<N>, dim3((a.rows_out + 127) / 128),
+             dim3(Cfg::THREADS), Cfg::SMEM_BYTES, s, a);
+  return FCV_OK;
+}
+
 template <typename Tin, typename T>
 int hift_conv(const hift::ConvArgs<T>& a, cudaStream_t s) {
   if (a.rows_out == 0) return FCV_OK;
+  if constexpr (sizeof(T) == 4 && sizeof(Tin) == 4) {
+    if (a.tw_hi && a.tw_lo) {
+      // tensor-core path: stride 1, no upsampling or reflection, no pre-activation,
+      // 32-channel K chunks, 16-byte aligned rows
+      if (a.stride != 1 || a.up != 1 || a.reflect_first || a.pre != hift::PRE_NONE || a.cin % 32 ||
+          a.cout != a.out_pitch || (a.x_pitch % 4) || (reinterpret_cast<uintptr_t>(a.x) & 15))
+        return fail(FCV_EUNSUPPORTED, "fcv_hift_forward: convolution not eligible for the tensor-core path");
+      if (a.cout == 64) return hift_res_conv_tc<64>(a, s);
+      if (a.cout == 128) return hift_res_conv_tc<128>(a, s);
+      if (a.cout == 256) return hift_res_conv_tc<256>(a, s);
+      return fail(FCV_EUNSUPPORTED, "fcv_hift_forward: tensor-core convolution needs 64, 128 or 256 channels");
+    }
+  }
   const dim3 grid((a.rows_out + 127) / 128, a.cout_pad / 64);
   FCV_LAUNCH("hift_conv_kernel", hift::conv_kernel<Tin, T>, grid, dim3(128), 0, s, a);
   return FCV_OK;
@@ -1348,6 +1377,10 @@ hift::ConvArgs<float> hift_args(const fcv_hift_weights* w, int idx, const void* 
   a.rows_out = rows_out;
   a.w = w->conv_w[idx];
   a.b = w->conv_b[idx];
+  if (idx >= 7 && idx <= 78) {
+    a.tw_hi = w->tc_w_hi[idx];
+    a.tw_lo = w->tc_w_lo[idx];
+  }
   a.cin = g.cin;
   a.cin_pad = round_up(g.cin, 16);
   a.cout = g.cout;

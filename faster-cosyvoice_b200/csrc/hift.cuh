@@ -65,6 +65,8 @@ struct ConvArgs {
   T* act_out[3];
   const float* act_alpha[3];
   const float* act_inv[3];
+  const float* tw_hi;  // tensor-core path: weights [k][cout][cin] split into a tf32 head ...
+  const float* tw_lo;  // ... and the float32 remainder (null: SIMT path)
 };
 
 __device__ __forceinline__ int find_doc(const int* __restrict__ cu, int n_docs, int r) {
@@ -251,6 +253,257 @@ __global__ void __launch_bounds__(128, sizeof(T) == 8 ? 2 : 4) conv_kernel(ConvA
       for (int q = 0; q < p.n_act; ++q)
         p.act_out[q][o] = T(snake(float(v), __ldg(p.act_alpha[q] + co), __ldg(p.act_inv[q] + co)));
     }
+  }
+}
+
+
+// ---------------------------------------------------------------- tensor-core residual convolutions
+// Stride-1 convolutions without upsampling and without a pre-activation (the 72
+// residual-block convolutions, 88 % of the vocoder's FLOPs) on tcgen05 kind::tf32
+// with float32 accuracy: each operand is split into a tf32 head h (low 13 mantissa
+// bits cleared) and the remainder l = x - h, and D += Ah*Bh + Ah*Bl + Al*Bh
+// (the Al*Bl term is below float32 rounding).
+//
+// One CTA computes 128 output rows x N (= C_out) channels, accumulating in N TMEM
+// columns.  Warps 0-3 produce: each thread gathers its output row's input row for
+// the current tap with cp.async (zero-filled outside the document), 32 channels
+// (128 bytes) per stage, splits it into head and remainder in shared memory and
+// loads 128-byte rows of the pre-split weights; warp 4 issues the MMAs; warps 0-3
+// then read the accumulator rows back and run the same epilogue as the SIMT kernel.
+// Shared-memory tiles use the 128-byte swizzle (16-byte chunk c of row r stored at
+// chunk c ^ (r & 7)), the layout the MMA descriptors describe.
+template <int N>
+struct ResConvCfg {
+  static constexpr int S = N == 256 ? 2 : (N == 128 ? 3 : 4);     // pipeline stages
+  static constexpr int A_BYTES = 128 * 128;                        // 128 rows x 32 floats
+  static constexpr int B_BYTES = N * 128;
+  static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;          // head and remainder of A and B
+  static constexpr int SMEM_BYTES = 1024 + S * STAGE + 256;
+  static constexpr int THREADS = 160;
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int PENDING>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(PENDING) : "memory"); }
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor: kind::tf32, A = B = tf32 (format 2), D = f32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+template <int N>
+__global__ void __launch_bounds__(160, 1) res_conv_tc_kernel(ConvArgs<float> p) {
+  using Cfg = ResConvCfg<N>;
+  constexpr int S = Cfg::S;
+  griddep_wait();
+  griddep_launch();
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u32 = (fcv::smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* base = smem_raw + (base_u32 - fcv::smem_u32(smem_raw));
+  const uint32_t bar0 = base_u32 + S * Cfg::STAGE;   // full[S], empty[S], done
+  int* abort_flag = reinterpret_cast<int*>(base + S * Cfg::STAGE + 8 * (2 * S + 1));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + S * Cfg::STAGE + 8 * (2 * S + 1) + 4);
+  auto full = [&](int st) { return bar0 + 8u * st; };
+  auto empty = [&](int st) { return bar0 + 8u * (S + st); };
+  const uint32_t done = bar0 + 8u * (2 * S);
+  auto a_hi = [&](int st) { return base_u32 + st * Cfg::STAGE; };
+  auto a_lo = [&](int st) { return a_hi(st) + Cfg::A_BYTES; };
+  auto b_hi = [&](int st) { return a_hi(st) + 2 * Cfg::A_BYTES; };
+  auto b_lo = [&](int st) { return b_hi(st) + Cfg::B_BYTES; };
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int m0 = blockIdx.x * 128;
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      fcv::mbar_init(full(i), 128);
+      fcv::mbar_init(empty(i), 1);
+    }
+    fcv::mbar_init(done, 1);
+    *abort_flag = 0;
+    fcv::fence_mbar_init();
+  }
+  if (warp == 4) {
+    fcv::tmem_alloc(fcv::smem_u32(tmem_slot), N);
+    fcv::tmem_relinquish();
+  }
+  fcv::tc_fence_before();
+  __syncthreads();
+  fcv::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int n_ci = p.cin / 32;
+  const int n_iter = p.k * n_ci;
+  volatile int* abrt = abort_flag;
+
+  if (warp < 4) {
+    // ---- producer: row tid of the tile
+    const int r = m0 + tid;
+    const bool row_ok = r < p.rows_out;
+    int rbase = 0, pos0 = 0, lim = 0;
+    if (row_ok) {
+      const int d = find_doc(p.out_cu, p.n_docs, r);
+      rbase = __ldg(p.in_off + d);
+      lim = __ldg(p.in_lim + d + 1) - __ldg(p.in_lim + d);
+      pos0 = (r - __ldg(p.out_cu + d)) - p.pad_left;
+    }
+    const float* xin = static_cast<const float*>(p.x);
+    auto issue = [&](int it) {
+      const int st = it % S, j = it / n_ci, ci0 = (it - j * n_ci) * 32;
+      const int idx = pos0 + j * p.dil;
+      const bool ok = row_ok && idx >= 0 && idx < lim;
+      const float* src = ok ? xin + (size_t)(rbase + idx) * p.x_pitch + ci0 : xin;
+      const uint32_t arow = a_hi(st) + tid * 128;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) cp_async16(arow + ((q ^ (tid & 7)) << 4), src + 4 * q, ok ? 16u : 0u);
+#pragma unroll
+      for (int m = 0; m < N / 16; ++m) {
+        const int e = tid + 128 * m, co = e >> 3, q = e & 7;
+        const size_t off = ((size_t)j * p.cout + co) * p.cin + ci0 + 4 * q;
+        const uint32_t dst = co * 128 + ((q ^ (co & 7)) << 4);
+        cp_async16(b_hi(st) + dst, p.tw_hi + off, 16u);
+        cp_async16(b_lo(st) + dst, p.tw_lo + off, 16u);
+      }
+    };
+    bool ok_run = true;
+    for (int it = 0; it < S - 1; ++it) {
+      if (it < n_iter) issue(it);
+      cp_async_commit();
+    }
+    for (int it = 0; it < n_iter && ok_run; ++it) {
+      // stage it has landed once at most S - 2 newer groups are pending
+      cp_async_wait<S - 2>();
+      // split this thread's row of stage it into head and remainder, hand it to the MMA
+      const int st = it % S;
+      float4* hrow = reinterpret_cast<float4*>(base + (a_hi(st) - base_u32) + tid * 128);
+      float4* lrow = reinterpret_cast<float4*>(base + (a_lo(st) - base_u32) + tid * 128);
+#pragma unroll
+      for (int qq = 0; qq < 8; ++qq) {
+        const int q = qq ^ (tid & 7);   // swizzled order: the 8 threads of a phase hit distinct banks
+        const float4 v = hrow[q];
+        float4 h, l;
+        h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+        h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+        h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+        h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+        l.x = v.x - h.x;
+        l.y = v.y - h.y;
+        l.z = v.z - h.z;
+        l.w = v.w - h.w;
+        hrow[q] = h;
+        lrow[q] = l;
+      }
+      fcv::fence_proxy_async_smem();
+      fcv::mbar_arrive(full(st));
+      // then refill the slot the previous step's MMAs read (stage it + S - 1)
+      const int nxt = it + S - 1;
+      if (nxt < n_iter) {
+        if (nxt >= S && !fcv::mbar_wait(empty(nxt % S), ((nxt - S) / S) & 1, 260, abrt)) { ok_run = false; break; }
+        issue(nxt);
+      }
+      cp_async_commit();
+    }
+    cp_async_wait<0>();
+    // ---- epilogue: accumulator row tid (TMEM lane 32 * warp + lane)
+    // tcgen05.ld is warp-collective: the whole warp reads the accumulator or none of it
+    const bool ready = __all_sync(0xffffffffu, ok_run && fcv::mbar_wait(done, 0, 261, abrt));
+    fcv::tc_fence_after();
+    if (ready) {
+      for (int c0 = 0; c0 < N; c0 += 32) {
+        uint32_t acc_r[32];
+        fcv::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, acc_r);
+        fcv::tmem_wait_ld();
+        if (!row_ok) continue;
+        // this thread's 32 consecutive outputs of row r: every operand is loaded before
+        // anything is stored (res / acc may alias out), 16 bytes at a time
+        const size_t o0 = (size_t)r * p.out_pitch + c0;
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) v[c] = __fadd_rn(__uint_as_float(acc_r[c]), __ldg(p.b + c0 + c));
+        if (p.epi == EPI_SNAKE) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[c] = snake(v[c], __ldg(p.post_alpha + c0 + c), __ldg(p.post_inv + c0 + c));
+        } else if (p.epi >= EPI_RES) {
+          float rv[32], av[32];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 t = reinterpret_cast<const float4*>(p.res + o0)[q];
+            rv[4 * q] = t.x;
+            rv[4 * q + 1] = t.y;
+            rv[4 * q + 2] = t.z;
+            rv[4 * q + 3] = t.w;
+          }
+          if (p.epi != EPI_RES) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 t = reinterpret_cast<const float4*>(p.acc + o0)[q];
+              av[4 * q] = t.x;
+              av[4 * q + 1] = t.y;
+              av[4 * q + 2] = t.z;
+              av[4 * q + 3] = t.w;
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            float u = __fadd_rn(v[c], rv[c]);
+            if (p.epi == EPI_RES_ACC) u = __fadd_rn(av[c], u);
+            if (p.epi == EPI_RES_ACC_AVG) u = __fdiv_rn(__fadd_rn(av[c], u), 3.0f);
+            v[c] = u;
+          }
+        }
+        float4* outv = reinterpret_cast<float4*>(p.out + o0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) outv[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        for (int a = 0; a < p.n_act; ++a) {
+          float4* actv = reinterpret_cast<float4*>(p.act_out[a] + o0);
+          const float* al = p.act_alpha[a] + c0;
+          const float* ai = p.act_inv[a] + c0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            actv[q] = make_float4(snake(v[4 * q], __ldg(al + 4 * q), __ldg(ai + 4 * q)),
+                                  snake(v[4 * q + 1], __ldg(al + 4 * q + 1), __ldg(ai + 4 * q + 1)),
+                                  snake(v[4 * q + 2], __ldg(al + 4 * q + 2), __ldg(ai + 4 * q + 2)),
+                                  snake(v[4 * q + 3], __ldg(al + 4 * q + 3), __ldg(ai + 4 * q + 3)));
+        }
+      }
+    }
+  } else if (tid == 128) {
+    // ---- MMA issuer
+    constexpr uint32_t idesc = idesc_tf32_f32(128, N);
+    bool ok_run = true;
+    for (int it = 0; it < n_iter; ++it) {
+      const int st = it % S;
+      if (!fcv::mbar_wait(full(st), (it / S) & 1, 262, abrt)) { ok_run = false; break; }
+      fcv::tc_fence_after();
+      const uint64_t dah = fcv::sdesc_sw128(a_hi(st)), dal = fcv::sdesc_sw128(a_lo(st));
+      const uint64_t dbh = fcv::sdesc_sw128(b_hi(st)), dbl = fcv::sdesc_sw128(b_lo(st));
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        umma_tf32(tmem, dah + 2 * kk, dbh + 2 * kk, idesc, (it | kk) != 0);
+        umma_tf32(tmem, dah + 2 * kk, dbl + 2 * kk, idesc, 1);
+        umma_tf32(tmem, dal + 2 * kk, dbh + 2 * kk, idesc, 1);
+      }
+      fcv::umma_commit(empty(st));
+    }
+    if (ok_run) fcv::umma_commit(done);
+  }
+  fcv::tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    fcv::tc_fence_after();
+    fcv::tmem_dealloc(tmem, N);
   }
 }
 

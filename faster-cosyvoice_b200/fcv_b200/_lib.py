@@ -168,6 +168,8 @@ class HiftWeights(ctypes.Structure):
         ("snake_inv", ctypes.c_void_p * HIFT_CONVS),
         ("snake2_alpha", ctypes.c_void_p * HIFT_CONVS),
         ("snake2_inv", ctypes.c_void_p * HIFT_CONVS),
+        ("tc_w_hi", ctypes.c_void_p * HIFT_CONVS),
+        ("tc_w_lo", ctypes.c_void_p * HIFT_CONVS),
         ("f0_w", ctypes.c_void_p * 5),
         ("f0_b", ctypes.c_void_p * 5),
         ("f0_cls_w", ctypes.c_void_p),

@@ -69,8 +69,12 @@ class HiftLayout:
 class B200HiFT:
     """HiFT vocoder on the B200 (``CausalHiFTGenerator`` drop-in for inference)."""
 
-    def __init__(self, state_dict: dict, noise: torch.Tensor, device: str | torch.device = "cuda"):
+    def __init__(self, state_dict: dict, noise: torch.Tensor, device: str | torch.device = "cuda",
+                 tensor_cores: bool = True):
+        """``tensor_cores``: run the 72 residual-block convolutions on tcgen05 with
+        split-tf32 operands (float32 accuracy), else on the SIMT float32 kernel."""
         self.device = torch.device(device)
+        self.tensor_cores = tensor_cores
         sd = {k: v.detach() for k, v in state_dict.items()}
         keep = []
         w = HiftWeights()
@@ -84,6 +88,11 @@ class B200HiFT:
             bias[:co] = sd[f"{name}.bias"].float().cpu()
             keep += [pad.to(**f32).contiguous(), bias.to(**f32)]
             w.conv_w[i], w.conv_b[i] = keep[-2].data_ptr(), keep[-1].data_ptr()
+            if tensor_cores and "resblocks." in name:
+                kmaj = wt.permute(2, 0, 1).contiguous()                # [k][C_out][C_in]
+                hi = (kmaj.view(torch.int32) & -8192).view(torch.float32)  # tf32 head: low 13 bits cleared
+                keep += [hi.to(**f32), (kmaj - hi).to(**f32)]
+                w.tc_w_hi[i], w.tc_w_lo[i] = keep[-2].data_ptr(), keep[-1].data_ptr()
             if ".convs1." in name:
                 block, s = name.split(".convs1.")
                 for fa, fi, act in (("snake_alpha", "snake_inv", "activations1"),
