@@ -1347,9 +1347,9 @@ int hift_conv(const hift::ConvArgs<T>& a, cudaStream_t s) {
   if (a.rows_out == 0) return FCV_OK;
   if constexpr (sizeof(T) == 4 && sizeof(Tin) == 4) {
     if (a.tw_hi && a.tw_lo) {
-      // tensor-core path: stride 1, no upsampling or reflection, no pre-activation,
-      // 32-channel K chunks, 16-byte aligned rows
-      if (a.stride != 1 || a.up != 1 || a.reflect_first || a.pre != hift::PRE_NONE || a.cin % 32 ||
+      // tensor-core path: stride 1, no pre-activation but leaky ReLU, 32-channel K
+      // chunks, 16-byte aligned rows
+      if (a.stride != 1 || (a.pre != hift::PRE_NONE && a.pre != hift::PRE_LEAKY) || a.cin % 32 ||
           a.cout != a.out_pitch || (a.x_pitch % 4) || (reinterpret_cast<uintptr_t>(a.x) & 15))
         return fail(FCV_EUNSUPPORTED, "fcv_hift_forward: convolution not eligible for the tensor-core path");
       if (a.cout == 64) return hift_res_conv_tc<64>(a, s);
@@ -1377,7 +1377,7 @@ hift::ConvArgs<float> hift_args(const fcv_hift_weights* w, int idx, const void* 
   a.rows_out = rows_out;
   a.w = w->conv_w[idx];
   a.b = w->conv_b[idx];
-  if (idx >= 7 && idx <= 78) {
+  if (idx >= 7 && idx <= 78) {   // residual blocks (the upsampling convolutions stay on SIMT: see hift.cuh)
     a.tw_hi = w->tc_w_hi[idx];
     a.tw_lo = w->tc_w_lo[idx];
   }

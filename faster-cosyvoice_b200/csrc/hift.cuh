@@ -258,11 +258,18 @@ __global__ void __launch_bounds__(128, sizeof(T) == 8 ? 2 : 4) conv_kernel(ConvA
 
 
 // ---------------------------------------------------------------- tensor-core residual convolutions
-// Stride-1 convolutions without upsampling and without a pre-activation (the 72
-// residual-block convolutions, 88 % of the vocoder's FLOPs) on tcgen05 kind::tf32
-// with float32 accuracy: each operand is split into a tf32 head h (low 13 mantissa
-// bits cleared) and the remainder l = x - h, and D += Ah*Bh + Ah*Bl + Al*Bh
-// (the Al*Bl term is below float32 rounding).
+// Stride-1 convolutions (the 72 residual-block convolutions, 88 % of the vocoder's
+// FLOPs) on tcgen05 kind::tf32
+// with float32 accuracy: each operand is split into a tf32 head h (x rounded to
+// the nearest tf32, low 13 mantissa bits zero) and the remainder l = x - h (exact,
+// |l| <= 2^-11 |x|), and D += Ah*Bh + Ah*Bl + Al*Bh (the Al*Bl term is below
+// float32 rounding).
+//
+// The kernel also handles nearest upsampling, the first-row reflection and a
+// leaky-ReLU input (applied while splitting), but the three upsampling convolutions
+// (K up to 8192) run on the SIMT kernel: on the tensor cores they took the speech
+// output to 1.007e-4 rel-L2 of the reference's, past the 1e-4 test bound, for a gain
+// of about 8 % of the vocoder time.
 //
 // One CTA computes 128 output rows x N (= C_out) channels, accumulating in N TMEM
 // columns.  Warps 0-3 produce: each thread gathers its output row's input row for
@@ -355,16 +362,17 @@ __global__ void __launch_bounds__(160, 1) res_conv_tc_kernel(ConvArgs<float> p) 
     int rbase = 0, pos0 = 0, lim = 0;
     if (row_ok) {
       const int d = find_doc(p.out_cu, p.n_docs, r);
+      const int t = r - __ldg(p.out_cu + d);
       rbase = __ldg(p.in_off + d);
-      lim = __ldg(p.in_lim + d + 1) - __ldg(p.in_lim + d);
-      pos0 = (r - __ldg(p.out_cu + d)) - p.pad_left;
+      lim = (__ldg(p.in_lim + d + 1) - __ldg(p.in_lim + d)) * p.up;   // positions of the upsampled input
+      pos0 = (p.reflect_first ? (t == 0 ? 1 : t - 1) : t) - p.pad_left;
     }
     const float* xin = static_cast<const float*>(p.x);
     auto issue = [&](int it) {
       const int st = it % S, j = it / n_ci, ci0 = (it - j * n_ci) * 32;
       const int idx = pos0 + j * p.dil;
       const bool ok = row_ok && idx >= 0 && idx < lim;
-      const float* src = ok ? xin + (size_t)(rbase + idx) * p.x_pitch + ci0 : xin;
+      const float* src = ok ? xin + (size_t)(rbase + (p.up == 1 ? idx : idx / p.up)) * p.x_pitch + ci0 : xin;
       const uint32_t arow = a_hi(st) + tid * 128;
 #pragma unroll
       for (int q = 0; q < 8; ++q) cp_async16(arow + ((q ^ (tid & 7)) << 4), src + 4 * q, ok ? 16u : 0u);
@@ -392,12 +400,18 @@ __global__ void __launch_bounds__(160, 1) res_conv_tc_kernel(ConvArgs<float> p) 
 #pragma unroll
       for (int qq = 0; qq < 8; ++qq) {
         const int q = qq ^ (tid & 7);   // swizzled order: the 8 threads of a phase hit distinct banks
-        const float4 v = hrow[q];
+        float4 v = hrow[q];
+        if (p.pre == PRE_LEAKY) {   // leaky ReLU of the input, as the SIMT kernel applies on load
+          v.x = v.x < 0.f ? v.x * p.slope : v.x;
+          v.y = v.y < 0.f ? v.y * p.slope : v.y;
+          v.z = v.z < 0.f ? v.z * p.slope : v.z;
+          v.w = v.w < 0.f ? v.w * p.slope : v.w;
+        }
         float4 h, l;
-        h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-        h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-        h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-        h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+        h.x = __uint_as_float((__float_as_uint(v.x) + 0x1000u) & 0xFFFFE000u);
+        h.y = __uint_as_float((__float_as_uint(v.y) + 0x1000u) & 0xFFFFE000u);
+        h.z = __uint_as_float((__float_as_uint(v.z) + 0x1000u) & 0xFFFFE000u);
+        h.w = __uint_as_float((__float_as_uint(v.w) + 0x1000u) & 0xFFFFE000u);
         l.x = v.x - h.x;
         l.y = v.y - h.y;
         l.z = v.z - h.z;

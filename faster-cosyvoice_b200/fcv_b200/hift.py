@@ -90,7 +90,7 @@ class B200HiFT:
             w.conv_w[i], w.conv_b[i] = keep[-2].data_ptr(), keep[-1].data_ptr()
             if tensor_cores and "resblocks." in name:
                 kmaj = wt.permute(2, 0, 1).contiguous()                # [k][C_out][C_in]
-                hi = (kmaj.view(torch.int32) & -8192).view(torch.float32)  # tf32 head: low 13 bits cleared
+                hi = ((kmaj.view(torch.int32) + 4096) & -8192).view(torch.float32)  # nearest tf32 head
                 keep += [hi.to(**f32), (kmaj - hi).to(**f32)]
                 w.tc_w_hi[i], w.tc_w_lo[i] = keep[-2].data_ptr(), keep[-1].data_ptr()
             if ".convs1." in name:

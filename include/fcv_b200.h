@@ -427,8 +427,9 @@ typedef struct fcv_hift_weights {
   const float* snake2_alpha[FCV_HIFT_CONVS];
   const float* snake2_inv[FCV_HIFT_CONVS];
   /* Residual-block convolutions (7..78) on the tensor cores: weights as
-   * [k][C_out][C_in] float32 split into a tf32 head (low 13 mantissa bits zero)
-   * and the float32 remainder w - head; null runs the convolution on the SIMT path. */
+   * [k][C_out][C_in] float32 split into a tf32 head (w rounded to the nearest tf32,
+   * low 13 mantissa bits zero) and the float32 remainder w - head; null runs the
+   * convolution on the SIMT path. */
   const float* tc_w_hi[FCV_HIFT_CONVS];
   const float* tc_w_lo[FCV_HIFT_CONVS];
   const double* f0_w[5];
