@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(128, sizeof(T) == 8 ? 2 : 4) conv_kernel(ConvA
 // chunk c ^ (r & 7)), the layout the MMA descriptors describe.
 template <int N>
 struct ResConvCfg {
-  static constexpr int S = N == 256 ? 2 : (N == 128 ? 3 : 4);     // pipeline stages
+  static constexpr int S = N == 128 ? 3 : 2;                       // pipeline stages (N = 64: two CTAs per SM)
   static constexpr int A_BYTES = 128 * 128;                        // 128 rows x 32 floats
   static constexpr int B_BYTES = N * 128;
   static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;          // head and remainder of A and B
@@ -313,7 +313,7 @@ __host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N) {
 }
 
 template <int N>
-__global__ void __launch_bounds__(160, 1) res_conv_tc_kernel(ConvArgs<float> p) {
+__global__ void __launch_bounds__(160, N == 64 ? 2 : 1) res_conv_tc_kernel(ConvArgs<float> p) {
   using Cfg = ResConvCfg<N>;
   constexpr int S = Cfg::S;
   griddep_wait();
