@@ -1,0 +1,65 @@
+"""Host-side logic of the HiFT vocoder, no GPU: the per-level row layout of a
+packed batch (the fcv_hift_batch.layout block), output lengths against the
+oracle, rejection of too-short non-final chunks, and the convolution order of
+the C ABI against the reference's state-dict keys."""
+
+from __future__ import annotations
+
+import types
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import hift_inputs
+from oracle import hift_oracle as H
+
+
+def _layout_host():
+    from fcv_b200.hift import B200HiFT
+
+    obj = types.SimpleNamespace(device=torch.device("cpu"), _layouts={})
+    return lambda n_mel, fin: B200HiFT.layout(obj, n_mel, fin)
+
+
+def test_layout_rows_per_level():
+    lay = _layout_host()([9, 14, 17], [True, True, False])
+    # mel, f0, x, source, stft, level0, level1, level2, audio
+    assert lay.counts == [[9, 14, 17], [9, 14, 14], [9, 14, 10], [4320, 6720, 6720], [1081, 1681, 1681],
+                          [72, 112, 80], [360, 560, 400], [1081, 1681, 1201], [4320, 6720, 4320]]
+    block = lay.block.numpy().reshape(9, 4)
+    for a in range(9):
+        assert block[a, 0] == 0
+        np.testing.assert_array_equal(np.diff(block[a]), lay.counts[a])
+        assert block[a, -1] == lay.rows[a]
+    assert lay.max_src == 6720
+
+
+def test_layout_audio_lengths_match_oracle_and_reference_golden():
+    _, _, _, z = hift_inputs()
+    layout = _layout_host()
+    for case in ("off0", "off1", "str0"):
+        L, fin = z[f"{case}_mel"].shape[1], bool(z[f"{case}_finalize"])
+        lay = layout([L], [fin])
+        assert lay.rows[8] == H.out_samples(L, fin) == z[f"{case}_speech"].shape[0]
+        assert lay.rows[3] == z[f"{case}_s"].shape[0]
+
+
+def test_layout_rejects_short_non_final_chunks():
+    layout = _layout_host()
+    with pytest.raises(ValueError):
+        layout([7], [False])
+    with pytest.raises(ValueError):
+        layout([0], [True])
+    assert layout([8], [False]).rows[8] == 0   # 8 frames: one decoded frame, all of it look-ahead
+
+
+def test_conv_order_covers_the_reference_state_dict():
+    from fcv_b200.hift import conv_names
+
+    sd, _, _, _ = hift_inputs()
+    names = conv_names()
+    assert len(names) == len(set(names)) == 80
+    convs = {k.rsplit(".parametrizations", 1)[0] if ".parametrizations." in k else k.rsplit(".", 1)[0]
+             for k in sd if k.endswith((".original1", ".weight")) and not k.startswith(("f0_predictor", "m_source"))}
+    assert convs == set(names)
