@@ -63,3 +63,17 @@ def test_conv_order_covers_the_reference_state_dict():
     convs = {k.rsplit(".parametrizations", 1)[0] if ".parametrizations." in k else k.rsplit(".", 1)[0]
              for k in sd if k.endswith((".original1", ".weight")) and not k.startswith(("f0_predictor", "m_source"))}
     assert convs == set(names)
+
+
+def test_oracle_non_final_chunks_are_prefixes_of_the_offline_output():
+    """The property the reference checks in its own streaming demo (generator.py:743-752):
+    every decode step is causal apart from the look-ahead a non-final chunk consumes, so
+    its 480 (L - 8) samples equal the first samples of the offline output of the whole mel."""
+    _, W, noise, _ = hift_inputs()
+    rng = np.random.default_rng(21)
+    mel = (1.5 * rng.standard_normal((20, 80)) - 3).astype(np.float32)
+    full, _, _ = H.inference(mel, W, noise.numpy(), True)
+    for L in (9, 13, 17):
+        part, _, _ = H.inference(mel[:L], W, noise.numpy(), False)
+        assert part.shape[0] == H.out_samples(L, False)
+        np.testing.assert_allclose(part, full[:part.shape[0]], rtol=0, atol=1e-5)
