@@ -420,6 +420,56 @@ def vocoder_arm(args, impl: str):
     print(json.dumps(line), flush=True)
 
 
+def vocoder_cpu_arm(args):
+    """The vocoder's CPU reference arm: the numpy port of CausalHiFTGenerator.inference
+    (oracle/hift_oracle.py, float32 with a float64 f0 predictor, BLAS on every host
+    thread) timed on one request of the config, trimmed so a step takes a few seconds.
+    Same metric and config as ``vocoder_arm``."""
+    from oracle import hift_oracle as H
+
+    req, chunk, seed = request_lengths(args.config)
+    finalize = chunk == 0
+    cores = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+
+        threadpool_limits(limits=cores)
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        pass
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import hift_weights as HW
+
+    W = HW.folded(HW.hift_state(0))
+    noise = HW.hift_noise(480 * (max(req) + 8), 1).numpy()
+    rng = np.random.default_rng(900 + seed)
+    mel = (1.5 * rng.standard_normal((req[0], 80)) - 3).astype(np.float32)
+    budget = max(0.5, min(6.0, 150.0 / (args.steps + args.warmup)))
+    t0 = time.perf_counter()
+    H.inference(mel[:16], W, noise, finalize)
+    per_frame = (time.perf_counter() - t0) / 16
+    L = int(max(16, min(req[0], budget / max(per_frame, 1e-6))))
+    for _ in range(args.warmup):
+        H.inference(mel[:L], W, noise, finalize)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        H.inference(mel[:L], W, noise, finalize)
+        times.append(time.perf_counter() - t0)
+    value = L / float(np.median(times))
+    sample = f"one request of {L} mel frames ({'offline' if finalize else 'non-final chunk'}, numpy port)"
+    line = {"metric": "vocoder mel-frames/s (HiFT decode)", "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f64 f0 predictor)",
+            "data": "synthetic (seeded mels, weights and noise table)",
+            "config": {"workload": f"HiFT vocoder, {CONFIG_NAMES[args.config]}", "requests": len(req),
+                       "mel_frames": sum(req), "finalize": finalize},
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------------------- streaming calls
 def stream_arm(args, impl: str, cached: bool):
     """One JSON line: a streaming session of 32 streams (config 3's prompts, 100-400
@@ -751,8 +801,11 @@ def main():
     if args.vocoder:
         if args.config not in ("2", "3"):
             raise SystemExit("--vocoder runs configs 2 (offline) and 3 (streaming)")
-        if rank == 0 and args.impl != "reference":
-            vocoder_arm(args, args.impl)
+        if rank == 0:
+            if args.impl == "reference":
+                vocoder_cpu_arm(args)
+            else:
+                vocoder_arm(args, args.impl)
         return
 
     if args.stream:

@@ -59,3 +59,12 @@ def test_gpu_comparison_arm_unavailable_without_gpu():
     assert r.returncode == 0, r.stderr[-2000:]
     line = _last_json(r.stdout)
     assert line["impl"] == "reference-gpu" and "unavailable" in line
+
+
+def test_vocoder_reference_arm_prints_a_line():
+    r = _run(["--vocoder", "--impl", "reference", "--steps", "1", "--warmup", "3"])
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = _last_json(r.stdout)
+    assert line["impl"] == "reference" and line["metric"] == "vocoder mel-frames/s (HiFT decode)"
+    assert line["value"] > 0 and line["cpu_baseline"]["value"] == line["value"] and line["cpu_baseline"]["sample"]
+    assert line["config"]["finalize"] is True and line["config"]["requests"] == 8
