@@ -1,7 +1,7 @@
 """Generate the golden vectors under ``tests/golden/`` from the reference itself.
 
 Run in a container where the reference project is present (read-only) at
-``$FCV_REFERENCE_ROOT`` (default ``/root/reference``)::
+``$FCV_REFERENCE_ROOT`` (default: the path in ``REF`` below)::
 
     python tests/golden/make_golden.py
 
