@@ -77,3 +77,38 @@ def test_oracle_non_final_chunks_are_prefixes_of_the_offline_output():
         part, _, _ = H.inference(mel[:L], W, noise.numpy(), False)
         assert part.shape[0] == H.out_samples(L, False)
         np.testing.assert_allclose(part, full[:part.shape[0]], rtol=0, atol=1e-5)
+
+
+def test_weight_preparation_on_the_host():
+    """B200HiFT built on the CPU: every convolution's padded [k][C_in][C_out] copy holds
+    the weight-norm-folded weights, the tensor-core copies split them exactly
+    (head + remainder == weight, heads with 13 zero mantissa bits), and the Snake
+    inverses are the reference's float32 1 / (alpha + 1e-9)."""
+    from fcv_b200.hift import B200HiFT, conv_names
+
+    sd, W, noise, _ = hift_inputs()
+    voc = B200HiFT(sd, noise, "cpu", tensor_cores=True)
+    by_ptr = {t.data_ptr(): t for t in voc._keep}
+    w = voc._w
+    for i, name in enumerate(conv_names()):
+        ref = torch.from_numpy(W[f"{name}.weight"])                      # (C_out, C_in, k)
+        co, ci, k = ref.shape
+        pad = by_ptr[w.conv_w[i]]
+        assert pad.shape == (k, -(-ci // 16) * 16, -(-co // 64) * 64)
+        assert torch.equal(pad[:, :ci, :co], ref.permute(2, 1, 0))
+        assert not pad[:, ci:, :].any() and not pad[:, :, co:].any()
+        if "resblocks." in name:
+            hi, lo = by_ptr[w.tc_w_hi[i]], by_ptr[w.tc_w_lo[i]]
+            assert torch.equal(hi + lo, ref.permute(2, 0, 1))
+            assert not (hi.view(torch.int32) & 8191).any()
+        else:
+            assert not w.tc_w_hi[i] and not w.tc_w_lo[i]
+        if ".convs1." in name:
+            block, s = name.split(".convs1.")
+            a = torch.from_numpy(W[f"{block}.activations1.{s}.alpha"])
+            assert torch.equal(by_ptr[w.snake_alpha[i]], a)
+            assert torch.equal(by_ptr[w.snake_inv[i]], 1.0 / (a + 1e-9))
+    f0w = by_ptr[w.f0_w[1]]
+    assert f0w.dtype == torch.float64
+    assert torch.equal(f0w, torch.from_numpy(W["f0_predictor.condnet.2.weight"]).permute(2, 1, 0))
+    assert w.noise_rows == noise.shape[0]
