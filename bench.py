@@ -3,19 +3,22 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5] [--impl b200|reference]
 
-Default workload ("config 2"): 22-layer bf16 DiT,
-8 requests with CFG doubling -> 16 sequences, lengths ~U[150, 600] frames
-(a CFG pair shares its length), inputs ~N(0,1), t ~U(0,1), random-init
-weights from seed 1, full (offline) mask, one estimator call per step.
+Default workload ("config 5", the configuration the
+metric is quoted on at 1/2/4/8 GPUs): 22-layer bf16 DiT, 16 requests x 3000 mel
+frames with CFG doubling -> 32 sequences, 96,000 packed rows, full (offline)
+mask, inputs ~N(0,1), t ~U(0,1), random-init weights from seed 5, one estimator
+call per step.  ``--config 2|3|4`` select the other estimator configs.
 Synthetic data of the reference's shapes; no dataset is involved.
 
-Under torchrun (N > 1) every rank runs its own batch of the same composition
-(weak scaling, no collective on the data path); ``--config 4`` and ``--config 5``
-instead shard one fixed request set across the ranks by LPT bins (strong).
+Under torchrun (N > 1) one fixed request set is sharded across the ranks by
+LPT bins of the per-request FLOP cost (strong scaling: the same total work at
+every N; no collective on the data path); ``--weak`` runs replicas instead.
 
-``--impl reference`` times the reference's CPU path (the oracle port of its
-torch DiT, float32, all host threads) on a bounded sample of the same
-workload; under torchrun only rank 0 runs it.
+``--impl reference`` times the reference's own CPU implementation of the path:
+its torch ``DiT`` (installed offline in ``baseline/_ref``), float32, all host
+threads, one request as its CFG pair per step in a stratified order over the
+config's requests; the oracle port stands in when the install is missing.
+Under torchrun only rank 0 runs it.
 
 ``--impl reference-gpu`` times the reference's own GPU estimator
 (``FlashInferDiT``: Triton row kernels, FlashInfer ragged prefill, cuBLAS; in
@@ -181,12 +184,128 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------- CPU baseline
+def _host_threads() -> int:
+    """Let torch and the BLAS pools use every host thread (torchrun pins
+    OMP_NUM_THREADS=1); returns the thread count in use."""
+    import torch
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=cores)
+    except Exception:
+        pass
+    return torch.get_num_threads()
+
+
+def stratified_order(lengths) -> list[int]:
+    """Request indices in an order whose every prefix spans the length
+    distribution: the median, the longest, the shortest, then the quartiles,
+    the octiles, ... of the sorted lengths, then everything left."""
+    n = len(lengths)
+    by_len = sorted(range(n), key=lambda i: (lengths[i], i))
+    fr = [0.5, 1.0, 0.0]
+    k = 4
+    while len(fr) < 4 * n and k <= 4 * n:
+        fr += [j / k for j in range(1, k, 2)]
+        k *= 2
+    seen, order = set(), []
+    for f in fr:
+        i = by_len[int(round(f * (n - 1)))]
+        if i not in seen:
+            seen.add(i)
+            order.append(i)
+    order += [i for i in by_len if i not in seen]
+    return order
+
+
+class ReferenceCpuDiT:
+    """The reference's own torch ``DiT`` (``cosyvoice/flow/DiT/dit.py:104-176``,
+    padded SDPA path) in float32 on the host cores, from the offline install in
+    ``baseline/_ref`` (its RoPE dependency ``x-transformers`` restated by the
+    test shim).  One call = one request as its CFG pair (B = 2, the second half
+    with mu, spks and cond zeroed, ``flashinfer_flow.py:45-51``), no padding.
+    ``available`` is False (with ``why``) when the install is missing."""
+
+    def __init__(self, seed: int, depth: int = 22):
+        self.available, self.why, self.model = False, "", None
+        ref_root = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.isdir(os.path.join(ref_root, "faster_cosyvoice")):
+            self.why = "reference not installed in baseline/_ref"
+            return
+        for p in (ref_root, os.path.join(ROOT, "tests", "golden", "_xt_shim")):
+            if p not in sys.path:
+                sys.path.insert(0, p)
+        try:
+            import torch
+            from faster_cosyvoice.token2wav.cosyvoice.flow.DiT.dit import DiT
+        except Exception as exc:
+            self.why = f"reference import failed: {type(exc).__name__}: {exc}"
+            return
+        self.cores = _host_threads()
+        torch.manual_seed(seed)  # the reference constructor's own random initialisation
+        self.model = DiT(dim=1024, depth=depth, heads=16, dim_head=64, ff_mult=2, mel_dim=80, mu_dim=80,
+                         spk_dim=80, out_channels=80, static_chunk_size=50, num_decoding_left_chunks=-1).eval()
+        self.available = True
+
+    def pair_seconds(self, L: int, streaming: bool, seed: int) -> float:
+        import torch
+
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn(1, 80, L, generator=g).repeat(2, 1, 1)
+        mu = torch.cat([torch.randn(1, 80, L, generator=g), torch.zeros(1, 80, L)])
+        cond = torch.cat([torch.randn(1, 80, L, generator=g), torch.zeros(1, 80, L)])
+        spks = torch.cat([torch.randn(1, 80, generator=g), torch.zeros(1, 80)])
+        t = torch.rand(1, generator=g).repeat(2)
+        mask = torch.ones(2, 1, L)
+        with torch.inference_mode():
+            t0 = time.perf_counter()
+            self.model(x, mask, mu, t, spks, cond, streaming=streaming)
+            return time.perf_counter() - t0
+
+
+def cpu_reference_rate(req_lengths, chunk, seed, budget_s: float):
+    """CPU baseline of the b200 arm: the reference torch DiT (``ReferenceCpuDiT``)
+    over request pairs in stratified order until ``budget_s`` seconds are spent
+    (at least one pair).  Falls back to the oracle port when the reference is
+    not installed.  Returns the ``cpu_baseline`` object."""
+    ref = ReferenceCpuDiT(seed)
+    if not ref.available:
+        r, dt, L, cores, sample = cpu_oracle_rate(None, req_lengths, seed, budget_s)
+        return {"value": r, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample + f" ({ref.why})",
+                "seconds": dt}
+    ref.pair_seconds(64, chunk > 0, 0)  # warm-up: thread pools, allocator
+    frames, secs, done = 0, 0.0, []
+    for i in stratified_order(req_lengths):
+        L = int(req_lengths[i])
+        secs += ref.pair_seconds(L, chunk > 0, 100 + i)
+        frames += 2 * L
+        done.append(L)
+        if secs >= budget_s:
+            break
+    sample = (f"{len(done)} of {len(req_lengths)} requests as CFG pairs (B=2, lengths {sorted(done)}), stratified "
+              f"over the config's lengths; reference torch DiT, fp32, "
+              f"{'chunk-%d streaming' % chunk if chunk else 'offline'} mask")
+    return {"value": frames / secs, "unit": UNIT, "cores": ref.cores, "kind": "reference", "sample": sample,
+            "seconds": secs}
+
+
 def cpu_oracle_rate(params, req_lengths, seed, budget_s: float):
     """Time the oracle port of the reference torch DiT (float32, numpy BLAS on
     every host thread) on one document of the workload, trimmed so one pass
-    takes about ``budget_s`` seconds.  Returns (frames/s, seconds, rows, cores, sample)."""
+    takes about ``budget_s`` seconds (the fallback when the reference itself is
+    not installed).  Returns (frames/s, seconds, rows, cores, sample)."""
     from oracle import dit_oracle as O
 
+    if params is None:
+        import torch
+
+        from fcv_b200.model import B200DiT
+
+        torch.manual_seed(seed)
+        params = {k: v.detach().float().numpy() for k, v in B200DiT(depth=22).eval().state_dict().items()}
     cores = os.cpu_count() or 1
     try:
         # torchrun pins OMP_NUM_THREADS=1; the CPU baseline uses every host thread
@@ -423,11 +542,16 @@ def vocoder_arm(args, impl: str):
 def vocoder_cpu_arm(args):
     """The vocoder's CPU reference arm: the numpy port of CausalHiFTGenerator.inference
     (oracle/hift_oracle.py, float32 with a float64 f0 predictor, BLAS on every host
-    thread) timed on one request of the config, trimmed so a step takes a few seconds.
-    Same metric and config as ``vocoder_arm``."""
+    thread) timed on the config's requests (``--requests`` honoured) one after the
+    other, each trimmed to the same length so a step takes a few seconds.  The
+    per-frame cost is calibrated after a warm-up call, from two lengths so that the
+    fixed per-call cost is subtracted.  Same metric and statistic (mean step time)
+    as ``vocoder_arm``; the line's ``sample`` says what was timed."""
     from oracle import hift_oracle as H
 
     req, chunk, seed = request_lengths(args.config)
+    if args.requests > 0:
+        req = req[:args.requests]
     finalize = chunk == 0
     cores = os.cpu_count() or 1
     try:
@@ -443,27 +567,46 @@ def vocoder_cpu_arm(args):
     W = HW.folded(HW.hift_state(0))
     noise = HW.hift_noise(480 * (max(req) + 8), 1).numpy()
     rng = np.random.default_rng(900 + seed)
-    mel = (1.5 * rng.standard_normal((req[0], 80)) - 3).astype(np.float32)
+    mels = [(1.5 * rng.standard_normal((L, 80)) - 3).astype(np.float32) for L in req]
     budget = max(0.5, min(6.0, 150.0 / (args.steps + args.warmup)))
-    t0 = time.perf_counter()
-    H.inference(mel[:16], W, noise, finalize)
-    per_frame = (time.perf_counter() - t0) / 16
-    L = int(max(16, min(req[0], budget / max(per_frame, 1e-6))))
+    longest = mels[int(np.argmax(req))]
+    H.inference(longest[:16], W, noise, finalize)  # warm-up (BLAS threads, allocations)
+
+    def once(L):
+        t0 = time.perf_counter()
+        H.inference(longest[:L], W, noise, finalize)
+        return time.perf_counter() - t0
+
+    l2 = min(48, max(req))
+    t16, t48 = once(16), once(l2)
+    per_frame = max((t48 - t16) / max(l2 - 16, 1), 1e-6)
+    fixed = max(t16 - 16 * per_frame, 0.0)
+    # every request trimmed to the same L frames, L sized so the step fits the budget
+    L = int(max(16, min(max(req), (budget - fixed * len(req)) / (per_frame * len(req)))))
+    use = [m[:min(L, m.shape[0])] for m in mels]
+    frames = sum(m.shape[0] for m in use)
+
+    def step():
+        for m in use:
+            H.inference(m, W, noise, finalize)
+
     for _ in range(args.warmup):
-        H.inference(mel[:L], W, noise, finalize)
+        step()
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        H.inference(mel[:L], W, noise, finalize)
+        step()
         times.append(time.perf_counter() - t0)
-    value = L / float(np.median(times))
-    sample = f"one request of {L} mel frames ({'offline' if finalize else 'non-final chunk'}, numpy port)"
+    value = frames / float(np.mean(times))
+    sample = (f"{len(use)} requests, each trimmed to at most {L} mel frames ({frames} frames per step; "
+              f"{'offline' if finalize else 'non-final chunks'}, numpy port)")
     line = {"metric": "vocoder mel-frames/s (HiFT decode)", "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f64 f0 predictor)",
             "data": "synthetic (seeded mels, weights and noise table)",
             "config": {"workload": f"HiFT vocoder, {CONFIG_NAMES[args.config]}", "requests": len(req),
-                       "mel_frames": sum(req), "finalize": finalize},
+                       "mel_frames": sum(req), "finalize": finalize,
+                       "measured_requests": len(use), "measured_mel_frames": frames},
             "impl": "reference",
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -758,12 +901,74 @@ def reference_gpu_arm(args, req_lengths, chunk, seed, cfg, strong):
     print(json.dumps(line), flush=True)
 
 
+def reference_cpu_arm(args, req_lengths, chunk, seed, cfg, strong):
+    """``--impl reference``: the reference's own CPU implementation of the path
+    -- its torch ``DiT`` (``dit.py:145-176``), fp32, every host thread -- timed
+    per request as its CFG pair.  Step k times request ``order[k % R]`` of a
+    stratified order (median, longest, shortest, quartiles, ...), so the steps
+    cover the length distribution; value = frames of the timed steps / their
+    time.  Warm-up steps run a short pair (thread pools, allocator).  Falls
+    back to the oracle port (``kind: "port"``) when the reference is not
+    installed."""
+    ref = ReferenceCpuDiT(seed)
+    base = {"metric": METRIC, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded N(0,1) inputs, random-init weights of the 22-layer DiT)",
+            "config": cfg, "impl": "reference"}
+    if not ref.available:
+        import torch
+
+        from fcv_b200.model import B200DiT
+
+        torch.manual_seed(seed)
+        params = {k: v.detach().float().numpy() for k, v in B200DiT(depth=22).eval().state_dict().items()}
+        budget = max(0.5, min(6.0, 150.0 / (args.steps + args.warmup)))
+        for _ in range(args.warmup):
+            cpu_oracle_rate(params, req_lengths, seed, budget)
+        rates, times = [], []
+        for _ in range(args.steps):
+            r, dt, L, cores, sample = cpu_oracle_rate(params, req_lengths, seed, budget)
+            rates.append(r)
+            times.append(dt)
+        value = float(statistics.median(rates))
+        line = {**base, "value": value, "ms_per_step": 1000 * float(np.mean(times)),
+                "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                                 "sample": sample + f" ({ref.why})"},
+                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    for w in range(args.warmup):
+        ref.pair_seconds(64, chunk > 0, w)
+    order = stratified_order(req_lengths)
+    times, frames, lens = [], 0, []
+    for k in range(args.steps):
+        i = order[k % len(order)]
+        L = int(req_lengths[i])
+        times.append(ref.pair_seconds(L, chunk > 0, 100 + i))
+        frames += 2 * L
+        lens.append(L)
+    value = frames / float(sum(times))
+    sample = (f"{args.steps} steps, each one request as its CFG pair (B=2, no padding) in stratified order over "
+              f"the config's {len(req_lengths)} requests ({len(set(order[:args.steps]))} distinct; lengths "
+              f"{min(lens)}-{max(lens)}, {frames} frames); reference torch DiT (baseline/_ref), fp32, "
+              f"{'chunk-%d streaming' % chunk if chunk else 'offline'} mask")
+    line = {**base, "value": value, "ms_per_step": 1000 * float(np.mean(times)),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": ref.cores, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="2", choices=["2", "3", "4", "5"])
+    ap.add_argument("--config", default="5", choices=["2", "3", "4", "5"],
+                    help="BASELINE.json config (default 5, the config the metric is quoted on at 1/2/4/8 GPUs)")
+    ap.add_argument("--weak", action="store_true",
+                    help="N > 1: every rank runs its own copy of the batch (replicas) instead of one fixed "
+                         "request set sharded across the ranks by LPT bins")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-gpu"])
     ap.add_argument("--ref-dtype", default="fp16", choices=["fp16", "bf16"],
                     help="element type of the reference GPU estimator (--impl reference-gpu)")
@@ -792,10 +997,13 @@ def main():
     req_lengths, chunk, seed = request_lengths(args.config)
     if args.requests > 0:
         req_lengths = req_lengths[:args.requests]
-    strong = args.config in ("4", "5") and world > 1
+    # N > 1: one fixed request set sharded across the ranks by LPT bins (strong
+    # scaling, the same total work at every N) unless --weak asks for replicas
+    strong = not args.weak
     cfg = {"workload": CONFIG_NAMES[args.config], "requests": len(req_lengths), "sequences": 2 * len(req_lengths),
            "packed_rows": 2 * sum(req_lengths), "chunk": chunk, "seed": seed,
-           "parallelism": f"dp{world} (request bins, no collective)",
+           "parallelism": f"dp{world} ({'LPT request bins of one fixed request set' if strong else 'replicas'}, "
+                          "no collective on the data path)",
            "l2": "working set (662 MB of weights per NFE) exceeds the 126 MB L2; L2 also flushed between steps"}
 
     if args.vocoder:
@@ -828,29 +1036,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        import torch
-
-        from fcv_b200.model import B200DiT
-
-        torch.manual_seed(seed)
-        model = B200DiT(depth=22).eval()
-        params = {k: v.detach().float().numpy() for k, v in model.state_dict().items()}
-        budget = max(0.5, min(6.0, 150.0 / (args.steps + args.warmup)))
-        for _ in range(args.warmup):
-            cpu_oracle_rate(params, req_lengths, seed, budget)
-        rates, times = [], []
-        for _ in range(args.steps):
-            r, dt, L, cores, sample = cpu_oracle_rate(params, req_lengths, seed, budget)
-            rates.append(r)
-            times.append(dt)
-        value = float(statistics.median(rates))
-        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": 1000 * float(np.mean(times)), "higher_is_better": True,
-                "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic", "config": cfg, "impl": "reference",
-                "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
-                "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
+        reference_cpu_arm(args, req_lengths, chunk, seed, cfg, strong)
         return
 
     if args.impl == "reference-gpu":
@@ -863,7 +1049,7 @@ def main():
 
     from fcv_b200 import _lib
     from fcv_b200.model import B200DiT
-    from fcv_b200.shard import lpt_bins
+    from fcv_b200.shard import bin_loads, lpt_bins
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
@@ -875,14 +1061,13 @@ def main():
     if strong:
         bins = lpt_bins(req_lengths, world, chunk or None)
         my_req = [req_lengths[i] for i in bins[rank]]
+        if not my_req:
+            raise SystemExit(f"config {args.config} has {len(req_lengths)} requests, fewer than {world} ranks")
     else:
         my_req = list(req_lengths)
 
     torch.manual_seed(seed)
     cpu_model = B200DiT(depth=22).eval()
-    cpu_params = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_params = {k: v.detach().float().numpy() for k, v in cpu_model.state_dict().items()}
     model = cpu_model.to(device=device, dtype=torch.bfloat16)
     model.finalize_weights()
     lengths, T, host, dev = make_batch(my_req, seed + 17 * rank, device, torch.bfloat16)
@@ -1002,13 +1187,19 @@ def main():
 
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_ms = float(sum(step_ms))
-    t_max = torch.tensor([total_ms], dtype=torch.float64, device=device)
-    rows = torch.tensor([float(N)], dtype=torch.float64, device=device)
+    mine = torch.tensor([total_ms, float(N)], dtype=torch.float64, device=device)
+    per_rank = [mine]
     if world > 1:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-        dist.all_reduce(rows, op=dist.ReduceOp.SUM)
-    total_ms_max = float(t_max.item())
-    all_rows = float(rows.item())
+        per_rank = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(per_rank, mine)
+    total_ms_max = max(float(v[0].item()) for v in per_rank)
+    all_rows = sum(float(v[1].item()) for v in per_rank)
+    shard = {"rows_per_rank": [int(v[1].item()) for v in per_rank],
+             "ms_per_step_per_rank": [float(v[0].item()) / args.steps for v in per_rank],
+             "requests_per_rank": [len(b) for b in bins] if strong and world > 1 else [len(my_req)] * world}
+    if strong and world > 1:
+        shard["bin_cost_imbalance"] = max(bin_loads(req_lengths, bins, chunk or None)) / (
+            sum(bin_loads(req_lengths, bins, chunk or None)) / world)
     value = all_rows * args.steps / (total_ms_max / 1000.0)
     ms_per_step = total_ms_max / args.steps
 
@@ -1018,37 +1209,50 @@ def main():
     from fcv_b200.flops import estimator_flops, visible_pairs
 
     gemm_flops_step = 22 * N * (2 ** 24)
-    gemm_ms = gemm_graph_ms
     gemm_launches = 88
-    peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-        peak_tf, peak_src = float(peaks["bf16_tflops_sustained"]), "measured (sustained)"
-        hbm = float(peaks["hbm_gbs"])
+        burst, sustained = float(peaks["bf16_tflops"]), float(peaks["bf16_tflops_sustained"])
+        peak_src = "of measured (MEASURED_PEAKS.json)"
     except Exception:
-        peak_tf, peak_src, hbm = 1400.0, "fallback (sustained)", 6650.0
-    gemm_tf = gemm_flops_step / (gemm_ms / 1000.0) / 1e12 if gemm_ms > 0 else None
-    per_launch_flops = gemm_flops_step / 88
+        burst, sustained, peak_src = 1590.0, 1400.0, "of fallback"
+    gemm_tf = gemm_flops_step / (gemm_graph_ms / 1000.0) / 1e12 if gemm_graph_ms > 0 else None
     attn_flops_step = 22 * 4096 * visible_pairs(lengths, chunk or None)
     attn_tf = attn_flops_step / (attn_graph_ms / 1000.0) / 1e12 if attn_graph_ms > 0 else None
     total_flops = estimator_flops(lengths, chunk or None, 22)
     nfe_tf = total_flops / (ms_per_step / 1000.0) / 1e12
-    traffic = None
+    tr = {}
     try:
-        tr = json.load(open(os.path.join(ROOT, "profiles", "traffic.json")))
-        traffic = tr.get(args.config, {}).get("gemm_bytes_per_launch")
+        tr = json.load(open(os.path.join(ROOT, "profiles", "traffic.json"))).get(args.config, {})
     except Exception:
         pass
-    roofline = {"bound": "tensor", "kernel": "tc_gemm_pair_kernel (tcgen05 cta_group::2; QKV, out, FF1, FF2 of each block)",
-                "timing": "22 x 4 block GEMMs of this workload in one CUDA graph, CUDA events around the graph, "
-                          "L2 flushed between replays; average per launch",
-                "achieved": gemm_tf, "peak": peak_tf, "unit": "TFLOP/s",
-                "frac": (gemm_tf / peak_tf) if gemm_tf else None, "peak_source": peak_src,
-                "flops_per_launch": per_launch_flops,
-                "avg_launch_ms": gemm_ms / max(gemm_launches, 1), "traffic": traffic,
-                "attention_tflops": attn_tf, "attention_frac": (attn_tf / peak_tf) if attn_tf else None,
-                "attention_avg_launch_ms": attn_graph_ms / 22,
-                "nfe_tflops": nfe_tf, "nfe_frac": nfe_tf / peak_tf}
+    # The two dominant kernel classes are timed alone (their own CUDA graphs of one
+    # step's launches), so both are held against the measured BURST bf16 peak; the
+    # whole NFE, timed inside the step loop, against the SUSTAINED one.
+    gemm = {"kernel": "tc_gemm_pair_kernel (tcgen05 cta_group::2; QKV, out, FF1, FF2 of each block)",
+            "bound": "tensor", "unit": "TFLOP/s", "achieved": gemm_tf, "peak": burst,
+            "frac": gemm_tf / burst if gemm_tf else None, "peak_kind": "burst",
+            "flops_per_launch": gemm_flops_step / gemm_launches, "avg_launch_ms": gemm_graph_ms / gemm_launches,
+            "launches_per_step": gemm_launches, "traffic": tr.get("gemm_bytes_per_launch"),
+            "timing": "22 x 4 block GEMMs of this workload in one CUDA graph, CUDA events around the graph, "
+                      "L2 flushed between replays; average per launch"}
+    attn = {"kernel": "attn_tc_kernel (tcgen05; ragged chunk-masked attention)", "bound": "tensor",
+            "unit": "TFLOP/s", "achieved": attn_tf, "peak": burst, "frac": attn_tf / burst if attn_tf else None,
+            "peak_kind": "burst", "flops_per_launch": attn_flops_step / 22, "avg_launch_ms": attn_graph_ms / 22,
+            "launches_per_step": 22, "traffic": tr.get("attention_bytes_per_launch"),
+            "timing": "the 22 attention launches of this workload in one CUDA graph, CUDA events around the graph, "
+                      "L2 flushed between replays; average per launch"}
+    dom = attn if attn_graph_ms > gemm_graph_ms else gemm
+    roofline = {"bound": dom["bound"], "kernel": dom["kernel"], "achieved": dom["achieved"], "peak": dom["peak"],
+                "unit": "TFLOP/s", "frac": dom["frac"], "traffic": dom["traffic"],
+                "peak_source": f"bf16 burst {peak_src}", "flops_per_launch": dom["flops_per_launch"],
+                "avg_launch_ms": dom["avg_launch_ms"], "timing": dom["timing"],
+                "dominant": "attention" if dom is attn else "gemm",
+                "share_of_step": {"gemm": gemm_graph_ms / max(ms_per_step, 1e-9),
+                                  "attention": attn_graph_ms / max(ms_per_step, 1e-9)},
+                "gemm": gemm, "attention": attn,
+                "nfe_tflops": nfe_tf, "nfe_frac": nfe_tf / sustained, "nfe_peak": sustained,
+                "nfe_peak_kind": "sustained (the NFE is timed inside the step loop)"}
 
     # ---- end to end through the public module API with host buffers
     e2e = None
@@ -1090,9 +1294,8 @@ def main():
 
     # ---- CPU baseline (rank 0, N=1 only)
     cpu = None
-    if rank == 0 and world == 1 and cpu_params is not None:
-        r, dt, L, cores, sample = cpu_oracle_rate(cpu_params, req_lengths, seed, 15.0)
-        cpu = {"value": r, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample, "seconds": dt}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference_rate(req_lengths, chunk, seed, 15.0)
 
     if world > 1:
         dist.barrier()
@@ -1101,7 +1304,7 @@ def main():
                 "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
                 "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded N(0,1) inputs, random-init weights of the 22-layer DiT)",
-                "config": cfg, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "config": cfg, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "shard": shard,
                 "gpu_launches": int(launches), "gpu_launches_note": "kernels per step counted at graph capture x steps",
                 "clocks": clocks.summary(),
                 "request_frames_per_s": value / 2, "kernel_ms_traced": prof,

@@ -1415,8 +1415,12 @@ int fcv_hift_forward(const fcv_hift_weights* w, const fcv_hift_batch* b, void* w
                      void* stream) {
   using namespace hift;
   if (!w || !b || b->n_docs < 0) return fail(FCV_EINVAL, "fcv_hift_forward: bad arguments");
-  if (b->n_docs == 0 || b->rows[8] == 0) return FCV_OK;
-  if (!b->mel || !b->layout || !b->audio) return fail(FCV_EINVAL, "fcv_hift_forward: null mel, layout or audio");
+  // A batch of non-final chunks that each hold only their look-ahead frames has no
+  // audio (rows[8] == 0) but still a source excitation and f0 (rows[3], rows[1]):
+  // the f0/source stage runs whenever any of them is non-empty.
+  if (b->n_docs == 0 || (b->rows[1] == 0 && b->rows[3] == 0 && b->rows[8] == 0)) return FCV_OK;
+  if (!b->mel || !b->layout || (!b->audio && b->rows[8] > 0))
+    return fail(FCV_EINVAL, "fcv_hift_forward: null mel, layout or audio");
   for (int i = 0; i < FCV_HIFT_CONVS; ++i)
     if (!w->conv_w[i] || !w->conv_b[i]) return fail(FCV_EINVAL, "fcv_hift_forward: convolution %d has no weights", i);
   for (int i = 0; i < 5; ++i)
@@ -1503,6 +1507,14 @@ int fcv_hift_forward(const fcv_hift_weights* w, const fcv_hift_batch* b, void* w
     FCV_LAUNCH("hift_stft_kernel", stft_kernel, dim3((rows[4] + 127) / 128), dim3(128), 0, s, s_src, src_cu, stft_cu,
                D, rows[4], spec_in);
 
+  auto copy_source_f0 = [&]() -> int {
+    if (b->source && rows[3] > 0)
+      FCV_CUDA(cudaMemcpyAsync(b->source, s_src, (size_t)rows[3] * 4, cudaMemcpyDeviceToDevice, s));
+    if (b->f0 && rows[1] > 0) FCV_CUDA(cudaMemcpyAsync(b->f0, f0, (size_t)rows[1] * 4, cudaMemcpyDeviceToDevice, s));
+    return FCV_OK;
+  };
+  if (rows[8] == 0) return copy_source_f0();  // no audio frame to decode
+
   // ---- decode: conv_pre reads the first F0 mel frames of each request (look-ahead 4 of them)
   FCV_TRY((hift_conv<float, float>(hift_args(w, 0, b->mel, mel_cu, f0_cu, x_cu, D, rows[2], x0), s)));
   const float* x_prev = x0;
@@ -1579,10 +1591,7 @@ int fcv_hift_forward(const fcv_hift_weights* w, const fcv_hift_batch* b, void* w
              spec_out);
   FCV_LAUNCH("hift_istft_kernel", istft_kernel, dim3((rows[8] + 255) / 256), dim3(256), 0, s, spec_out, lvl_cu[2],
              audio_cu, D, rows[8], b->audio);
-  if (b->source && rows[3] > 0)
-    FCV_CUDA(cudaMemcpyAsync(b->source, s_src, (size_t)rows[3] * 4, cudaMemcpyDeviceToDevice, s));
-  if (b->f0 && rows[1] > 0) FCV_CUDA(cudaMemcpyAsync(b->f0, f0, (size_t)rows[1] * 4, cudaMemcpyDeviceToDevice, s));
-  return FCV_OK;
+  return copy_source_f0();
 }
 
 }  // extern "C"

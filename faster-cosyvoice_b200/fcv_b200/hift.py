@@ -151,7 +151,9 @@ class B200HiFT:
                 raise ValueError("HiFT batch too large for int32 row offsets")
             cu.append(t)
             rows.append(int(t[-1]))
-        block = torch.cat(cu).to(torch.int32).to(self.device)
+        # the nine cu arrays, then [0, total mel rows]: the row offsets of the one
+        # pack call that transposes all requests' (80, sum L) mels into rows
+        block = torch.cat(cu + [torch.tensor([0, rows[0]], dtype=torch.int64)]).to(torch.int32).to(self.device)
         lay = HiftLayout(key[0], key[1], counts, rows, block, max(counts[3], default=0))
         if len(self._layouts) >= 64:
             self._layouts.pop(next(iter(self._layouts)))
@@ -191,15 +193,18 @@ class B200HiFT:
         return audio[:lay.rows[8]], (src[:lay.rows[3]] if src is not None else None)
 
     def _pack(self, mels: Sequence[torch.Tensor], lay: HiftLayout) -> torch.Tensor:
-        rows = torch.empty(max(lay.rows[0], 1), MEL, dtype=torch.float32, device=self.device)
-        off = 0
-        stream = torch.cuda.current_stream(self.device).cuda_stream
-        for m, L in zip(mels, lay.n_mel):
-            m = m.reshape(MEL, -1).to(device=self.device, dtype=torch.float32).contiguous()
-            cu = torch.tensor([0, L], dtype=torch.int32, device=self.device)
-            call("fcv_pack_rows", m.data_ptr(), 0, 0, int(m.shape[1]), cu.data_ptr(), 1, L,
-                 rows[off:].data_ptr(), 0, stream)
-            off += L
+        """(80, L_i) request mels -> packed (sum L_i, 80) rows: the mels side by side
+        as one (80, sum L_i) matrix, transposed by a single ``fcv_pack_rows`` call
+        whose row offsets [0, sum L_i] sit at the end of the layout block."""
+        total = lay.rows[0]
+        rows = torch.empty(max(total, 1), MEL, dtype=torch.float32, device=self.device)
+        if total == 0:
+            return rows
+        flat = [m.reshape(MEL, -1).to(device=self.device, dtype=torch.float32) for m in mels]
+        wide = flat[0].contiguous() if len(flat) == 1 else torch.cat(flat, 1)
+        cu = lay.block[HIFT_LAYOUT_ARRAYS * (len(lay.n_mel) + 1):]
+        call("fcv_pack_rows", wide.data_ptr(), 0, 0, total, cu.data_ptr(), 1, total, rows.data_ptr(), 0,
+             torch.cuda.current_stream(self.device).cuda_stream)
         return rows
 
     def inference_batched(self, mels: Sequence[torch.Tensor], finalize: bool | Sequence[bool] = True,

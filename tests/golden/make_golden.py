@@ -1,9 +1,10 @@
 """Generate the golden vectors under ``tests/golden/`` from the reference itself.
 
-Run in a container where the reference project is present (read-only) at
-``$FCV_REFERENCE_ROOT`` (default: the path in ``REF`` below)::
+Run in a container where the reference project is present (read-only), with
+``FCV_REFERENCE_ROOT`` naming its root (the directory that holds the
+``faster_cosyvoice`` package)::
 
-    python tests/golden/make_golden.py
+    FCV_REFERENCE_ROOT=<reference root> python tests/golden/make_golden.py
 
 The reference's own code is imported and executed on the CPU in float32:
 
@@ -46,7 +47,12 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("FCV_REFERENCE_ROOT", "/root/reference"))
+if not os.environ.get("FCV_REFERENCE_ROOT"):
+    raise SystemExit("set FCV_REFERENCE_ROOT to the reference project's root (the directory holding "
+                     "the faster_cosyvoice package)")
+REF = Path(os.environ["FCV_REFERENCE_ROOT"])
+if not (REF / "faster_cosyvoice").is_dir():
+    raise SystemExit(f"FCV_REFERENCE_ROOT={REF} holds no faster_cosyvoice package")
 sys.path.insert(0, str(HERE / "_xt_shim"))
 sys.path.insert(0, str(REF))
 

@@ -1,7 +1,8 @@
-"""bench.py's output contract, on the CPU: the reference arm (the oracle port of
-the reference's torch path on the host cores) prints one JSON line with every
-key the contract names; the GPU comparison arm says it is unavailable without a
-GPU; a non-zero rank of the reference arm exits quietly."""
+"""bench.py's output contract, on the CPU: the reference arm (the reference's own
+torch DiT on the host cores, from the offline install in baseline/_ref, or the
+oracle port when that is missing) prints one JSON line with every key the
+contract names, on the default config (5); the GPU comparison arm says it is
+unavailable without a GPU; a non-zero rank of the reference arm exits quietly."""
 
 from __future__ import annotations
 
@@ -39,9 +40,12 @@ def test_reference_arm_prints_the_contract_line():
     assert line["impl"] == "reference"
     assert line["metric"] == "DiT estimator mel-frames/s (per NFE)" and line["unit"] == "mel-frames/s"
     assert line["value"] > 0 and line["steps"] == 1 and line["warmup"] == 3 and line["higher_is_better"] is True
-    assert "workload" in line["config"]
+    assert "workload" in line["config"] and line["config"]["workload"].startswith("config5")
+    assert line["config"]["packed_rows"] == 96000
     cb = line["cpu_baseline"]
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["value"] == line["value"] and cb["sample"]
+    if (ROOT / "baseline" / "_ref" / "faster_cosyvoice").is_dir():
+        assert cb["kind"] == "reference", cb
     assert line["e2e"] == {"value": line["value"], "unit": "mel-frames/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
 
@@ -55,16 +59,17 @@ def test_reference_arm_other_ranks_do_nothing():
 
 @pytest.mark.skipif(__import__("torch").cuda.is_available(), reason="checks the no-GPU answer")
 def test_gpu_comparison_arm_unavailable_without_gpu():
-    r = _run(["--impl", "reference-gpu"])
+    r = _run(["--impl", "reference-gpu", "--config", "2"])
     assert r.returncode == 0, r.stderr[-2000:]
     line = _last_json(r.stdout)
     assert line["impl"] == "reference-gpu" and "unavailable" in line
 
 
 def test_vocoder_reference_arm_prints_a_line():
-    r = _run(["--vocoder", "--impl", "reference", "--steps", "1", "--warmup", "3"])
+    r = _run(["--vocoder", "--config", "2", "--impl", "reference", "--steps", "1", "--warmup", "3"])
     assert r.returncode == 0, r.stderr[-2000:]
     line = _last_json(r.stdout)
     assert line["impl"] == "reference" and line["metric"] == "vocoder mel-frames/s (HiFT decode)"
     assert line["value"] > 0 and line["cpu_baseline"]["value"] == line["value"] and line["cpu_baseline"]["sample"]
     assert line["config"]["finalize"] is True and line["config"]["requests"] == 8
+    assert 1 <= line["config"]["measured_requests"] <= 8 and line["config"]["measured_mel_frames"] > 0

@@ -99,6 +99,32 @@ def test_hift_longer_documents_match_oracle(vocoder):
         assert rel_l2(g.cpu().numpy()[0], ref) <= SPEECH_TOL
 
 
+def test_hift_audio_free_chunk_still_gives_source_and_f0(vocoder):
+    """An 8-frame non-final chunk decodes no audio (all of its frames are
+    look-ahead) but the reference still returns its excitation ``s`` and f0
+    (generator.py:728-740): both must match the oracle, alone and packed with a
+    chunk that has audio."""
+    import torch
+
+    voc, W, noise, _ = vocoder
+    rng = np.random.default_rng(14)
+    short = (1.5 * rng.standard_normal((80, 8)) - 3).astype(np.float32)
+    longer = (1.5 * rng.standard_normal((80, 15)) - 3).astype(np.float32)
+    ref_speech, ref_s, ref_f0 = H.inference(short.T.copy(), W, noise.numpy(), False)
+    assert ref_speech.shape == (0,)
+    speech, s = voc.inference(torch.from_numpy(short)[None].cuda(), finalize=False)
+    assert speech.shape == (1, 0)
+    assert rel_l2(s.cpu().numpy()[0, 0], ref_s) <= SOURCE_TOL
+    lay = voc.layout([8], [False])
+    f0 = torch.full((lay.rows[1],), float("nan"), device="cuda")
+    voc.forward_packed(voc._pack([torch.from_numpy(short).cuda()], lay), lay, f0_out=f0)
+    np.testing.assert_allclose(f0.cpu().numpy(), ref_f0, rtol=F0_TOL, atol=0)
+    both, srcs = voc.inference_batched([torch.from_numpy(short).cuda(), torch.from_numpy(longer).cuda()],
+                                       [False, False], want_source=True)
+    assert both[0].shape == (1, 0)
+    assert torch.equal(srcs[0], s)
+
+
 def test_hift_rejects_short_chunks_and_short_noise(vocoder):
     import torch
 

@@ -27,7 +27,9 @@ def test_layout_rows_per_level():
     # mel, f0, x, source, stft, level0, level1, level2, audio
     assert lay.counts == [[9, 14, 17], [9, 14, 14], [9, 14, 10], [4320, 6720, 6720], [1081, 1681, 1681],
                           [72, 112, 80], [360, 560, 400], [1081, 1681, 1201], [4320, 6720, 4320]]
-    block = lay.block.numpy().reshape(9, 4)
+    block = lay.block.numpy()
+    np.testing.assert_array_equal(block[36:], [0, lay.rows[0]])  # offsets of the one pack call
+    block = block[:36].reshape(9, 4)
     for a in range(9):
         assert block[a, 0] == 0
         np.testing.assert_array_equal(np.diff(block[a]), lay.counts[a])
