@@ -28,6 +28,7 @@ sinusoid is cast back to the input dtype (``modules.py:614``).
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -280,28 +281,110 @@ def input_embed(params, x, cond, mu, spk):
     return (c2 + h).astype(np.float32)
 
 
-def attention_doc(q, k, v, chunk: int | None):
+_POOL = None
+
+
+def _head_pool():
+    """Threads for the per-head attention loop (numpy releases the GIL in its
+    BLAS calls and ufuncs; no processes are forked)."""
+    global _POOL
+    if _POOL is None:
+        from concurrent.futures import ThreadPoolExecutor
+
+        _POOL = ThreadPoolExecutor(max_workers=min(HEADS, os.cpu_count() or 1))
+    return _POOL
+
+
+def attention_doc(q, k, v, chunk: int | None, threaded_heads: bool = True):
     """Per-document multi-head attention with scale 1/8 and the optional
-    chunk-causal mask (``modules.py:349-407``; mask ``mask.py:127-158, 223-229``)."""
+    chunk-causal mask (``modules.py:349-407``; mask ``mask.py:127-158, 223-229``).
+
+    One head per thread (``threaded_heads``; else the heads in turn, for callers
+    that already run documents in parallel), plain 2-D BLAS matmuls on one BLAS thread:
+    s = (q/8) k^T (+ the 0/-inf chunk mask), p = exp(s - rowmax),
+    o = (p v) / rowsum(p).  Scaling q by 1/8 is exact in float32."""
     L = q.shape[0]
-    qh = q.reshape(L, HEADS, DIM_HEAD).transpose(1, 0, 2)
-    kh = k.reshape(L, HEADS, DIM_HEAD).transpose(1, 0, 2)
-    vh = v.reshape(L, HEADS, DIM_HEAD).transpose(1, 0, 2)
-    s = np.einsum("hqd,hkd->hqk", qh, kh, optimize=True) * np.float32(DIM_HEAD ** -0.5)
+    qh = np.ascontiguousarray((q * np.float32(DIM_HEAD ** -0.5)).reshape(L, HEADS, DIM_HEAD).transpose(1, 0, 2),
+                              dtype=np.float32)
+    kt = np.ascontiguousarray(k.reshape(L, HEADS, DIM_HEAD).transpose(1, 2, 0), dtype=np.float32)
+    vh = np.ascontiguousarray(v.reshape(L, HEADS, DIM_HEAD).transpose(1, 0, 2), dtype=np.float32)
+    add = None
     if chunk:
         p = np.arange(L)
-        vis = (p[None, :] // chunk) <= (p[:, None] // chunk)
-        s = np.where(vis[None], s, -np.inf)
-    s = s - s.max(-1, keepdims=True)
-    e = np.exp(s)
-    pr = e / e.sum(-1, keepdims=True)
-    o = np.einsum("hqk,hkd->hqd", pr.astype(np.float32), vh, optimize=True)
-    return o.transpose(1, 0, 2).reshape(L, DIM).astype(np.float32)
+        add = np.where((p[None, :] // chunk) <= (p[:, None] // chunk), np.float32(0), np.float32(-np.inf))
+        add = add.astype(np.float32)
+    out = np.empty((L, HEADS, DIM_HEAD), np.float32)
+
+    def head(h):
+        s = qh[h] @ kt[h]
+        if add is not None:
+            s += add
+        s -= s.max(-1, keepdims=True)
+        np.exp(s, out=s)
+        out[:, h] = (s @ vh[h]) / s.sum(-1, keepdims=True)
+
+    if not threaded_heads:
+        for h in range(HEADS):
+            head(h)
+        return out.reshape(L, DIM)
+    with _blas_threads(1):
+        list(_head_pool().map(head, range(HEADS)))
+    return out.reshape(L, DIM)
+
+
+class _blas_threads:
+    """Limit the BLAS thread pool inside a block (no-op without threadpoolctl)."""
+
+    def __init__(self, n: int):
+        self.n, self.limit = n, None
+
+    def __enter__(self):
+        try:
+            from threadpoolctl import threadpool_limits
+
+            self.limit = threadpool_limits(limits=self.n, user_api="blas")
+        except Exception:
+            self.limit = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.limit is not None:
+            self.limit.restore_original_limits()
 
 
 # ---------------------------------------------------------------------------
 # The estimator
 # ---------------------------------------------------------------------------
+
+def _doc_forward(params, depth, blocks, final, d, doc, chunk, threaded_heads):
+    """One document of :func:`dit_forward_docs` (its modulation rows are row d)."""
+    x, mu, cond, spk = doc
+    fsh, fsc = final
+    L = x.shape[1]
+    h = input_embed(params, x.T.astype(np.float32), cond.T.astype(np.float32),
+                    mu.T.astype(np.float32), np.asarray(spk, np.float32))
+    pos = np.arange(L, dtype=np.int32)
+    for i in range(depth):
+        sh_a, sc_a, g_a, sh_f, sc_f, g_f = (m[d] for m in blocks[i])
+        norm = layer_norm_modulate(h, sh_a, sc_a)
+        wq = np.concatenate([params[block_key(i, f"attn.to_{n}.weight")] for n in "qkv"], 0)
+        bq = np.concatenate([params[block_key(i, f"attn.to_{n}.bias")] for n in "qkv"], 0)
+        qkv = _linear(norm, wq, bq)
+        q = apply_partial_rope(qkv[:, :DIM], pos)
+        k = apply_partial_rope(qkv[:, DIM:2 * DIM], pos)
+        v = qkv[:, 2 * DIM:]
+        o = attention_doc(q, k, v, chunk, threaded_heads)
+        a = _linear(o, params[block_key(i, "attn.to_out.0.weight")],
+                    params[block_key(i, "attn.to_out.0.bias")])
+        h, ffin = gate_residual_layer_norm_modulate(h, g_a, a, sh_f, sc_f)
+        f = _gelu_tanh(_linear(ffin, params[block_key(i, "ff.ff.0.0.weight")],
+                               params[block_key(i, "ff.ff.0.0.bias")]))
+        f = _linear(f, params[block_key(i, "ff.ff.2.weight")], params[block_key(i, "ff.ff.2.bias")])
+        h = (h + g_f * f).astype(np.float32)
+    norm = layer_norm_modulate(h, fsh[d], fsc[d])
+    out = _linear(norm, params["proj_out.weight"], params["proj_out.bias"])
+    return out.T.copy()
+
 
 def dit_forward_docs(params, docs, t, chunk: int | None = None, emulate_bf16_time=False):
     """DiT forward over a list of documents.
@@ -311,36 +394,32 @@ def dit_forward_docs(params, docs, t, chunk: int | None = None, emulate_bf16_tim
     (80, L_i) float32 outputs.  Semantics: ``DiT.forward`` (``dit.py:145-176``)
     restricted to the valid frames of each padded row, which is exactly what
     ``FlashInferDiT._forward_packed`` (``flashinfer_dit.py:447-543``) computes.
+
+    Documents are independent.  Long ones (>= 1024 frames) run one after the
+    other with all BLAS threads and one thread per attention head; the short
+    ones run on parallel threads (longest first) with one BLAS thread each.
+    The arithmetic of each document is the same either way.
     """
     depth = count_blocks(params)
     temb = time_embedding(params, np.asarray(t, np.float32), emulate_bf16_time)
-    blocks, (fsh, fsc) = modulations(params, temb, depth)
-    outs = []
-    for d, (x, mu, cond, spk) in enumerate(docs):
-        L = x.shape[1]
-        h = input_embed(params, x.T.astype(np.float32), cond.T.astype(np.float32),
-                        mu.T.astype(np.float32), np.asarray(spk, np.float32))
-        pos = np.arange(L, dtype=np.int32)
-        for i in range(depth):
-            sh_a, sc_a, g_a, sh_f, sc_f, g_f = (m[d] for m in blocks[i])
-            norm = layer_norm_modulate(h, sh_a, sc_a)
-            wq = np.concatenate([params[block_key(i, f"attn.to_{n}.weight")] for n in "qkv"], 0)
-            bq = np.concatenate([params[block_key(i, f"attn.to_{n}.bias")] for n in "qkv"], 0)
-            qkv = _linear(norm, wq, bq)
-            q = apply_partial_rope(qkv[:, :DIM], pos)
-            k = apply_partial_rope(qkv[:, DIM:2 * DIM], pos)
-            v = qkv[:, 2 * DIM:]
-            o = attention_doc(q, k, v, chunk)
-            a = _linear(o, params[block_key(i, "attn.to_out.0.weight")],
-                        params[block_key(i, "attn.to_out.0.bias")])
-            h, ffin = gate_residual_layer_norm_modulate(h, g_a, a, sh_f, sc_f)
-            f = _gelu_tanh(_linear(ffin, params[block_key(i, "ff.ff.0.0.weight")],
-                                   params[block_key(i, "ff.ff.0.0.bias")]))
-            f = _linear(f, params[block_key(i, "ff.ff.2.weight")], params[block_key(i, "ff.ff.2.bias")])
-            h = (h + g_f * f).astype(np.float32)
-        norm = layer_norm_modulate(h, fsh[d], fsc[d])
-        out = _linear(norm, params["proj_out.weight"], params["proj_out.bias"])
-        outs.append(out.T.copy())
+    blocks, final = modulations(params, temb, depth)
+    outs = [None] * len(docs)
+    short = []
+    for d, doc in enumerate(docs):
+        if doc[0].shape[1] >= 1024 or len(docs) == 1:
+            outs[d] = _doc_forward(params, depth, blocks, final, d, doc, chunk, True)
+        else:
+            short.append(d)
+    if short:
+        from concurrent.futures import ThreadPoolExecutor
+
+        short.sort(key=lambda d: -docs[d][0].shape[1])
+
+        def run(d):
+            outs[d] = _doc_forward(params, depth, blocks, final, d, docs[d], chunk, False)
+
+        with _blas_threads(1), ThreadPoolExecutor(max_workers=min(len(short), os.cpu_count() or 1)) as pool:
+            list(pool.map(run, short))
     return outs
 
 
@@ -381,7 +460,8 @@ def cosine_time_span(num_steps: int = 10, emulate_bf16=False):
 
 
 def solve_euler_docs(params, noise_docs, mu_docs, cond_docs, spks, num_steps=10,
-                     streaming=False, chunk=50, cfg_rate=CFG_RATE, emulate_bf16=False):
+                     streaming=False, chunk=50, cfg_rate=CFG_RATE, emulate_bf16=False,
+                     bf16_sample=False):
     """CFG-doubled Euler solver over documents (``flashinfer_flow.py:16-74``):
     the unconditional half has mu, spks and cond zeroed (``:45-51``), the
     sample is repeated (``:55``), ``d = (1+r) d_c - r d_u`` (``:66-69``),
@@ -390,12 +470,20 @@ def solve_euler_docs(params, noise_docs, mu_docs, cond_docs, spks, num_steps=10,
     ``emulate_bf16=True`` reproduces the semantics of a bf16 solver call: the
     schedule, t and dt are computed in bf16 (the solver works in
     ``speaker_embeddings.dtype``, ``:34-43, 70-73``), the estimator sees
-    bf16-rounded inputs and ``bf16(1000 t)``; the sample itself stays float32."""
+    bf16-rounded inputs and ``bf16(1000 t)``; the sample itself stays float32.
+
+    ``bf16_sample=True`` (with ``emulate_bf16``) also follows the reference
+    solver's own bf16 arithmetic: the sample starts as bf16(noise) and every
+    operation of the CFG combine and the Euler update (``:57-70``) -- the scaled
+    halves, their difference, the step and the sum -- is rounded to bf16, the
+    estimator output being bf16 as well."""
     ts = cosine_time_span(num_steps, emulate_bf16)
     rnd = (lambda v: np.float32(bf16_round(np.asarray(v, np.float32)))) if emulate_bf16 else np.float32
     inp = bf16_round if emulate_bf16 else (lambda a: a)
     R = len(noise_docs)
     xs = [np.asarray(n, np.float32).copy() for n in noise_docs]
+    b16 = bf16_round if (emulate_bf16 and bf16_sample) else (lambda a: a)
+    xs = [b16(x) for x in xs]
     t = ts[0]
     dt = rnd(ts[1] - ts[0])
     for step in range(1, num_steps + 1):
@@ -405,6 +493,11 @@ def solve_euler_docs(params, noise_docs, mu_docs, cond_docs, spks, num_steps=10,
         tt = np.full(2 * R, t, np.float32)
         d = dit_forward_docs(params, docs, tt, chunk if streaming else None, emulate_bf16_time=emulate_bf16)
         for i in range(R):
+            if emulate_bf16 and bf16_sample:
+                a = bf16_round(np.float32(1.0 + cfg_rate) * bf16_round(d[i]))
+                b = bf16_round(np.float32(cfg_rate) * bf16_round(d[R + i]))
+                xs[i] = bf16_round(xs[i] + bf16_round(dt * bf16_round(a - b)))
+                continue
             der = (np.float32(1.0 + cfg_rate) * d[i] - np.float32(cfg_rate) * d[R + i]).astype(np.float32)
             xs[i] = (xs[i] + dt * der).astype(np.float32)
         t = rnd(t + dt)

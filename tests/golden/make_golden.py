@@ -14,7 +14,9 @@ The reference's own code is imported and executed on the CPU in float32:
   (``flashinfer_attention.py:16-33, 82-86``);
 * ``flashinfer_kernels.layer_norm_modulate_torch`` (``flashinfer_kernels.py:288-296``);
 * ``flashinfer_flow.solve_euler_batched`` (``flashinfer_flow.py:16-74``) with
-  ``CausalConditionalCFM`` (``flow_matching.py:196-200``);
+  ``CausalConditionalCFM`` (``flow_matching.py:196-200``): a depth-2 case and the
+  full 22-layer DiT at config-3 lengths (``python tests/golden/make_golden.py ode3``
+  regenerates only the latter);
 * ``modules.TimestepEmbedding`` in bf16 (``modules.py:71-83, 606-616``);
 * ``flashinfer_flow.flow_inference_batched`` / ``flow_inference_batched_streaming``
   (``flashinfer_flow.py:118-281``) on a ``CausalMaskedDiffWithDiT`` built as
@@ -201,6 +203,45 @@ def ode_case():
                         rand_noise_head=decoder.rand_noise[0, :, :8].numpy(), **out)
 
 
+# Four of config 3's request lengths (the median, the longest, the shortest and
+# the lower quartile of bench.request_lengths("3")): prompt ~U[100, 400] plus a
+# generated chunk of 30, 60 or 120 frames.
+ODE3_LENGTHS = [309, 518, 157, 257]
+
+
+@torch.no_grad()
+def ode_config3_case():
+    """The reference's ``solve_euler_batched`` (``flashinfer_flow.py:16-74``) at
+    config-3 document lengths on the full 22-layer DiT (seed 6), streaming
+    chunk-50 mask, 10 steps, CFG 0.7, float32; the noise is the CFM's fixed
+    ``rand_noise`` prefix (``flow_matching.py:199-200``), as the streaming flow
+    uses it (``flashinfer_flow.py:266``)."""
+    model = build_ref_dit(6, 22)
+    cfm = types.SimpleNamespace(sigma_min=1e-6, solver="euler", t_scheduler="cosine",
+                                training_cfg_rate=0.2, inference_cfg_rate=0.7, reg_loss_type="l1")
+    decoder = CausalConditionalCFM(in_channels=240, cfm_params=cfm, n_spks=1, spk_emb_dim=80,
+                                   estimator=model)
+    lengths = ODE3_LENGTHS
+    R, T = len(lengths), max(lengths)
+    rng = np.random.default_rng(41)
+    mu = rng.standard_normal((R, 80, T)).astype(np.float32)
+    cond = rng.standard_normal((R, 80, T)).astype(np.float32)
+    spks = rng.standard_normal((R, 80)).astype(np.float32)
+    mask = np.zeros((R, 1, T), np.float32)
+    for b, L in enumerate(lengths):
+        mask[b, 0, :L] = 1
+        mu[b, :, L:] = 0
+        cond[b, :, L:] = 0
+    noise = decoder.rand_noise[:, :, :T].expand(R, -1, -1).contiguous()
+    y = ref_flow.solve_euler_batched(decoder, noise, torch.from_numpy(mu), torch.from_numpy(mask),
+                                     torch.from_numpy(spks), torch.from_numpy(cond), num_timesteps=10,
+                                     streaming=True)
+    np.savez_compressed(HERE / "ode_config3.npz", mu=mu, cond=cond, spks=spks, mask=mask,
+                        lengths=np.asarray(lengths, np.int64), noise=noise.numpy(),
+                        out_streaming=y.float().numpy(), seed=6, depth=22)
+    return fingerprint(model)
+
+
 def build_ref_flow(dit_seed: int, depth: int):
     """``builders.py:16-45`` (DiT depth reduced), random init.  The DiT draws from
     ``dit_seed``; the CFM constructor then reseeds 0 and draws ``rand_noise``
@@ -345,6 +386,12 @@ def hift_case():
 
 
 def main():
+    if sys.argv[1:] == ["ode3"]:
+        fps = json.loads((HERE / "weights_fingerprint.json").read_text())
+        fps["seed6_depth22"] = ode_config3_case()
+        (HERE / "weights_fingerprint.json").write_text(json.dumps(fps, indent=0, sort_keys=True))
+        print("config-3 ODE golden vectors written to", HERE)
+        return
     if sys.argv[1:] == ["hift"]:
         fps = json.loads((HERE / "weights_fingerprint.json").read_text())
         fps["hift_seed0"] = hift_case()
@@ -376,6 +423,8 @@ def main():
     rownorm_case()
     time_embed_case()
     ode_case()
+    fps["seed6_depth22"] = ode_config3_case()
+    (HERE / "weights_fingerprint.json").write_text(json.dumps(fps, indent=0, sort_keys=True))
     print("golden vectors written to", HERE)
 
 

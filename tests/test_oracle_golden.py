@@ -57,7 +57,7 @@ def test_time_sinusoid_matches_reference_fp32_and_bf16():
 
 @pytest.mark.parametrize("key,seed,depth", [("seed0_depth1", 0, 1), ("seed2_depth2", 2, 2),
                                             ("seed3_depth2", 3, 2), ("seed4_depth2", 4, 2),
-                                            ("seed1_depth22", 1, 22)])
+                                            ("seed1_depth22", 1, 22), ("seed6_depth22", 6, 22)])
 def test_module_tree_reproduces_reference_init(key, seed, depth):
     fp = golden_fingerprints()[key]
     sd = make_model(seed, depth).state_dict()
@@ -101,6 +101,21 @@ def test_ode_matches_reference():
         xs = O.solve_euler_docs(params, noise, mu, cond, list(z["spks"]), 10, streaming=streaming)
         for i, L in enumerate(lengths):
             assert np.abs(xs[i] - z[key][i, :, :L]).max() < 1e-4, (key, i)
+
+
+def test_ode_config3_lengths_matches_reference():
+    """The oracle's CFG Euler solver against the reference's own
+    solve_euler_batched on the full 22-layer DiT at four of config 3's document
+    lengths (157-518 frames), streaming chunk-50 mask, 10 steps, float32."""
+    z = load_golden("ode_config3")
+    params = numpy_params(make_model(int(z["seed"]), int(z["depth"])))
+    lengths = z["lengths"]
+    noise = [z["noise"][i, :, :L] for i, L in enumerate(lengths)]
+    mu = [z["mu"][i, :, :L] for i, L in enumerate(lengths)]
+    cond = [z["cond"][i, :, :L] for i, L in enumerate(lengths)]
+    xs = O.solve_euler_docs(params, noise, mu, cond, list(z["spks"]), 10, streaming=True)
+    for i, L in enumerate(lengths):
+        assert np.abs(xs[i] - z["out_streaming"][i, :, :L]).max() < 1e-4, i
 
 
 def test_flop_model_matches_survey_formula():
