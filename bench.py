@@ -959,6 +959,123 @@ def reference_cpu_arm(args, req_lengths, chunk, seed, cfg, strong):
     print(json.dumps(line), flush=True)
 
 
+def gemm_compare(args, req_lengths, seed, cfg):
+    """One JSON line: per block GEMM shape of the config (M = packed rows; QKV
+    1024 -> 3072 with the RoPE epilogue, out 1024 -> 1024 and FF2 2048 -> 1024
+    with the gated-residual epilogue, FF1 1024 -> 2048 with GELU), the mean time
+    of 22 back-to-back launches in a CUDA graph for this build's tcgen05 GEMM and
+    for cuBLAS through torch ``F.linear`` (bias, bf16 out; the reference's
+    ``flashinfer_dit.py:490-512``, with its separate GELU / residual passes left
+    out, so cuBLAS is timed on less work).  L2 flushed between graph replays."""
+    import torch
+    import torch.nn.functional as F
+
+    from fcv_b200 import _lib, ops
+    from fcv_b200.model import B200DiT
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    torch.manual_seed(seed)
+    model = B200DiT(depth=22).eval().to(device=device, dtype=torch.bfloat16)
+    model.finalize_weights()
+    lengths = list(req_lengths) + list(req_lengths)
+    layout = model.prepare_layout(lengths, max(lengths), False, device)
+    N = sum(lengths)
+    d = model._derived
+    A = torch.randn(N, 2048, device=device, dtype=torch.bfloat16)
+    H = torch.zeros(N, 1024, device=device)
+    O3 = torch.empty(N, 3072, device=device, dtype=torch.bfloat16)
+    O2 = torch.empty(N, 2048, device=device, dtype=torch.bfloat16)
+    O1 = torch.empty(N, 1024, device=device, dtype=torch.bfloat16)
+    gate = torch.ones(len(lengths), 4096, device=device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    b16 = {k: d[k].to(torch.bfloat16) for k in ("qkv_b", "o_b", "ff1_b", "ff2_b")}  # cuBLAS bias in bf16
+    shapes = {
+        "qkv": (1024, 3072, lambda i: ops.linear(A[:, :1024], d["qkv_w"][i], d["qkv_b"][i], epilogue=_lib.EPI_BIAS_ROPE_QKV,
+                                                  out=O3, aux=layout.positions, rope_cos=d["rope_cos"],
+                                                  rope_sin=d["rope_sin"]),
+                lambda i: torch.addmm(b16["qkv_b"][i], A[:, :1024], d["qkv_w"][i].t(), out=O3)),
+        "out": (1024, 1024, lambda i: ops.linear(A[:, :1024], d["o_w"][i], d["o_b"][i], epilogue=_lib.EPI_BIAS_GATE_RES,
+                                                  out=H, aux=layout.document_ids, gate=gate, gate_stride=4096),
+                lambda i: torch.addmm(b16["o_b"][i], A[:, :1024], d["o_w"][i].t(), out=O1)),
+        "ff1": (1024, 2048, lambda i: ops.linear(A[:, :1024], d["ff1_w"][i], d["ff1_b"][i], epilogue=_lib.EPI_BIAS_GELU,
+                                                  out=O2),
+                lambda i: torch.addmm(b16["ff1_b"][i], A[:, :1024], d["ff1_w"][i].t(), out=O2)),
+        "ff2": (2048, 1024, lambda i: ops.linear(A, d["ff2_w"][i], d["ff2_b"][i], epilogue=_lib.EPI_BIAS_GATE_RES,
+                                                  out=H, aux=layout.document_ids, gate=gate, gate_stride=4096),
+                lambda i: torch.addmm(b16["ff2_b"][i], A, d["ff2_w"][i].t(), out=O1)),
+    }
+
+    def time_graph(fn, reps):
+        fn()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        g.replay()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            tot += e0.elapsed_time(e1)
+        return tot / reps
+
+    res = {}
+    with ClockSampler(0) as clocks:
+        for name, (K, Nout, ours, cublas) in shapes.items():
+            flops = 2.0 * N * K * Nout
+            row = {"M": N, "K": K, "N": Nout}
+            for impl, fn in (("b200", ours), ("cublas", cublas)):
+                ms = time_graph(lambda: [fn(i) for i in range(22)], max(3, args.steps)) / 22
+                row[impl] = {"ms": ms, "tflops": flops / (ms / 1000.0) / 1e12}
+            row["speedup"] = row["cublas"]["ms"] / row["b200"]["ms"]
+            res[name] = row
+    print(json.dumps({"metric": "block GEMM TFLOP/s, this build vs cuBLAS (F.linear), per shape",
+                      "config": cfg, "results": res, "clocks": clocks.summary(),
+                      "note": "ours includes its fused epilogue (RoPE / gated residual into fp32 h / GELU); "
+                              "cuBLAS computes bias + bf16 output only"}), flush=True)
+
+
+def ncu_case(req_lengths, chunk, seed):
+    """One pass of every kernel of the path on a config's inputs, for ncu: the
+    packed layout from the device mask (fcv_mask_lengths, fcv_pack_layout), one
+    eager estimator call (embed gather, convolutions, AdaLN, the 22 blocks,
+    proj_out, unpack and padding zeroing) and one fused CFG + Euler step on its
+    output (fcv_cfg_euler).  Prints one line naming the sizes."""
+    import torch
+
+    from fcv_b200 import _lib
+    from fcv_b200.model import B200DiT
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    torch.manual_seed(seed)
+    model = B200DiT(depth=22).eval().to(device=device, dtype=torch.bfloat16)
+    model.finalize_weights()
+    lengths, T, _, dev = make_batch(req_lengths, seed, device, torch.bfloat16)
+    layout = model.layout_from_mask(dev["mask"], chunk > 0)
+    out = torch.empty(len(lengths), 80, T, dtype=torch.float32, device=device)
+    model.forward_layout(layout, dev["x"], dev["mu"], dev["t"], dev["spks"], dev["cond"], out=out)
+    R = len(lengths) // 2
+    x = torch.randn(R, 80, T, device=device)
+    x_next = torch.empty(2 * R, 80, T, dtype=torch.bfloat16, device=device)
+    _lib.call("fcv_cfg_euler", x.data_ptr(), out.data_ptr(), _lib.DTYPE_F32, R, T, 0.1, 0.7, x_next.data_ptr(),
+              _lib.DTYPE_BF16, torch.cuda.current_stream(device).cuda_stream)
+    torch.cuda.synchronize()
+    from fcv_b200 import ops
+
+    err = ops.device_error(device)
+    print(json.dumps({"ncu_case": True, "rows": sum(lengths), "sequences": len(lengths), "T": T, "chunk": chunk,
+                      "device_error": err}), flush=True)
+    if err:
+        raise SystemExit(f"device error word {err}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -987,6 +1104,12 @@ def main():
                     help="time the HiFT vocoder over --config 2 (offline) or 3 (non-final chunks) request mels")
     ap.add_argument("--requests", type=int, default=0,
                     help="use only the first R requests of the config (small cases for profiling)")
+    ap.add_argument("--gemm-compare", action="store_true",
+                    help="the four block GEMM shapes of the config (M = its packed rows): this build's tcgen05 "
+                         "GEMM against cuBLAS (torch F.linear with bias, bf16), CUDA events, L2 flushed")
+    ap.add_argument("--ncu-case", action="store_true",
+                    help="no timing: one layout from a device mask, one eager estimator call and one CFG + Euler "
+                         "step on the config's inputs, each kernel launched once (a target for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1037,6 +1160,16 @@ def main():
         if rank != 0:
             return
         reference_cpu_arm(args, req_lengths, chunk, seed, cfg, strong)
+        return
+
+    if args.ncu_case:
+        if rank == 0:
+            ncu_case(req_lengths, chunk, seed)
+        return
+
+    if args.gemm_compare:
+        if rank == 0:
+            gemm_compare(args, req_lengths, seed, cfg)
         return
 
     if args.impl == "reference-gpu":
@@ -1236,7 +1369,7 @@ def main():
             "launches_per_step": gemm_launches, "traffic": tr.get("gemm_bytes_per_launch"),
             "timing": "22 x 4 block GEMMs of this workload in one CUDA graph, CUDA events around the graph, "
                       "L2 flushed between replays; average per launch"}
-    attn = {"kernel": "attn_tc_kernel (tcgen05; ragged chunk-masked attention)", "bound": "tensor",
+    attn = {"kernel": "attn_fa_kernel (tcgen05; ragged chunk-masked attention)", "bound": "tensor",
             "unit": "TFLOP/s", "achieved": attn_tf, "peak": burst, "frac": attn_tf / burst if attn_tf else None,
             "peak_kind": "burst", "flops_per_launch": attn_flops_step / 22, "avg_launch_ms": attn_graph_ms / 22,
             "launches_per_step": 22, "traffic": tr.get("attention_bytes_per_launch"),

@@ -10,7 +10,7 @@
 // document's result depends only on its own rows (no split-KV), so outputs
 // are invariant to batch composition.
 //
-// Work list: (128-row query tile, head) items; tiles come from the host as
+// Work list: (256-row query block, head) items; blocks come from the host as
 // (doc, q0) pairs ordered by cost, most expensive first.
 #pragma once
 
@@ -19,14 +19,7 @@
 namespace fcv {
 
 constexpr int kQkvStride = 3072;
-constexpr int kAttnQTile = 128;
-
-// Last visible key (exclusive) for the query rows [q0, q0+rows) of a document of length L.
-__device__ __forceinline__ int kv_limit(int q0, int rows, int L, int chunk) {
-  const int q_last = min(q0 + rows - 1, L - 1);
-  if (chunk <= 0) return L;
-  return min(L, (q_last / chunk + 1) * chunk);
-}
+constexpr int kAttnQTile = 256;  // query rows of one work-list entry
 
 // Where a document's queries and keys live.  Queries (and outputs) are rows
 // [cu[d], cu[d+1]) of the packed Q buffer.  A document may continue a cached
@@ -41,88 +34,68 @@ struct AttnSrc {
 };
 
 // ------------------------------------------------------------------ bf16 (tcgen05)
-// Persistent: each CTA walks work items (128-row query tile, head) c, c+grid, ...
-// (tiles arrive most expensive first).  6 warps per CTA, 2 CTAs per SM:
-//   warp 0   TMA: Q of each item into one of two buffers, K/V tiles of 64 keys
-//            into a 4-stage ring
-//   warp 1   owns TMEM (S at columns 0..63, P at 64..95, two O buffers of 80
-//            columns at 96 and 176) and issues tcgen05.mma: S_g = Q K_g^T, then
-//            O += P_g [V_g | 1] with P_g read from TMEM
-//   warps 2-5 softmax: TMEM lane quarter = warp % 4, one query row per lane and
-//            all 64 keys of a tile per thread, so row maxima stay in registers.
-//            A 32-key half that no row of the warp can see (past the document
-//            or the chunk limit) is neither loaded nor exponentiated: its P is 0.
-// The softmax row sum comes from the tensor core: V is extended by a constant
-// shared block whose first column is 1 (reached through the descriptor's
-// leading byte offset), so O column 64 holds sum_k P[q,k] in the same bf16 P
-// that multiplies V.  Exponentials use a per-row reference max that moves only
-// when a tile max exceeds it by more than 8 (log2 units); O (with its sum
-// column) in TMEM is rescaled only then.  S_{g+1} -- possibly the next item's
-// first tile -- is issued as soon as S_g has been read, and the next item's Q is
-// loaded while the current item finishes, so items overlap.
-// Barrier invariant: every mbarrier is waited on with a parity that its
-// producer cannot have advanced past by two phases (per-buffer barriers for Q
-// and O; P is written only after the previous P.V is done), so parity waits
-// never alias.  P lives in TMEM, so no shared-memory round trip per tile.
-constexpr int kTcKv = 64;
-constexpr int kTcSmemQ = 128 * 128;      // 16 KB per Q buffer
-constexpr int kTcSmemKV = kTcKv * 128;   // 8 KB per K or V tile
-constexpr int kTcKvStages = 4;
-constexpr int kTcOffK = 2 * kTcSmemQ;
-constexpr int kTcOffV = kTcOffK + kTcKvStages * kTcSmemKV;
-constexpr int kTcOffOnes = kTcOffV + kTcKvStages * kTcSmemKV;  // 64 x 64 bf16, column 0 = 1
-// TMEM columns: S [0, 64), P [64, 96) (bf16 pairs), O buffers [96, 176) and [176, 256)
-constexpr int kTcColP = 64;
-constexpr int kTcColO = 96;
-constexpr int kTcOffBar = kTcOffOnes + kTcSmemKV;
-// mbarrier slots (8 bytes each), derived from the stage count
-constexpr int kBarQFull = 0;
-constexpr int kBarQEmpty = kBarQFull + 2;
-constexpr int kBarKvFull = kBarQEmpty + 2;
-constexpr int kBarKvEmpty = kBarKvFull + kTcKvStages;
-constexpr int kBarSFull = kBarKvEmpty + kTcKvStages;
-constexpr int kBarSEmpty = kBarSFull + 1;
-constexpr int kBarPFull = kBarSEmpty + 1;
-constexpr int kBarODone = kBarPFull + 1;
-constexpr int kBarOEmpty = kBarODone + 1;
-constexpr int kBarOFinal = kBarOEmpty + 2;  // [2] last P.V of an item done, per O buffer
-constexpr int kBarDrain = kBarOFinal + 2;
-constexpr int kBarCount = kBarDrain + 1;
-constexpr int kTcBarBytes = 256;
-static_assert(kBarCount * 8 + 8 <= kTcBarBytes, "attention barrier area too small");
-constexpr int kTcSmemBytes = 1024 + kTcOffBar + kTcBarBytes;
-constexpr int kTcOCols = 80;  // 64 output columns + the row sum + 15 zero columns
-constexpr float kRescaleThreshold = 8.0f;
+// Work list: (doc, q0) entries of up to kAttnQTile = 256 query rows, most
+// expensive first; an item is an entry and one head.  Its rows form two
+// 128-row query tiles (TMEM lanes) that share every K/V tile.
+constexpr int kFaRows = 128;   // rows of one query tile
+constexpr int kFaKv = 128;     // keys of one K/V tile (S tiles are 128 x 128: N = 128 MMAs)
+constexpr int kFaStages = 3;   // K/V ring depth
+constexpr int kFaSmemQ = 2 * kFaRows * 128;   // both query tiles of an item, 32 KB
+constexpr int kFaSmemKV = kFaKv * 128;        // one K or V tile, 16 KB
+constexpr int kFaOffK = 2 * kFaSmemQ;         // Q of two items in flight
+constexpr int kFaOffV = kFaOffK + kFaStages * kFaSmemKV;
+constexpr int kFaOffBar = kFaOffV + kFaStages * kFaSmemKV;
+// mbarriers, per query tile t where indexed [2]
+constexpr int kFbQFull = 0, kFbQEmpty = 2, kFbKvFull = 4, kFbKvEmpty = kFbKvFull + kFaStages;
+constexpr int kFbSFull = kFbKvEmpty + kFaStages, kFbSEmpty = kFbSFull + 2, kFbPFull = kFbSEmpty + 2;
+constexpr int kFbODone = kFbPFull + 2, kFbOFinal = kFbODone + 2, kFbOEmpty = kFbOFinal + 2;
+constexpr int kFaRing = 4;  // slots of the work-item ring
+constexpr int kFbInfoFull = kFbOEmpty + 2, kFbInfoEmpty = kFbInfoFull + kFaRing;
+constexpr int kFbDrain = kFbInfoEmpty + kFaRing, kFbCount = kFbDrain + 1;
+constexpr int kFaBarBytes = 512;  // barriers, the TMEM slot and abort flag, then the item ring
+constexpr int kFaRingOff = 256;  // byte offset of the item ring inside the barrier area
+static_assert(kFbCount * 8 + 8 <= kFaRingOff, "attention barrier area too small");
+constexpr int kFaSmemBytes = 1024 + kFaOffBar + kFaBarBytes;
+// TMEM: all 512 columns (one CTA per SM).  S_t (fp32, 128 columns) at 128 t,
+// P_t (bf16 pairs, 64 columns) at 256 + 64 t, O_t (fp32, 64 columns) at 384 + 64 t.
+constexpr int kFaColS = 0, kFaColP = 256, kFaColO = 384;
+// warps 0-3 softmax of tile 0, 4-7 of tile 1; warpgroup 8-11: warp 8 TMA, warp 9 MMA
+constexpr int kFaThreads = 384;
+// Register budgets (setmaxnreg, per warpgroup): launched at 168 per thread
+// (384 x 168 = 64,512 of the 65,536), the producer warpgroup gives back down to
+// 88 and the softmax warpgroups grow to 208: 4 x 32 x 88 + 8 x 32 x 208 = 64,512.
+constexpr int kFaRegsLaunch = 168, kFaRegsProducer = 88, kFaRegsSoftmax = 208;
+static_assert(4 * 32 * kFaRegsProducer + 8 * 32 * kFaRegsSoftmax <= kFaThreads * kFaRegsLaunch,
+              "register split exceeds the launch allocation");
+constexpr int kFaSoftmaxWarps = 4;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Exponentials of pairs p with p % 8 < kFaPolyPairs run as a polynomial on the FMA
+// pipe, the rest on the special-function unit (whose 16 results per clock per SM
+// would otherwise bound the kernel at head dim 64).
+#ifndef FCV_FA_POLY_PAIRS
+#define FCV_FA_POLY_PAIRS 3
+#endif
+constexpr int kFaPolyPairs = FCV_FA_POLY_PAIRS;
 
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-// 32 TMEM lanes x 32 consecutive columns <- 32 registers per thread.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
-      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
-      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
-      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-
-// One work item: query rows [q0, q0 + 128) of a document (local indices), one
-// head.  base / L: the document's query rows; pos0: absolute position of local
-// row 0; kvb / Lkv: its first key row and key count (pos0 + L).
-struct AttnItem {
-  int base, L, q0, head, n_kv, pos0, kvb, Lkv;
+struct FaItem {
+  int base, L, q0, head, pos0, kvb, Lkv;
+  int n0, n1, nkv;  // key tiles of query tile 0, of tile 1 (0: no tile 1), of the item
 };
+// What the MMA and softmax roles need of an item, published by the TMA thread
+// through a ring in shared memory (n0 == 0 marks the end of the CTA's items).
+struct FaSlot {
+  int base, L, q0, head, pos0, Lkv, n0, n1;
+};
+static_assert(kFaRingOff + kFaRing * sizeof(FaSlot) <= kFaBarBytes, "item ring does not fit");
 
-// Item `it` from its work-list entry tl (already loaded).
-__device__ __forceinline__ AttnItem attn_item_at(const AttnSrc& src, int2 tl, int chunk, int it) {
-  AttnItem a;
+// Key tiles visible to query rows ending at absolute position q_last.
+__device__ __forceinline__ int fa_key_tiles(int q_last, int Lkv, int chunk) {
+  const int lim = chunk > 0 ? min(Lkv, (q_last / chunk + 1) * chunk) : Lkv;
+  return (lim + kFaKv - 1) / kFaKv;
+}
+
+__device__ __forceinline__ FaItem fa_item_at(const AttnSrc& src, int2 tl, int chunk, int it) {
+  FaItem a;
   a.head = it & 15;
   a.q0 = tl.y;
   a.base = src.cu[tl.x];
@@ -130,35 +103,30 @@ __device__ __forceinline__ AttnItem attn_item_at(const AttnSrc& src, int2 tl, in
   a.pos0 = src.pos0 ? __ldg(src.pos0 + tl.x) : 0;
   a.kvb = src.kv_base ? __ldg(src.kv_base + tl.x) : a.base;
   a.Lkv = a.pos0 + a.L;
-  // the tile's last query row in absolute positions bounds its visible keys
-  const int q_last = a.pos0 + min(a.q0 + kAttnQTile - 1, a.L - 1);
-  const int lim = chunk > 0 ? min(a.Lkv, (q_last / chunk + 1) * chunk) : a.Lkv;
-  a.n_kv = (lim + kTcKv - 1) / kTcKv;
+  a.n0 = fa_key_tiles(a.pos0 + min(a.q0 + kFaRows - 1, a.L - 1), a.Lkv, chunk);
+  a.n1 = a.q0 + kFaRows < a.L ? fa_key_tiles(a.pos0 + min(a.q0 + 2 * kFaRows - 1, a.L - 1), a.Lkv, chunk) : 0;
+  a.nkv = max(a.n0, a.n1);
   return a;
 }
 
-__device__ __forceinline__ AttnItem attn_item(const AttnSrc& src, const int2* tiles, int chunk, int it) {
-  return attn_item_at(src, tiles[it >> 4], chunk, it);
-}
-
 // A CTA's items with the descriptor lookups run ahead: while item `it` is
-// processed, the item after it is already resolved (its cu loads in flight)
-// and the work-list entry of the one after that is loading, so no role waits
-// on a dependent global load at an item boundary.  Items come either round
-// robin (positions first, first + stride, ... of the work list) or from a
-// host-built schedule: positions [beg, end) of a per-CTA item list.
-struct ItemFeed {
-  AttnSrc cu;
+// processed, the item after it is already resolved and the work-list entry of
+// the one after that is loading, so no role waits on a dependent global load at
+// an item boundary.  Items come round robin (first, first + stride, ... of the
+// work list) or from a host-built schedule: positions [beg, end) of a per-CTA
+// item list.
+struct FaFeed {
+  AttnSrc src;
   const int2* tiles;
   const int32_t* list;  // schedule items, or null for round robin
   int chunk, end, stride, pos, it, it1, it2;
-  AttnItem cur, nxt;
+  FaItem cur, nxt;
   int2 tl2;
   __device__ __forceinline__ int item_at(int p) const { return list ? __ldg(list + p) : p; }
   // Round robin when sched is null; else sched = [offsets (gridDim + 1) | items].
-  __device__ __forceinline__ bool init(const AttnSrc& cu_, const int2* tiles_, int chunk_, int n_items,
+  __device__ __forceinline__ bool init(const AttnSrc& src_, const int2* tiles_, int chunk_, int n_items,
                                        const int32_t* sched) {
-    cu = cu_;
+    src = src_;
     tiles = tiles_;
     chunk = chunk_;
     if (sched) {
@@ -174,10 +142,10 @@ struct ItemFeed {
     }
     if (pos >= end) return false;
     it = item_at(pos);
-    cur = attn_item(cu, tiles, chunk, it);
+    cur = fa_item_at(src, tiles[it >> 4], chunk, it);
     if (pos + stride < end) {
       it1 = item_at(pos + stride);
-      nxt = attn_item(cu, tiles, chunk, it1);
+      nxt = fa_item_at(src, tiles[it1 >> 4], chunk, it1);
     }
     if (pos + 2 * stride < end) {
       it2 = item_at(pos + 2 * stride);
@@ -192,7 +160,7 @@ struct ItemFeed {
     cur = nxt;
     if (pos + stride < end) {
       it1 = it2;
-      nxt = attn_item_at(cu, tl2, chunk, it1);
+      nxt = fa_item_at(src, tl2, chunk, it1);
     }
     if (pos + 2 * stride < end) {
       it2 = item_at(pos + 2 * stride);
@@ -202,71 +170,123 @@ struct ItemFeed {
   }
 };
 
-__device__ __forceinline__ void named_bar_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+// ---- packed float32 pairs (sm_100 f32x2 instructions: one issue slot per pair)
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                     float c1) {
+  asm("{\n\t.reg .b64 a, b, c, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+      "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 a, b, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// 2^x for a pair on the FMA pipe.  Range reduction x = n + f with n = rint(x)
+// (adding 1.5 * 2^23 leaves rint(x) in the low mantissa bits), f in [-1/2, 1/2];
+// 2^f from a cubic with p(0) = 1 whose other coefficients minimise the maximum
+// relative error on [-1/2, 1/2] (a linear program; max 1.0e-4, far below the
+// bf16 rounding of P); 2^n by adding n to the exponent field.  x is clamped at
+// -127: there f = 0 and p = 1 exactly, so the sum of the fields is +0.0 -- the
+// -inf of a masked key gives exactly 0, like ex2 -- and every x >= -127 keeps a
+// non-negative exponent field.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c1 = 0.6932829022407532f, c2 = 0.2422109693288803f, c3 = 0.055009059607982635f;
+  x0 = fmaxf(x0, -127.0f);
+  x1 = fmaxf(x1, -127.0f);
+  float t0, t1, n0, n1, f0, f1, p0, p1;
+  add2(t0, t1, x0, x1, kRound, kRound);
+  add2(n0, n1, t0, t1, -kRound, -kRound);
+  fma2(f0, f1, n0, n1, -1.0f, -1.0f, x0, x1);
+  fma2(p0, p1, c3, c3, f0, f1, c2, c2);
+  fma2(p0, p1, p0, p1, f0, f1, c1, c1);
+  fma2(p0, p1, p0, p1, f0, f1, 1.0f, 1.0f);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
-constexpr int kTcThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax (one per TMEM lane quarter)
-constexpr int kTcSoftmaxWarps = 4;
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
 
-__global__ void __launch_bounds__(kTcThreads, 2)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
+// Persistent, one CTA per SM.  Per item (two query tiles t = 0, 1 of one head):
+//   warp 8   TMA: both Q tiles into one of two buffers, K/V tiles of 128 keys into
+//            a 3-stage ring shared by the two query tiles
+//   warp 9   owns TMEM and issues tcgen05.mma: S_t = Q_t K_j^T (N = 128), then
+//            O_t += P_t V_j with P_t read from TMEM; S of key tile j+1 is issued
+//            before P.V of tile j, so the tensor core works while softmax runs
+//   warps 0-3 / 4-7  softmax of tile 0 / tile 1, one query row per thread (TMEM
+//            lane quarter = warp % 4); the two warpgroups take turns on the tensor
+//            core and together keep the exponential units busy.  Packed f32x2
+//            arithmetic for the scaling and the row sums; part of the
+//            exponentials on the FMA pipe (exp2_poly2).
+// Row maxima move only when a tile exceeds the reference max by more than
+// kRescaleThreshold (log2 units); O in TMEM and the row sum are then rescaled
+// (rare).  An item's O is read after the next item's first P is written (its
+// last P.V has finished by then), and that item's first P.V waits for the read.
+// Barrier invariant: every wait uses a parity its producer cannot have advanced
+// past by two phases.
+__global__ void __launch_bounds__(kFaThreads, 1)
+    attn_fa_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKV,
                    const AttnSrc src, const int2* __restrict__ tiles, int n_tiles,
                    const int32_t* __restrict__ n_tiles_dev, const int32_t* __restrict__ sched, int chunk,
                    int k_col, int v_col, bf16* __restrict__ out) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t s0 = smem_u32(smem);
-  const uint32_t sQ = s0, sK = s0 + kTcOffK, sV = s0 + kTcOffV, sOnes = s0 + kTcOffOnes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcOffBar);
-  uint64_t* q_full = bars + kBarQFull;     // [2]
-  uint64_t* q_empty = bars + kBarQEmpty;   // [2]
-  uint64_t* kv_full = bars + kBarKvFull;   // [kTcKvStages]
-  uint64_t* kv_empty = bars + kBarKvEmpty; // [kTcKvStages]
-  uint64_t* s_full = bars + kBarSFull;
-  uint64_t* s_empty = bars + kBarSEmpty;
-  uint64_t* p_full = bars + kBarPFull;     // P_g written
-  uint64_t* o_done = bars + kBarODone;     // P_g [V_g|1] complete (P free, O updated)
-  uint64_t* o_empty = bars + kBarOEmpty;   // [2] final O of an item read, per O buffer
-  uint64_t* o_final = bars + kBarOFinal;   // [2] final O of an item complete, per O buffer
-  uint64_t* drain = bars + kBarDrain;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBarCount);
+  const uint32_t sQ = s0, sK = s0 + kFaOffK, sV = s0 + kFaOffV;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kFaOffBar);
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kFbCount);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
+  FaSlot* ring = reinterpret_cast<FaSlot*>(smem + kFaOffBar + kFaRingOff);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&q_full[i]), 1);
-      mbar_init(smem_u32(&q_empty[i]), 1);
-      mbar_init(smem_u32(&o_empty[i]), kTcSoftmaxWarps);
-      mbar_init(smem_u32(&o_final[i]), 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(kFbQFull + t), 1);
+      mbar_init(bar(kFbQEmpty + t), 1);
+      mbar_init(bar(kFbSFull + t), 1);
+      mbar_init(bar(kFbSEmpty + t), kFaSoftmaxWarps);
+      mbar_init(bar(kFbPFull + t), kFaSoftmaxWarps);
+      mbar_init(bar(kFbODone + t), 1);
+      mbar_init(bar(kFbOFinal + t), 1);
+      mbar_init(bar(kFbOEmpty + t), kFaSoftmaxWarps);
     }
-    for (int i = 0; i < kTcKvStages; ++i) {
-      mbar_init(smem_u32(&kv_full[i]), 1);
-      mbar_init(smem_u32(&kv_empty[i]), 1);
+    for (int i = 0; i < kFaStages; ++i) {
+      mbar_init(bar(kFbKvFull + i), 1);
+      mbar_init(bar(kFbKvEmpty + i), 1);
     }
-    mbar_init(smem_u32(p_full), kTcSoftmaxWarps);
-    mbar_init(smem_u32(o_done), 1);
-    mbar_init(smem_u32(s_full), 1);
-    mbar_init(smem_u32(s_empty), kTcSoftmaxWarps);
-    mbar_init(smem_u32(drain), 1);
+    for (int i = 0; i < kFaRing; ++i) {
+      mbar_init(bar(kFbInfoFull + i), 1);
+      mbar_init(bar(kFbInfoEmpty + i), 1 + 2 * kFaSoftmaxWarps);  // the MMA thread and every softmax warp
+    }
+    mbar_init(bar(kFbDrain), 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmKV);
   }
-  if (warp >= 2 && threadIdx.x - 64 < 64) {
-    // constant [1 0 ... 0] rows extending V (128-byte swizzle: chunk c of row r at c ^ (r % 8))
-    const int r = threadIdx.x - 64;
-    uint8_t* row = smem + kTcOffOnes + r * 128;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(row + c * 16) = make_uint4(0, 0, 0, 0);
-    *reinterpret_cast<uint4*>(row + ((0 ^ (r & 7)) << 4)) = make_uint4(0x3F80u, 0, 0, 0);  // bf16 1.0 in column 0
-    fence_proxy_async_smem();
-  }
-  if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -278,292 +298,324 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   // work-list length: a launch parameter, or (CUDA-graph buckets) read from the
   // device and clamped to the capacity the launch was sized for
   const int n_items = (n_tiles_dev ? min(max(__ldg(n_tiles_dev), 0), n_tiles) : n_tiles) * 16;
-
-  if (warp == 0) {
-    if (lane == 0) {
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kFaRegsProducer));
+    if (warp == 8 && lane == 0) {
       // ---------------- TMA producer
       int g = 0, i = 0;
       bool ok = true;
-      ItemFeed feed;
-      for (bool have = feed.init(src, tiles, chunk, n_items, sched); have && ok;
-           have = feed.advance(), ++i) {
-        const AttnItem a = feed.cur;
+      FaFeed feed;
+      auto publish = [&](const FaItem& a, bool last) -> bool {
+        const int sl = i % kFaRing;
+        if (!mbar_wait(bar(kFbInfoEmpty + sl), ((i / kFaRing) & 1) ^ 1, 240, abort_flag)) return false;
+        FaSlot& o = ring[sl];
+        o.base = a.base, o.L = a.L, o.q0 = a.q0, o.head = a.head, o.pos0 = a.pos0, o.Lkv = a.Lkv;
+        o.n0 = last ? 0 : a.n0;
+        o.n1 = a.n1;
+        mbar_arrive(bar(kFbInfoFull + sl));
+        return true;
+      };
+      bool have = feed.init(src, tiles, chunk, n_items, sched);
+      for (; have && ok; have = feed.advance(), ++i) {
+        const FaItem a = feed.cur;
         const int qb = i & 1;
-        if (!mbar_wait(smem_u32(&q_empty[qb]), ((i >> 1) & 1) ^ 1, 221, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(smem_u32(&q_full[qb]), kTcSmemQ);
-        tma_load_2d(sQ + qb * kTcSmemQ, &tmQ, smem_u32(&q_full[qb]), a.head * 64, a.base + a.q0);
-        for (int j = 0; j < a.n_kv; ++j, ++g) {
-          const int st = g % kTcKvStages;
-          if (!mbar_wait(smem_u32(&kv_empty[st]), ((g / kTcKvStages) & 1) ^ 1, 222, abort_flag)) { ok = false; break; }
-          const uint32_t fb = smem_u32(&kv_full[st]);
-          mbar_arrive_expect_tx(fb, 2 * kTcSmemKV);
-          tma_load_2d(sK + st * kTcSmemKV, &tmKV, fb, k_col + a.head * 64, a.kvb + j * kTcKv);
-          tma_load_2d(sV + st * kTcSmemKV, &tmKV, fb, v_col + a.head * 64, a.kvb + j * kTcKv);
+        if (!publish(a, false)) { ok = false; break; }
+        if (!mbar_wait(bar(kFbQEmpty + qb), ((i >> 1) & 1) ^ 1, 241, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(bar(kFbQFull + qb), kFaSmemQ);
+        tma_load_2d(sQ + qb * kFaSmemQ, &tmQ, bar(kFbQFull + qb), a.head * 64, a.base + a.q0);
+        tma_load_2d(sQ + qb * kFaSmemQ + kFaRows * 128, &tmQ, bar(kFbQFull + qb), a.head * 64,
+                    a.base + a.q0 + kFaRows);
+        for (int j = 0; j < a.nkv; ++j, ++g) {
+          const int st = g % kFaStages;
+          if (!mbar_wait(bar(kFbKvEmpty + st), ((g / kFaStages) & 1) ^ 1, 242, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(bar(kFbKvFull + st), 2 * kFaSmemKV);
+          tma_load_2d(sK + st * kFaSmemKV, &tmKV, bar(kFbKvFull + st), k_col + a.head * 64, a.kvb + j * kFaKv);
+          tma_load_2d(sV + st * kFaSmemKV, &tmKV, bar(kFbKvFull + st), v_col + a.head * 64, a.kvb + j * kFaKv);
         }
       }
+      if (ok) publish(FaItem{}, true);  // end of the CTA's items
       // wait for our own copies before the CTA may exit (all phases already issued)
-      for (int k = (g > kTcKvStages ? g - kTcKvStages : 0); k < g; ++k)
-        mbar_wait(smem_u32(&kv_full[k % kTcKvStages]), (k / kTcKvStages) & 1, 223, nullptr);
-      for (int k = (i > 2 ? i - 2 : 0); k < i; ++k) mbar_wait(smem_u32(&q_full[k & 1]), (k >> 1) & 1, 224, nullptr);
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer: S of the next tile, then P.V of the current one
-      constexpr uint32_t idesc_s = idesc_bf16_f32(128, kTcKv, false, false);
-      constexpr uint32_t idesc_o = idesc_bf16_f32(128, kTcOCols, false, true);  // [V|1] is MN-major
-      struct Cur {
-        int it, i, j, n_kv;
-      };
-      // the S cursor runs at most one tile ahead of the P.V cursor, and the feed
-      // follows the S cursor's item
-      ItemFeed feed;
-      auto first = [&](Cur& c) -> bool {
-        c.i = 0;
-        c.j = 0;
-        if (!feed.init(src, tiles, chunk, n_items, sched)) return false;
-        c.it = feed.it;
-        c.n_kv = feed.cur.n_kv;
-        return true;
-      };
-      auto next = [&](Cur& c) -> bool {
-        if (++c.j < c.n_kv) return true;
-        if (!feed.advance()) return false;
-        c.it = feed.it;
-        c.i += 1;
-        c.j = 0;
-        c.n_kv = feed.cur.n_kv;
-        return true;
-      };
-      auto issue_s = [&](const Cur& c, int g) -> bool {
-        const int qb = c.i & 1;
-        if (c.j == 0 && !mbar_wait(smem_u32(&q_full[qb]), (c.i >> 1) & 1, 225, abort_flag)) return false;
-        if (!mbar_wait(smem_u32(&kv_full[g % kTcKvStages]), (g / kTcKvStages) & 1, 226, abort_flag)) return false;
-        if (g > 0 && !mbar_wait(smem_u32(s_empty), (g - 1) & 1, 227, abort_flag)) return false;
+      for (int k = (g > kFaStages ? g - kFaStages : 0); k < g; ++k)
+        mbar_wait(bar(kFbKvFull + k % kFaStages), (k / kFaStages) & 1, 243, nullptr);
+      for (int k = (i > 2 ? i - 2 : 0); k < i; ++k) mbar_wait(bar(kFbQFull + (k & 1)), (k >> 1) & 1, 244, nullptr);
+    } else if (warp == 9 && lane == 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, kFaKv, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, 64, false, true);  // V is MN-major
+      // P.V of one key tile waits until S of the next key tile has been issued
+      int sc0 = 0, sc1 = 0;    // S tiles issued per query tile
+      int pvc0 = 0, pvc1 = 0;  // P.V tiles issued per query tile
+      int items1 = 0;          // items having a tile 1 so far (tile 0: every item)
+      bool ok = true, pend = false;
+      // pending P.V: key-tile index g, per tile: issued?, first / last key tile of its item, item index
+      int pv_g = 0, pv_item0 = 0, pv_item1 = 0;
+      bool pv_on0 = false, pv_on1 = false, pv_first = false, pv_last0 = false, pv_last1 = false;
+      auto pv_tile = [&](int t, int& cntr, bool last, int item) -> bool {
+        if (!mbar_wait(bar(kFbPFull + t), cntr & 1, 245, abort_flag)) return false;
+        if (pv_first && !mbar_wait(bar(kFbOEmpty + t), (item & 1) ^ 1, 246, abort_flag)) return false;
         tc_fence_after();
-        const uint64_t dq = sdesc_sw128(sQ + qb * kTcSmemQ);
-        const uint64_t dk = sdesc_sw128(sK + (g % kTcKvStages) * kTcSmemKV);
+        const uint64_t dv = sdesc_sw128(sV + (pv_g % kFaStages) * kFaSmemKV);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) umma_bf16(tmem, dq + 2 * k, dk + 2 * k, idesc_s, k != 0);
-        umma_commit(smem_u32(s_full));
-        if (c.j == c.n_kv - 1) umma_commit(smem_u32(&q_empty[qb]));  // Q free once this S is done
+        for (int k = 0; k < kFaKv / 16; ++k)  // 16 keys per step: P +8 TMEM columns, V +2048 B (16 rows of 128 B)
+          umma_bf16_ts(tmem + kFaColO + 64 * t, tmem + kFaColP + 64 * t + 8 * k, dv + 128 * k, idesc_o,
+                       (!pv_first || k != 0) ? 1u : 0u);
+        umma_commit(bar(kFbODone + t));
+        if (last) umma_commit(bar(kFbOFinal + t));
+        ++cntr;
         return true;
       };
-      auto issue_pv = [&](const Cur& c, int g) -> bool {
-        const int ob = c.i & 1;
-        if (!mbar_wait(smem_u32(p_full), g & 1, 228, abort_flag)) return false;
-        if (c.j == 0 && !mbar_wait(smem_u32(&o_empty[ob]), ((c.i >> 1) & 1) ^ 1, 229, abort_flag)) return false;
+      auto issue_pv = [&]() -> bool {
+        if (pv_on0 && !pv_tile(0, pvc0, pv_last0, pv_item0)) return false;
+        if (pv_on1 && !pv_tile(1, pvc1, pv_last1, pv_item1)) return false;
+        umma_commit(bar(kFbKvEmpty + pv_g % kFaStages));
+        return true;
+      };
+      auto s_tile = [&](int t, int& cntr, int qb, uint64_t dk) -> bool {
+        if (cntr > 0 && !mbar_wait(bar(kFbSEmpty + t), (cntr - 1) & 1, 249, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t va = sV + (g % kTcKvStages) * kTcSmemKV;
-        const uint64_t dv = sdesc_sw128_lbo(va, sOnes - va);
+        const uint64_t dq = sdesc_sw128(sQ + qb * kFaSmemQ + t * kFaRows * 128);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)  // 16 keys per step: P +8 TMEM columns, V +2048 B (16 rows of 128 B)
-          umma_bf16_ts(tmem + kTcColO + ob * kTcOCols, tmem + kTcColP + 8 * k, dv + 128 * k, idesc_o,
-                       (c.j | k) != 0);
-        umma_commit(smem_u32(o_done));
-        umma_commit(smem_u32(&kv_empty[g % kTcKvStages]));
-        if (c.j == c.n_kv - 1) umma_commit(smem_u32(&o_final[ob]));  // the item's O is complete
+        for (int k = 0; k < 4; ++k) umma_bf16(tmem + kFaColS + 128 * t, dq + 2 * k, dk + 2 * k, idesc_s, k != 0);
+        umma_commit(bar(kFbSFull + t));
+        ++cntr;
         return true;
       };
-      Cur pc, sc;
-      bool have = first(pc);
-      sc = pc;
-      bool ok = !have || issue_s(sc, 0);
       int g = 0;
-      while (have && ok) {
-        sc = pc;
-        const bool more = next(sc);
-        if (more && !issue_s(sc, g + 1)) break;
-        if (!issue_pv(pc, g)) break;
-        pc = sc;
-        have = more;
-        ++g;
+      for (int i = 0; ok; ++i) {
+        const int sl = i % kFaRing;
+        if (!mbar_wait(bar(kFbInfoFull + sl), (i / kFaRing) & 1, 239, abort_flag)) { ok = false; break; }
+        FaSlot a = ring[sl];
+        mbar_arrive(bar(kFbInfoEmpty + sl));
+        if (a.n0 == 0) break;  // no more items
+        const int nkv = max(a.n0, a.n1);
+        const int qb = i & 1;
+        for (int j = 0; j < nkv; ++j, ++g) {
+          const int st = g % kFaStages;
+          if (j == 0 && !mbar_wait(bar(kFbQFull + qb), (i >> 1) & 1, 247, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(bar(kFbKvFull + st), (g / kFaStages) & 1, 248, abort_flag)) { ok = false; break; }
+          const uint64_t dk = sdesc_sw128(sK + st * kFaSmemKV);
+          if (j < a.n0 && !s_tile(0, sc0, qb, dk)) { ok = false; break; }
+          if (j < a.n1 && !s_tile(1, sc1, qb, dk)) { ok = false; break; }
+          if (j == nkv - 1) umma_commit(bar(kFbQEmpty + qb));  // Q free once these S are done
+          if (pend && !issue_pv()) { ok = false; break; }
+          pv_g = g;
+          pv_on0 = j < a.n0;
+          pv_on1 = j < a.n1;
+          pv_first = j == 0;
+          pv_last0 = j == a.n0 - 1;
+          pv_last1 = j == a.n1 - 1;
+          pv_item0 = i;
+          pv_item1 = items1;
+          pend = true;
+        }
+        items1 += a.n1 > 0 ? 1 : 0;
       }
-      umma_commit(smem_u32(drain));
-      mbar_wait(smem_u32(drain), 0, 230, nullptr);
+      if (ok && pend) issue_pv();
+      umma_commit(bar(kFbDrain));
+      mbar_wait(bar(kFbDrain), 0, 250, nullptr);
     }
   } else {
-    // ---------------- softmax warps 2..5: TMEM lane quarter qd = warp % 4, one query row per lane
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kFaRegsSoftmax));
+    // ---------------- softmax of query tile t: one row per thread
+    const int t = warp >> 2;
     const int qd = warp & 3;
     const int r = qd * 32 + lane;  // row within the tile = TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(qd * 32) << 16);
+    const uint32_t colS = lane_base + kFaColS + 128 * t, colP = lane_base + kFaColP + 64 * t,
+                   colO = lane_base + kFaColO + 64 * t;
     const float sl2 = 0.125f * kLog2e;  // softmax scale in log2 units
-    int g = 0, i = 0;
+    int cnt = 0, it_t = 0;
     bool ok = true;
-    // An item's output is read from TMEM after the next item's first tile: by
-    // then its last P.V has long finished (o_final), so that wait is off the
-    // critical path.  The pending item's O buffer is not written again before
-    // that read (its next user is two items later and waits for o_empty).
-    bool pend = false;
-    int p_i = 0, p_row = 0;
+    // deferred epilogue of the previous item of this tile
+    bool pend = false, p_row = false;
+    int p_idx = 0;
     long p_out = 0;
+    float p_l = 1.f;
     auto epilogue = [&]() -> bool {
-      if (!mbar_wait(smem_u32(&o_final[p_i & 1]), (p_i >> 1) & 1, 234, abort_flag)) return false;
+      if (!mbar_wait(bar(kFbOFinal + t), p_idx & 1, 251, abort_flag)) return false;
       tc_fence_after();
-      const uint32_t po = lane_base + kTcColO + (p_i & 1) * kTcOCols;
-      // two 32-column halves, then the row sum (column 64); O is released after the last read
-      uint32_t oa[32];
-      const uint32_t lsum = tmem_ld1(po + 64);
-      tmem_ld32(po, oa);
-      tmem_wait_ld();
-      const float l = __uint_as_float(lsum);
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float inv = p_l > 0.f ? 1.f / p_l : 0.f;
       bf16* orow = out + p_out;
-      if (p_row) {
+      // four 16-column pieces, each stored as it arrives; O is released after the last read
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint4 u;
-          u.x = pack_bf16x2(__uint_as_float(oa[8 * c]) * inv, __uint_as_float(oa[8 * c + 1]) * inv);
-          u.y = pack_bf16x2(__uint_as_float(oa[8 * c + 2]) * inv, __uint_as_float(oa[8 * c + 3]) * inv);
-          u.z = pack_bf16x2(__uint_as_float(oa[8 * c + 4]) * inv, __uint_as_float(oa[8 * c + 5]) * inv);
-          u.w = pack_bf16x2(__uint_as_float(oa[8 * c + 6]) * inv, __uint_as_float(oa[8 * c + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + 8 * c) = u;
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[16];
+        tmem_ld16(colO + 16 * c, o);
+        tmem_wait_ld();
+        if (c == 3) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(kFbOEmpty + t));
         }
-      }
-      tmem_ld32(po + 32, oa);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&o_empty[p_i & 1]));
-      if (p_row) {
+        if (p_row) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint4 u;
-          u.x = pack_bf16x2(__uint_as_float(oa[8 * c]) * inv, __uint_as_float(oa[8 * c + 1]) * inv);
-          u.y = pack_bf16x2(__uint_as_float(oa[8 * c + 2]) * inv, __uint_as_float(oa[8 * c + 3]) * inv);
-          u.z = pack_bf16x2(__uint_as_float(oa[8 * c + 4]) * inv, __uint_as_float(oa[8 * c + 5]) * inv);
-          u.w = pack_bf16x2(__uint_as_float(oa[8 * c + 6]) * inv, __uint_as_float(oa[8 * c + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + 32 + 8 * c) = u;
+          for (int h = 0; h < 2; ++h) {
+            uint4 u;
+            u.x = pack_bf16x2(__uint_as_float(o[8 * h + 0]) * inv, __uint_as_float(o[8 * h + 1]) * inv);
+            u.y = pack_bf16x2(__uint_as_float(o[8 * h + 2]) * inv, __uint_as_float(o[8 * h + 3]) * inv);
+            u.z = pack_bf16x2(__uint_as_float(o[8 * h + 4]) * inv, __uint_as_float(o[8 * h + 5]) * inv);
+            u.w = pack_bf16x2(__uint_as_float(o[8 * h + 6]) * inv, __uint_as_float(o[8 * h + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + 16 * c + 8 * h) = u;
+          }
         }
       }
       pend = false;
       return true;
     };
-    ItemFeed feed;
-    for (bool have = feed.init(src, tiles, chunk, n_items, sched); have && ok;
-         have = feed.advance(), ++i) {
-      const AttnItem a = feed.cur;
-      const int qa = a.q0 + r;                                   // local query row
-      const int qabs = a.pos0 + qa;                              // its absolute position
+    for (int i = 0; ok; ++i) {
+      const int sl = i % kFaRing;
+      if (!mbar_wait(bar(kFbInfoFull + sl), (i / kFaRing) & 1, 238, abort_flag)) { ok = false; break; }
+      const FaSlot a = ring[sl];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(kFbInfoEmpty + sl));
+      if (a.n0 == 0) break;  // no more items
+      const int ntile = t == 0 ? a.n0 : a.n1;
+      if (ntile == 0) continue;
+      const int qa = a.q0 + kFaRows * t + r;  // local query row
+      const int qabs = a.pos0 + qa;           // its absolute position
       const int lim = chunk > 0 ? min(a.Lkv, (qabs / chunk + 1) * chunk) : a.Lkv;  // visible keys [0, lim)
-      const int wlim = __reduce_max_sync(0xffffffffu, lim);                    // any row of this warp
-      const uint32_t o_addr = lane_base + kTcColO + (i & 1) * kTcOCols;
+      const bool row_ok = qa < a.L;
+      const bool warp_rows = __any_sync(0xffffffffu, row_ok);  // the warp has a row of the document
+      const int wmax = __reduce_max_sync(0xffffffffu, lim), wmin = __reduce_min_sync(0xffffffffu, lim);
       float m_ref = -INFINITY;
-      for (int j = 0; j < a.n_kv; ++j, ++g) {
-        if (!mbar_wait(smem_u32(s_full), g & 1, 231, abort_flag)) { ok = false; break; }
+      float lsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // four independent pair accumulators of the row sum
+      for (int j = 0; j < ntile; ++j, ++cnt) {
+        if (!mbar_wait(bar(kFbSFull + t), cnt & 1, 252, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const int k0 = j * kTcKv;
-        const bool hi = wlim > k0 + 32;  // warp-uniform: keys k0+32.. visible to some row
-        uint32_t s0[32], s1[32];
-        tmem_ld32(lane_base, s0);
-        if (hi) tmem_ld32(lane_base + 32, s1);
+        const int k0 = j * kFaKv;
+        // 32-key chunks that some row of the warp sees (warp-uniform)
+        const int nch = warp_rows ? min(4, max(0, (wmax - k0 + 31) / 32)) : 0;
+        uint32_t s[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (c < nch) tmem_ld32(colS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c));
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(s_empty));
-        const int nvis = lim - k0;
-        if (nvis < 64) {
+        if (lane == 0) mbar_arrive(bar(kFbSEmpty + t));
+        if (wmin < k0 + kFaKv) {  // a row of the warp stops inside this tile: mask its invisible keys
+          const int nvis = lim - k0;
 #pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (c >= nvis) s0[c] = __float_as_uint(-INFINITY);
-          if (hi) {
+          for (int c = 0; c < 128; ++c)
+            if (c >= nvis) s[c] = __float_as_uint(-INFINITY);
+        }
+        float mt = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < 32; ++c)
-              if (c + 32 >= nvis) s1[c] = __float_as_uint(-INFINITY);
+        for (int c = 0; c < 4; ++c) {
+          if (c < nch) {
+            float m8[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const uint32_t* v = s + 32 * c + 8 * u;
+              m8[u] = fmax3(fmax3(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2])),
+                            fmax3(__uint_as_float(v[3]), __uint_as_float(v[4]), __uint_as_float(v[5])),
+                            fmaxf(__uint_as_float(v[6]), __uint_as_float(v[7])));
+            }
+            mt = fmax3(mt, fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3]));
           }
         }
-        float m4[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          m4[t] = fmax3(fmax3(__uint_as_float(s0[8 * t]), __uint_as_float(s0[8 * t + 1]), __uint_as_float(s0[8 * t + 2])),
-                        fmax3(__uint_as_float(s0[8 * t + 3]), __uint_as_float(s0[8 * t + 4]), __uint_as_float(s0[8 * t + 5])),
-                        fmaxf(__uint_as_float(s0[8 * t + 6]), __uint_as_float(s0[8 * t + 7])));
-        if (hi) {
-#pragma unroll
-          for (int t = 0; t < 4; ++t)
-            m4[t] = fmax3(m4[t],
-                          fmax3(__uint_as_float(s1[8 * t]), __uint_as_float(s1[8 * t + 1]), __uint_as_float(s1[8 * t + 2])),
-                          fmax3(fmax3(__uint_as_float(s1[8 * t + 3]), __uint_as_float(s1[8 * t + 4]),
-                                      __uint_as_float(s1[8 * t + 5])),
-                                __uint_as_float(s1[8 * t + 6]), __uint_as_float(s1[8 * t + 7])));
-        }
-        const float m_tile = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+        const float m_tile = mt * sl2;
         const bool need = m_tile > m_ref + kRescaleThreshold;
         const float m_new = need ? m_tile : m_ref;
+        // O_t must hold P.V of every earlier key tile before it is rescaled, and P_t is
+        // free once P.V of this tile's previous key tile is done: the exponentials
+        // below run first, overlapping that P.V, unless a rescale needs O now (rare)
+        bool o_ready = cnt == 0;
         if (j > 0 && __any_sync(0xffffffffu, need)) {
-          // rescale this row of O and its sum column: wait for P_{g-1} [V|1], then scale
-          if (!mbar_wait(smem_u32(o_done), (g - 1) & 1, 232, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(bar(kFbODone + t), (cnt - 1) & 1, 253, abort_flag)) { ok = false; break; }
           tc_fence_after();
+          o_ready = true;
+          // rescale this row of O and its sum (the max grew by more than the threshold)
           const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;
-          // O columns 0..63 in two pieces, then the sum column (rare path: one buffer)
 #pragma unroll 1
-          for (int piece = 0; piece < 2; ++piece) {
-            uint32_t oa[32];
-            tmem_ld32(o_addr + 32 * piece, oa);
+          for (int piece = 0; piece < 4; ++piece) {
+            uint32_t o[16];
+            tmem_ld16(colO + 16 * piece, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int d = 0; d < 32; ++d) oa[d] = __float_as_uint(__uint_as_float(oa[d]) * alpha);
-            tmem_st32(o_addr + 32 * piece, oa);
+            for (int d = 0; d < 16; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
+            tmem_st16(colO + 16 * piece, o);
           }
-          const uint32_t lsum = tmem_ld1(o_addr + 64);
-          tmem_wait_ld();
-          tmem_st1(o_addr + 64, __float_as_uint(__uint_as_float(lsum) * alpha));
           tmem_wait_st();
+#pragma unroll
+          for (int u = 0; u < 8; ++u) lsum[u] *= alpha;
         }
         m_ref = m_new;
         const float mo = m_ref == -INFINITY ? 0.f : m_ref;
-        uint32_t pw[32];  // P_g of this row: 64 keys as bf16 pairs
+        // P of this row in two halves of 64 keys (bf16 pairs): the first half's
+        // exponentials overlap the previous P.V; it is stored once that P.V has
+        // released P_t, then the second half is computed and stored
 #pragma unroll
-        for (int c = 0; c < 16; ++c)
-          pw[c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(s0[2 * c]), sl2, -mo)),
-                              ex2_approx(fmaf(__uint_as_float(s0[2 * c + 1]), sl2, -mo)));
-        if (hi) {
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pw[32];
 #pragma unroll
-          for (int c = 0; c < 16; ++c)
-            pw[16 + c] = pack_bf16x2(ex2_approx(fmaf(__uint_as_float(s1[2 * c]), sl2, -mo)),
-                                     ex2_approx(fmaf(__uint_as_float(s1[2 * c + 1]), sl2, -mo)));
-        } else {
+          for (int cc = 0; cc < 2; ++cc) {
+            const int c = 2 * half + cc;
+            if (c < nch) {
 #pragma unroll
-          for (int c = 16; c < 32; ++c) pw[c] = 0u;
+              for (int p = 0; p < 16; ++p) {
+                float x0, x1, e0, e1;
+                fma2(x0, x1, __uint_as_float(s[32 * c + 2 * p]), __uint_as_float(s[32 * c + 2 * p + 1]), sl2, sl2,
+                     -mo, -mo);
+                if (p % 8 < kFaPolyPairs) {
+                  exp2_poly2(x0, x1, e0, e1);
+                } else {
+                  e0 = ex2_approx(x0);
+                  e1 = ex2_approx(x1);
+                }
+                add2(lsum[2 * (p & 3)], lsum[2 * (p & 3) + 1], lsum[2 * (p & 3)], lsum[2 * (p & 3) + 1], e0, e1);
+                pw[16 * cc + p] = pack_bf16x2(e0, e1);
+              }
+            } else {
+#pragma unroll
+              for (int p = 0; p < 16; ++p) pw[16 * cc + p] = 0u;
+            }
+          }
+          if (half == 0 && !o_ready) {
+            if (!mbar_wait(bar(kFbODone + t), (cnt - 1) & 1, 254, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+          }
+          tmem_st32(colP + 32 * half, pw);
         }
-        // P_g -> TMEM; its columns were last read by P.V of tile g-1
-        if (g >= 1 && !mbar_wait(smem_u32(o_done), (g - 1) & 1, 233, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        tmem_st32(lane_base + kTcColP, pw);
+        if (!ok) break;
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(p_full));
+        if (lane == 0) mbar_arrive(bar(kFbPFull + t));
         if (pend && !epilogue()) { ok = false; break; }
       }
       if (!ok) break;
       pend = true;
-      p_i = i;
-      p_row = qa < a.L;
+      p_idx = it_t++;
+      p_row = row_ok;
       p_out = (long)(a.base + qa) * 1024 + a.head * 64;
+      p_l = ((lsum[0] + lsum[1]) + (lsum[2] + lsum[3])) + ((lsum[4] + lsum[5]) + (lsum[6] + lsum[7]));
     }
     if (ok && pend) epilogue();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 9) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
 // ------------------------------------------------------------------ fp32 (CUDA cores)
-// One thread per query row (128 per CTA), 32-key tiles in shared memory.
-__global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__ qkv, const AttnSrc src,
-                                                       const float* __restrict__ kv, long kv_rows, long kv_stride,
-                                                       int k_col, int v_col, const int2* __restrict__ tiles,
-                                                       const int32_t* __restrict__ n_tiles_dev, int chunk,
-                                                       float* __restrict__ out) {
+// One thread per query row (256 per CTA: one work-list entry), 32-key tiles in
+// shared memory.
+__global__ void __launch_bounds__(kAttnQTile) attn_f32_kernel(const float* __restrict__ qkv, const AttnSrc src,
+                                                              const float* __restrict__ kv, long kv_rows,
+                                                              long kv_stride, int k_col, int v_col,
+                                                              const int2* __restrict__ tiles,
+                                                              const int32_t* __restrict__ n_tiles_dev, int chunk,
+                                                              float* __restrict__ out) {
   griddep_wait();
   griddep_launch();
   if (n_tiles_dev && (int)blockIdx.x >= __ldg(n_tiles_dev)) return;  // grid sized for the capacity
   __shared__ float sK[32][64];
   __shared__ float sV[32][64];
-  const AttnItem a = attn_item_at(src, tiles[blockIdx.x], chunk, (int)blockIdx.y);
+  const FaItem a = fa_item_at(src, tiles[blockIdx.x], chunk, (int)blockIdx.y);
   const int head = blockIdx.y;
   const int q = a.q0 + threadIdx.x;  // local query row
   const bool valid = q < a.L;
@@ -575,12 +627,12 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const float* __restrict__
     o[d] = 0.f;
   }
   float m = -INFINITY, l = 0.f;
-  const int kv_end = a.n_kv * kTcKv < a.Lkv ? a.n_kv * kTcKv : a.Lkv;
+  const int kv_end = a.nkv * kFaKv < a.Lkv ? a.nkv * kFaKv : a.Lkv;
   const int qabs = a.pos0 + q;
   const int my_end = valid ? (chunk > 0 ? min(a.Lkv, (qabs / chunk + 1) * chunk) : a.Lkv) : 0;
   for (int k0 = 0; k0 < kv_end; k0 += 32) {
     __syncthreads();
-    for (int i = threadIdx.x; i < 32 * 64; i += 128) {
+    for (int i = threadIdx.x; i < 32 * 64; i += blockDim.x) {
       const int r = i >> 6, c = i & 63;
       const int k = k0 + r;
       const long row = (long)a.kvb + k;

@@ -444,28 +444,28 @@ int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, cons
   src.kv_base = cached ? kvs.kv_base : nullptr;
   const int k_col = cached ? 0 : 1024, v_col = cached ? 1024 : 2048;
   if (dtype == FCV_DTYPE_BF16) {
-    // Q tiles of 128 rows from the (N, 3072) [Q|K|V] buffer; K/V tiles of 64 rows from it or the cache
+    // Q tiles of 128 rows from the (N, 3072) [Q|K|V] buffer; K/V tiles of 128 rows from it or the cache
     CUtensorMap tq, tkv;
-    FCV_TRY(make_tmap(&tq, qkv, false, n_rows, 3072, 3072, 64, 128));
+    FCV_TRY(make_tmap(&tq, qkv, false, n_rows, 3072, 3072, 64, kFaRows));
     if (cached)
-      FCV_TRY(make_tmap(&tkv, kvs.kv, false, kvs.rows, 2048, 2048, 64, kTcKv));
+      FCV_TRY(make_tmap(&tkv, kvs.kv, false, kvs.rows, 2048, 2048, 64, kFaKv));
     else
-      FCV_TRY(make_tmap(&tkv, qkv, false, n_rows, 3072, 3072, 64, kTcKv));
+      FCV_TRY(make_tmap(&tkv, qkv, false, n_rows, 3072, 3072, 64, kFaKv));
     static bool attr[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {
-      FCV_CUDA(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes));
+      FCV_CUDA(cudaFuncSetAttribute(attn_fa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFaSmemBytes));
       attr[dev & 63] = true;
     }
     const int items = n_tiles * FCV_HEADS;
-    // persistent, 2 CTAs per SM; a host schedule fixes the CTA count it was built for
-    const int ctas = sched ? sched_ctas : std::min(items, 2 * num_sms());
-    if (sched && (sched_ctas < 1 || sched_ctas > 2 * num_sms()))
+    // persistent, one CTA per SM (all 512 TMEM columns); a host schedule fixes the CTA count it was built for
+    const int ctas = sched ? sched_ctas : std::min(items, num_sms());
+    if (sched && (sched_ctas < 1 || sched_ctas > num_sms()))
       return fail(FCV_EINVAL, "attention schedule built for %d CTAs", sched_ctas);
     // Plain stream order: the work items are dealt to CTAs by index, and CTAs that
     // start early on the SMs freed first by the previous kernel would unbalance it.
-    const int rc = launch_k_opt(false, "attn_tc_kernel", attn_tc_kernel, dim3(ctas), dim3(kTcThreads), kTcSmemBytes,
+    const int rc = launch_k_opt(false, "attn_fa_kernel", attn_fa_kernel, dim3(ctas), dim3(kFaThreads), kFaSmemBytes,
                                 s, tq, tkv, src, t2, n_tiles, n_tiles_dev, sched, chunk, k_col, v_col,
                                 static_cast<bf16*>(out));
     if (rc != FCV_OK) return rc;
@@ -473,7 +473,7 @@ int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, cons
     const float* kv = cached ? static_cast<const float*>(kvs.kv) : static_cast<const float*>(qkv);
     const long kv_stride = cached ? 2048 : 3072;
     const long kv_rows = cached ? kvs.rows : n_rows;
-    FCV_LAUNCH("attn_f32_kernel", attn_f32_kernel, dim3(grid), dim3(128), 0, s, static_cast<const float*>(qkv), src,
+    FCV_LAUNCH("attn_f32_kernel", attn_f32_kernel, dim3(grid), dim3(kAttnQTile), 0, s, static_cast<const float*>(qkv), src,
                kv, kv_rows, kv_stride, k_col, v_col, t2, n_tiles_dev, chunk, static_cast<float*>(out));
   }
   return FCV_OK;
@@ -944,7 +944,7 @@ int fcv_attn_tiles(const int32_t* lengths_host, int B, int chunk, int32_t* tiles
 
 int fcv_attn_ctas(int n_tiles) {
   if (n_tiles < 0) return fail(FCV_EINVAL, "fcv_attn_ctas: negative tile count");
-  return std::max(1, std::min(n_tiles * FCV_HEADS, 2 * num_sms()));
+  return std::max(1, std::min(n_tiles * FCV_HEADS, num_sms()));
 }
 
 int fcv_attn_schedule(const int32_t* lengths_host, int B, int chunk, const int32_t* tiles, int n_tiles, int n_ctas,
@@ -954,16 +954,20 @@ int fcv_attn_schedule(const int32_t* lengths_host, int B, int chunk, const int32
   const long items = (long)n_tiles * FCV_HEADS;
   const long need = n_ctas + 1 + items;
   if (need > cap) return fail(FCV_EINVAL, "fcv_attn_schedule: capacity %d < %ld", cap, need);
-  // item cost: its key tiles plus one for the per-item work (Q load, first S, output)
+  // item cost: the 128 x 128 S and P.V tiles of its (up to two) query tiles plus
+  // one for the per-item work (Q load, output)
   std::vector<std::pair<long, int>> order;  // (cost, item), most expensive first
   order.reserve(items);
+  auto key_tiles = [&](int L, int q_last) {
+    const int kv = chunk > 0 ? std::min(L, (q_last / chunk + 1) * chunk) : L;
+    return (long)((kv + kFaKv - 1) / kFaKv);
+  };
   for (int t = 0; t < n_tiles; ++t) {
     const int d = tiles[2 * t], q0 = tiles[2 * t + 1];
     if (d < 0 || d >= B) return fail(FCV_EINVAL, "fcv_attn_schedule: tile %d names document %d", t, d);
     const int L = lengths_host[d];
-    const int q_last = std::min(q0 + kAttnQTile, L) - 1;
-    const int kv = chunk > 0 ? std::min(L, (q_last / chunk + 1) * chunk) : L;
-    const long cost = (kv + kTcKv - 1) / kTcKv + 1;
+    long cost = 1 + key_tiles(L, std::min(q0 + kFaRows, L) - 1);
+    if (q0 + kFaRows < L) cost += key_tiles(L, std::min(q0 + 2 * kFaRows, L) - 1);
     for (int h = 0; h < FCV_HEADS; ++h) order.push_back({cost, t * FCV_HEADS + h});
   }
   std::stable_sort(order.begin(), order.end(), [](const auto& a, const auto& b) { return a.first > b.first; });

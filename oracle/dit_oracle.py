@@ -461,7 +461,7 @@ def cosine_time_span(num_steps: int = 10, emulate_bf16=False):
 
 def solve_euler_docs(params, noise_docs, mu_docs, cond_docs, spks, num_steps=10,
                      streaming=False, chunk=50, cfg_rate=CFG_RATE, emulate_bf16=False,
-                     bf16_sample=False):
+                     bf16_sample=False, bf16_schedule=None):
     """CFG-doubled Euler solver over documents (``flashinfer_flow.py:16-74``):
     the unconditional half has mu, spks and cond zeroed (``:45-51``), the
     sample is repeated (``:55``), ``d = (1+r) d_c - r d_u`` (``:66-69``),
@@ -472,13 +472,18 @@ def solve_euler_docs(params, noise_docs, mu_docs, cond_docs, spks, num_steps=10,
     ``speaker_embeddings.dtype``, ``:34-43, 70-73``), the estimator sees
     bf16-rounded inputs and ``bf16(1000 t)``; the sample itself stays float32.
 
+    ``bf16_schedule=False`` (with ``emulate_bf16``) keeps the schedule, t and dt
+    in float32 -- a solver call whose speaker rows are float32 -- while the
+    bf16 estimator still sees bf16(t) and bf16(1000 bf16(t)).
+
     ``bf16_sample=True`` (with ``emulate_bf16``) also follows the reference
     solver's own bf16 arithmetic: the sample starts as bf16(noise) and every
     operation of the CFG combine and the Euler update (``:57-70``) -- the scaled
     halves, their difference, the step and the sum -- is rounded to bf16, the
     estimator output being bf16 as well."""
-    ts = cosine_time_span(num_steps, emulate_bf16)
-    rnd = (lambda v: np.float32(bf16_round(np.asarray(v, np.float32)))) if emulate_bf16 else np.float32
+    sched16 = emulate_bf16 if bf16_schedule is None else (emulate_bf16 and bf16_schedule)
+    ts = cosine_time_span(num_steps, sched16)
+    rnd = (lambda v: np.float32(bf16_round(np.asarray(v, np.float32)))) if sched16 else np.float32
     inp = bf16_round if emulate_bf16 else (lambda a: a)
     R = len(noise_docs)
     xs = [np.asarray(n, np.float32).copy() for n in noise_docs]
@@ -490,7 +495,7 @@ def solve_euler_docs(params, noise_docs, mu_docs, cond_docs, spks, num_steps=10,
         docs = [(inp(xs[i]), inp(mu_docs[i]), inp(cond_docs[i]), inp(spks[i])) for i in range(R)]
         docs += [(inp(xs[i]), np.zeros_like(mu_docs[i]), np.zeros_like(cond_docs[i]),
                   np.zeros_like(spks[i])) for i in range(R)]
-        tt = np.full(2 * R, t, np.float32)
+        tt = np.full(2 * R, bf16_round(np.float32(t)) if emulate_bf16 else t, np.float32)
         d = dit_forward_docs(params, docs, tt, chunk if streaming else None, emulate_bf16_time=emulate_bf16)
         for i in range(R):
             if emulate_bf16 and bf16_sample:

@@ -99,8 +99,8 @@ def test_attention_work_list_covers_rows_and_orders_by_cost(lib, chunk):
     seen = set()
     costs = []
     for d, q0 in tiles:
-        rows = min(128, lengths[d] - q0)
-        assert rows > 0
+        rows = min(256, lengths[d] - q0)  # a work-list entry: up to two 128-row query tiles
+        assert rows > 0 and q0 % 256 == 0
         for q in range(q0, q0 + rows):
             assert (d, q) not in seen
             seen.add((d, q))
@@ -165,13 +165,14 @@ def test_graph_bucket_presets_become_row_capacities():
 def test_attention_schedule_assigns_every_item_once_and_balances(lib, chunk):
     """fcv_attn_schedule: a permutation of the 16 * n_tiles items grouped by CTA,
     longest first to the least loaded CTA; its worst CTA carries no more work
-    than round robin's (config-2 lengths, 296 CTAs)."""
+    than round robin's (config-2 lengths, one CTA per SM: 148 on a B200).  The
+    cost of an item is the 128 x 128 tiles of its (up to two) query tiles + 1."""
     rng = np.random.default_rng(1)
     req = [int(v) for v in rng.integers(150, 601, size=8)]
     lengths = req + req + [1, 0, 3000]
     n, tiles = _tiles(lib, lengths, chunk)
     ctas = lib.fcv_attn_ctas(n)
-    assert ctas == min(16 * n, 296) or ctas == min(16 * n, 2 * ctas)
+    assert ctas == min(16 * n, 148)
     cap = ctas + 1 + 16 * n
     buf = (ctypes.c_int32 * cap)()
     lens = (ctypes.c_int32 * len(lengths))(*lengths)
@@ -183,12 +184,15 @@ def test_attention_schedule_assigns_every_item_once_and_balances(lib, chunk):
     assert off[0] == 0 and off[-1] == 16 * n and np.all(np.diff(off) >= 0)
     assert sorted(items.tolist()) == list(range(16 * n))
 
+    def key_tiles(L, q_last):
+        kv = min(L, (q_last // chunk + 1) * chunk) if chunk else L
+        return -(-kv // 128)
+
     def cost(it):
         d, q0 = tiles[it // 16]
         L = lengths[d]
-        q_last = min(q0 + 128, L) - 1
-        kv = min(L, (q_last // chunk + 1) * chunk) if chunk else L
-        return -(-kv // 64) + 1
+        c = 1 + key_tiles(L, min(q0 + 128, L) - 1)
+        return c + (key_tiles(L, min(q0 + 256, L) - 1) if q0 + 128 < L else 0)
 
     lpt = max(sum(cost(i) for i in items[off[c]:off[c + 1]]) for c in range(ctas))
     rr = max(sum(cost(i) for i in range(c, 16 * n, ctas)) for c in range(ctas))
