@@ -10,7 +10,7 @@
 // document's result depends only on its own rows (no split-KV), so outputs
 // are invariant to batch composition.
 //
-// Work list: (256-row query block, head) items; blocks come from the host as
+// Work list: (384-row query block, head) items; blocks come from the host as
 // (doc, q0) pairs ordered by cost, most expensive first.
 #pragma once
 
@@ -19,7 +19,7 @@
 namespace fcv {
 
 constexpr int kQkvStride = 3072;
-constexpr int kAttnQTile = 256;  // query rows of one work-list entry
+constexpr int kAttnQTile = 384;  // query rows of one work-list entry
 
 // Where a document's queries and keys live.  Queries (and outputs) are rows
 // [cu[d], cu[d+1]) of the packed Q buffer.  A document may continue a cached
@@ -34,59 +34,63 @@ struct AttnSrc {
 };
 
 // ------------------------------------------------------------------ bf16 (tcgen05)
-// Work list: (doc, q0) entries of up to kAttnQTile = 256 query rows, most
-// expensive first; an item is an entry and one head.  Its rows form two
+// Work list: (doc, q0) entries of up to kAttnQTile = 384 query rows, most
+// expensive first; an item is an entry and one head.  Its rows form three
 // 128-row query tiles (TMEM lanes) that share every K/V tile.
+constexpr int kFaTiles = 3;    // query tiles per item
 constexpr int kFaRows = 128;   // rows of one query tile
-constexpr int kFaKv = 128;     // keys of one K/V tile (S tiles are 128 x 128: N = 128 MMAs)
-constexpr int kFaStages = 3;   // K/V ring depth
-constexpr int kFaSmemQ = 2 * kFaRows * 128;   // both query tiles of an item, 32 KB
-constexpr int kFaSmemKV = kFaKv * 128;        // one K or V tile, 16 KB
-constexpr int kFaOffK = 2 * kFaSmemQ;         // Q of two items in flight
+constexpr int kFaKv = 64;      // keys of one K/V tile (S tiles are 128 x 64)
+constexpr int kFaStages = 6;   // K/V ring depth (4 to 8 measured within 1 %; 6 best on short chunked documents)
+constexpr int kFaSmemQ = kFaTiles * kFaRows * 128;  // the query tiles of an item, 48 KB
+constexpr int kFaSmemKV = kFaKv * 128;               // one K or V tile, 8 KB
+constexpr int kFaOffK = 2 * kFaSmemQ;                // Q of two items in flight
 constexpr int kFaOffV = kFaOffK + kFaStages * kFaSmemKV;
 constexpr int kFaOffBar = kFaOffV + kFaStages * kFaSmemKV;
-// mbarriers, per query tile t where indexed [2]
+static_assert(kAttnQTile == kFaTiles * kFaRows, "work-list entries are whole items");
+// mbarriers, per query tile t where indexed [kFaTiles]
 constexpr int kFbQFull = 0, kFbQEmpty = 2, kFbKvFull = 4, kFbKvEmpty = kFbKvFull + kFaStages;
-constexpr int kFbSFull = kFbKvEmpty + kFaStages, kFbSEmpty = kFbSFull + 2, kFbPFull = kFbSEmpty + 2;
-constexpr int kFbODone = kFbPFull + 2, kFbOFinal = kFbODone + 2, kFbOEmpty = kFbOFinal + 2;
+constexpr int kFbSFull = kFbKvEmpty + kFaStages, kFbSEmpty = kFbSFull + kFaTiles, kFbPFull = kFbSEmpty + kFaTiles;
+constexpr int kFbODone = kFbPFull + kFaTiles, kFbOFinal = kFbODone + kFaTiles, kFbOEmpty = kFbOFinal + kFaTiles;
 constexpr int kFaRing = 4;  // slots of the work-item ring
-constexpr int kFbInfoFull = kFbOEmpty + 2, kFbInfoEmpty = kFbInfoFull + kFaRing;
-constexpr int kFbDrain = kFbInfoEmpty + kFaRing, kFbCount = kFbDrain + 1;
-constexpr int kFaBarBytes = 512;  // barriers, the TMEM slot and abort flag, then the item ring
-constexpr int kFaRingOff = 256;  // byte offset of the item ring inside the barrier area
-static_assert(kFbCount * 8 + 8 <= kFaRingOff, "attention barrier area too small");
-constexpr int kFaSmemBytes = 1024 + kFaOffBar + kFaBarBytes;
-// TMEM: all 512 columns (one CTA per SM).  S_t (fp32, 128 columns) at 128 t,
-// P_t (bf16 pairs, 64 columns) at 256 + 64 t, O_t (fp32, 64 columns) at 384 + 64 t.
-constexpr int kFaColS = 0, kFaColP = 256, kFaColO = 384;
-// warps 0-3 softmax of tile 0, 4-7 of tile 1; warpgroup 8-11: warp 8 TMA, warp 9 MMA
-constexpr int kFaThreads = 384;
-// Register budgets (setmaxnreg, per warpgroup): launched at 168 per thread
-// (384 x 168 = 64,512 of the 65,536), the producer warpgroup gives back down to
-// 88 and the softmax warpgroups grow to 208: 4 x 32 x 88 + 8 x 32 x 208 = 64,512.
-constexpr int kFaRegsLaunch = 168, kFaRegsProducer = 88, kFaRegsSoftmax = 208;
-static_assert(4 * 32 * kFaRegsProducer + 8 * 32 * kFaRegsSoftmax <= kFaThreads * kFaRegsLaunch,
+constexpr int kFbInfoFull = kFbOEmpty + kFaTiles, kFbInfoEmpty = kFbInfoFull + kFaRing;
+constexpr int kFbDrain = kFbInfoEmpty + kFaRing, kFbCount = kFbDrain + kFaTiles;
+// barrier area: the mbarriers, the TMEM slot and abort flag, then the item ring
+constexpr int kFaRingOff = (kFbCount * 8 + 8 + 15) / 16 * 16;
+// TMEM (one CTA per SM): S_t (fp32, 64 columns) at 64 t, P_t (bf16 pairs, 32
+// columns) at 192 + 32 t, O_t (fp32, 64 columns) at 288 + 64 t; 480 of 512.
+constexpr int kFaColS = 0, kFaColP = kFaTiles * kFaKv, kFaColO = kFaColP + kFaTiles * kFaKv / 2;
+static_assert(kFaColO + 64 * kFaTiles <= 512, "TMEM columns");
+constexpr int kFaSoftmaxWarps = 4;  // per query tile: one per TMEM lane quarter
+// warps 0..11 softmax (query tile = warp / 4); warpgroup 12-15: warp 12 TMA, warp 13 + t
+// issues the MMAs of query tile t
+constexpr int kFaThreads = 32 * (kFaSoftmaxWarps * kFaTiles + 4);
+// Register budgets (setmaxnreg, per warpgroup): launched at 128 per thread
+// (512 x 128 = 65,536), the producer warpgroup gives back down to 96 and the
+// three softmax warpgroups grow to 136: 4 x 32 x 96 + 12 x 32 x 136 = 64,512.
+constexpr int kFaRegsLaunch = 128, kFaRegsProducer = 96, kFaRegsSoftmax = 136;
+static_assert(4 * 32 * kFaRegsProducer + kFaTiles * 4 * 32 * kFaRegsSoftmax <= kFaThreads * kFaRegsLaunch,
               "register split exceeds the launch allocation");
-constexpr int kFaSoftmaxWarps = 4;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // Exponentials of pairs p with p % 8 < kFaPolyPairs run as a polynomial on the FMA
-// pipe, the rest on the special-function unit (whose 16 results per clock per SM
-// would otherwise bound the kernel at head dim 64).
-#ifndef FCV_FA_POLY_PAIRS
-#define FCV_FA_POLY_PAIRS 3
-#endif
-constexpr int kFaPolyPairs = FCV_FA_POLY_PAIRS;
+// pipe, the rest on the special-function unit (16 results per clock per SM, the
+// bound of this kernel at head dim 64).  Measured on a B200 for 32 documents of
+// 3000 rows: 0 of 8 pairs 682 TFLOP/s, 1 727, 2 741, 3 699, 4 671.
+constexpr int kFaPolyPairs = 2;
 
 struct FaItem {
   int base, L, q0, head, pos0, kvb, Lkv;
-  int n0, n1, nkv;  // key tiles of query tile 0, of tile 1 (0: no tile 1), of the item
+  int n[kFaTiles];  // key tiles of each query tile (0: the tile lies past the document)
+  int nkv;          // key tiles of the item
 };
 // What the MMA and softmax roles need of an item, published by the TMA thread
-// through a ring in shared memory (n0 == 0 marks the end of the CTA's items).
+// through a ring in shared memory (n[0] == 0 marks the end of the CTA's items).
 struct FaSlot {
-  int base, L, q0, head, pos0, Lkv, n0, n1;
+  int base, L, q0, head, pos0, Lkv;
+  int n[kFaTiles];
 };
-static_assert(kFaRingOff + kFaRing * sizeof(FaSlot) <= kFaBarBytes, "item ring does not fit");
+constexpr int kFaBarBytes = (kFaRingOff + kFaRing * static_cast<int>(sizeof(FaSlot)) + 127) / 128 * 128;
+constexpr int kFaSmemBytes = 1024 + kFaOffBar + kFaBarBytes;
+static_assert(kFaSmemBytes <= 227 * 1024, "attention shared memory");
 
 // Key tiles visible to query rows ending at absolute position q_last.
 __device__ __forceinline__ int fa_key_tiles(int q_last, int Lkv, int chunk) {
@@ -103,16 +107,20 @@ __device__ __forceinline__ FaItem fa_item_at(const AttnSrc& src, int2 tl, int ch
   a.pos0 = src.pos0 ? __ldg(src.pos0 + tl.x) : 0;
   a.kvb = src.kv_base ? __ldg(src.kv_base + tl.x) : a.base;
   a.Lkv = a.pos0 + a.L;
-  a.n0 = fa_key_tiles(a.pos0 + min(a.q0 + kFaRows - 1, a.L - 1), a.Lkv, chunk);
-  a.n1 = a.q0 + kFaRows < a.L ? fa_key_tiles(a.pos0 + min(a.q0 + 2 * kFaRows - 1, a.L - 1), a.Lkv, chunk) : 0;
-  a.nkv = max(a.n0, a.n1);
+  a.nkv = 0;
+#pragma unroll
+  for (int t = 0; t < kFaTiles; ++t) {
+    const int r0 = a.q0 + kFaRows * t;
+    a.n[t] = r0 < a.L ? fa_key_tiles(a.pos0 + min(r0 + kFaRows - 1, a.L - 1), a.Lkv, chunk) : 0;
+    a.nkv = max(a.nkv, a.n[t]);
+  }
   return a;
 }
 
-// A CTA's items with the descriptor lookups run ahead: while item `it` is
-// processed, the item after it is already resolved and the work-list entry of
-// the one after that is loading, so no role waits on a dependent global load at
-// an item boundary.  Items come round robin (first, first + stride, ... of the
+// A CTA's items with the descriptor lookups run ahead (used by the TMA thread,
+// which publishes each item to the others): while item `it` is processed, the
+// item after it is already resolved and the work-list entry of the one after
+// that is loading.  Items come round robin (first, first + stride, ... of the
 // work list) or from a host-built schedule: positions [beg, end) of a per-CTA
 // item list.
 struct FaFeed {
@@ -227,17 +235,20 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
-// Persistent, one CTA per SM.  Per item (two query tiles t = 0, 1 of one head):
-//   warp 8   TMA: both Q tiles into one of two buffers, K/V tiles of 128 keys into
-//            a 3-stage ring shared by the two query tiles
-//   warp 9   owns TMEM and issues tcgen05.mma: S_t = Q_t K_j^T (N = 128), then
+// Persistent, one CTA per SM.  Per item (three query tiles t of one head):
+//   warp 12  TMA: the item's query tiles into one of two buffers, K/V tiles of 64
+//            keys into a 4-stage ring shared by the query tiles; it also resolves
+//            each item once and publishes it to the other roles (item ring)
+//   warp 13+t  issues query tile t's tcgen05.mma: S_t = Q_t K_j^T, then
 //            O_t += P_t V_j with P_t read from TMEM; S of key tile j+1 is issued
-//            before P.V of tile j, so the tensor core works while softmax runs
-//   warps 0-3 / 4-7  softmax of tile 0 / tile 1, one query row per thread (TMEM
-//            lane quarter = warp % 4); the two warpgroups take turns on the tensor
-//            core and together keep the exponential units busy.  Packed f32x2
-//            arithmetic for the scaling and the row sums; part of the
-//            exponentials on the FMA pipe (exp2_poly2).
+//            before P.V of tile j, so the tensor core works while softmax runs.
+//            One issuer per query tile keeps the tiles independent (a tile's slow
+//            softmax never holds back another tile's MMAs); they share only the
+//            K/V ring, whose stages return when every tile is done with them.
+//            Warp 13 also owns TMEM.
+//   warps 4t..4t+3  softmax of query tile t, one row per thread (TMEM lane quarter
+//            = warp % 4).  Three warps per SM sub-partition keep the exponential
+//            units busy while the others load S, take row maxima or wait.
 // Row maxima move only when a tile exceeds the reference max by more than
 // kRescaleThreshold (log2 units); O in TMEM and the row sum are then rescaled
 // (rare).  An item's O is read after the next item's first P is written (its
@@ -259,11 +270,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   FaSlot* ring = reinterpret_cast<FaSlot*>(smem + kFaOffBar + kFaRingOff);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kProducerWarp = kFaSoftmaxWarps * kFaTiles;  // first warp of the producer warpgroup
 
   if (threadIdx.x == 0) {
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(bar(kFbQFull + t), 1);
-      mbar_init(bar(kFbQEmpty + t), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(kFbQFull + i), 1);
+      mbar_init(bar(kFbQEmpty + i), kFaTiles);  // one arrival per MMA issuer
+    }
+    for (int t = 0; t < kFaTiles; ++t) {
       mbar_init(bar(kFbSFull + t), 1);
       mbar_init(bar(kFbSEmpty + t), kFaSoftmaxWarps);
       mbar_init(bar(kFbPFull + t), kFaSoftmaxWarps);
@@ -273,19 +287,19 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     }
     for (int i = 0; i < kFaStages; ++i) {
       mbar_init(bar(kFbKvFull + i), 1);
-      mbar_init(bar(kFbKvEmpty + i), 1);
+      mbar_init(bar(kFbKvEmpty + i), kFaTiles);  // one arrival per MMA issuer
     }
     for (int i = 0; i < kFaRing; ++i) {
       mbar_init(bar(kFbInfoFull + i), 1);
-      mbar_init(bar(kFbInfoEmpty + i), 1 + 2 * kFaSoftmaxWarps);  // the MMA thread and every softmax warp
+      mbar_init(bar(kFbInfoEmpty + i), kFaTiles + kFaSoftmaxWarps * kFaTiles);  // the MMA issuers, every softmax warp
     }
-    mbar_init(bar(kFbDrain), 1);
+    for (int t = 0; t < kFaTiles; ++t) mbar_init(bar(kFbDrain + t), 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmKV);
   }
-  if (warp == 9) {
+  if (warp == kProducerWarp + 1) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -298,9 +312,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   // work-list length: a launch parameter, or (CUDA-graph buckets) read from the
   // device and clamped to the capacity the launch was sized for
   const int n_items = (n_tiles_dev ? min(max(__ldg(n_tiles_dev), 0), n_tiles) : n_tiles) * 16;
-  if (warp >= 8) {
+
+  if (warp >= kProducerWarp) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kFaRegsProducer));
-    if (warp == 8 && lane == 0) {
+    if (warp == kProducerWarp && lane == 0) {
       // ---------------- TMA producer
       int g = 0, i = 0;
       bool ok = true;
@@ -310,8 +325,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         if (!mbar_wait(bar(kFbInfoEmpty + sl), ((i / kFaRing) & 1) ^ 1, 240, abort_flag)) return false;
         FaSlot& o = ring[sl];
         o.base = a.base, o.L = a.L, o.q0 = a.q0, o.head = a.head, o.pos0 = a.pos0, o.Lkv = a.Lkv;
-        o.n0 = last ? 0 : a.n0;
-        o.n1 = a.n1;
+#pragma unroll
+        for (int t = 0; t < kFaTiles; ++t) o.n[t] = a.n[t];
+        if (last) o.n[0] = 0;
         mbar_arrive(bar(kFbInfoFull + sl));
         return true;
       };
@@ -322,9 +338,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         if (!publish(a, false)) { ok = false; break; }
         if (!mbar_wait(bar(kFbQEmpty + qb), ((i >> 1) & 1) ^ 1, 241, abort_flag)) { ok = false; break; }
         mbar_arrive_expect_tx(bar(kFbQFull + qb), kFaSmemQ);
-        tma_load_2d(sQ + qb * kFaSmemQ, &tmQ, bar(kFbQFull + qb), a.head * 64, a.base + a.q0);
-        tma_load_2d(sQ + qb * kFaSmemQ + kFaRows * 128, &tmQ, bar(kFbQFull + qb), a.head * 64,
-                    a.base + a.q0 + kFaRows);
+#pragma unroll
+        for (int t = 0; t < kFaTiles; ++t)  // tiles past the document load rows of the next one (or zeros): unused
+          tma_load_2d(sQ + qb * kFaSmemQ + t * kFaRows * 128, &tmQ, bar(kFbQFull + qb), a.head * 64,
+                      a.base + a.q0 + kFaRows * t);
         for (int j = 0; j < a.nkv; ++j, ++g) {
           const int st = g % kFaStages;
           if (!mbar_wait(bar(kFbKvEmpty + st), ((g / kFaStages) & 1) ^ 1, 242, abort_flag)) { ok = false; break; }
@@ -338,81 +355,82 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       for (int k = (g > kFaStages ? g - kFaStages : 0); k < g; ++k)
         mbar_wait(bar(kFbKvFull + k % kFaStages), (k / kFaStages) & 1, 243, nullptr);
       for (int k = (i > 2 ? i - 2 : 0); k < i; ++k) mbar_wait(bar(kFbQFull + (k & 1)), (k >> 1) & 1, 244, nullptr);
-    } else if (warp == 9 && lane == 0) {
-      // ---------------- MMA issuer
+    } else if (warp > kProducerWarp && warp <= kProducerWarp + kFaTiles && lane == 0) {
+      // ---------------- MMA issuer of query tile t
+      const int t = warp - kProducerWarp - 1;
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, kFaKv, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, 64, false, true);  // V is MN-major
-      // P.V of one key tile waits until S of the next key tile has been issued
-      int sc0 = 0, sc1 = 0;    // S tiles issued per query tile
-      int pvc0 = 0, pvc1 = 0;  // P.V tiles issued per query tile
-      int items1 = 0;          // items having a tile 1 so far (tile 0: every item)
-      bool ok = true, pend = false;
-      // pending P.V: key-tile index g, per tile: issued?, first / last key tile of its item, item index
-      int pv_g = 0, pv_item0 = 0, pv_item1 = 0;
-      bool pv_on0 = false, pv_on1 = false, pv_first = false, pv_last0 = false, pv_last1 = false;
-      auto pv_tile = [&](int t, int& cntr, bool last, int item) -> bool {
-        if (!mbar_wait(bar(kFbPFull + t), cntr & 1, 245, abort_flag)) return false;
-        if (pv_first && !mbar_wait(bar(kFbOEmpty + t), (item & 1) ^ 1, 246, abort_flag)) return false;
-        tc_fence_after();
-        const uint64_t dv = sdesc_sw128(sV + (pv_g % kFaStages) * kFaSmemKV);
-#pragma unroll
-        for (int k = 0; k < kFaKv / 16; ++k)  // 16 keys per step: P +8 TMEM columns, V +2048 B (16 rows of 128 B)
-          umma_bf16_ts(tmem + kFaColO + 64 * t, tmem + kFaColP + 64 * t + 8 * k, dv + 128 * k, idesc_o,
-                       (!pv_first || k != 0) ? 1u : 0u);
-        umma_commit(bar(kFbODone + t));
-        if (last) umma_commit(bar(kFbOFinal + t));
-        ++cntr;
-        return true;
-      };
+      int sc = 0, pvc = 0, items_t = 0;  // S / P.V tiles issued, items having this tile
+      // pending P.V (issued after S of the next key tile) of key tile pv_g
+      int pv_g = 0, pv_item = 0;
+      bool pv_on = false, pv_first = false, pv_last = false, ok = true, pend = false;
+      // P.V of the pending key tile (if this tile has one), then its K/V stage returned
       auto issue_pv = [&]() -> bool {
-        if (pv_on0 && !pv_tile(0, pvc0, pv_last0, pv_item0)) return false;
-        if (pv_on1 && !pv_tile(1, pvc1, pv_last1, pv_item1)) return false;
-        umma_commit(bar(kFbKvEmpty + pv_g % kFaStages));
-        return true;
-      };
-      auto s_tile = [&](int t, int& cntr, int qb, uint64_t dk) -> bool {
-        if (cntr > 0 && !mbar_wait(bar(kFbSEmpty + t), (cntr - 1) & 1, 249, abort_flag)) return false;
-        tc_fence_after();
-        const uint64_t dq = sdesc_sw128(sQ + qb * kFaSmemQ + t * kFaRows * 128);
+        if (pv_on) {
+          if (!mbar_wait(bar(kFbPFull + t), pvc & 1, 245, abort_flag)) return false;
+          if (pv_first && !mbar_wait(bar(kFbOEmpty + t), (pv_item & 1) ^ 1, 246, abort_flag)) return false;
+          tc_fence_after();
+          const uint64_t dv = sdesc_sw128(sV + (pv_g % kFaStages) * kFaSmemKV);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) umma_bf16(tmem + kFaColS + 128 * t, dq + 2 * k, dk + 2 * k, idesc_s, k != 0);
-        umma_commit(bar(kFbSFull + t));
-        ++cntr;
+          for (int k = 0; k < kFaKv / 16; ++k)  // 16 keys per step: P +8 TMEM columns, V +2048 B (16 rows of 128 B)
+            umma_bf16_ts(tmem + kFaColO + 64 * t, tmem + kFaColP + (kFaKv / 2) * t + 8 * k, dv + 128 * k, idesc_o,
+                         (!pv_first || k != 0) ? 1u : 0u);
+          umma_commit(bar(kFbODone + t));
+          if (pv_last) umma_commit(bar(kFbOFinal + t));
+          ++pvc;
+          umma_commit(bar(kFbKvEmpty + pv_g % kFaStages));  // after this tile's MMAs that read the stage
+        } else {
+          mbar_arrive(bar(kFbKvEmpty + pv_g % kFaStages));  // this tile never read the stage
+        }
         return true;
       };
       int g = 0;
       for (int i = 0; ok; ++i) {
         const int sl = i % kFaRing;
         if (!mbar_wait(bar(kFbInfoFull + sl), (i / kFaRing) & 1, 239, abort_flag)) { ok = false; break; }
-        FaSlot a = ring[sl];
+        const FaSlot a = ring[sl];
         mbar_arrive(bar(kFbInfoEmpty + sl));
-        if (a.n0 == 0) break;  // no more items
-        const int nkv = max(a.n0, a.n1);
+        if (a.n[0] == 0) break;  // no more items
+        int nkv = 0, nt = 0;
+#pragma unroll
+        for (int u = 0; u < kFaTiles; ++u) {
+          nkv = max(nkv, a.n[u]);
+          if (u == t) nt = a.n[u];
+        }
         const int qb = i & 1;
-        for (int j = 0; j < nkv; ++j, ++g) {
+        // Arrivals that release a Q buffer or a K/V stage without an MMA behind them
+        // come only after that buffer's load completed: the load cannot complete
+        // before the buffer's previous phase did, so no issuer can arrive twice in
+        // one phase however far ahead of the others it runs.
+        if (!mbar_wait(bar(kFbQFull + qb), (i >> 1) & 1, 247, abort_flag)) { ok = false; break; }
+        if (nt == 0) mbar_arrive(bar(kFbQEmpty + qb));  // this tile reads no Q of the item
+        for (int j = 0; j < nkv && ok; ++j, ++g) {
           const int st = g % kFaStages;
-          if (j == 0 && !mbar_wait(bar(kFbQFull + qb), (i >> 1) & 1, 247, abort_flag)) { ok = false; break; }
           if (!mbar_wait(bar(kFbKvFull + st), (g / kFaStages) & 1, 248, abort_flag)) { ok = false; break; }
-          const uint64_t dk = sdesc_sw128(sK + st * kFaSmemKV);
-          if (j < a.n0 && !s_tile(0, sc0, qb, dk)) { ok = false; break; }
-          if (j < a.n1 && !s_tile(1, sc1, qb, dk)) { ok = false; break; }
-          if (j == nkv - 1) umma_commit(bar(kFbQEmpty + qb));  // Q free once these S are done
+          if (j < nt) {
+            if (sc > 0 && !mbar_wait(bar(kFbSEmpty + t), (sc - 1) & 1, 249, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint64_t dq = sdesc_sw128(sQ + qb * kFaSmemQ + t * kFaRows * 128);
+            const uint64_t dk = sdesc_sw128(sK + st * kFaSmemKV);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) umma_bf16(tmem + kFaColS + kFaKv * t, dq + 2 * k, dk + 2 * k, idesc_s, k != 0);
+            umma_commit(bar(kFbSFull + t));
+            ++sc;
+            if (j == nt - 1) umma_commit(bar(kFbQEmpty + qb));  // Q_t free once this S is done
+          }
           if (pend && !issue_pv()) { ok = false; break; }
           pv_g = g;
-          pv_on0 = j < a.n0;
-          pv_on1 = j < a.n1;
+          pv_on = j < nt;
           pv_first = j == 0;
-          pv_last0 = j == a.n0 - 1;
-          pv_last1 = j == a.n1 - 1;
-          pv_item0 = i;
-          pv_item1 = items1;
+          pv_last = j == nt - 1;
+          pv_item = items_t;
           pend = true;
         }
-        items1 += a.n1 > 0 ? 1 : 0;
+        items_t += nt > 0 ? 1 : 0;
       }
       if (ok && pend) issue_pv();
-      umma_commit(bar(kFbDrain));
-      mbar_wait(bar(kFbDrain), 0, 250, nullptr);
+      umma_commit(bar(kFbDrain + t));
+      mbar_wait(bar(kFbDrain + t), 0, 250, nullptr);
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kFaRegsSoftmax));
@@ -421,7 +439,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     const int qd = warp & 3;
     const int r = qd * 32 + lane;  // row within the tile = TMEM lane
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-    const uint32_t colS = lane_base + kFaColS + 128 * t, colP = lane_base + kFaColP + 64 * t,
+    const uint32_t colS = lane_base + kFaColS + kFaKv * t, colP = lane_base + kFaColP + (kFaKv / 2) * t,
                    colO = lane_base + kFaColO + 64 * t;
     const float sl2 = 0.125f * kLog2e;  // softmax scale in log2 units
     int cnt = 0, it_t = 0;
@@ -468,9 +486,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       const FaSlot a = ring[sl];
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kFbInfoEmpty + sl));
-      if (a.n0 == 0) break;  // no more items
-      const int ntile = t == 0 ? a.n0 : a.n1;
-      if (ntile == 0) continue;
+      if (a.n[0] == 0) break;  // no more items
+      int ntile = 0;
+#pragma unroll
+      for (int u = 0; u < kFaTiles; ++u)
+        if (u == t) ntile = a.n[u];
+      if (ntile == 0) continue;  // this query tile lies past the document
       const int qa = a.q0 + kFaRows * t + r;  // local query row
       const int qabs = a.pos0 + qa;           // its absolute position
       const int lim = chunk > 0 ? min(a.Lkv, (qabs / chunk + 1) * chunk) : a.Lkv;  // visible keys [0, lim)
@@ -483,12 +504,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         if (!mbar_wait(bar(kFbSFull + t), cnt & 1, 252, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const int k0 = j * kFaKv;
-        // 32-key chunks that some row of the warp sees (warp-uniform)
-        const int nch = warp_rows ? min(4, max(0, (wmax - k0 + 31) / 32)) : 0;
-        uint32_t s[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          if (c < nch) tmem_ld32(colS + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c));
+        // 32-key halves that some row of the warp sees (warp-uniform)
+        const int nch = warp_rows ? min(2, max(0, (wmax - k0 + 31) / 32)) : 0;
+        uint32_t s[64];
+        tmem_ld32(colS, *reinterpret_cast<uint32_t(*)[32]>(s));
+        if (nch > 1) tmem_ld32(colS + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
@@ -496,12 +516,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         if (wmin < k0 + kFaKv) {  // a row of the warp stops inside this tile: mask its invisible keys
           const int nvis = lim - k0;
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
+          for (int c = 0; c < 64; ++c)
             if (c >= nvis) s[c] = __float_as_uint(-INFINITY);
         }
         float mt = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           if (c < nch) {
             float m8[4];
 #pragma unroll
@@ -542,42 +562,34 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         }
         m_ref = m_new;
         const float mo = m_ref == -INFINITY ? 0.f : m_ref;
-        // P of this row in two halves of 64 keys (bf16 pairs): the first half's
-        // exponentials overlap the previous P.V; it is stored once that P.V has
-        // released P_t, then the second half is computed and stored
+        uint32_t pw[32];  // P of this row: 64 keys as bf16 pairs
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pw[32];
+        for (int c = 0; c < 2; ++c) {
+          if (c < nch) {
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            const int c = 2 * half + cc;
-            if (c < nch) {
-#pragma unroll
-              for (int p = 0; p < 16; ++p) {
-                float x0, x1, e0, e1;
-                fma2(x0, x1, __uint_as_float(s[32 * c + 2 * p]), __uint_as_float(s[32 * c + 2 * p + 1]), sl2, sl2,
-                     -mo, -mo);
-                if (p % 8 < kFaPolyPairs) {
-                  exp2_poly2(x0, x1, e0, e1);
-                } else {
-                  e0 = ex2_approx(x0);
-                  e1 = ex2_approx(x1);
-                }
-                add2(lsum[2 * (p & 3)], lsum[2 * (p & 3) + 1], lsum[2 * (p & 3)], lsum[2 * (p & 3) + 1], e0, e1);
-                pw[16 * cc + p] = pack_bf16x2(e0, e1);
+            for (int p = 0; p < 16; ++p) {
+              float x0, x1, e0, e1;
+              fma2(x0, x1, __uint_as_float(s[32 * c + 2 * p]), __uint_as_float(s[32 * c + 2 * p + 1]), sl2, sl2, -mo,
+                   -mo);
+              if (p % 8 < kFaPolyPairs) {
+                exp2_poly2(x0, x1, e0, e1);
+              } else {
+                e0 = ex2_approx(x0);
+                e1 = ex2_approx(x1);
               }
-            } else {
-#pragma unroll
-              for (int p = 0; p < 16; ++p) pw[16 * cc + p] = 0u;
+              add2(lsum[2 * (p & 3)], lsum[2 * (p & 3) + 1], lsum[2 * (p & 3)], lsum[2 * (p & 3) + 1], e0, e1);
+              pw[16 * c + p] = pack_bf16x2(e0, e1);
             }
+          } else {
+#pragma unroll
+            for (int p = 0; p < 16; ++p) pw[16 * c + p] = 0u;
           }
-          if (half == 0 && !o_ready) {
-            if (!mbar_wait(bar(kFbODone + t), (cnt - 1) & 1, 254, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-          }
-          tmem_st32(colP + 32 * half, pw);
         }
-        if (!ok) break;
+        if (!o_ready) {
+          if (!mbar_wait(bar(kFbODone + t), (cnt - 1) & 1, 254, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+        }
+        tmem_st32(colP, pw);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -595,7 +607,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == kProducerWarp + 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

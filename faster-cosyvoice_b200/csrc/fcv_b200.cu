@@ -444,7 +444,7 @@ int run_attention(const void* qkv, int dtype, const int32_t* cu, int chunk, cons
   src.kv_base = cached ? kvs.kv_base : nullptr;
   const int k_col = cached ? 0 : 1024, v_col = cached ? 1024 : 2048;
   if (dtype == FCV_DTYPE_BF16) {
-    // Q tiles of 128 rows from the (N, 3072) [Q|K|V] buffer; K/V tiles of 128 rows from it or the cache
+    // Q tiles of 128 rows from the (N, 3072) [Q|K|V] buffer; K/V tiles of kFaKv rows from it or the cache
     CUtensorMap tq, tkv;
     FCV_TRY(make_tmap(&tq, qkv, false, n_rows, 3072, 3072, 64, kFaRows));
     if (cached)
@@ -954,7 +954,7 @@ int fcv_attn_schedule(const int32_t* lengths_host, int B, int chunk, const int32
   const long items = (long)n_tiles * FCV_HEADS;
   const long need = n_ctas + 1 + items;
   if (need > cap) return fail(FCV_EINVAL, "fcv_attn_schedule: capacity %d < %ld", cap, need);
-  // item cost: the 128 x 128 S and P.V tiles of its (up to two) query tiles plus
+  // item cost: the S and P.V tiles (128 rows x kFaKv keys) of its query tiles plus
   // one for the per-item work (Q load, output)
   std::vector<std::pair<long, int>> order;  // (cost, item), most expensive first
   order.reserve(items);
@@ -966,8 +966,9 @@ int fcv_attn_schedule(const int32_t* lengths_host, int B, int chunk, const int32
     const int d = tiles[2 * t], q0 = tiles[2 * t + 1];
     if (d < 0 || d >= B) return fail(FCV_EINVAL, "fcv_attn_schedule: tile %d names document %d", t, d);
     const int L = lengths_host[d];
-    long cost = 1 + key_tiles(L, std::min(q0 + kFaRows, L) - 1);
-    if (q0 + kFaRows < L) cost += key_tiles(L, std::min(q0 + 2 * kFaRows, L) - 1);
+    long cost = 1;
+    for (int u = 0; u < kFaTiles && q0 + kFaRows * u < L; ++u)
+      cost += key_tiles(L, std::min(q0 + kFaRows * (u + 1), L) - 1);
     for (int h = 0; h < FCV_HEADS; ++h) order.push_back({cost, t * FCV_HEADS + h});
   }
   std::stable_sort(order.begin(), order.end(), [](const auto& a, const auto& b) { return a.first > b.first; });

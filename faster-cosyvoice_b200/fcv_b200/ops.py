@@ -61,7 +61,7 @@ def pack_layout(lengths: torch.Tensor, padded_length: int, num_rows: int):
 
 
 def attention_tiles(lengths: Sequence[int], chunk: int, device) -> tuple[torch.Tensor, int]:
-    """Work-list entries (doc, q0) of up to 256 query rows (two 128-row query
+    """Work-list entries (doc, q0) of up to 384 query rows (three 128-row query
     tiles sharing K/V), most expensive first (host-built work list)."""
     lengths = [int(x) for x in lengths]
     cap = max(1, sum((L + 127) // 128 for L in lengths))

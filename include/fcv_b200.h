@@ -235,8 +235,8 @@ int fcv_gemm(const void* A, const void* W, const float* bias, int M, int Nout, i
  * head h and query row q: softmax(Q K^T / 8 + mask) V, where the mask keeps
  * keys k < L_d, and, when chunk > 0, only k // chunk <= q // chunk.
  * qkv: (N, 3072) [Q|K|V] element type dtype; out: (N, 1024); N = cu_seqlens[B].
- * tiles: (n_tiles, 2) int32 (doc, q0) list of work-list entries of up to 256
- * query rows (two 128-row query tiles sharing their K/V tiles), built by
+ * tiles: (n_tiles, 2) int32 (doc, q0) list of work-list entries of up to 384
+ * query rows (three 128-row query tiles sharing their K/V tiles), built by
  * fcv_attn_tiles().  sched (device, optional): the balanced per-CTA item
  * list of fcv_attn_schedule for sched_ctas CTAs; null deals items round
  * robin (the result is the same either way).  Replaces the FlashInfer ragged
@@ -246,7 +246,7 @@ int fcv_attention(const void* qkv, int dtype, const int32_t* cu_seqlens, int B, 
                   const int32_t* sched, int sched_ctas, void* out, void* stream);
 
 /* Host helper: fill `tiles` (capacity `cap` pairs, host memory) with the
- * 256-row work-list entries of the documents, most expensive first.  Returns the
+ * 384-row work-list entries of the documents, most expensive first.  Returns the
  * number of tiles or a negative status. */
 int fcv_attn_tiles(const int32_t* lengths_host, int B, int chunk, int32_t* tiles, int cap);
 
@@ -255,8 +255,8 @@ int fcv_attn_tiles(const int32_t* lengths_host, int B, int chunk, int32_t* tiles
  * composition).  fcv_attn_ctas: the CTA count of the persistent attention
  * launch for n_tiles work-list entries on the current device.
  * fcv_attn_schedule: assign the 16 * n_tiles items (tile t, head h) = t*16+h
- * to n_ctas CTAs, longest first to the least loaded (cost = the 128 x 128
- * key tiles of its one or two query tiles + 1; one CTA per SM);
+ * to n_ctas CTAs, longest first to the least loaded (cost = the 128 x 64
+ * key tiles of its one to three query tiles + 1; one CTA per SM);
  * writes offsets (n_ctas + 1) then the items grouped by CTA into `sched`
  * (capacity cap ints).  Returns the ints written or a negative status. */
 int fcv_attn_ctas(int n_tiles);

@@ -99,8 +99,8 @@ def test_attention_work_list_covers_rows_and_orders_by_cost(lib, chunk):
     seen = set()
     costs = []
     for d, q0 in tiles:
-        rows = min(256, lengths[d] - q0)  # a work-list entry: up to two 128-row query tiles
-        assert rows > 0 and q0 % 256 == 0
+        rows = min(384, lengths[d] - q0)  # a work-list entry: up to three 128-row query tiles
+        assert rows > 0 and q0 % 384 == 0
         for q in range(q0, q0 + rows):
             assert (d, q) not in seen
             seen.add((d, q))
@@ -166,7 +166,7 @@ def test_attention_schedule_assigns_every_item_once_and_balances(lib, chunk):
     """fcv_attn_schedule: a permutation of the 16 * n_tiles items grouped by CTA,
     longest first to the least loaded CTA; its worst CTA carries no more work
     than round robin's (config-2 lengths, one CTA per SM: 148 on a B200).  The
-    cost of an item is the 128 x 128 tiles of its (up to two) query tiles + 1."""
+    cost of an item is the 128 x 64 tiles of its (up to three) query tiles + 1."""
     rng = np.random.default_rng(1)
     req = [int(v) for v in rng.integers(150, 601, size=8)]
     lengths = req + req + [1, 0, 3000]
@@ -186,13 +186,12 @@ def test_attention_schedule_assigns_every_item_once_and_balances(lib, chunk):
 
     def key_tiles(L, q_last):
         kv = min(L, (q_last // chunk + 1) * chunk) if chunk else L
-        return -(-kv // 128)
+        return -(-kv // 64)
 
     def cost(it):
         d, q0 = tiles[it // 16]
         L = lengths[d]
-        c = 1 + key_tiles(L, min(q0 + 128, L) - 1)
-        return c + (key_tiles(L, min(q0 + 256, L) - 1) if q0 + 128 < L else 0)
+        return 1 + sum(key_tiles(L, min(q0 + 128 * (u + 1), L) - 1) for u in range(3) if q0 + 128 * u < L)
 
     lpt = max(sum(cost(i) for i in items[off[c]:off[c + 1]]) for c in range(ctas))
     rr = max(sum(cost(i) for i in range(c, 16 * n, ctas)) for c in range(ctas))

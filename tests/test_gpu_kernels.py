@@ -278,7 +278,7 @@ def test_attention_tiles_cover_every_query_row_once():
         tiles, n = ops.attention_tiles(lengths, chunk, "cpu")
         seen = set()
         for d, q0 in tiles.view(-1, 2)[:n].tolist():
-            for q in range(q0, min(q0 + 256, lengths[d])):  # a work-list entry: two 128-row query tiles
+            for q in range(q0, min(q0 + 384, lengths[d])):  # a work-list entry: three 128-row query tiles
                 assert (d, q) not in seen
                 seen.add((d, q))
         assert len(seen) == sum(lengths)
