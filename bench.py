@@ -834,6 +834,18 @@ def reference_gpu_arm(args, req_lengths, chunk, seed, cfg, strong):
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     rdt = torch.float16 if args.ref_dtype == "fp16" else torch.bfloat16
+    # FlashInferDiT counts each document's length by summing its mask in the activation
+    # dtype (flashinfer_dit.py:460).  A length that rounds up past the padded length T
+    # makes its packing gather read past the row: in bf16, 3000 rounds to 3008, and on
+    # the B200 that raised a device-side assert.  Such a batch is not run again.
+    T_pad = max(req_lengths)
+    rounded = [int(torch.tensor(float(L), dtype=rdt).item()) for L in req_lengths]
+    if any(r > T_pad for r in rounded):
+        bad = sorted({(L, r) for L, r in zip(req_lengths, rounded) if r > T_pad})
+        print(json.dumps({**base, "unavailable": f"the reference counts lengths in {args.ref_dtype} "
+                          f"(flashinfer_dit.py:460): {bad[0][0]} frames round to {bad[0][1]} > T={T_pad}, "
+                          "an out-of-range gather that raised a device-side assert on B200"}), flush=True)
+        return
     torch.manual_seed(seed)
     sd = B200DiT(depth=22).eval().state_dict()
     ref = FlashInferDiT(device=device, static_chunk_size=50)
