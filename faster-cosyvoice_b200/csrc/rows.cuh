@@ -363,12 +363,23 @@ __global__ void __launch_bounds__(256) embed_gather_kernel(const T* __restrict__
     for (int k = 0; k < 30; ++k) tile[w + 8 * k][pp] = v[k];
   }
   __syncthreads();
+  // rows of 320 elements written as 16-byte vectors of V consecutive channels
+  constexpr int V = 16 / static_cast<int>(sizeof(T));
+  constexpr int kVecs = 320 / V;
   const long row0 = cu[b] + p0;
-  for (int i = threadIdx.x; i < 32 * 320; i += blockDim.x) {
-    const int pp = i / 320, c = i - pp * 320;
+  for (int i = threadIdx.x; i < 32 * kVecs; i += blockDim.x) {
+    const int pp = i / kVecs, c0 = (i - pp * kVecs) * V;
     if (p0 + pp >= L) continue;
-    const float v = c < 240 ? tile[c][pp] : to_f<T>(spks[(long)b * 80 + (c - 240)]);
-    a_in[(row0 + pp) * 320 + c] = from_f<T>(v);
+    union {
+      uint4 u;
+      T e[V];
+    } pk;
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int c = c0 + k;
+      pk.e[k] = from_f<T>(c < 240 ? tile[c][pp] : to_f<T>(spks[(long)b * 80 + (c - 240)]));
+    }
+    *reinterpret_cast<uint4*>(a_in + (row0 + pp) * 320 + c0) = pk.u;
   }
 }
 
