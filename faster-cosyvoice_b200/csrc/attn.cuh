@@ -235,20 +235,25 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
-// Persistent, one CTA per SM.  Per item (three query tiles t of one head):
+// Persistent, one CTA per SM.  Per item (three 128-row query tiles of one head):
 //   warp 12  TMA: the item's query tiles into one of two buffers, K/V tiles of 64
-//            keys into a 4-stage ring shared by the query tiles; it also resolves
+//            keys into a 6-stage ring shared by the query tiles; it also resolves
 //            each item once and publishes it to the other roles (item ring)
-//   warp 13+t  issues query tile t's tcgen05.mma: S_t = Q_t K_j^T, then
-//            O_t += P_t V_j with P_t read from TMEM; S of key tile j+1 is issued
-//            before P.V of tile j, so the tensor core works while softmax runs.
-//            One issuer per query tile keeps the tiles independent (a tile's slow
-//            softmax never holds back another tile's MMAs); they share only the
-//            K/V ring, whose stages return when every tile is done with them.
-//            Warp 13 also owns TMEM.
-//   warps 4t..4t+3  softmax of query tile t, one row per thread (TMEM lane quarter
-//            = warp % 4).  Three warps per SM sub-partition keep the exponential
+//   warp 13+t  issues slot t's tcgen05.mma: S_t = Q K_j^T, then O_t += P_t V_j
+//            with P_t read from TMEM; S of key tile j+1 is issued before P.V of
+//            tile j, so the tensor core works while softmax runs.  One issuer per
+//            slot keeps the slots independent (a slot's slow softmax never holds
+//            back another slot's MMAs); they share only the K/V ring, whose
+//            stages return when every slot is done with them.  Warp 13 also owns
+//            TMEM.
+//   warps 4t..4t+3  softmax of slot t, one row per thread (TMEM lane quarter =
+//            warp % 4).  Three warps per SM sub-partition keep the exponential
 //            units busy while the others load S, take row maxima or wait.
+// Slot t takes query tile (t + i) mod 3 of the CTA's i-th item: under a causal
+// chunk mask the last tile of an item sees the most keys, and a short item has
+// tiles past its document, so a fixed assignment would give one slot most of the
+// work; rotating spreads it, and slots whose tile ends early run ahead into the
+// next item as far as the Q buffers and the K/V ring allow.
 // Row maxima move only when a tile exceeds the reference max by more than
 // kRescaleThreshold (log2 units); O in TMEM and the row sum are then rescaled
 // (rare).  An item's O is read after the next item's first P is written (its
@@ -391,11 +396,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         const FaSlot a = ring[sl];
         mbar_arrive(bar(kFbInfoEmpty + sl));
         if (a.n[0] == 0) break;  // no more items
+        const int rt = (t + i) % kFaTiles;  // the item's query tile this issuer takes (rotates per item)
         int nkv = 0, nt = 0;
 #pragma unroll
         for (int u = 0; u < kFaTiles; ++u) {
           nkv = max(nkv, a.n[u]);
-          if (u == t) nt = a.n[u];
+          if (u == rt) nt = a.n[u];
         }
         const int qb = i & 1;
         // Arrivals that release a Q buffer or a K/V stage without an MMA behind them
@@ -410,7 +416,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           if (j < nt) {
             if (sc > 0 && !mbar_wait(bar(kFbSEmpty + t), (sc - 1) & 1, 249, abort_flag)) { ok = false; break; }
             tc_fence_after();
-            const uint64_t dq = sdesc_sw128(sQ + qb * kFaSmemQ + t * kFaRows * 128);
+            const uint64_t dq = sdesc_sw128(sQ + qb * kFaSmemQ + rt * kFaRows * 128);
             const uint64_t dk = sdesc_sw128(sK + st * kFaSmemKV);
 #pragma unroll
             for (int k = 0; k < 4; ++k) umma_bf16(tmem + kFaColS + kFaKv * t, dq + 2 * k, dk + 2 * k, idesc_s, k != 0);
@@ -487,12 +493,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(kFbInfoEmpty + sl));
       if (a.n[0] == 0) break;  // no more items
+      const int rt = (t + i) % kFaTiles;  // the item's query tile this slot takes (rotates per item)
       int ntile = 0;
 #pragma unroll
       for (int u = 0; u < kFaTiles; ++u)
-        if (u == t) ntile = a.n[u];
+        if (u == rt) ntile = a.n[u];
       if (ntile == 0) continue;  // this query tile lies past the document
-      const int qa = a.q0 + kFaRows * t + r;  // local query row
+      const int qa = a.q0 + kFaRows * rt + r;  // local query row
       const int qabs = a.pos0 + qa;           // its absolute position
       const int lim = chunk > 0 ? min(a.Lkv, (qabs / chunk + 1) * chunk) : a.Lkv;  // visible keys [0, lim)
       const bool row_ok = qa < a.L;
