@@ -271,6 +271,38 @@ def test_ragged_attention(dtype, chunk):
         assert rel_l2(out.float().cpu().numpy(), ref.cpu().numpy()) < 5e-3
 
 
+@pytest.mark.parametrize("key_boost", [60.0, 300.0])
+@pytest.mark.parametrize("chunk", [0, 50])
+def test_attention_logits_rising_far_above_the_first_key_tile(key_boost, chunk):
+    """The bf16 kernel takes a row's reference maximum on its first 64-key tile
+    and rescales only when a later tile's exponentials would pass 2^32.  Here
+    every query has 4 in dimension 0 of each head and every 37th key of the
+    second half of each document has `key_boost` there: those logits sit ~43
+    (boost 60: the tile sum passes 2^32) or ~216 (boost 300: the exponentials
+    overflow to inf) log2 units above everything before them, so the row is
+    rescaled and the tile redone.  Within bf16 rounding of torch fp32, with the
+    streaming mask too (early rows never see the boosted keys)."""
+    ops = _ops()
+    lengths = [700, 300, 1000, 129]
+    N = sum(lengths)
+    g = torch.Generator().manual_seed(11)
+    qkv = torch.randn(N, 3072, generator=g) * 0.5
+    qkv[:, 0:1024:64] = 4.0
+    off = 0
+    for L in lengths:
+        qkv[torch.arange(off + L // 2, off + L, 37), 1024:2048:64] = key_boost
+        off += L
+    qkv = qkv.to(DEV, torch.bfloat16)
+    _, _, _, cu, _ = ops.pack_layout(torch.tensor(lengths, dtype=torch.int32, device=DEV), max(lengths), N)
+    tiles, n = ops.attention_tiles(lengths, chunk, DEV)
+    out = ops.ragged_attention(qkv, cu, tiles, n, chunk)
+    ref = _ref_attention(qkv, lengths, chunk)
+    assert torch.isfinite(out.float()).all()
+    err = ((out.float() - ref).abs() / (1.0 + ref.abs())).max().item()
+    assert err < 1e-2, err
+    assert rel_l2(out.float().cpu().numpy(), ref.cpu().numpy()) < 5e-3
+
+
 def test_attention_tiles_cover_every_query_row_once():
     ops = _ops()
     lengths = [1, 127, 128, 129, 1000, 0, 3000]
