@@ -621,7 +621,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 }
 
 // ------------------------------------------------------------------ fp32 (CUDA cores)
-// One thread per query row (256 per CTA: one work-list entry), 32-key tiles in
+// One thread per query row (384 per CTA: one work-list entry), 32-key tiles in
 // shared memory.
 __global__ void __launch_bounds__(kAttnQTile) attn_f32_kernel(const float* __restrict__ qkv, const AttnSrc src,
                                                               const float* __restrict__ kv, long kv_rows,
