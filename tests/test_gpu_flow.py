@@ -234,3 +234,39 @@ def test_prefix_cache_matches_full_recompute_bit_exact(dtype):
             assert torch.equal(got[r], ref[r]), (dtype, call_i, r, (got[r] - ref[r]).abs().max().item())
     assert cache.stable_frames("a") == 0  # finalised and released
     assert cache.stable_frames("b") == (2 * (90 - 3) // 50) * 50
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_interleaved_streams_match_solo_runs_bit_exact(dtype):
+    """Restates the reference's interleave gate (tests/gpu/test_stream_flashinfer.py:63-90,
+    bit-exact there too) on this build's streaming flow: two sessions advanced call by
+    call in alternation on one model instance and one PrefixCache give exactly what each
+    session gives when it runs alone with a cache of its own -- the cache keeps each
+    stream's state under its id and nothing leaks between streams."""
+    from fcv_b200.flow import PrefixCache, flow_inference_batched_streaming
+
+    dt = getattr(torch, dtype)
+    flow = _flow(dt)
+    rng = np.random.default_rng(23)
+    toks = {s: rng.integers(0, 6561, size=200).tolist() for s in ("a", "b")}
+    prompts = {"a": torch.tensor(rng.standard_normal((1, 30, 80)), device=DEV, dtype=torch.float32),
+               "b": torch.tensor(rng.standard_normal((1, 21, 80)), device=DEV, dtype=torch.float32)}
+    spk = {s: torch.tensor(rng.standard_normal((1, 192)), device=DEV, dtype=torch.float32) for s in ("a", "b")}
+    steps = {"a": (63, 88, 113), "b": (40, 65, 90)}
+
+    def advance(cache, s, k):
+        fin = k == len(steps[s]) - 1
+        return flow_inference_batched_streaming(flow, [toks[s][:steps[s][k]]], [prompts[s]], spk[s], [fin],
+                                                cache=cache, stream_ids=[s])[0]
+
+    solo = {}
+    for s in ("a", "b"):
+        cache = PrefixCache(flow, max_streams=2, max_frames=400)
+        solo[s] = [advance(cache, s, k) for k in range(3)]
+    cache = PrefixCache(flow, max_streams=2, max_frames=400)
+    for k in range(3):
+        for s in ("a", "b"):
+            out = advance(cache, s, k)
+            assert out.shape == solo[s][k].shape, (dtype, s, k)
+            assert torch.equal(out, solo[s][k]), (dtype, s, k, (out - solo[s][k]).abs().max().item())
+    assert cache.stable_frames("a") == 0 and cache.stable_frames("b") == 0  # both finalised and released
