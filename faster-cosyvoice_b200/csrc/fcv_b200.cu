@@ -794,6 +794,34 @@ int fcv_device_error(int* code, void* stream) {
   return FCV_OK;
 }
 
+// Self-test of the bounded waits every pipelined kernel uses: thread 0 waits on an
+// mbarrier that nothing completes and gives up after limit_ns, recording code 901
+// and raising the CTA's abort flag; thread 32 waits on the same barrier with four
+// times the limit and leaves when it sees the flag.  observed[i] = 1 if waiter i's
+// wait succeeded (never expected), 0 if it returned false.
+__global__ void __launch_bounds__(64) wait_expiry_kernel(unsigned long long limit_ns, int* observed) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    observed[0] = mbar_wait(smem_u32(&bar), 0, 901, &abort_flag, limit_ns) ? 1 : 0;
+  else if (threadIdx.x == 32)
+    observed[1] = mbar_wait(smem_u32(&bar), 0, 902, &abort_flag, 4 * limit_ns) ? 1 : 0;
+}
+
+int fcv_selftest_wait_expiry(unsigned long long limit_ns, int32_t* observed, void* stream) {
+  if (!observed || limit_ns == 0 || limit_ns > kWaitLimitNs)
+    return fail(FCV_EINVAL, "fcv_selftest_wait_expiry: observed must be a device int[2], 0 < limit_ns <= %llu",
+                kWaitLimitNs);
+  FCV_LAUNCH("wait_expiry_kernel", wait_expiry_kernel, dim3(1), dim3(64), 0, as_stream(stream), limit_ns, observed);
+  return FCV_OK;
+}
+
 int fcv_mask_lengths(const void* mask, int dtype, int B, int T, int32_t* lengths, void* stream) {
   if (!mask || !lengths || B < 0 || T < 0) return fail(FCV_EINVAL, "fcv_mask_lengths: bad arguments");
   if (!valid_dtype(dtype)) return fail(FCV_EINVAL, "fcv_mask_lengths: bad dtype");

@@ -70,9 +70,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait for the phase of parity `parity`.  Returns false (and records
-// `code`) when the limit expires, or immediately when *abort is set.
+// `code`) when `limit_ns` expires, or immediately when *abort is set.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int code,
-                                          volatile int* abort_flag) {
+                                          volatile int* abort_flag, unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
@@ -80,7 +80,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int cod
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (abort_flag != nullptr && *abort_flag) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       record_error(code);
       if (abort_flag != nullptr) *abort_flag = 1;
       return false;

@@ -39,6 +39,7 @@ EXPORTS = (
     "fcv_version",
     "fcv_last_error",
     "fcv_device_error",
+    "fcv_selftest_wait_expiry",
     "fcv_mask_lengths",
     "fcv_pack_layout",
     "fcv_unpack_output",
@@ -205,6 +206,7 @@ _SIGNATURES = {
     "fcv_version": (_i, []),
     "fcv_last_error": (ctypes.c_char_p, []),
     "fcv_device_error": (_i, [ctypes.POINTER(ctypes.c_int), _vp]),
+    "fcv_selftest_wait_expiry": (_i, [ctypes.c_ulonglong, _vp, _vp]),
     "fcv_mask_lengths": (_i, [_vp, _i, _i, _i, _vp, _vp]),
     "fcv_pack_layout": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp]),
     "fcv_unpack_output": (_i, [_vp, _i, _vp, _i, _i, _i, _vp, _vp]),

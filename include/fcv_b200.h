@@ -74,6 +74,16 @@ const char* fcv_last_error(void);
 /* Reads and clears the device error word of the current device (synchronises
  * the given stream).  *code = 0 when no kernel has reported an error. */
 int fcv_device_error(int* code, void* stream);
+/* Self-test of the bounded waits (no counterpart in the reference, whose
+ * kernels come from FlashInfer, Triton and cuBLAS): one CTA in which one
+ * thread waits on an mbarrier that nothing completes.  After limit_ns
+ * (0 < limit_ns <= 4 s) the wait gives up, records device error 901 and
+ * raises the CTA's abort flag, on which a second waiter (4 x limit_ns)
+ * returns at once; observed (a device int32[2]) gets 0 for each wait that
+ * returned false.  Lets a caller check that a stalled pipeline ends with an
+ * error code the host can read (fcv_device_error) and leaves the context
+ * usable, without faulting the GPU. */
+int fcv_selftest_wait_expiry(unsigned long long limit_ns, int32_t* observed, void* stream);
 
 /* Weights ---------------------------------------------------------------- */
 /* Derived inference weights (FlashInferDiT.finalize_weights,

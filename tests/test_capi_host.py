@@ -58,6 +58,10 @@ def test_version_and_error_paths_without_gpu(lib):
     assert lib.fcv_dit_forward(None, None, None, 0, None) == -1
     assert lib.fcv_attention(None, 1, None, 0, 0, 0, 0, None, 0, None, 0, None, None) == -1
     assert lib.fcv_ln_modulate(None, 0, None, None, None, 0, 0, None, 0, None) == -1
+    assert lib.fcv_selftest_wait_expiry(1000, None, None) == -1  # no observed buffer
+    assert lib.fcv_selftest_wait_expiry(0, 16, None) == -1  # limit outside (0, 4 s]
+    assert lib.fcv_selftest_wait_expiry(5_000_000_000, 16, None) == -1
+    assert b"fcv_selftest_wait_expiry" in lib.fcv_last_error()
     assert lib.fcv_pack_layout(None, 0, 0, 0, None, None, None, None, None, None) == -1
 
 

@@ -8,6 +8,7 @@ their bf16 output rounding (|err| <= 1e-2 * max|ref| or rel-L2 <= 5e-3)."""
 from __future__ import annotations
 
 import math
+import time
 
 import numpy as np
 import pytest
@@ -39,6 +40,38 @@ def _ops():
     from fcv_b200 import ops
 
     return ops
+
+
+# ---------------------------------------------------------------- bounded waits
+
+def test_bounded_wait_expires_with_an_error_code_and_the_context_survives():
+    """Every pipelined kernel here (GEMM, convolution, attention) waits on mbarriers
+    with a time limit, so a stalled pipeline ends with an error word the host reads
+    instead of a hung GPU.  fcv_selftest_wait_expiry runs that wait on a barrier that
+    nothing completes (limit 20 ms): both waiters return false, the first code (901)
+    reaches the host, reading it clears it, and the context still computes (a GEMM
+    checked against torch right after)."""
+    from fcv_b200 import _lib
+    from fcv_b200._lib import call
+
+    ops = _ops()
+    assert ops.device_error() == 0
+    observed = torch.full((2,), 7, dtype=torch.int32, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    t0 = time.perf_counter()
+    call("fcv_selftest_wait_expiry", 20_000_000, observed.data_ptr(), stream)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert observed.tolist() == [0, 0]
+    assert 0.015 < elapsed < 2.0, elapsed
+    assert ops.device_error() == 901
+    assert ops.device_error() == 0  # read and cleared
+    x = torch.randn(300, 1024, device=DEV).to(torch.bfloat16)
+    w = torch.randn(256, 1024, device=DEV).to(torch.bfloat16)
+    y = ops.linear(x, w, epilogue=_lib.EPI_BIAS_F32)
+    ref = x.float() @ w.float().t()
+    assert rel_l2(y.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+    assert ops.device_error() == 0
 
 
 # ---------------------------------------------------------------- layout (bit-exact)
