@@ -599,7 +599,18 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     g.epi = make_epi(EPI_F32, B, (int)MS, ws.mods, MS, w->ada_b);
     FCV_TRY(run_gemm(g, dtype, s));
   }
-  if (N == 0) return FCV_OK;
+  // frames p >= L_b of a padded (B, 80, T) output are zero (all of them when N = 0)
+  auto zero_pad = [&]() -> int {
+    const dim3 zgrid(80, B);
+    if (bt->out_f32)
+      FCV_LAUNCH("zero_padding_kernel", zero_padding_kernel<float>, zgrid, dim3(128), 0, s, bt->cu_seqlens, B, bt->T,
+                 static_cast<float*>(bt->out));
+    else
+      FCV_LAUNCH("zero_padding_kernel", zero_padding_kernel<T>, zgrid, dim3(128), 0, s, bt->cu_seqlens, B, bt->T,
+                 static_cast<T*>(bt->out));
+    return FCV_OK;
+  };
+  if (N == 0) return (bt->packed || B == 0 || bt->T == 0) ? FCV_OK : zero_pad();
 
   // 2. input embedding: gather, proj (K=320), causal grouped conv x2 + Mish + residual
   {
@@ -728,11 +739,7 @@ int forward_impl(const fcv_dit_weights* w, const fcv_dit_batch* bt, const Worksp
     FCV_TRY(run_gemm(po, dtype, s));
     return FCV_OK;
   }
-  const dim3 zgrid(80, B);
-  if (bt->out_f32)
-    FCV_LAUNCH("zero_padding_kernel", zero_padding_kernel<float>, zgrid, dim3(128), 0, s, bt->cu_seqlens, B, bt->T, static_cast<float*>(bt->out));
-  else
-    FCV_LAUNCH("zero_padding_kernel", zero_padding_kernel<T>, zgrid, dim3(128), 0, s, bt->cu_seqlens, B, bt->T, static_cast<T*>(bt->out));
+  FCV_TRY(zero_pad());
   GemmCall po{};
   po.A = ws.norm; po.lda = 1024; po.a_rows = N; po.M = N; po.N = 80; po.K = 1024; po.W = w->out_w;
   po.epi = make_epi(EPI_UNPACK, N, 80, bt->out, 0, w->out_b);

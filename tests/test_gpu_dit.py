@@ -133,6 +133,43 @@ def test_batch_composition_invariance_bit_exact():
                 assert torch.equal(packed[b:b + 1, :, :L], solo), (streaming, b)
 
 
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_empty_sequences_give_zero_output_and_leave_the_others_unchanged(dtype):
+    """Sequences whose mask is all zero (length 0: the reference's packed path gives
+    them no rows, flashinfer_dit.py:364-405, 460) come out as exact zeros, in any
+    position of the batch, and the other sequences' outputs equal those of the batch
+    without them, bit for bit -- offline and streaming, fp32 and bf16.  A batch in
+    which every sequence is empty returns an all-zero padded output."""
+    dt = getattr(torch, dtype)
+    model = _model(4, 2, dt)
+    rng = np.random.default_rng(12)
+    lengths = [0, 90, 0, 1, 130, 0]
+    T = 140
+    B = len(lengths)
+    x = torch.tensor(rng.standard_normal((B, 80, T)), device=DEV, dtype=dt)
+    mu = torch.tensor(rng.standard_normal((B, 80, T)), device=DEV, dtype=dt)
+    cond = torch.tensor(rng.standard_normal((B, 80, T)), device=DEV, dtype=dt)
+    spks = torch.tensor(rng.standard_normal((B, 80)), device=DEV, dtype=dt)
+    t = torch.tensor(rng.uniform(size=B), device=DEV, dtype=dt)
+    mask = torch.zeros(B, 1, T, device=DEV, dtype=dt)
+    for b, L in enumerate(lengths):
+        mask[b, 0, :L] = 1
+    keep = [b for b, L in enumerate(lengths) if L > 0]
+    with torch.inference_mode():
+        for streaming in (False, True):
+            y = model(x, mask, mu, t, spks, cond, streaming=streaming)
+            assert torch.isfinite(y).all()
+            for b, L in enumerate(lengths):
+                if L == 0:
+                    assert not torch.any(y[b]), (dtype, streaming, b)
+            ref = model(x[keep], mask[keep], mu[keep], t[keep], spks[keep], cond[keep], streaming=streaming)
+            assert torch.equal(y[keep], ref), (dtype, streaming)
+            # a batch with no frames at all: the whole padded output is zero
+            empty = torch.zeros_like(mask)
+            y0 = model(x, empty, mu, t, spks, cond, streaming=streaming)
+            assert y0.shape == (B, 80, T) and not torch.any(y0), (dtype, streaming)
+
+
 def test_gate_a_streaming_prefix_stability():
     """Reference Gate A (tests/gpu/test_flashinfer_streaming_estimator.py:58-89):
     with the chunk-50 mask the first floor(160/50)*50 = 150 output frames for
