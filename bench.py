@@ -1053,6 +1053,56 @@ def gemm_compare(args, req_lengths, seed, cfg):
                               "cuBLAS computes bias + bf16 output only"}), flush=True)
 
 
+def bin_times(args, req_lengths, chunk, seed, cfg):
+    """One JSON line: the config's requests dealt into ``args.bin_times`` LPT bins
+    (fcv_b200.shard.lpt_bins, as ``--gpus N`` under torchrun deals them), each bin's
+    estimator call timed alone on this one GPU (CUDA-graph replays, median of 6,
+    L2 flushed between replays).  The spread of the bins' times is the partition's
+    own imbalance, free of per-GPU clock differences between the ranks of a run."""
+    import torch
+
+    from fcv_b200.model import B200DiT
+    from fcv_b200.shard import bin_loads, lpt_bins
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    torch.manual_seed(seed)
+    model = B200DiT(depth=22).eval().to(device=device, dtype=torch.bfloat16)
+    model.finalize_weights()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    bins = lpt_bins(req_lengths, args.bin_times, chunk or None)
+
+    def time_bin(sub):
+        lengths, T, _, dev = make_batch(sub, seed, device, torch.bfloat16)
+        layout = model.layout_from_mask(dev["mask"], chunk > 0)
+        out = torch.empty(len(lengths), 80, T, dtype=torch.bfloat16, device=device)
+        run = lambda: model.forward_layout(layout, dev["x"], dev["mu"], dev["t"], dev["spks"], dev["cond"],  # noqa: E731
+                                           out=out)
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(6):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            run()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sorted(ts)[len(ts) // 2]
+
+    with ClockSampler(0) as clocks:
+        ms = [time_bin([req_lengths[i] for i in b]) for b in bins]
+    loads = bin_loads(req_lengths, bins, chunk or None)
+    print(json.dumps({"metric": "LPT bins timed alone on one GPU", "config": cfg, "bins": args.bin_times,
+                      "requests_per_bin": [len(b) for b in bins],
+                      "rows_per_bin": [2 * sum(req_lengths[i] for i in b) for b in bins],
+                      "cost_max_over_mean": max(loads) / (sum(loads) / len(loads)),
+                      "ms_per_bin": ms, "time_max_over_mean": max(ms) / (sum(ms) / len(ms)),
+                      "clocks": clocks.summary()}), flush=True)
+
+
 def ncu_case(req_lengths, chunk, seed):
     """One pass of every kernel of the path on a config's inputs, for ncu: the
     packed layout from the device mask (fcv_mask_lengths, fcv_pack_layout), one
@@ -1119,6 +1169,9 @@ def main():
     ap.add_argument("--gemm-compare", action="store_true",
                     help="the four block GEMM shapes of the config (M = its packed rows): this build's tcgen05 "
                          "GEMM against cuBLAS (torch F.linear with bias, bf16), CUDA events, L2 flushed")
+    ap.add_argument("--bin-times", type=int, default=0,
+                    help="deal the config's requests into N LPT bins (as --gpus N does) and time each bin's "
+                         "estimator call alone on one GPU")
     ap.add_argument("--ncu-case", action="store_true",
                     help="no timing: one layout from a device mask, one eager estimator call and one CFG + Euler "
                          "step on the config's inputs, each kernel launched once (a target for ncu captures)")
@@ -1182,6 +1235,11 @@ def main():
     if args.gemm_compare:
         if rank == 0:
             gemm_compare(args, req_lengths, seed, cfg)
+        return
+
+    if args.bin_times > 0:
+        if rank == 0:
+            bin_times(args, req_lengths, chunk, seed, cfg)
         return
 
     if args.impl == "reference-gpu":
