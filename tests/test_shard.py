@@ -27,6 +27,21 @@ def test_lpt_bins_partition_and_balance():
     assert lpt_bins([3000] * 16, 8) == [[k, k + 8] for k in range(8)]
 
 
+def test_benchmark_configs_shard_evenly():
+    """The request sets bench.py shards under --gpus N: config 5 (16 x 3000 frames)
+    splits into bins of exactly equal cost at 2, 4 and 8 ranks, and config 4's 128
+    log-normal requests into bins within 0.5 % of the mean cost."""
+    import bench
+
+    c5 = bench.request_lengths("5")[0]
+    c4 = bench.request_lengths("4")[0]
+    for n in (2, 4, 8):
+        loads = bin_loads(c5, lpt_bins(c5, n))
+        assert max(loads) == min(loads)
+        loads = bin_loads(c4, lpt_bins(c4, n))
+        assert max(loads) / (sum(loads) / n) < 1.005, (n, max(loads) / (sum(loads) / n))
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
