@@ -118,8 +118,10 @@ def test_ode_config3_lengths_matches_reference():
         assert np.abs(xs[i] - z["out_streaming"][i, :, :L]).max() < 1e-4, i
 
 
-def test_flop_model_matches_survey_formula():
-    # per-row constant 378,044,416 and the 4096 FLOPs per visible pair and layer
+def test_flop_model_matches_closed_form():
+    # the estimator FLOPs per NFE in closed form: 378,044,416 per packed row (22 blocks of
+    # 2^24 in the four block GEMMs, plus input projection, the two convolutions and
+    # proj_out), 4096 per visible (q, k) pair and block, and the time MLP and AdaLN per sequence
     f1 = O.estimator_flops([1], None, 22)
     per_seq = 2 * 1024 * 137216 + 2 * (256 * 1024 + 1024 * 1024)
     assert f1 == 378044416 + 22 * 4096 * 1 + per_seq
